@@ -1,0 +1,307 @@
+"""Torch-facing attention ops over the C ABI of ``libasrback_attn.so``.
+
+Each op takes the tensors the reference has at its attention call site, checks
+them, and launches the sm_100a kernel on the current CUDA stream through
+:mod:`asrback_b200._native`. The ops allocate only their outputs (from torch's
+caching allocator, so they can be captured in a CUDA graph) plus, once per
+device, a small status word and the split-KV workspace.
+
+Reference call sites (asrback project paths):
+
+- :func:`whisper_self_attention_step`: ``DecoderLayer.forward`` step branch,
+  ``src/asrback/models/whisper.py:222-237`` (``scatter_`` then masked attend);
+- :func:`whisper_cross_attention_step`: ``whisper.py:239-240``;
+- :func:`qwen3_attention_step`: ``TextAttention.step``,
+  ``src/asrback/models/qwen3_asr.py:392-432`` with ``_project`` (``:366-372``);
+- :func:`whisper_encoder_attention`: ``MultiHeadAttention.forward``,
+  ``whisper.py:108-110``.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+from torch import Tensor
+
+from . import _native
+
+__all__ = [
+    "whisper_self_attention_step",
+    "whisper_cross_attention_step",
+    "qwen3_attention_step",
+    "whisper_encoder_attention",
+    "reserve_workspace",
+    "read_status",
+    "DeviceStatusError",
+]
+
+_DTYPES = {torch.bfloat16: _native.BF16, torch.float32: _native.F32}
+
+
+class DeviceStatusError(RuntimeError):
+    """A kernel flagged a row it could not process (see :func:`read_status`)."""
+
+
+class _DeviceState:
+    """Per-device status word and split-KV workspace (zero-filled, grown on
+    demand outside graph capture; the kernels leave its counters at zero)."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.workspace = torch.zeros(0, dtype=torch.uint8, device=device)
+
+    def workspace_for(self, nbytes: int) -> Tensor:
+        if nbytes > self.workspace.numel():
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(
+                    "asrback_b200: the split-KV workspace must grow during CUDA graph "
+                    "capture; run the step once before capturing it (CapturedGraph's "
+                    "warm-up does) or call reserve_workspace() first"
+                )
+            self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.status.device)
+        return self.workspace
+
+
+_states: dict[int, _DeviceState] = {}
+_states_lock = threading.Lock()
+
+
+def _state(device: torch.device) -> _DeviceState:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    state = _states.get(index)
+    if state is None:
+        with _states_lock:
+            state = _states.get(index)
+            if state is None:
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError(
+                        "asrback_b200: first call on a device happened during CUDA graph "
+                        "capture; warm the step up first"
+                    )
+                state = _states[index] = _DeviceState(torch.device("cuda", index))
+    return state
+
+
+def _dtype_code(*tensors: Tensor) -> int:
+    dtype = tensors[0].dtype
+    for tensor in tensors:
+        if tensor.dtype != dtype:
+            raise TypeError(f"asrback_b200: mixed dtypes {dtype} and {tensor.dtype}")
+        if not tensor.is_cuda:
+            raise ValueError("asrback_b200: tensors must be on a CUDA device")
+    if dtype not in _DTYPES:
+        raise TypeError(f"asrback_b200: dtype {dtype} is not supported (bfloat16, float32)")
+    return _DTYPES[dtype]
+
+
+def _heads(t: Tensor, name: str) -> Tensor:
+    """``(B, H, D)`` view of a ``(B, H, D)`` or ``(B, H, 1, D)`` tensor."""
+    if t.dim() == 4:
+        if t.shape[2] != 1:
+            raise ValueError(f"asrback_b200: {name} must hold one token per row, got {tuple(t.shape)}")
+        t = t[:, :, 0]
+    if t.dim() != 3 or t.stride(-1) != 1:
+        raise ValueError(f"asrback_b200: {name} must be (batch, heads, head_dim) with unit last stride")
+    return t
+
+
+def _cache(t: Tensor, name: str) -> Tensor:
+    """A ``(B, H, L, D)`` cache view whose rows of one head are contiguous."""
+    if t.dim() != 4 or t.stride(-1) != 1 or t.stride(2) != t.shape[3]:
+        raise ValueError(
+            f"asrback_b200: {name} must be (batch, heads, length, head_dim) with contiguous rows"
+        )
+    return t
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def reserve_workspace(device: torch.device | int | str, batch: int, heads: int, head_dim: int,
+                      max_keys: int) -> None:
+    """Grows the device's split-KV workspace to cover calls up to these sizes,
+    so no later call (e.g. inside graph capture) needs to grow it."""
+    device = torch.device(device) if not isinstance(device, torch.device) else device
+    if device.type != "cuda":
+        device = torch.device("cuda", device.index if device.index is not None else 0)
+    lib = _native.load()
+    with torch.cuda.device(device):
+        need = lib.asrback_decode_workspace_bytes(batch, heads, head_dim, max_keys)
+        _state(device).workspace_for(need)
+
+
+def _workspace(state: _DeviceState, batch: int, heads: int, head_dim: int, max_keys: int):
+    lib = _native.load()
+    need = lib.asrback_decode_workspace_bytes(batch, heads, head_dim, max_keys)
+    workspace = state.workspace_for(need)
+    return workspace.data_ptr() if workspace.numel() else None, workspace.numel()
+
+
+def read_status(device: torch.device | int | None = None, clear: bool = True) -> int:
+    """The device's status bits (``_native.STATUS_*``) set by kernels since the
+    last clear. Synchronizes with the device, so never call it inside capture."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif not isinstance(device, torch.device):
+        device = torch.device("cuda", device)
+    state = _state(device)
+    value = int(state.status.item())
+    if clear and value:
+        state.status.zero_()
+    return value
+
+
+def whisper_self_attention_step(query: Tensor, key: Tensor, value: Tensor, key_cache: Tensor,
+                                value_cache: Tensor, positions: Tensor,
+                                scale: float | None = None) -> Tensor:
+    """Writes each row's ``key``/``value`` into the caches at ``positions[b]``
+    and attends with ``query`` to keys ``0..positions[b]``.
+
+    ``query``/``key``/``value``: ``(B, H, D)`` or ``(B, H, 1, D)`` (the
+    reference's ``_split_heads`` views); caches ``(B, H, L, D)`` views of
+    ``DecoderCache``; ``positions`` ``(B,)`` int64. Returns ``(B, 1, H*D)``, the
+    layout ``attend`` hands to ``out_proj``.
+    """
+    query, key, value = _heads(query, "query"), _heads(key, "key"), _heads(value, "value")
+    key_cache, value_cache = _cache(key_cache, "key_cache"), _cache(value_cache, "value_cache")
+    dtype = _dtype_code(query, key, value, key_cache, value_cache)
+    batch, heads, head_dim = query.shape
+    if key.shape != query.shape or value.shape != query.shape:
+        raise ValueError("asrback_b200: query, key and value shapes differ")
+    if key.stride() != value.stride():
+        raise ValueError("asrback_b200: key and value must share strides")
+    if key_cache.shape[:2] != (batch, heads) or key_cache.shape[3] != head_dim:
+        raise ValueError(f"asrback_b200: cache {tuple(key_cache.shape)} does not match query {tuple(query.shape)}")
+    if value_cache.shape != key_cache.shape or value_cache.stride() != key_cache.stride():
+        raise ValueError("asrback_b200: key and value caches differ in shape or strides")
+    if positions.dtype != torch.int64 or positions.shape != (batch,) or positions.device != query.device:
+        raise ValueError("asrback_b200: positions must be (batch,) int64 on the query's device")
+    positions = positions.contiguous()
+    length = key_cache.shape[2]
+    out = torch.empty((batch, 1, heads * head_dim), dtype=query.dtype, device=query.device)
+    state = _state(query.device)
+    ws, ws_bytes = _workspace(state, batch, heads, head_dim, length)
+    _native.call(
+        "asrback_whisper_self_attention_step",
+        dtype, batch, heads, head_dim, length,
+        query.data_ptr(), query.stride(0), query.stride(1),
+        key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1),
+        key_cache.data_ptr(), value_cache.data_ptr(), key_cache.stride(0), key_cache.stride(1),
+        positions.data_ptr(),
+        out.data_ptr(), heads * head_dim, head_dim,
+        scale if scale is not None else 1.0 / math.sqrt(head_dim),
+        ws, ws_bytes, state.status.data_ptr(), _stream(query.device),
+    )
+    return out
+
+
+def whisper_cross_attention_step(query: Tensor, key_cache: Tensor, value_cache: Tensor,
+                                 scale: float | None = None) -> Tensor:
+    """Unmasked attention of one query per row over the window's encoder keys.
+    ``query`` ``(B, H, D)`` or ``(B, H, 1, D)``; caches ``(B, H, S, D)``.
+    Returns ``(B, 1, H*D)``."""
+    query = _heads(query, "query")
+    key_cache, value_cache = _cache(key_cache, "key_cache"), _cache(value_cache, "value_cache")
+    dtype = _dtype_code(query, key_cache, value_cache)
+    batch, heads, head_dim = query.shape
+    if key_cache.shape[:2] != (batch, heads) or key_cache.shape[3] != head_dim:
+        raise ValueError(f"asrback_b200: cache {tuple(key_cache.shape)} does not match query {tuple(query.shape)}")
+    if value_cache.shape != key_cache.shape or value_cache.stride() != key_cache.stride():
+        raise ValueError("asrback_b200: key and value caches differ in shape or strides")
+    length = key_cache.shape[2]
+    out = torch.empty((batch, 1, heads * head_dim), dtype=query.dtype, device=query.device)
+    state = _state(query.device)
+    ws, ws_bytes = _workspace(state, batch, heads, head_dim, length)
+    _native.call(
+        "asrback_whisper_cross_attention_step",
+        dtype, batch, heads, head_dim, length,
+        query.data_ptr(), query.stride(0), query.stride(1),
+        key_cache.data_ptr(), value_cache.data_ptr(), key_cache.stride(0), key_cache.stride(1),
+        out.data_ptr(), heads * head_dim, head_dim,
+        scale if scale is not None else 1.0 / math.sqrt(head_dim),
+        ws, ws_bytes, state.status.data_ptr(), _stream(query.device),
+    )
+    return out
+
+
+def qwen3_attention_step(qkv: Tensor, q_norm_weight: Tensor, k_norm_weight: Tensor, eps: float,
+                         cos: Tensor, sin: Tensor, positions: Tensor, keys: Tensor, values: Tensor,
+                         heads: int, kv_heads: int, scale: float | None = None) -> Tensor:
+    """Qwen3 attention for one token per row, from ``qkv_proj``'s output to
+    ``o_proj``'s input: q/k RMSNorm + RoPE at ``positions``, the key/value
+    written into ``keys``/``values`` ``(B, L, kv_heads, D)`` at each row's
+    position, then grouped-query attention over keys ``0..positions[b]``.
+    ``cos``/``sin`` are the full ``(table_length, D)`` tables. Returns
+    ``(B, heads*D)``."""
+    dtype = _dtype_code(qkv, q_norm_weight, k_norm_weight, cos, sin, keys, values)
+    if qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise ValueError("asrback_b200: qkv must be (batch, width) with unit last stride")
+    batch = qkv.shape[0]
+    if keys.dim() != 4:
+        raise ValueError("asrback_b200: keys must be (batch, length, kv_heads, head_dim)")
+    _, length, kvh, head_dim = keys.shape
+    if kvh != kv_heads or qkv.shape[1] != (heads + 2 * kv_heads) * head_dim:
+        raise ValueError("asrback_b200: qkv width or cache heads do not match heads/kv_heads")
+    if keys.shape[0] != batch or values.shape != keys.shape or values.stride() != keys.stride():
+        raise ValueError("asrback_b200: keys/values shapes or strides differ from the batch")
+    if keys.stride(3) != 1 or keys.stride(2) != head_dim or keys.stride(1) != kv_heads * head_dim:
+        raise ValueError("asrback_b200: each cache row (position) must be contiguous kv_heads x head_dim")
+    for table in (cos, sin):
+        if table.dim() != 2 or table.shape[1] != head_dim or table.stride(1) != 1:
+            raise ValueError("asrback_b200: cos/sin must be (table_length, head_dim)")
+    if cos.stride(0) != sin.stride(0) or cos.shape != sin.shape:
+        raise ValueError("asrback_b200: cos and sin must share shape and strides")
+    for weight in (q_norm_weight, k_norm_weight):
+        if weight.shape != (head_dim,) or not weight.is_contiguous():
+            raise ValueError("asrback_b200: norm weights must be contiguous (head_dim,)")
+    if positions.dtype != torch.int64 or positions.shape != (batch,) or positions.device != qkv.device:
+        raise ValueError("asrback_b200: positions must be (batch,) int64 on qkv's device")
+    positions = positions.contiguous()
+    out = torch.empty((batch, heads * head_dim), dtype=qkv.dtype, device=qkv.device)
+    state = _state(qkv.device)
+    ws, ws_bytes = _workspace(state, batch, heads, head_dim, length)
+    _native.call(
+        "asrback_qwen3_attention_step",
+        dtype, batch, heads, kv_heads, head_dim, length,
+        qkv.data_ptr(), qkv.stride(0),
+        q_norm_weight.data_ptr(), k_norm_weight.data_ptr(), float(eps),
+        cos.data_ptr(), sin.data_ptr(), cos.stride(0), cos.shape[0],
+        positions.data_ptr(),
+        keys.data_ptr(), values.data_ptr(), keys.stride(0),
+        out.data_ptr(), out.stride(0),
+        scale if scale is not None else 1.0 / math.sqrt(head_dim),
+        ws, ws_bytes, state.status.data_ptr(), _stream(qkv.device),
+    )
+    return out
+
+
+def whisper_encoder_attention(q: Tensor, k: Tensor, v: Tensor, scale: float | None = None) -> Tensor:
+    """Non-causal self-attention over ``(B, H, S, D)`` views sharing strides
+    (the reference's ``_split_heads`` of ``(B, S, H*D)`` projections). Returns
+    ``(B, S, H*D)``, the layout ``attend`` hands to ``out_proj``."""
+    dtype = _dtype_code(q, k, v)
+    if q.dim() != 4 or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("asrback_b200: q, k, v must be (batch, heads, length, head_dim) of one shape")
+    if q.stride() != k.stride() or q.stride() != v.stride():
+        raise ValueError("asrback_b200: q, k and v must share strides")
+    if q.stride(3) != 1:
+        raise ValueError("asrback_b200: head_dim must have unit stride")
+    batch, heads, length, head_dim = q.shape
+    out = torch.empty((batch, length, heads * head_dim), dtype=q.dtype, device=q.device)
+    view = out.view(batch, length, heads, head_dim).transpose(1, 2)
+    if view.stride() != q.stride():
+        # Inputs not in the (B, S, H*D) projection layout: lay q/k/v out that way.
+        q, k, v = (t.transpose(1, 2).contiguous().transpose(1, 2) for t in (q, k, v))
+    state = _state(q.device)
+    _native.call(
+        "asrback_whisper_encoder_attention",
+        dtype, batch, heads, head_dim, length,
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+        q.stride(0), q.stride(1), q.stride(2),
+        scale if scale is not None else 1.0 / math.sqrt(head_dim),
+        state.status.data_ptr(), _stream(q.device),
+    )
+    return out

@@ -1,0 +1,822 @@
+// Split-KV decode attention for one query token per row, sm_100a.
+//
+// One template serves the three decode call sites of asrback:
+//   kWhisperSelf  - DecoderLayer.forward step branch (whisper.py:222-237):
+//                   the step's key/value are written at positions[b] and the
+//                   row attends to keys 0..positions[b];
+//   kWhisperCross - the cross-attention call (whisper.py:239-240): all keys;
+//   kQwen3        - TextAttention.step (qwen3_asr.py:392-432): q/k RMSNorm and
+//                   rotate-half RoPE (qwen3_asr.py:366-372) in the prologue,
+//                   the key/value write (:409-411), then grouped-query
+//                   attention, query head h reading key/value head h / QPK.
+//
+// Work split. A CTA owns one row b, one group of G key/value heads and one
+// chunk of key positions (a "split"). Its keys stream through shared memory
+// in tiles of TP positions x G heads x D, each tile one contiguous block of
+// the cache moved by the TMA engine (cp.async.bulk) into a STAGES-deep ring
+// guarded by mbarriers; one producer warp issues the copies, the consumer
+// warps compute. Only the positions a row has written are read (positions[b]
+// is read on the device, so the launch shape depends only on the cache view).
+//
+// Compute. LPK = D/8 lanes share a key row, each lane holding eight elements
+// (16 bytes of bf16); a warp covers KPW = 32/LPK keys per pass. Scores are
+// reduced with xor-shuffles inside the LPK lanes and folded into an online
+// softmax (base-2, the scale pre-multiplied by log2 e) once per tile. The key
+// at the row's own position (the one this step writes) is taken from
+// registers, so the cache write and the tile reads never overlap.
+//
+// Splits. A row's splits each leave (m, l, o) partials in the workspace; the
+// last CTA of the row to finish (an atomic counter, re-armed to zero by that
+// CTA) merges them and writes the output. A row with a single active split
+// writes its output directly.
+#include <cfloat>
+#include <cstdio>
+#include <cstdlib>
+
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace asrback {
+
+enum DecodeMode { kWhisperSelf = 0, kWhisperCross = 1, kQwen3 = 2 };
+
+constexpr int kMaxSplits = 64;
+
+struct DecodeParams {
+  // query (Whisper): element (b, h, d) at q[b*q_sb + h*q_sh + d]
+  const void* q;
+  int64_t q_sb, q_sh;
+  // the step's new key/value (Whisper self): (b, h, d) at [b*kn_sb + h*kn_sh + d]
+  const void* k_new;
+  const void* v_new;
+  int64_t kn_sb, kn_sh;
+  // caches: element (b, kv head h, position p, d) at [b*c_sb + h*c_sh + p*c_sp + d]
+  void* k_cache;
+  void* v_cache;
+  int64_t c_sb, c_sh, c_sp;
+  const int64_t* positions;  // (batch,) or null for a fixed key count
+  int length;                // cross: key count; self/Qwen3: cache view length
+  void* out;                 // (b, q head h, d) at out[b*o_sb + h*o_sh + d]
+  int64_t o_sb, o_sh;
+  float scale_log2;          // softmax scale * log2(e)
+  int groups;                // key/value head groups (grid.y)
+  int chunk;                 // key positions per split
+  int num_splits;            // grid.x
+  float* partial;            // workspace partials
+  int* counters;             // workspace counters, one per (row, group)
+  int32_t* status;           // device status word (may be null)
+  // Qwen3 prologue
+  const void* qkv;
+  int64_t qkv_sb;
+  const void* q_norm_w;
+  const void* k_norm_w;
+  float eps;
+  const void* cos;
+  const void* sin;
+  int64_t table_s;
+  int q_heads;
+  int kv_heads;
+};
+
+template <typename T, int D, int G, int QPK, int WPH, int TP, int STAGES, int MODE>
+struct DecodeConfig {
+  static constexpr int LPK = D / 8;
+  static constexpr int KPW = 32 / LPK;
+  static constexpr int NP = TP / (WPH * KPW);
+  static constexpr int CWARPS = G * WPH;
+  static constexpr int CTHREADS = CWARPS * 32;
+  static constexpr int THREADS = CTHREADS + 32;
+  static constexpr int QH = G * QPK;
+  static constexpr int ROW_BYTES = G * D * (int)sizeof(T);
+  static constexpr int TILE_BYTES = TP * ROW_BYTES;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = STAGES * TILE_BYTES;
+  static constexpr int OFF_MERGE = 2 * STAGES * TILE_BYTES;
+  static constexpr int MERGE_FLOATS = CWARPS * QPK * (D + 2);
+  static constexpr int OFF_WEIGHTS = OFF_MERGE + MERGE_FLOATS * 4;
+  static constexpr int OFF_BAR = (OFF_WEIGHTS + QH * kMaxSplits * 4 + 15) / 16 * 16;
+  static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8 + 16;
+  static_assert(NP >= 1 && NP * WPH * KPW == TP, "tile must split evenly over warps");
+  static_assert(LPK >= 1 && LPK <= 32 && (32 % LPK) == 0, "head_dim must be 8..256");
+  static_assert(TILE_BYTES % 16 == 0, "bulk copies move 16-byte multiples");
+};
+
+template <int LPK>
+__device__ __forceinline__ float group_sum(float x) {
+#pragma unroll
+  for (int off = LPK / 2; off >= 1; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  return x;
+}
+
+// Per-head RMSNorm then rotate-half RoPE of one head row held as lane slices
+// (LPK = D/8 lanes per row). Rounds like the reference's elementwise ops in T:
+// F.rms_norm rounds x * rsqrt(mean(x^2) + eps) * w once; the rotation rounds
+// x*cos, rotated*sin and their sum (each torch op rounds its result).
+template <typename T, int D>
+__device__ __forceinline__ void norm_rope(float* x, const T* weight, const T* cos_row,
+                                          const T* sin_row, float eps, int c) {
+  using S = Slice<T, D>;
+  constexpr int LPK = D / 8;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss = fmaf(x[j], x[j], ss);
+  ss = group_sum<LPK>(ss);
+  const float r = rsqrtf(ss / (float)D + eps);
+  float w[8], cs[8], sn[8];
+  S::load_global_nc(weight, c, w);
+  S::load_global_nc(cos_row, c, cs);
+  S::load_global_nc(sin_row, c, sn);
+  float y[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) y[j] = S::round(__fmul_rn(__fmul_rn(x[j], r), w[j]));
+  float partner[8];
+  bool first_half[8];
+  if constexpr (sizeof(T) == 2) {
+    // Element 8c+j pairs with 8c+j +- D/2, held by lane c ^ (LPK/2).
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      partner[j] = __shfl_xor_sync(0xffffffffu, y[j], LPK / 2);
+      first_half[j] = c < LPK / 2;
+    }
+  } else {
+    // f32 slices hold 4c+j and D/2+4c+j in the same lane.
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      partner[j] = y[j ^ 4];
+      first_half[j] = j < 4;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float rotated = first_half[j] ? -partner[j] : partner[j];
+    const float a = S::round(__fmul_rn(y[j], cs[j]));
+    const float b = S::round(__fmul_rn(rotated, sn[j]));
+    x[j] = S::round(__fadd_rn(a, b));
+  }
+}
+
+// Folds state (m2, l2, o2) into (m, l, o); m in log2 units, -inf = empty.
+__device__ __forceinline__ void merge_state(float& m, float& l, float* o, float m2, float l2,
+                                            const float* o2) {
+  const float mm = fmaxf(m, m2);
+  if (mm == -INFINITY) return;
+  const float a = fast_exp2(m - mm);
+  const float b = fast_exp2(m2 - mm);
+  l = l * a + l2 * b;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = o[j] * a + o2[j] * b;
+  m = mm;
+}
+
+template <typename T, int D, int G, int QPK, int WPH, int TP, int STAGES, int MODE>
+__global__ void __launch_bounds__(DecodeConfig<T, D, G, QPK, WPH, TP, STAGES, MODE>::THREADS)
+    decode_attention_kernel(const __grid_constant__ DecodeParams p) {
+  using C = DecodeConfig<T, D, G, QPK, WPH, TP, STAGES, MODE>;
+  using S = Slice<T, D>;
+  constexpr int LPK = C::LPK, KPW = C::KPW, NP = C::NP, QH = C::QH;
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int split = blockIdx.x;
+  const int grp = blockIdx.y;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Keys of this row: n_cached read from the cache, plus (self/Qwen3) the
+  // step's own key at index `pos`.
+  int pos = 0, n_cached, n_total;
+  if constexpr (MODE == kWhisperCross) {
+    n_cached = n_total = p.length;
+  } else {
+    const int64_t given = p.positions[b];
+    if (given < 0 || given >= p.length) {
+      if (split == 0) {
+        T* out = static_cast<T*>(p.out) + b * p.o_sb;
+        for (int i = threadIdx.x; i < QH * D; i += C::THREADS) {
+          const int h = grp * QH + i / D;
+          out[h * p.o_sh + i % D] = T(0.f);
+        }
+        if (threadIdx.x == 0 && p.status) atomicOr(p.status, ASRBACK_STATUS_POSITION);
+      }
+      return;
+    }
+    pos = static_cast<int>(given);
+    n_cached = pos;
+    n_total = pos + 1;
+  }
+  const int active = (n_total + p.chunk - 1) / p.chunk;
+  if (split >= active) return;
+  const int k0 = split * p.chunk;
+  const int k1 = min(k0 + p.chunk, n_cached);
+  const int n_tiles = k1 > k0 ? (k1 - k0 + TP - 1) / TP : 0;
+  const bool has_own_key = MODE != kWhisperCross && split == active - 1;
+  const uint64_t deadline = global_timer_ns() + kWaitBudgetNs;
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  int* last_flag = reinterpret_cast<int*>(empty + STAGES);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], C::CWARPS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int64_t head0 = (int64_t)grp * G;
+  const T* kbase = static_cast<const T*>(p.k_cache) + b * p.c_sb + head0 * p.c_sh;
+  const T* vbase = static_cast<const T*>(p.v_cache) + b * p.c_sb + head0 * p.c_sh;
+
+  if (warp == C::CWARPS) {
+    // Producer: one lane streams this split's tiles into the ring.
+    if (lane == 0) {
+      const uint64_t policy = l2_evict_first_policy();
+      for (int t = 0; t < n_tiles; ++t) {
+        const int s = t % STAGES;
+        if (t >= STAGES && !mbar_wait(&empty[s], ((t / STAGES) - 1) & 1, deadline)) {
+          if (p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+          break;
+        }
+        const int first = k0 + t * TP;
+        const int rows = min(TP, k1 - first);
+        const uint32_t bytes = static_cast<uint32_t>(rows * C::ROW_BYTES);
+        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+        bulk_g2s(smem + C::OFF_K + s * C::TILE_BYTES, kbase + first * p.c_sp, bytes, &full[s],
+                 policy);
+        bulk_g2s(smem + C::OFF_V + s * C::TILE_BYTES, vbase + first * p.c_sp, bytes, &full[s],
+                 policy);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int g = warp / WPH;   // head within the group
+  const int wh = warp % WPH;  // warp within the head
+  const int ks = lane / LPK;  // key slot within a warp pass
+  const int c = lane % LPK;   // slice of the row
+  const int kv_head = grp * G + g;
+  const bool owner = wh == 0 && ks == 0;  // lanes that hold the row's own key state
+
+  float q[QPK][8];
+  float m[QPK], l[QPK], o[QPK][8];
+#pragma unroll
+  for (int qi = 0; qi < QPK; ++qi) {
+    m[qi] = -INFINITY;
+    l[qi] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[qi][j] = 0.f;
+  }
+
+  float own_k[8], own_v[8];
+  if constexpr (MODE == kQwen3) {
+    const T* row = static_cast<const T*>(p.qkv) + b * p.qkv_sb;
+    const T* cos_row = static_cast<const T*>(p.cos) + pos * p.table_s;
+    const T* sin_row = static_cast<const T*>(p.sin) + pos * p.table_s;
+#pragma unroll
+    for (int qi = 0; qi < QPK; ++qi) {
+      const int qh = kv_head * QPK + qi;
+      S::load_global_nc(row + qh * D, c, q[qi]);
+      norm_rope<T, D>(q[qi], static_cast<const T*>(p.q_norm_w), cos_row, sin_row, p.eps, c);
+    }
+    if (has_own_key) {
+      S::load_global_nc(row + (p.q_heads + kv_head) * D, c, own_k);
+      norm_rope<T, D>(own_k, static_cast<const T*>(p.k_norm_w), cos_row, sin_row, p.eps, c);
+      S::load_global_nc(row + (p.q_heads + p.kv_heads + kv_head) * D, c, own_v);
+    }
+  } else {
+    const T* qrow = static_cast<const T*>(p.q) + b * p.q_sb + (int64_t)kv_head * p.q_sh;
+    S::load_global_nc(qrow, c, q[0]);
+    if constexpr (MODE == kWhisperSelf) {
+      if (has_own_key) {
+        const int64_t off = b * p.kn_sb + (int64_t)kv_head * p.kn_sh;
+        S::load_global_nc(static_cast<const T*>(p.k_new) + off, c, own_k);
+        S::load_global_nc(static_cast<const T*>(p.v_new) + off, c, own_v);
+      }
+    }
+  }
+#pragma unroll
+  for (int qi = 0; qi < QPK; ++qi)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[qi][j] *= p.scale_log2;
+
+  if constexpr (MODE != kWhisperCross) {
+    if (has_own_key) {
+      if (owner) {
+        const int64_t off = b * p.c_sb + (int64_t)kv_head * p.c_sh + (int64_t)pos * p.c_sp;
+        S::store(static_cast<T*>(p.k_cache) + off, c, own_k);
+        S::store(static_cast<T*>(p.v_cache) + off, c, own_v);
+      }
+#pragma unroll
+      for (int qi = 0; qi < QPK; ++qi) {
+        float dot = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dot = fmaf(q[qi][j], own_k[j], dot);
+        dot = group_sum<LPK>(dot);
+        if (owner) {
+          m[qi] = dot;
+          l[qi] = 1.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[qi][j] = own_v[j];
+        }
+      }
+    }
+  }
+
+  // Main loop over this split's tiles.
+  bool timed_out = false;
+  for (int t = 0; t < n_tiles; ++t) {
+    const int s = t % STAGES;
+    if (!mbar_wait(&full[s], (t / STAGES) & 1, deadline)) {
+      timed_out = true;
+      break;
+    }
+    const int rows = min(TP, k1 - (k0 + t * TP));
+    const T* ktile = reinterpret_cast<const T*>(smem + C::OFF_K + s * C::TILE_BYTES);
+    const T* vtile = reinterpret_cast<const T*>(smem + C::OFF_V + s * C::TILE_BYTES);
+    float sc[QPK][NP];
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const int kt = wh * KPW + ks + i * (WPH * KPW);
+      float kv[8];
+      if (kt < rows) {
+        S::load(ktile + (kt * G + g) * D, c, kv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) kv[j] = 0.f;
+      }
+#pragma unroll
+      for (int qi = 0; qi < QPK; ++qi) {
+        float dot = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dot = fmaf(q[qi][j], kv[j], dot);
+        dot = group_sum<LPK>(dot);
+        sc[qi][i] = kt < rows ? dot : -INFINITY;
+      }
+    }
+    float pr[QPK][NP];
+#pragma unroll
+    for (int qi = 0; qi < QPK; ++qi) {
+      float mt = m[qi];
+#pragma unroll
+      for (int i = 0; i < NP; ++i) mt = fmaxf(mt, sc[qi][i]);
+      const float base = mt == -INFINITY ? 0.f : mt;
+      const float alpha = fast_exp2(m[qi] - base);
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        pr[qi][i] = fast_exp2(sc[qi][i] - base);
+        sum += pr[qi][i];
+      }
+      l[qi] = l[qi] * alpha + sum;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[qi][j] *= alpha;
+      m[qi] = mt;
+    }
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const int kt = wh * KPW + ks + i * (WPH * KPW);
+      if (kt < rows) {
+        float vv[8];
+        S::load(vtile + (kt * G + g) * D, c, vv);
+#pragma unroll
+        for (int qi = 0; qi < QPK; ++qi)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[qi][j] = fmaf(pr[qi][i], vv[j], o[qi][j]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (timed_out && lane == 0 && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+
+  // Merge the KPW key slots of the warp (lanes c, c+LPK, ...).
+#pragma unroll
+  for (int off = LPK; off < 32; off <<= 1) {
+#pragma unroll
+    for (int qi = 0; qi < QPK; ++qi) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m[qi], off);
+      const float l2 = __shfl_xor_sync(0xffffffffu, l[qi], off);
+      float o2[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o2[j] = __shfl_xor_sync(0xffffffffu, o[qi][j], off);
+      merge_state(m[qi], l[qi], o[qi], m2, l2, o2);
+    }
+  }
+
+  // Merge the WPH warps of each head through shared memory.
+  if constexpr (WPH > 1) {
+    float* merge = reinterpret_cast<float*>(smem + C::OFF_MERGE);
+    if (ks == 0) {
+#pragma unroll
+      for (int qi = 0; qi < QPK; ++qi) {
+        float* slot = merge + (warp * QPK + qi) * (D + 2);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) slot[S::elem(c, j)] = o[qi][j];
+        if (c == 0) {
+          slot[D] = m[qi];
+          slot[D + 1] = l[qi];
+        }
+      }
+    }
+    named_sync(1, C::CTHREADS);
+    if (wh == 0) {
+      for (int w2 = 1; w2 < WPH; ++w2) {
+#pragma unroll
+        for (int qi = 0; qi < QPK; ++qi) {
+          const float* slot = merge + ((g * WPH + w2) * QPK + qi) * (D + 2);
+          float o2[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o2[j] = slot[S::elem(c, j)];
+          merge_state(m[qi], l[qi], o[qi], slot[D], slot[D + 1], o2);
+        }
+      }
+    }
+  }
+
+  T* out_row = static_cast<T*>(p.out) + b * p.o_sb;
+  if (active == 1) {
+    if (owner) {
+#pragma unroll
+      for (int qi = 0; qi < QPK; ++qi) {
+        const float inv = 1.f / l[qi];
+        float r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = o[qi][j] * inv;
+        S::store(out_row + (int64_t)(kv_head * QPK + qi) * p.o_sh, c, r);
+      }
+    }
+    return;
+  }
+
+  // Several splits: publish this split's partial state, then the last CTA of
+  // the (row, group) to arrive merges all of them.
+  const int unit = b * p.groups + grp;
+  float* part = p.partial + (size_t)unit * p.num_splits * QH * (D + 2);
+  if (owner) {
+#pragma unroll
+    for (int qi = 0; qi < QPK; ++qi) {
+      float* slot = part + ((size_t)split * QH + g * QPK + qi) * (D + 2);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) slot[S::elem(c, j)] = o[qi][j];
+      if (c == 0) {
+        slot[D] = m[qi];
+        slot[D + 1] = l[qi];
+      }
+    }
+  }
+  __threadfence();
+  named_sync(1, C::CTHREADS);
+  if (threadIdx.x == 0) {
+    const int previous = atomicAdd(&p.counters[unit], 1);
+    *last_flag = previous == active - 1;
+  }
+  named_sync(1, C::CTHREADS);
+  if (!*last_flag) return;
+  __threadfence();
+
+  float* weights = reinterpret_cast<float*>(smem + C::OFF_WEIGHTS);
+  for (int h = threadIdx.x; h < QH; h += C::CTHREADS) {
+    float mx = -INFINITY;
+    for (int s = 0; s < active; ++s) mx = fmaxf(mx, __ldcg(part + ((size_t)s * QH + h) * (D + 2) + D));
+    float den = 0.f;
+    for (int s = 0; s < active; ++s) {
+      const float* slot = part + ((size_t)s * QH + h) * (D + 2);
+      const float w = __ldcg(slot + D) == -INFINITY ? 0.f : fast_exp2(__ldcg(slot + D) - mx);
+      weights[h * kMaxSplits + s] = w;
+      den += w * __ldcg(slot + D + 1);
+    }
+    const float inv = 1.f / den;
+    for (int s = 0; s < active; ++s) weights[h * kMaxSplits + s] *= inv;
+  }
+  named_sync(1, C::CTHREADS);
+  for (int i = threadIdx.x; i < QH * D; i += C::CTHREADS) {
+    const int h = i / D, d = i % D;
+    float acc = 0.f;
+    for (int s = 0; s < active; ++s)
+      acc = fmaf(weights[h * kMaxSplits + s], __ldcg(part + ((size_t)s * QH + h) * (D + 2) + d), acc);
+    out_row[(int64_t)(grp * QH + h) * p.o_sh + d] = T(acc);
+  }
+  if (threadIdx.x == 0) p.counters[unit] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+namespace {
+
+// Workspace layout, the same for every entry point so that one zero-filled
+// workspace serves them all: a fixed region of kCounterCap counters (one per
+// (row, group) unit of a split call, zero between calls), then the partials of
+// the current call. Calls that do not split use no workspace.
+constexpr int kCounterCap = 16384;
+constexpr size_t kCounterBytes = kCounterCap * sizeof(int);
+
+size_t workspace_bytes_for(int units, int qh_per_unit, int head_dim, int splits) {
+  if (splits <= 1) return 0;
+  return kCounterBytes + (size_t)units * splits * qh_per_unit * (head_dim + 2) * sizeof(float);
+}
+
+// Points the call's counters and partials into `workspace` after checking it.
+int bind_workspace(DecodeParams& p, int units, int qh_per_unit, int head_dim, void* workspace,
+                   size_t have) {
+  if (p.num_splits <= 1) return ASRBACK_OK;
+  if (units > kCounterCap)
+    return fail(ASRBACK_ERR_ARGUMENT, "%d split units exceed the workspace's %d counters", units,
+                kCounterCap);
+  const size_t need = workspace_bytes_for(units, qh_per_unit, head_dim, p.num_splits);
+  if (need > have || workspace == nullptr)
+    return fail(ASRBACK_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu needed", have,
+                need);
+  p.counters = static_cast<int*>(workspace);
+  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+  return ASRBACK_OK;
+}
+
+// Optional override of the keys per split (tuning; 0 = heuristic).
+int chunk_override() {
+  static int value = [] {
+    const char* env = std::getenv("ASRBACK_SPLIT_CHUNK");
+    return env ? std::atoi(env) : 0;
+  }();
+  return value;
+}
+
+// Keys per split for `units` independent (row, group) units of at most
+// `max_keys` keys: enough CTAs for `waves` full waves of `ctas_per_sm` per SM,
+// whole tiles per split, at most kMaxSplits splits.
+void choose_split(int units, int max_keys, int tile, int ctas_per_sm, int* chunk, int* splits) {
+  const int tiles = (max_keys + tile - 1) / tile;
+  int want = 1;
+  const int override_keys = chunk_override();
+  if (override_keys > 0) {
+    int c = (override_keys + tile - 1) / tile;
+    want = (tiles + c - 1) / c;
+  } else {
+    const int target = sm_count() * ctas_per_sm * 2;
+    want = (target + units - 1) / units;
+  }
+  want = want < 1 ? 1 : want;
+  want = want > tiles ? tiles : want;
+  want = want > kMaxSplits ? kMaxSplits : want;
+  const int chunk_tiles = (tiles + want - 1) / want;
+  *chunk = chunk_tiles * tile;
+  *splits = (tiles + chunk_tiles - 1) / chunk_tiles;
+}
+
+template <typename Kernel>
+int prepare(Kernel kernel, int smem, bool* done) {
+  if (*done) return ASRBACK_OK;
+  const int rc = check_cuda(
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+      "cudaFuncSetAttribute(max dynamic shared memory)");
+  if (rc == ASRBACK_OK) *done = true;
+  return rc;
+}
+
+template <typename T, int D, int G, int QPK, int WPH, int TP, int STAGES, int MODE>
+int launch(const DecodeParams& p, int batch, cudaStream_t stream) {
+  using C = DecodeConfig<T, D, G, QPK, WPH, TP, STAGES, MODE>;
+  auto kernel = decode_attention_kernel<T, D, G, QPK, WPH, TP, STAGES, MODE>;
+  static thread_local int prepared_device = -1;
+  int device = 0;
+  cudaGetDevice(&device);
+  bool done = prepared_device == device;
+  if (int rc = prepare(kernel, C::SMEM, &done)) return rc;
+  prepared_device = device;
+  dim3 grid(p.num_splits, p.groups, batch);
+  kernel<<<grid, C::THREADS, C::SMEM, stream>>>(p);
+  return check_cuda(cudaGetLastError(), "decode attention launch");
+}
+
+// CTAs of a configuration that fit on one SM (by shared memory).
+int ctas_per_sm(int smem) {
+  const int per_sm = 228 * 1024;
+  int n = per_sm / (smem + 1024);
+  return n < 1 ? 1 : n;
+}
+
+// Configurations (tile sizes chosen so a stage is 8 KB x2 for Whisper and
+// 32 KB x2 for Qwen3, whatever the dtype; the bf16 ones set the occupancy).
+using WhisperSelfBf16 = DecodeConfig<__nv_bfloat16, 64, 1, 1, 4, 64, 4, kWhisperSelf>;
+using Qwen3Bf16 = DecodeConfig<__nv_bfloat16, 128, 8, 2, 1, 16, 3, kQwen3>;
+
+int whisper_tile(int dtype) { return dtype == ASRBACK_BF16 ? 64 : 32; }
+int whisper_ctas_per_sm() { return ctas_per_sm(WhisperSelfBf16::SMEM); }
+int qwen3_tile(int dtype) { return dtype == ASRBACK_BF16 ? 16 : 8; }
+int qwen3_ctas_per_sm() { return ctas_per_sm(Qwen3Bf16::SMEM); }
+
+int check_dtype(int dtype) {
+  if (dtype != ASRBACK_BF16 && dtype != ASRBACK_F32)
+    return fail(ASRBACK_ERR_ARGUMENT, "dtype must be ASRBACK_BF16 or ASRBACK_F32, got %d", dtype);
+  return ASRBACK_OK;
+}
+
+int check_strides_aligned(int dtype, std::initializer_list<int64_t> strides) {
+  const int64_t elem = dtype == ASRBACK_BF16 ? 2 : 4;
+  for (int64_t s : strides)
+    if (s < 0 || (s * elem) % 16 != 0)
+      return fail(ASRBACK_ERR_ARGUMENT, "every stride must be a non-negative multiple of 16 bytes");
+  return ASRBACK_OK;
+}
+
+int whisper_common(int dtype, int batch, int heads, int head_dim, int length, const void* query,
+                   int64_t q_sb, int64_t q_sh, const void* kc, const void* vc, int64_t c_sb,
+                   int64_t c_sh, const void* out, int64_t o_sb, int64_t o_sh) {
+  if (int rc = check_dtype(dtype)) return rc;
+  if (head_dim != 64)
+    return fail(ASRBACK_ERR_ARGUMENT, "head_dim must be 64 (Whisper), got %d", head_dim);
+  if (batch < 1 || heads < 1 || length < 1 || batch > 65535 || heads > 65535)
+    return fail(ASRBACK_ERR_ARGUMENT, "batch, heads and length must be positive (got %d, %d, %d)",
+                batch, heads, length);
+  if (!query || !kc || !vc || !out) return fail(ASRBACK_ERR_ARGUMENT, "null tensor pointer");
+  if (!aligned16(query) || !aligned16(kc) || !aligned16(vc) || !aligned16(out))
+    return fail(ASRBACK_ERR_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  if (c_sh < (int64_t)length * head_dim || c_sb < (int64_t)heads * c_sh)
+    return fail(ASRBACK_ERR_ARGUMENT,
+                "cache strides (%lld, %lld) do not hold (heads=%d, length=%d, head_dim=%d) rows",
+                (long long)c_sb, (long long)c_sh, heads, length, head_dim);
+  return check_strides_aligned(dtype, {q_sb, q_sh, c_sb, c_sh, o_sb, o_sh});
+}
+
+}  // namespace
+
+size_t decode_workspace_bytes(int batch, int heads, int head_dim, int max_keys) {
+  if (batch < 1 || heads < 1 || head_dim < 1 || max_keys < 1) return 0;
+  // Whisper layout: one unit per (row, head); Qwen3: one per row, all heads.
+  int chunk, splits;
+  choose_split(batch * heads, max_keys, 32, whisper_ctas_per_sm(), &chunk, &splits);
+  size_t a = workspace_bytes_for(batch * heads, 1, head_dim, splits);
+  choose_split(batch, max_keys, 8, qwen3_ctas_per_sm(), &chunk, &splits);
+  size_t b = workspace_bytes_for(batch, heads, head_dim, splits);
+  return a > b ? a : b;
+}
+
+}  // namespace asrback
+
+using namespace asrback;
+
+extern "C" {
+
+size_t asrback_decode_workspace_bytes(int batch, int heads, int head_dim, int max_keys) {
+  return decode_workspace_bytes(batch, heads, head_dim, max_keys);
+}
+
+int asrback_whisper_self_attention_step(
+    int dtype, int batch, int heads, int head_dim, int cache_length, const void* query,
+    int64_t q_stride_batch, int64_t q_stride_head, const void* key, const void* value,
+    int64_t kv_stride_batch, int64_t kv_stride_head, void* key_cache, void* value_cache,
+    int64_t cache_stride_batch, int64_t cache_stride_head, const int64_t* positions, void* out,
+    int64_t out_stride_batch, int64_t out_stride_head, float scale, void* workspace,
+    size_t workspace_bytes, int32_t* status, void* stream) {
+  if (int rc = whisper_common(dtype, batch, heads, head_dim, cache_length, query, q_stride_batch,
+                              q_stride_head, key_cache, value_cache, cache_stride_batch,
+                              cache_stride_head, out, out_stride_batch, out_stride_head))
+    return rc;
+  if (!key || !value || !positions || !aligned16(key) || !aligned16(value))
+    return fail(ASRBACK_ERR_ARGUMENT, "key, value and positions must be non-null, 16-byte aligned");
+  if (int rc = check_strides_aligned(dtype, {kv_stride_batch, kv_stride_head})) return rc;
+  DecodeParams p{};
+  p.q = query;
+  p.q_sb = q_stride_batch;
+  p.q_sh = q_stride_head;
+  p.k_new = key;
+  p.v_new = value;
+  p.kn_sb = kv_stride_batch;
+  p.kn_sh = kv_stride_head;
+  p.k_cache = key_cache;
+  p.v_cache = value_cache;
+  p.c_sb = cache_stride_batch;
+  p.c_sh = cache_stride_head;
+  p.c_sp = head_dim;
+  p.positions = positions;
+  p.length = cache_length;
+  p.out = out;
+  p.o_sb = out_stride_batch;
+  p.o_sh = out_stride_head;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.groups = heads;
+  p.status = status;
+  choose_split(batch * heads, cache_length, whisper_tile(dtype), whisper_ctas_per_sm(), &p.chunk,
+               &p.num_splits);
+  if (int rc = bind_workspace(p, batch * heads, 1, head_dim, workspace, workspace_bytes)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = dtype == ASRBACK_BF16
+               ? launch<__nv_bfloat16, 64, 1, 1, 4, 64, 4, kWhisperSelf>(p, batch, s)
+               : launch<float, 64, 1, 1, 4, 32, 4, kWhisperSelf>(p, batch, s);
+  return rc ? rc : ok();
+}
+
+int asrback_whisper_cross_attention_step(int dtype, int batch, int heads, int head_dim, int length,
+                                         const void* query, int64_t q_stride_batch,
+                                         int64_t q_stride_head, const void* key_cache,
+                                         const void* value_cache, int64_t cache_stride_batch,
+                                         int64_t cache_stride_head, void* out,
+                                         int64_t out_stride_batch, int64_t out_stride_head,
+                                         float scale, void* workspace, size_t workspace_bytes,
+                                         int32_t* status, void* stream) {
+  if (int rc = whisper_common(dtype, batch, heads, head_dim, length, query, q_stride_batch,
+                              q_stride_head, key_cache, value_cache, cache_stride_batch,
+                              cache_stride_head, out, out_stride_batch, out_stride_head))
+    return rc;
+  DecodeParams p{};
+  p.q = query;
+  p.q_sb = q_stride_batch;
+  p.q_sh = q_stride_head;
+  p.k_cache = const_cast<void*>(key_cache);
+  p.v_cache = const_cast<void*>(value_cache);
+  p.c_sb = cache_stride_batch;
+  p.c_sh = cache_stride_head;
+  p.c_sp = head_dim;
+  p.length = length;
+  p.out = out;
+  p.o_sb = out_stride_batch;
+  p.o_sh = out_stride_head;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.groups = heads;
+  p.status = status;
+  choose_split(batch * heads, length, whisper_tile(dtype), whisper_ctas_per_sm(), &p.chunk,
+               &p.num_splits);
+  if (int rc = bind_workspace(p, batch * heads, 1, head_dim, workspace, workspace_bytes)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = dtype == ASRBACK_BF16
+               ? launch<__nv_bfloat16, 64, 1, 1, 4, 64, 4, kWhisperCross>(p, batch, s)
+               : launch<float, 64, 1, 1, 4, 32, 4, kWhisperCross>(p, batch, s);
+  return rc ? rc : ok();
+}
+
+int asrback_qwen3_attention_step(int dtype, int batch, int heads, int kv_heads, int head_dim,
+                                 int cache_length, const void* qkv, int64_t qkv_stride_batch,
+                                 const void* q_norm_weight, const void* k_norm_weight, float eps,
+                                 const void* cos, const void* sin, int64_t table_stride,
+                                 int table_length, const int64_t* positions, void* key_cache,
+                                 void* value_cache, int64_t cache_stride_batch, void* out,
+                                 int64_t out_stride_batch, float scale, void* workspace,
+                                 size_t workspace_bytes, int32_t* status, void* stream) {
+  if (int rc = check_dtype(dtype)) return rc;
+  if (head_dim != 128 || kv_heads != 8 || (heads != 8 && heads != 16))
+    return fail(ASRBACK_ERR_ARGUMENT,
+                "Qwen3 attention supports head_dim 128, 8 key/value heads and 8 or 16 query heads "
+                "(got %d, %d, %d)",
+                head_dim, kv_heads, heads);
+  if (batch < 1 || batch > 65535 || cache_length < 1)
+    return fail(ASRBACK_ERR_ARGUMENT, "batch and cache_length must be positive");
+  if (table_length < cache_length)
+    return fail(ASRBACK_ERR_ARGUMENT, "RoPE tables have %d rows, fewer than the cache's %d",
+                table_length, cache_length);
+  if (!qkv || !q_norm_weight || !k_norm_weight || !cos || !sin || !positions || !key_cache ||
+      !value_cache || !out)
+    return fail(ASRBACK_ERR_ARGUMENT, "null tensor pointer");
+  for (const void* ptr : {qkv, q_norm_weight, k_norm_weight, cos, sin, (const void*)key_cache,
+                          (const void*)value_cache, (const void*)out})
+    if (!aligned16(ptr)) return fail(ASRBACK_ERR_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  if (cache_stride_batch < (int64_t)cache_length * kv_heads * head_dim)
+    return fail(ASRBACK_ERR_ARGUMENT, "cache batch stride %lld is smaller than a row (%lld)",
+                (long long)cache_stride_batch, (long long)cache_length * kv_heads * head_dim);
+  if (qkv_stride_batch < (int64_t)(heads + 2 * kv_heads) * head_dim ||
+      out_stride_batch < (int64_t)heads * head_dim || table_stride < head_dim)
+    return fail(ASRBACK_ERR_ARGUMENT, "qkv, out or table row stride is smaller than a row");
+  if (int rc = check_strides_aligned(dtype, {qkv_stride_batch, cache_stride_batch, out_stride_batch,
+                                             table_stride}))
+    return rc;
+  DecodeParams p{};
+  p.qkv = qkv;
+  p.qkv_sb = qkv_stride_batch;
+  p.q_norm_w = q_norm_weight;
+  p.k_norm_w = k_norm_weight;
+  p.eps = eps;
+  p.cos = cos;
+  p.sin = sin;
+  p.table_s = table_stride;
+  p.q_heads = heads;
+  p.kv_heads = kv_heads;
+  p.k_cache = key_cache;
+  p.v_cache = value_cache;
+  p.c_sb = cache_stride_batch;
+  p.c_sh = head_dim;
+  p.c_sp = (int64_t)kv_heads * head_dim;
+  p.positions = positions;
+  p.length = cache_length;
+  p.out = out;
+  p.o_sb = out_stride_batch;
+  p.o_sh = head_dim;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.groups = 1;
+  p.status = status;
+  choose_split(batch, cache_length, qwen3_tile(dtype), qwen3_ctas_per_sm(), &p.chunk, &p.num_splits);
+  if (int rc = bind_workspace(p, batch, heads, head_dim, workspace, workspace_bytes)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (heads == 16)
+    rc = dtype == ASRBACK_BF16 ? launch<__nv_bfloat16, 128, 8, 2, 1, 16, 3, kQwen3>(p, batch, s)
+                               : launch<float, 128, 8, 2, 1, 8, 3, kQwen3>(p, batch, s);
+  else
+    rc = dtype == ASRBACK_BF16 ? launch<__nv_bfloat16, 128, 8, 1, 1, 16, 3, kQwen3>(p, batch, s)
+                               : launch<float, 128, 8, 1, 1, 8, 3, kQwen3>(p, batch, s);
+  return rc ? rc : ok();
+}
+
+}  // extern "C"

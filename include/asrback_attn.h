@@ -1,0 +1,166 @@
+/*
+ * asrback_attn.h: C ABI of the B200 (sm_100a) attention kernels that replace
+ * the attention calls on asrback's decode and encoder hot path.
+ *
+ * Every entry point takes plain device pointers, element strides (in
+ * elements, not bytes), sizes and a CUDA stream, launches its kernels on that
+ * stream and returns at once: nothing here synchronizes, allocates device
+ * memory or reads device memory back, so every call can be recorded in a CUDA
+ * graph. Each call returns ASRBACK_OK or an error code; asrback_last_error()
+ * then holds a one-line message for the calling thread.
+ *
+ * Faults found on the device (a row position outside the cache) cannot be
+ * returned by a launch. The kernels skip that row, write zeros for it and set
+ * a bit in the caller's `status` word (device memory, int32), which the caller
+ * may read after the stream has finished.
+ *
+ * Reference call sites (paths inside the asrback project):
+ *   - asrback_whisper_self_attention_step  replaces the fixed-shape step branch
+ *     of DecoderLayer.forward, src/asrback/models/whisper.py:222-237
+ *     (scatter_ of the step's key/value at each row's position, then
+ *     MultiHeadAttention.attend with the step mask of whisper.py:262-264);
+ *   - asrback_whisper_cross_attention_step replaces the cross-attention call
+ *     whisper.py:239-240 (attend over the window's encoder keys, no mask);
+ *   - asrback_qwen3_attention_step replaces TextAttention.step between
+ *     qkv_proj and o_proj, src/asrback/models/qwen3_asr.py:392-432, with
+ *     _project (qwen3_asr.py:366-372: per-head RMSNorm of q and k, rotate-half
+ *     RoPE) and the cache write (qwen3_asr.py:409-411) fused in;
+ *   - asrback_whisper_encoder_attention replaces the unmasked SDPA call of
+ *     MultiHeadAttention.forward, whisper.py:108-110 (via attend, :102-104),
+ *     in the encoder layers (whisper.py:123-125).
+ */
+#ifndef ASRBACK_ATTN_H_
+#define ASRBACK_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ASRBACK_API __attribute__((visibility("default")))
+#else
+#define ASRBACK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types (the reference runs bfloat16 on CUDA, float32 on CPU). */
+#define ASRBACK_BF16 0
+#define ASRBACK_F32 1
+
+/* Return codes. */
+#define ASRBACK_OK 0
+#define ASRBACK_ERR_ARGUMENT 1 /* a size, stride, alignment or pointer is invalid */
+#define ASRBACK_ERR_CUDA 2     /* a CUDA call failed (launch, attribute, ...) */
+#define ASRBACK_ERR_WORKSPACE 3 /* the workspace is smaller than needed */
+
+/* Bits of the device-side status word. */
+#define ASRBACK_STATUS_POSITION 1 /* a row's position was < 0 or >= cache length */
+#define ASRBACK_STATUS_TIMEOUT 2  /* a bounded wait inside a kernel gave up */
+
+/* Version of this ABI: (major << 16) | minor. */
+ASRBACK_API int asrback_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+ASRBACK_API const char* asrback_last_error(void);
+
+/* Number of SMs of the current device (for callers sizing their work). */
+ASRBACK_API int asrback_device_sm_count(void);
+
+/*
+ * Bytes of workspace the decode entry points need for `batch` rows with
+ * `heads` query heads of `head_dim` over at most `max_keys` keys per row
+ * (cache view length). The workspace holds per-row completion counters and the
+ * partial results of split rows. It must be zero-filled before its first use;
+ * every call leaves its counters at zero again, so one workspace serves any
+ * number of calls in stream order. Calls that run concurrently on different
+ * streams need separate workspaces.
+ */
+ASRBACK_API size_t asrback_decode_workspace_bytes(int batch, int heads, int head_dim, int max_keys);
+
+/*
+ * Whisper decoder self-attention for one step (one query per row).
+ *
+ * query       (batch, heads, head_dim)  at query[b*q_stride_batch + h*q_stride_head + d]
+ * key, value  (batch, heads, head_dim)  the step's new key/value, strides kv_stride_*
+ * key_cache,  (batch, heads, cache_length, head_dim) at
+ * value_cache   [b*cache_stride_batch + h*cache_stride_head + p*head_dim + d]
+ *             (rows of one head contiguous: the layout of DecoderCache,
+ *              whisper.py:156-196, possibly narrowed to a KV bucket)
+ * positions   (batch,) int64, device: row b writes its key/value at
+ *             positions[b] and attends to keys 0..positions[b]
+ * out         (batch, heads, head_dim) at out[b*out_stride_batch + h*out_stride_head + d]
+ * scale       softmax scale (1/sqrt(head_dim) in the reference)
+ * head_dim    64 (Whisper); dtype ASRBACK_BF16 or ASRBACK_F32; all tensors
+ *             share the dtype; pointers 16-byte aligned.
+ */
+ASRBACK_API int asrback_whisper_self_attention_step(
+    int dtype, int batch, int heads, int head_dim, int cache_length,
+    const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+    const void* key, const void* value, int64_t kv_stride_batch, int64_t kv_stride_head,
+    void* key_cache, void* value_cache, int64_t cache_stride_batch, int64_t cache_stride_head,
+    const int64_t* positions,
+    void* out, int64_t out_stride_batch, int64_t out_stride_head,
+    float scale, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Whisper decoder cross-attention for one step: every row attends, without a
+ * mask, to all `length` encoder keys of its window. Layouts as above
+ * (caches (batch, heads, length, head_dim), rows of one head contiguous).
+ */
+ASRBACK_API int asrback_whisper_cross_attention_step(
+    int dtype, int batch, int heads, int head_dim, int length,
+    const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+    const void* key_cache, const void* value_cache,
+    int64_t cache_stride_batch, int64_t cache_stride_head,
+    void* out, int64_t out_stride_batch, int64_t out_stride_head,
+    float scale, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Qwen3 decoder attention for one step, between qkv_proj and o_proj.
+ *
+ * qkv          (batch, (heads + 2*kv_heads)*head_dim) at qkv[b*qkv_stride_batch + j]:
+ *              q | k | v as qkv_proj writes them (qwen3_asr.py:366-369)
+ * q_norm_weight, k_norm_weight  (head_dim,) RMSNorm weights, eps their epsilon
+ * cos, sin     RoPE tables (table_length, head_dim), row stride table_stride;
+ *              row positions[b] is used (qwen3_asr.py:507)
+ * positions    (batch,) int64, device
+ * key_cache,   (batch, cache_length, kv_heads, head_dim) at
+ * value_cache    [b*cache_stride_batch + p*kv_heads*head_dim + h*head_dim + d]
+ *              (KVCache, qwen3_asr.py:333-347, possibly narrowed to a bucket)
+ * out          (batch, heads*head_dim) at out[b*out_stride_batch + h*head_dim + d]
+ * Query head h reads key/value head h / (heads / kv_heads). head_dim 128,
+ * kv_heads 8, heads 8 or 16 (grouped-query factor 1 or 2).
+ */
+ASRBACK_API int asrback_qwen3_attention_step(
+    int dtype, int batch, int heads, int kv_heads, int head_dim, int cache_length,
+    const void* qkv, int64_t qkv_stride_batch,
+    const void* q_norm_weight, const void* k_norm_weight, float eps,
+    const void* cos, const void* sin, int64_t table_stride, int table_length,
+    const int64_t* positions,
+    void* key_cache, void* value_cache, int64_t cache_stride_batch,
+    void* out, int64_t out_stride_batch,
+    float scale, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Whisper encoder self-attention (non-causal) over `length` frames.
+ *
+ * q, k, v, out  (batch, heads, length, head_dim) at
+ *               [b*stride_batch + h*stride_head + s*stride_seq + d]; the four
+ *               tensors share the strides (the reference's transposed views
+ *               of (batch, length, heads*head_dim) projections have
+ *               stride_seq = heads*head_dim, stride_head = head_dim).
+ * head_dim 64, dtype ASRBACK_BF16; 16-byte aligned rows.
+ */
+ASRBACK_API int asrback_whisper_encoder_attention(
+    int dtype, int batch, int heads, int head_dim, int length,
+    const void* q, const void* k, const void* v, void* out,
+    int64_t stride_batch, int64_t stride_head, int64_t stride_seq,
+    float scale, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASRBACK_ATTN_H_ */

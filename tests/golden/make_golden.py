@@ -1,0 +1,312 @@
+"""Generates the golden fixtures in this folder by running the reference's own
+PyTorch modules (asrback, imported read-only) on CPU.
+
+    python tests/golden/make_golden.py [--reference /path/to/asrback]
+
+The reference imports ``asrfront`` (its audio front end), which is not
+installed; none of the code run here calls into it, so a stub module with the
+constants read at import time stands in for it. Each fixture records the
+tensors at one attention call site: what the reference's modules passed to
+``F.scaled_dot_product_attention`` and got back, plus the cache state around the
+call. Two model-level fixtures record whole greedy decoder steps (hidden states
+and argmax tokens) with weights from ``asrback_b200.synthetic.seeded_parameters``
+so that the GPU tests can rebuild the same network without the reference.
+
+Output: ``*.npz`` files; bf16 tensors are stored as their raw bits under
+``<name>__bf16`` (``tests/golden/__init__.py`` decodes them to float32).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+
+from asrback_b200.synthetic import seeded_normal, seeded_parameters  # noqa: E402
+
+
+def install_asrfront_stub() -> None:
+    """An ``asrfront`` with the module constants the reference reads at import."""
+    constants = dict(SAMPLE_RATE=16000, N_SAMPLES=480000, HOP_LENGTH=160, MAX_SAMPLES=480000,
+                     N_MELS=128)
+    stub = types.ModuleType("asrfront")
+    for name in ("whisper", "qwen3_asr", "sensevoice", "gemma4"):
+        setattr(stub, name, types.SimpleNamespace(**constants))
+
+    def unavailable(*args, **kwargs):
+        raise RuntimeError("asrfront is not installed (stub)")
+
+    stub.load = unavailable
+    sys.modules["asrfront"] = stub
+
+
+class SdpaRecorder:
+    """Wraps ``F.scaled_dot_product_attention`` and records every call."""
+
+    def __init__(self) -> None:
+        self.calls: list[dict] = []
+        self.original = F.scaled_dot_product_attention
+
+    def __enter__(self):
+        def recorded(q, k, v, attn_mask=None, *args, **kwargs):
+            out = self.original(q, k, v, attn_mask=attn_mask, *args, **kwargs)
+            self.calls.append(dict(q=q.detach().clone(), k=k.detach().clone(),
+                                   v=v.detach().clone(),
+                                   mask=None if attn_mask is None else attn_mask.detach().clone(),
+                                   out=out.detach().clone(), kwargs=dict(kwargs)))
+            return out
+
+        F.scaled_dot_product_attention = recorded
+        return self
+
+    def __exit__(self, *exc):
+        F.scaled_dot_product_attention = self.original
+
+
+def f32(t: torch.Tensor) -> np.ndarray:
+    """float32 array, or for bfloat16 tensors their raw bits (``uint16``)."""
+    t = t.detach().cpu()
+    if t.dtype == torch.bfloat16:
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return t.float().numpy()
+
+
+def save(name: str, meta: dict, **arrays) -> None:
+    path = HERE / f"{name}.npz"
+    # bfloat16 bits go under "<name>__bf16"; tests/golden/__init__.py decodes them.
+    arrays = {(f"{key}__bf16" if value.dtype == np.uint16 else key): value
+              for key, value in arrays.items()}
+    np.savez_compressed(path, meta=np.array(json.dumps(meta)), **arrays)
+    print(f"{path.name}: {path.stat().st_size / 1024:.0f} KB")
+
+
+def whisper_step(whisper, dtype: torch.dtype, tag: str) -> None:
+    """One fixed-shape decoder step (``WhisperDecoder.forward`` with
+    ``length=None``) of a 1-layer decoder: self call (scatter, then masked
+    SDPA) and cross call."""
+    config = dict(d_model=384, encoder_attention_heads=6, decoder_attention_heads=6,
+                  encoder_layers=1, decoder_layers=1, encoder_ffn_dim=64, decoder_ffn_dim=64,
+                  num_mel_bins=80, max_source_positions=40, max_target_positions=48,
+                  vocab_size=128)
+    torch.manual_seed(0)
+    model = whisper.WhisperForConditionalGeneration(config)
+    seeded_parameters(model.model.decoder, 0)
+    model = model.to(dtype)
+    batch = 4
+    positions = torch.tensor([0, 7, 20, 47])
+    cache = model.allocate_cache(batch)
+    states = seeded_normal((batch, 40, 384), 11).to(dtype)
+    with torch.no_grad():
+        model.set_encoder_output(cache, states)
+        for b, p in enumerate(positions.tolist()):
+            filled = seeded_normal((1, 6, p, 64), 100 + b, 0.5).to(dtype)
+            cache.self_keys[0, b, :, :p] = filled[0]
+            cache.self_values[0, b, :, :p] = -filled[0].flip(-1)
+        k_before = cache.self_keys[0].clone()
+        v_before = cache.self_values[0].clone()
+        tokens = torch.tensor([[3], [50], [77], [127]])
+        with SdpaRecorder() as rec:
+            model.decode(tokens, positions, cache)
+    self_call, cross_call = rec.calls
+    rows = torch.arange(batch)
+    # The attended cache is the old one with the step's rows written (scatter_).
+    expected = k_before.clone()
+    expected[rows, :, positions] = self_call["k"][rows, :, positions]
+    assert torch.equal(expected, self_call["k"])
+    save(f"whisper_step_{tag}",
+         dict(config=config, dtype=str(dtype), site="whisper.py:222-240"),
+         positions=positions.numpy(),
+         self_q=f32(self_call["q"][:, :, 0]),
+         self_k_new=f32(self_call["k"][rows, :, positions]),
+         self_v_new=f32(self_call["v"][rows, :, positions]),
+         self_k_before=f32(k_before), self_v_before=f32(v_before),
+         self_mask=self_call["mask"][:, 0, 0].numpy(),
+         self_out=f32(self_call["out"][:, :, 0]),
+         cross_q=f32(cross_call["q"][:, :, 0]), cross_k=f32(cross_call["k"]),
+         cross_v=f32(cross_call["v"]), cross_out=f32(cross_call["out"][:, :, 0]))
+
+
+def qwen3_step(qwen3, dtype: torch.dtype, tag: str) -> None:
+    """One ``TextModel.step`` (bucket-mask path) of a 1-layer Qwen3 text model
+    with 16 query / 8 key-value heads of 128."""
+    config = dict(vocab_size=64, hidden_size=256, num_hidden_layers=1, num_attention_heads=16,
+                  num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6, intermediate_size=64)
+    model = qwen3.TextModel(config)
+    seeded_parameters(model, 3)
+    model = model.to(dtype)
+    batch, length = 4, 40
+    positions = torch.tensor([0, 9, 25, 39])
+    inverse = 1.0 / (1e6 ** (torch.arange(0, 128, 2).float() / 128))
+    angles = torch.arange(length).float()[:, None] * inverse[None, :]
+    angles = torch.cat((angles, angles), dim=-1)
+    cos, sin = angles.cos().to(dtype), angles.sin().to(dtype)
+    keys = torch.zeros((1, batch, length, 8, 128), dtype=dtype)
+    values = torch.zeros_like(keys)
+    for b, p in enumerate(positions.tolist()):
+        filled = seeded_normal((p, 8, 128), 200 + b, 0.5).to(dtype)
+        keys[0, b, :p] = filled
+        values[0, b, :p] = filled.flip(-1) * 0.7
+    cache = qwen3.KVCache(keys, values)
+    k_before, v_before = keys[0].clone(), values[0].clone()
+    attention = model.layers[0].self_attn
+    captured = {}
+    hooks = [
+        attention.qkv_proj.register_forward_hook(lambda m, i, o: captured.__setitem__("qkv", o.clone())),
+        attention.o_proj.register_forward_pre_hook(lambda m, i: captured.__setitem__("out", i[0].clone())),
+    ]
+    with torch.no_grad(), SdpaRecorder() as rec:
+        model.step(torch.tensor([1, 5, 9, 63]), positions, cache, cos, sin, varlen=False)
+    for hook in hooks:
+        hook.remove()
+    (call,) = rec.calls
+    rows = torch.arange(batch)
+    expected = k_before.clone()
+    expected[rows, positions] = keys[0][rows, positions]
+    assert torch.equal(expected, keys[0])
+    save(f"qwen3_step_{tag}",
+         dict(config=config, dtype=str(dtype), site="qwen3_asr.py:366-432", rope_theta=1e6),
+         positions=positions.numpy(), qkv=f32(captured["qkv"]),
+         q_norm_weight=f32(attention.q_norm.weight), k_norm_weight=f32(attention.k_norm.weight),
+         eps=np.float64(config["rms_norm_eps"]), cos=f32(cos), sin=f32(sin),
+         k_before=f32(k_before), v_before=f32(v_before),
+         k_new=f32(keys[0][rows, positions]), v_new=f32(values[0][rows, positions]),
+         sdpa_q=f32(call["q"]), sdpa_mask=call["mask"][:, 0, 0].numpy(),
+         out=f32(captured["out"]))
+
+
+def encoder_attention(whisper, dtype: torch.dtype, tag: str) -> None:
+    """``MultiHeadAttention.forward`` (unmasked encoder self-attention)."""
+    module = whisper.MultiHeadAttention(384, 6)
+    seeded_parameters(module, 2)
+    module = module.to(dtype)
+    x = seeded_normal((1, 136, 384), 12).to(dtype)
+    with torch.no_grad(), SdpaRecorder() as rec:
+        module(x)
+    (call,) = rec.calls
+    save(f"encoder_attention_{tag}", dict(dtype=str(dtype), site="whisper.py:108-110"),
+         q=f32(call["q"]), k=f32(call["k"]), v=f32(call["v"]), out=f32(call["out"]))
+
+
+WHISPER_PREFIX = [50258, 50259, 50359, 50363]  # SOT, <|en|>, <|transcribe|>, <|notimestamps|>
+
+
+def whisper_tiny_decode(whisper) -> None:
+    """Greedy decoder steps of the Whisper-tiny architecture (fp32, seed 0) over
+    N(0,1) encoder states. Each row first takes its own prefix one token per
+    step (batch-of-one views of its cache row), so the batched steps that follow
+    run at ragged positions."""
+    config = dict(d_model=384, encoder_attention_heads=6, decoder_attention_heads=6,
+                  encoder_layers=4, decoder_layers=4, encoder_ffn_dim=1536, decoder_ffn_dim=1536,
+                  num_mel_bins=80, max_source_positions=1500, max_target_positions=448,
+                  vocab_size=51865)
+    model = whisper.WhisperForConditionalGeneration(config)
+    seeded_parameters(model.model.decoder, 0)
+    model.eval()
+    batch, steps = 8, 48
+    offsets = [4, 9, 17, 30, 5, 60, 12, 100]
+    prompts = []
+    for b, off in enumerate(offsets):
+        extra = seeded_normal((off - 4,), 300 + b).abs().mul(7000).long().clamp(max=50256).tolist()
+        prompts.append(WHISPER_PREFIX + extra)
+    cache = model.allocate_cache(batch)
+    with torch.no_grad():
+        model.set_encoder_output(cache, seeded_normal((batch, 1500, 384), 21))
+        for b, prompt in enumerate(prompts):
+            row = cache.rows(b, b + 1)
+            for p, token in enumerate(prompt):
+                model.decode(torch.tensor([[token]]), torch.tensor([p]), row)
+        positions = torch.tensor(offsets)
+        tokens = torch.tensor([[p[-1]] for p in prompts])
+        positions -= 1  # the prompt's last token is re-fed at its own position
+        hidden_all, argmax_all, tokens_all, positions_all = [], [], [], []
+        for _ in range(steps):
+            hidden = model.decode(tokens, positions, cache)[:, -1]
+            logits = model.logits(hidden).float()
+            choice = logits.argmax(dim=-1)
+            hidden_all.append(f32(hidden))
+            argmax_all.append(choice.numpy())
+            tokens_all.append(tokens[:, 0].numpy())
+            positions_all.append(positions.numpy().copy())
+            tokens = choice[:, None]
+            positions = positions + 1
+    save("whisper_tiny_decode",
+         dict(config=config, seed=0, encoder_seed=21, prompts=prompts, steps=steps,
+              site="whisper.py:942-960 (decode + logits + argmax)"),
+         tokens=np.stack(tokens_all, 1), positions=np.stack(positions_all, 1),
+         argmax=np.stack(argmax_all, 1), hidden=np.stack(hidden_all, 1))
+
+
+def qwen3_small_decode(qwen3) -> None:
+    """Greedy ``TextModel.step`` calls of a 2-layer Qwen3 text model (fp32,
+    seed 3), rows prefilled one position per step to ragged lengths."""
+    config = dict(vocab_size=4096, hidden_size=512, num_hidden_layers=2, num_attention_heads=16,
+                  num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6, intermediate_size=1024)
+    model = qwen3.TextModel(config)
+    lm_head = torch.nn.Linear(512, 4096, bias=False)
+    seeded_parameters(model, 3)
+    seeded_parameters(lm_head, 4)
+    batch, steps, length = 4, 32, 1024
+    offsets = [20, 45, 7, 90]
+    prompts = [seeded_normal((off,), 400 + b).abs().mul(1500).long().clamp(max=4095).tolist()
+               for b, off in enumerate(offsets)]
+    inverse = 1.0 / (1e6 ** (torch.arange(0, 128, 2).float() / 128))
+    angles = torch.arange(length).float()[:, None] * inverse[None, :]
+    angles = torch.cat((angles, angles), dim=-1)
+    cos, sin = angles.cos(), angles.sin()
+    shape = (2, batch, length, 8, 128)
+    cache = qwen3.KVCache(torch.zeros(shape), torch.zeros(shape))
+    with torch.no_grad():
+        for b, prompt in enumerate(prompts):
+            row = qwen3.KVCache(cache.keys[:, b:b + 1], cache.values[:, b:b + 1])
+            for p, token in enumerate(prompt[:-1]):
+                model.step(torch.tensor([token]), torch.tensor([p]), row, cos, sin, varlen=False)
+        tokens = torch.tensor([p[-1] for p in prompts])
+        positions = torch.tensor(offsets) - 1
+        hidden_all, argmax_all, tokens_all, positions_all = [], [], [], []
+        for _ in range(steps):
+            hidden = model.step(tokens, positions, cache, cos, sin, varlen=False)
+            choice = lm_head(hidden).argmax(dim=-1)
+            hidden_all.append(f32(hidden))
+            argmax_all.append(choice.numpy())
+            tokens_all.append(tokens.numpy())
+            positions_all.append(positions.numpy().copy())
+            tokens = choice
+            positions = positions + 1
+    save("qwen3_small_decode",
+         dict(config=config, seed=3, lm_head_seed=4, prompts=prompts, steps=steps,
+              rope_theta=1e6, site="qwen3_asr.py:494-524 (TextModel.step) + lm_head argmax"),
+         tokens=np.stack(tokens_all, 1), positions=np.stack(positions_all, 1),
+         argmax=np.stack(argmax_all, 1), hidden=np.stack(hidden_all, 1))
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--reference", default="/root/reference",
+                        help="checkout of sjjeong94/asrback (read-only)")
+    args = parser.parse_args()
+    install_asrfront_stub()
+    sys.path.insert(0, str(Path(args.reference) / "src"))
+    from asrback.models import qwen3_asr as qwen3  # noqa: E402
+    from asrback.models import whisper  # noqa: E402
+
+    torch.set_num_threads(8)
+    for dtype, tag in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
+        whisper_step(whisper, dtype, tag)
+        qwen3_step(qwen3, dtype, tag)
+        encoder_attention(whisper, dtype, tag)
+    whisper_tiny_decode(whisper)
+    qwen3_small_decode(qwen3)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,120 @@
+"""The C ABI library loads and exports what include/asrback_attn.h declares;
+host-side argument checks reject bad calls before any launch (no GPU needed)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from asrback_b200 import _native
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "asrback_attn.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"ASRBACK_API\s+[\w\s\*]+?\b(asrback_\w+)\s*\(", text)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _native.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "asrback_whisper_self_attention_step" in names
+    assert "asrback_qwen3_attention_step" in names
+    assert len(names) == len(set(names))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    # ... and the binding types every one of them.
+    assert set(declared_functions()) <= set(_native.SIGNATURES)
+
+
+def test_abi_version(lib):
+    assert lib.asrback_abi_version() >> 16 == _native.ABI_MAJOR
+
+
+def test_workspace_size_is_host_only(lib):
+    small = lib.asrback_decode_workspace_bytes(64, 20, 64, 448)
+    assert small >= 256
+    big = lib.asrback_decode_workspace_bytes(1, 20, 64, 1500)
+    assert big > 256  # one row: keys split over many CTAs, partials needed
+    assert lib.asrback_decode_workspace_bytes(0, 20, 64, 448) == 0
+
+
+def _self_call(lib, **overrides):
+    args = dict(dtype=_native.BF16, batch=2, heads=20, head_dim=64, length=448,
+                q=16, k=16, v=16, kc=16, vc=16, pos=16, out=16)
+    args.update(overrides)
+    return lib.asrback_whisper_self_attention_step(
+        args["dtype"], args["batch"], args["heads"], args["head_dim"], args["length"],
+        args["q"], 1280, 64, args["k"], args["v"], 1280, 64,
+        args["kc"], args["vc"], 20 * 448 * 64, 448 * 64, args["pos"],
+        args["out"], 1280, 64, 0.125, None, 0, None, None)
+
+
+@pytest.mark.parametrize("overrides,fragment", [
+    (dict(head_dim=32), "head_dim must be 64"),
+    (dict(dtype=7), "dtype"),
+    (dict(batch=0), "positive"),
+    (dict(q=0), "null"),
+    (dict(q=8), "aligned"),
+    (dict(pos=0), "positions"),
+])
+def test_invalid_arguments_are_rejected_on_the_host(lib, overrides, fragment):
+    rc = _self_call(lib, **overrides)
+    assert rc == _native.ERR_ARGUMENT
+    assert fragment in lib.asrback_last_error().decode()
+
+
+def test_missing_workspace_is_rejected(lib):
+    # One row over 1500 keys splits, so a workspace is required.
+    rc = lib.asrback_whisper_cross_attention_step(
+        _native.BF16, 1, 20, 64, 1500, 16, 1280, 64, 16, 16, 20 * 1500 * 64, 1500 * 64,
+        16, 1280, 64, 0.125, None, 0, None, None)
+    assert rc == _native.ERR_WORKSPACE
+
+
+def test_qwen3_shape_limits(lib):
+    rc = lib.asrback_qwen3_attention_step(
+        _native.BF16, 4, 16, 4, 128, 1024, 16, 4096, 16, 16, 1e-6, 16, 16, 128, 1024, 16,
+        16, 16, 1024 * 1024, 16, 2048, 0.088, None, 0, None, None)
+    assert rc == _native.ERR_ARGUMENT
+    assert "8 key/value heads" in lib.asrback_last_error().decode()
+
+
+def test_ops_refuse_cpu_tensors():
+    """No CPU fallback: the product path raises on host tensors."""
+    import torch
+
+    from asrback_b200 import attention
+
+    q = torch.zeros(2, 20, 64)
+    cache = torch.zeros(2, 20, 1500, 64)
+    with pytest.raises(ValueError, match="CUDA"):
+        attention.whisper_cross_attention_step(q, cache, cache)
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setenv("ASRBACK_LIBRARY", str(tmp_path / "absent.so"))
+    with pytest.raises(_native.NativeError, match="no CPU or PyTorch fallback"):
+        _native.load()
+
+
+def test_ctypes_signatures_cover_argument_counts(lib):
+    header = HEADER.read_text()
+    for name, (argtypes, _) in _native.SIGNATURES.items():
+        match = re.search(rf"ASRBACK_API[\w\s\*]+?\b{name}\s*\(([^;]*)\);", header)
+        assert match, name
+        params = [p for p in match.group(1).split(",") if p.strip() and p.strip() != "void"]
+        assert len(params) == len(argtypes), name
+        assert isinstance(getattr(lib, name), ctypes._CFuncPtr)
