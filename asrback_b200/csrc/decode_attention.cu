@@ -536,13 +536,11 @@ int bind_workspace(DecodeParams& p, int units, int qh_per_unit, int head_dim, vo
   return ASRBACK_OK;
 }
 
-// Optional override of the keys per split (tuning; 0 = heuristic).
+// Optional override of the keys per split (tuning sweeps; unset or 0 = the
+// heuristic). Read at every call so that one process can sweep it.
 int chunk_override() {
-  static int value = [] {
-    const char* env = std::getenv("ASRBACK_SPLIT_CHUNK");
-    return env ? std::atoi(env) : 0;
-  }();
-  return value;
+  const char* env = std::getenv("ASRBACK_SPLIT_CHUNK");
+  return env ? std::atoi(env) : 0;
 }
 
 // Keys per split for `units` independent (row, group) units of at most

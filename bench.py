@@ -90,57 +90,70 @@ def attention_bytes(positions: np.ndarray) -> tuple[float, float]:
 # ---------------------------------------------------------------- clocks ----
 
 class ClockSampler:
-    """nvidia-smi samples of this GPU's clocks and throttle reasons."""
+    """Samples this GPU's SM clock and clock-event (throttle) reasons through
+    NVML every 5 ms while the timed region runs (read-only queries)."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {  # NVML clocks-event reason bits
+        0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+        0x4: "sw_power_cap",
+    }
 
     def __init__(self, uuid: str | None) -> None:
         self.uuid = uuid
-        self.proc = None
+        self.samples: list[tuple[float, float, int]] = []
+        self.error = None
+
+    def _handle(self, nvml):
+        count = nvml.nvmlDeviceGetCount()
+        for i in range(count):
+            handle = nvml.nvmlDeviceGetHandleByIndex(i)
+            uuid = nvml.nvmlDeviceGetUUID(handle)
+            uuid = uuid.decode() if isinstance(uuid, bytes) else uuid
+            if self.uuid and self.uuid.lower().replace("gpu-", "") in uuid.lower():
+                return handle
+        return nvml.nvmlDeviceGetHandleByIndex(0) if count == 1 else None
+
+    def _run(self):
+        import threading  # noqa: F401
+
+        try:
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            handle = self._handle(nvml)
+            if handle is None:
+                self.error = "no NVML device matches this GPU"
+                return
+            max_sm = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+            while not self._stop.is_set():
+                sm = float(nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM))
+                reasons = int(nvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+                self.samples.append((sm, max_sm, reasons))
+                self._stop.wait(0.005)
+        except Exception as exc:  # pragma: no cover - depends on the driver
+            self.error = repr(exc)
 
     def __enter__(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-               "-lms", "100"]
-        if self.uuid:
-            cmd += ["-i", self.uuid]
-        try:
-            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                                         text=True)
-        except OSError:
-            self.proc = None
+        import threading
+
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [line for line in out.splitlines() if line.strip()]
+        self._stop.set()
+        self._thread.join(timeout=5)
 
     def summary(self) -> dict | None:
-        samples = []
-        for line in getattr(self, "lines", []):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                samples.append((float(parts[0]), float(parts[1]), parts[4:8]))
-            except ValueError:
-                continue
-        if not samples:
-            return None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, flags in samples for i, f in enumerate(flags)
-                          if f.lower() == "active"})
-        return {"sm_mhz": statistics.median(s[0] for s in samples),
-                "sm_max_mhz": max(s[1] for s in samples), "reasons": reasons,
-                "samples": len(samples)}
+        if not self.samples:
+            return {"error": self.error or "no samples"}
+        # Samples taken while the GPU was busy (the timed region is all busy).
+        reasons = sorted({name for _, _, bits in self.samples
+                          for bit, name in self.REASONS.items() if bits & bit})
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": reasons,
+                "samples": len(self.samples)}
 
 
 # ------------------------------------------------------------- CPU oracle ----
@@ -316,12 +329,14 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
+        torch.cuda.nvtx.range_push("timed")
         start_ev.record(stream)
         for t in range(args.warmup, total):
             step_in.copy_(inputs[t])
             pos.copy_(positions_all[t])
             graph.replay()
         end_ev.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -333,28 +348,40 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     ms_per_step = ms / args.steps
     value = BATCH * world * args.steps / (ms / 1e3)
 
-    # ---- kernel timing: average launch duration of the two kernels ----
-    launches = max(8, args.steps)
+    # ---- kernel timing: average launch duration of each kernel, launched
+    # back to back from a captured graph (no host launch cost in the way) ----
     kernel_ms = {}
-    for name in ("cross", "self"):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        a.record(stream)
+    launches = 4 * LAYERS
+    t_kernel = args.warmup
+
+    def cross_only():
         for i in range(launches):
             layer = i % LAYERS
-            t = args.warmup + (i % args.steps)
-            if name == "cross":
-                attention.whisper_cross_attention_step(
-                    inputs[t, layer, 3], cache.cross_keys[layer], cache.cross_values[layer])
-            else:
-                attention.whisper_self_attention_step(
-                    inputs[t, layer, 0], inputs[t, layer, 1], inputs[t, layer, 2],
-                    cache.self_keys[layer], cache.self_values[layer], positions_all[t])
+            attention.whisper_cross_attention_step(
+                inputs[t_kernel, layer, 3], cache.cross_keys[layer], cache.cross_values[layer])
+
+    def self_only():
+        for i in range(launches):
+            layer = i % LAYERS
+            attention.whisper_self_attention_step(
+                inputs[t_kernel, layer, 0], inputs[t_kernel, layer, 1], inputs[t_kernel, layer, 2],
+                cache.self_keys[layer], cache.self_values[layer], positions_all[t_kernel])
+
+    for name, fn in (("cross", cross_only), ("self", self_only)):
+        kgraph = CapturedGraph(fn, warmup=1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        kgraph.replay()
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(4):
+            kgraph.replay()
         b.record(stream)
         torch.cuda.synchronize()
-        kernel_ms[name] = a.elapsed_time(b) / launches
+        kernel_ms[name] = a.elapsed_time(b) / (4 * launches)
+        del kgraph
     self_bytes, cross_bytes = attention_bytes(schedule[args.warmup:])
-    self_bytes_per_launch = self_bytes / args.steps / LAYERS  # averaged over the timed steps
+    self_bytes_kernel, _ = attention_bytes(schedule[t_kernel:t_kernel + 1])
+    self_bytes_per_launch = self_bytes_kernel / LAYERS
     cross_bytes_per_launch = cross_bytes / LAYERS
     peak, peak_kind = measured_peak()
     achieved = cross_bytes_per_launch / (kernel_ms["cross"] * 1e-3) / 1e9
