@@ -59,6 +59,14 @@ SIGNATURES: dict[str, tuple[list, object]] = {
          _c_f, _c_p, _c_size, _c_p, _c_p],
         _c_int,
     ),
+    "asrback_whisper_cross_attention_step_noalloc": (
+        [_c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_p, _c_i64, _c_i64,
+         _c_p, _c_p, _c_i64, _c_i64,
+         _c_p, _c_i64, _c_i64,
+         _c_f, _c_p, _c_p],
+        _c_int,
+    ),
     "asrback_qwen3_attention_step": (
         [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
          _c_p, _c_i64,

@@ -32,6 +32,7 @@
 #include <cfloat>
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 
 #include "capi_internal.h"
 #include "common.cuh"
@@ -818,3 +819,105 @@ int asrback_qwen3_attention_step(int dtype, int batch, int heads, int kv_heads, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Cross-attention step that allocates nothing
+// ---------------------------------------------------------------------------
+//
+// Some callers cannot hand this library a workspace: a host that binds the C
+// ABI from another language (Go, Java, Rust) often has no device allocator of
+// its own, and a serving loop must not call cudaMalloc per request because it
+// synchronizes the whole device and stalls every other stream of the process.
+// For them this entry point keeps its split-KV scratch (completion counters,
+// then partial results) in a file-scope device array instead.
+
+namespace asrback {
+namespace {
+
+// 1 MiB per device that loads the library, held until the process exits:
+// room for kNoallocCounters split (row, head) units and their partials. The
+// split heuristic needs at most ~0.5 MiB for any batch of Whisper heads.
+constexpr int kNoallocCounters = 4096;
+constexpr size_t kNoallocScratchBytes = size_t(1) << 20;
+constexpr size_t kNoallocCounterBytes = kNoallocCounters * sizeof(int);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device. The lookup runs
+// once per device (with that device current) and is cached; on a host, the
+// name g_noalloc_scratch is only a stand-in for the device symbol, never an
+// address a kernel may be given.
+int noalloc_scratch(void** out) {
+  static std::mutex lock;
+  static void* addresses[64] = {nullptr};
+  int device = 0;
+  if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
+  if (device < 0 || device >= 64) return fail(ASRBACK_ERR_ARGUMENT, "device %d out of range", device);
+  std::lock_guard<std::mutex> guard(lock);
+  if (addresses[device] == nullptr) {
+    void* ptr = nullptr;
+    if (int rc = check_cuda(cudaGetSymbolAddress(&ptr, g_noalloc_scratch),
+                            "cudaGetSymbolAddress(no-allocation scratch)"))
+      return rc;
+    addresses[device] = ptr;
+  }
+  *out = addresses[device];
+  return ASRBACK_OK;
+}
+
+}  // namespace
+}  // namespace asrback
+
+extern "C" int asrback_whisper_cross_attention_step_noalloc(
+    int dtype, int batch, int heads, int head_dim, int length, const void* query,
+    int64_t q_stride_batch, int64_t q_stride_head, const void* key_cache, const void* value_cache,
+    int64_t cache_stride_batch, int64_t cache_stride_head, void* out, int64_t out_stride_batch,
+    int64_t out_stride_head, float scale, int32_t* status, void* stream) {
+  if (int rc = whisper_common(dtype, batch, heads, head_dim, length, query, q_stride_batch,
+                              q_stride_head, key_cache, value_cache, cache_stride_batch,
+                              cache_stride_head, out, out_stride_batch, out_stride_head))
+    return rc;
+  // Set-up on the first call on each device: the scratch's device address.
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  DecodeParams p{};
+  p.q = query;
+  p.q_sb = q_stride_batch;
+  p.q_sh = q_stride_head;
+  p.k_cache = const_cast<void*>(key_cache);
+  p.v_cache = const_cast<void*>(value_cache);
+  p.c_sb = cache_stride_batch;
+  p.c_sh = cache_stride_head;
+  p.c_sp = head_dim;
+  p.length = length;
+  p.out = out;
+  p.o_sb = out_stride_batch;
+  p.o_sh = out_stride_head;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.groups = heads;
+  p.status = status;
+  choose_split(batch * heads, length, whisper_tile(dtype), whisper_ctas_per_sm(), &p.chunk,
+               &p.num_splits);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p.num_splits > 1) {
+    const int units = batch * heads;
+    const size_t partial_bytes =
+        (size_t)units * p.num_splits * (head_dim + 2) * sizeof(float);
+    if (units > kNoallocCounters || partial_bytes > kNoallocScratchBytes - kNoallocCounterBytes)
+      return fail(ASRBACK_ERR_ARGUMENT,
+                  "this call splits %d (row, head) units %d ways and needs %zu bytes of scratch; "
+                  "the no-allocation entry point holds %d units and %zu bytes (use "
+                  "asrback_whisper_cross_attention_step with a workspace instead)",
+                  units, p.num_splits, partial_bytes + kNoallocCounterBytes, kNoallocCounters,
+                  kNoallocScratchBytes);
+    // The array keeps the previous call's contents: the counters must start at zero.
+    if (int rc = check_cuda(cudaMemsetAsync(scratch, 0, units * sizeof(int), s),
+                            "cudaMemsetAsync(no-allocation counters)"))
+      return rc;
+    p.counters = static_cast<int*>(scratch);
+    p.partial = reinterpret_cast<float*>(static_cast<char*>(scratch) + kNoallocCounterBytes);
+  }
+  int rc = dtype == ASRBACK_BF16
+               ? launch<__nv_bfloat16, 64, 1, 1, 4, 64, 4, kWhisperCross>(p, batch, s)
+               : launch<float, 64, 1, 1, 4, 32, 4, kWhisperCross>(p, batch, s);
+  return rc ? rc : ok();
+}

@@ -118,6 +118,33 @@ ASRBACK_API int asrback_whisper_cross_attention_step(
     float scale, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * The cross-attention step above, for callers that cannot allocate device
+ * memory: no counterpart in the reference (which always runs inside PyTorch
+ * and its caching allocator). A host that binds this C ABI from another
+ * language may have no device allocator to hand out a workspace, and a serving
+ * loop must not call cudaMalloc per request, since it synchronizes the device
+ * and stalls every other stream. This entry point takes no workspace and
+ * allocates nothing: its split-KV scratch is a 1 MiB file-scope device array
+ * (per device that loads the library, held until exit) that covers up to 4096
+ * split (row, head) units; larger splits are rejected with
+ * ASRBACK_ERR_ARGUMENT. Same arguments and results as
+ * asrback_whisper_cross_attention_step otherwise.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current) and should come before any stream capture. All calls share
+ * the one array and clear its counters on their stream first, so calls that
+ * overlap on the GPU (different streams, no ordering) race and must not be
+ * issued.
+ */
+ASRBACK_API int asrback_whisper_cross_attention_step_noalloc(
+    int dtype, int batch, int heads, int head_dim, int length,
+    const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+    const void* key_cache, const void* value_cache,
+    int64_t cache_stride_batch, int64_t cache_stride_head,
+    void* out, int64_t out_stride_batch, int64_t out_stride_head,
+    float scale, int32_t* status, void* stream);
+
+/*
  * Qwen3 decoder attention for one step, between qkv_proj and o_proj.
  *
  * qkv          (batch, (heads + 2*kv_heads)*head_dim) at qkv[b*qkv_stride_batch + j]:
