@@ -79,8 +79,11 @@ struct DecodeParams {
   int kv_heads;
 };
 
-template <typename T, int D, int G, int QPK, int WPH, int TP, int STAGES, int MODE>
+template <typename T_, int D_, int G_, int QPK_, int WPH_, int TP_, int STAGES_, int MODE_>
 struct DecodeConfig {
+  using T = T_;
+  static constexpr int D = D_, G = G_, QPK = QPK_, WPH = WPH_, TP = TP_, STAGES = STAGES_;
+  static constexpr int MODE = MODE_;
   static constexpr int LPK = D / 8;
   static constexpr int KPW = 32 / LPK;
   static constexpr int NP = TP / (WPH * KPW);
@@ -92,11 +95,24 @@ struct DecodeConfig {
   static constexpr int TILE_BYTES = TP * ROW_BYTES;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = STAGES * TILE_BYTES;
-  static constexpr int OFF_MERGE = 2 * STAGES * TILE_BYTES;
+  static constexpr int RING_BYTES = 2 * STAGES * TILE_BYTES;
+  // The cross-warp merge slots and the split-merge weights are used only once
+  // the ring has drained, so they share its shared memory when they fit.
   static constexpr int MERGE_FLOATS = CWARPS * QPK * (D + 2);
+  static constexpr int SCRATCH_BYTES = MERGE_FLOATS * 4 + QH * kMaxSplits * 4;
+  static constexpr bool SCRATCH_IN_RING = SCRATCH_BYTES <= RING_BYTES;
+  static constexpr int OFF_MERGE = SCRATCH_IN_RING ? 0 : RING_BYTES;
   static constexpr int OFF_WEIGHTS = OFF_MERGE + MERGE_FLOATS * 4;
-  static constexpr int OFF_BAR = (OFF_WEIGHTS + QH * kMaxSplits * 4 + 15) / 16 * 16;
+  static constexpr int OFF_BAR =
+      ((SCRATCH_IN_RING ? RING_BYTES : RING_BYTES + SCRATCH_BYTES) + 15) / 16 * 16;
   static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8 + 16;
+  // CTAs per SM that shared memory (228 KB, 1 KB reserved per CTA) and the
+  // 2048-thread limit allow; registers are budgeted to match.
+  static constexpr int BY_SMEM = (228 * 1024) / (SMEM + 1024);
+  static constexpr int BY_THREADS = 2048 / THREADS;
+  static constexpr int MIN_BLOCKS =
+      (BY_SMEM < BY_THREADS ? BY_SMEM : BY_THREADS) < 1 ? 1
+                                                        : (BY_SMEM < BY_THREADS ? BY_SMEM : BY_THREADS);
   static_assert(NP >= 1 && NP * WPH * KPW == TP, "tile must split evenly over warps");
   static_assert(LPK >= 1 && LPK <= 32 && (32 % LPK) == 0, "head_dim must be 8..256");
   static_assert(TILE_BYTES % 16 == 0, "bulk copies move 16-byte multiples");
@@ -169,10 +185,12 @@ __device__ __forceinline__ void merge_state(float& m, float& l, float* o, float 
   m = mm;
 }
 
-template <typename T, int D, int G, int QPK, int WPH, int TP, int STAGES, int MODE>
-__global__ void __launch_bounds__(DecodeConfig<T, D, G, QPK, WPH, TP, STAGES, MODE>::THREADS)
+template <class C>
+__global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
     decode_attention_kernel(const __grid_constant__ DecodeParams p) {
-  using C = DecodeConfig<T, D, G, QPK, WPH, TP, STAGES, MODE>;
+  using T = typename C::T;
+  constexpr int D = C::D, G = C::G, QPK = C::QPK, WPH = C::WPH, TP = C::TP;
+  constexpr int STAGES = C::STAGES, MODE = C::MODE;
   using S = Slice<T, D>;
   constexpr int LPK = C::LPK, KPW = C::KPW, NP = C::NP, QH = C::QH;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -231,23 +249,38 @@ __global__ void __launch_bounds__(DecodeConfig<T, D, G, QPK, WPH, TP, STAGES, MO
   const T* vbase = static_cast<const T*>(p.v_cache) + b * p.c_sb + head0 * p.c_sh;
 
   if (warp == C::CWARPS) {
-    // Producer: one lane streams this split's tiles into the ring.
-    if (lane == 0) {
-      const uint64_t policy = l2_evict_first_policy();
-      for (int t = 0; t < n_tiles; ++t) {
-        const int s = t % STAGES;
-        if (t >= STAGES && !mbar_wait(&empty[s], ((t / STAGES) - 1) & 1, deadline)) {
-          if (p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
-          break;
+    // Producer warp. When a tile's rows are contiguous in the cache (each
+    // position holds exactly this group's heads: Whisper, or Qwen3 with every
+    // key/value head in one group), lane 0 moves it with one bulk copy per
+    // tensor; otherwise each lane copies one position's slice of the group.
+    const bool contiguous = p.c_sp == (int64_t)G * D;
+    const uint64_t policy = l2_evict_first_policy();
+    for (int t = 0; t < n_tiles; ++t) {
+      const int s = t % STAGES;
+      int ready = 1;
+      if (t >= STAGES && lane == 0) ready = mbar_wait(&empty[s], ((t / STAGES) - 1) & 1, deadline);
+      if (!__shfl_sync(0xffffffffu, ready, 0)) {
+        if (lane == 0 && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+        break;
+      }
+      const int first = k0 + t * TP;
+      const int rows = min(TP, k1 - first);
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(2 * rows * C::ROW_BYTES));
+      __syncwarp();
+      uint8_t* kdst = smem + C::OFF_K + s * C::TILE_BYTES;
+      uint8_t* vdst = smem + C::OFF_V + s * C::TILE_BYTES;
+      if (contiguous) {
+        if (lane == 0) {
+          const uint32_t bytes = static_cast<uint32_t>(rows * C::ROW_BYTES);
+          bulk_g2s(kdst, kbase + first * p.c_sp, bytes, &full[s], policy);
+          bulk_g2s(vdst, vbase + first * p.c_sp, bytes, &full[s], policy);
         }
-        const int first = k0 + t * TP;
-        const int rows = min(TP, k1 - first);
-        const uint32_t bytes = static_cast<uint32_t>(rows * C::ROW_BYTES);
-        mbar_arrive_expect_tx(&full[s], 2 * bytes);
-        bulk_g2s(smem + C::OFF_K + s * C::TILE_BYTES, kbase + first * p.c_sp, bytes, &full[s],
-                 policy);
-        bulk_g2s(smem + C::OFF_V + s * C::TILE_BYTES, vbase + first * p.c_sp, bytes, &full[s],
-                 policy);
+      } else {
+        for (int r = lane; r < rows; r += 32) {
+          const int64_t off = (int64_t)(first + r) * p.c_sp;
+          bulk_g2s(kdst + r * C::ROW_BYTES, kbase + off, C::ROW_BYTES, &full[s], policy);
+          bulk_g2s(vdst + r * C::ROW_BYTES, vbase + off, C::ROW_BYTES, &full[s], policy);
+        }
       }
     }
     return;
@@ -410,6 +443,8 @@ __global__ void __launch_bounds__(DecodeConfig<T, D, G, QPK, WPH, TP, STAGES, MO
   // Merge the WPH warps of each head through shared memory.
   if constexpr (WPH > 1) {
     float* merge = reinterpret_cast<float*>(smem + C::OFF_MERGE);
+    // The slots may share the ring: every warp must be done with its tiles.
+    if constexpr (C::SCRATCH_IN_RING) named_sync(1, C::CTHREADS);
     if (ks == 0) {
 #pragma unroll
       for (int qi = 0; qi < QPK; ++qi) {
@@ -545,9 +580,9 @@ int chunk_override() {
 }
 
 // Keys per split for `units` independent (row, group) units of at most
-// `max_keys` keys: enough CTAs for `waves` full waves of `ctas_per_sm` per SM,
-// whole tiles per split, at most kMaxSplits splits.
-void choose_split(int units, int max_keys, int tile, int ctas_per_sm, int* chunk, int* splits) {
+// `max_keys` keys: about two CTAs per SM in all, whole tiles (rounded up to
+// `granule_tiles`) per split, at most kMaxSplits splits.
+void choose_split(int units, int max_keys, int tile, int granule_tiles, int* chunk, int* splits) {
   const int tiles = (max_keys + tile - 1) / tile;
   int want = 1;
   const int override_keys = chunk_override();
@@ -555,58 +590,111 @@ void choose_split(int units, int max_keys, int tile, int ctas_per_sm, int* chunk
     int c = (override_keys + tile - 1) / tile;
     want = (tiles + c - 1) / c;
   } else {
-    const int target = sm_count() * ctas_per_sm * 2;
+    // About two CTAs per SM: enough to fill the GPU, few enough that each
+    // split keeps a pipeline's worth of tiles (sweeps on B200).
+    const int target = sm_count() * 2;
     want = (target + units - 1) / units;
   }
   want = want < 1 ? 1 : want;
   want = want > tiles ? tiles : want;
   want = want > kMaxSplits ? kMaxSplits : want;
-  const int chunk_tiles = (tiles + want - 1) / want;
+  int chunk_tiles = (tiles + want - 1) / want;
+  if (override_keys <= 0 && granule_tiles > 1)
+    chunk_tiles = (chunk_tiles + granule_tiles - 1) / granule_tiles * granule_tiles;
   *chunk = chunk_tiles * tile;
   *splits = (tiles + chunk_tiles - 1) / chunk_tiles;
 }
 
-template <typename Kernel>
-int prepare(Kernel kernel, int smem, bool* done) {
-  if (*done) return ASRBACK_OK;
-  const int rc = check_cuda(
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-      "cudaFuncSetAttribute(max dynamic shared memory)");
-  if (rc == ASRBACK_OK) *done = true;
-  return rc;
+// Kernel shape per call site and dtype: warps per key/value head, key
+// positions per tile, ring stages. A tile is 16 KB (bf16 Whisper) or 32 KB
+// (Qwen3) of keys, as much of values. The defaults come from sweeps on B200;
+// a build may override them with -D for new sweeps.
+#ifndef ASRBACK_SHAPE_WHISPER_SELF_BF16
+#define ASRBACK_SHAPE_WHISPER_SELF_BF16 4, 64, 3
+#endif
+#ifndef ASRBACK_SHAPE_WHISPER_CROSS_BF16
+#define ASRBACK_SHAPE_WHISPER_CROSS_BF16 8, 128, 2
+#endif
+#ifndef ASRBACK_SHAPE_WHISPER_F32
+#define ASRBACK_SHAPE_WHISPER_F32 4, 32, 4
+#endif
+// Qwen3: key/value heads per CTA (a divisor of 8), then the shape.
+#ifndef ASRBACK_QWEN3_GROUP
+#define ASRBACK_QWEN3_GROUP 8
+#endif
+#ifndef ASRBACK_SHAPE_QWEN3_BF16
+#define ASRBACK_SHAPE_QWEN3_BF16 2, 16, 2
+#endif
+#ifndef ASRBACK_SHAPE_QWEN3_F32
+#define ASRBACK_SHAPE_QWEN3_F32 1, 8, 3
+#endif
+
+using bf16 = __nv_bfloat16;
+using WhisperSelfBf16 = DecodeConfig<bf16, 64, 1, 1, ASRBACK_SHAPE_WHISPER_SELF_BF16, kWhisperSelf>;
+using WhisperSelfF32 = DecodeConfig<float, 64, 1, 1, ASRBACK_SHAPE_WHISPER_F32, kWhisperSelf>;
+using WhisperCrossBf16 = DecodeConfig<bf16, 64, 1, 1, ASRBACK_SHAPE_WHISPER_CROSS_BF16, kWhisperCross>;
+using WhisperCrossF32 = DecodeConfig<float, 64, 1, 1, ASRBACK_SHAPE_WHISPER_F32, kWhisperCross>;
+template <int QPK>
+using Qwen3Bf16 = DecodeConfig<bf16, 128, ASRBACK_QWEN3_GROUP, QPK, ASRBACK_SHAPE_QWEN3_BF16, kQwen3>;
+template <int QPK>
+using Qwen3F32 = DecodeConfig<float, 128, ASRBACK_QWEN3_GROUP, QPK, ASRBACK_SHAPE_QWEN3_F32, kQwen3>;
+
+// Splits `units` (row, group) units of at most p.length keys for config C.
+// Splits are whole tiles; Qwen3 rounds them to 64 positions, which on
+// bucket-length views (1024) gives the 256-position splits its rows of
+// ~410-540 positions stream fastest with (sweeps on B200).
+template <class C>
+constexpr int split_granule_tiles() {
+  return C::MODE == kQwen3 ? (64 + C::TP - 1) / C::TP : 1;
 }
 
-template <typename T, int D, int G, int QPK, int WPH, int TP, int STAGES, int MODE>
+template <class C>
+void split_for(DecodeParams& p, int units) {
+  choose_split(units, p.length, C::TP, split_granule_tiles<C>(), &p.chunk, &p.num_splits);
+}
+
+// Workspace bytes config C needs for `units` units of `qh` query heads.
+template <class C>
+size_t workspace_for(int units, int qh, int max_keys) {
+  int chunk, splits;
+  choose_split(units, max_keys, C::TP, split_granule_tiles<C>(), &chunk, &splits);
+  return workspace_bytes_for(units, qh, C::D, splits);
+}
+
+template <class C>
 int launch(const DecodeParams& p, int batch, cudaStream_t stream) {
-  using C = DecodeConfig<T, D, G, QPK, WPH, TP, STAGES, MODE>;
-  auto kernel = decode_attention_kernel<T, D, G, QPK, WPH, TP, STAGES, MODE>;
+  auto kernel = decode_attention_kernel<C>;
   static thread_local int prepared_device = -1;
   int device = 0;
-  cudaGetDevice(&device);
-  bool done = prepared_device == device;
-  if (int rc = prepare(kernel, C::SMEM, &done)) return rc;
-  prepared_device = device;
+  if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
+  if (prepared_device != device) {
+    if (int rc = check_cuda(
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+            "cudaFuncSetAttribute(max dynamic shared memory)"))
+      return rc;
+    prepared_device = device;
+  }
   dim3 grid(p.num_splits, p.groups, batch);
   kernel<<<grid, C::THREADS, C::SMEM, stream>>>(p);
   return check_cuda(cudaGetLastError(), "decode attention launch");
 }
 
-// CTAs of a configuration that fit on one SM (by shared memory).
-int ctas_per_sm(int smem) {
-  const int per_sm = 228 * 1024;
-  int n = per_sm / (smem + 1024);
-  return n < 1 ? 1 : n;
+// Splits, binds the workspace and launches config C.
+template <class C>
+int run(DecodeParams& p, int batch, int units, int qh_per_unit, void* workspace, size_t bytes,
+        cudaStream_t stream) {
+  split_for<C>(p, units);
+  if (int rc = bind_workspace(p, units, qh_per_unit, C::D, workspace, bytes)) return rc;
+  return launch<C>(p, batch, stream);
 }
 
-// Configurations (tile sizes chosen so a stage is 8 KB x2 for Whisper and
-// 32 KB x2 for Qwen3, whatever the dtype; the bf16 ones set the occupancy).
-using WhisperSelfBf16 = DecodeConfig<__nv_bfloat16, 64, 1, 1, 4, 64, 4, kWhisperSelf>;
-using Qwen3Bf16 = DecodeConfig<__nv_bfloat16, 128, 8, 2, 1, 16, 3, kQwen3>;
-
-int whisper_tile(int dtype) { return dtype == ASRBACK_BF16 ? 64 : 32; }
-int whisper_ctas_per_sm() { return ctas_per_sm(WhisperSelfBf16::SMEM); }
-int qwen3_tile(int dtype) { return dtype == ASRBACK_BF16 ? 16 : 8; }
-int qwen3_ctas_per_sm() { return ctas_per_sm(Qwen3Bf16::SMEM); }
+// Qwen3: one unit per (row, group of C::G key/value heads).
+template <class C>
+int run_qwen3(DecodeParams& p, int batch, void* workspace, size_t bytes, cudaStream_t stream) {
+  static_assert(8 % C::G == 0, "key/value head groups must divide 8");
+  p.groups = p.kv_heads / C::G;
+  return run<C>(p, batch, batch * p.groups, C::QH, workspace, bytes, stream);
+}
 
 int check_dtype(int dtype) {
   if (dtype != ASRBACK_BF16 && dtype != ASRBACK_F32)
@@ -645,13 +733,18 @@ int whisper_common(int dtype, int batch, int heads, int head_dim, int length, co
 
 size_t decode_workspace_bytes(int batch, int heads, int head_dim, int max_keys) {
   if (batch < 1 || heads < 1 || head_dim < 1 || max_keys < 1) return 0;
-  // Whisper layout: one unit per (row, head); Qwen3: one per row, all heads.
-  int chunk, splits;
-  choose_split(batch * heads, max_keys, 32, whisper_ctas_per_sm(), &chunk, &splits);
-  size_t a = workspace_bytes_for(batch * heads, 1, head_dim, splits);
-  choose_split(batch, max_keys, 8, qwen3_ctas_per_sm(), &chunk, &splits);
-  size_t b = workspace_bytes_for(batch, heads, head_dim, splits);
-  return a > b ? a : b;
+  // Whisper: one unit per (row, head); Qwen3: one per row, all heads. The
+  // largest need of any configuration that a call with these sizes may use.
+  const int units = batch * heads;
+  size_t need = 0;
+  for (size_t n : {workspace_for<WhisperSelfBf16>(units, 1, max_keys),
+                   workspace_for<WhisperSelfF32>(units, 1, max_keys),
+                   workspace_for<WhisperCrossBf16>(units, 1, max_keys),
+                   workspace_for<WhisperCrossF32>(units, 1, max_keys),
+                   workspace_for<Qwen3Bf16<2>>(batch * (8 / Qwen3Bf16<2>::G), Qwen3Bf16<2>::QH, max_keys),
+                   workspace_for<Qwen3F32<2>>(batch * (8 / Qwen3F32<2>::G), Qwen3F32<2>::QH, max_keys)})
+    need = n > need ? n : need;
+  return need;
 }
 
 }  // namespace asrback
@@ -699,13 +792,11 @@ int asrback_whisper_self_attention_step(
   p.scale_log2 = scale * 1.4426950408889634f;
   p.groups = heads;
   p.status = status;
-  choose_split(batch * heads, cache_length, whisper_tile(dtype), whisper_ctas_per_sm(), &p.chunk,
-               &p.num_splits);
-  if (int rc = bind_workspace(p, batch * heads, 1, head_dim, workspace, workspace_bytes)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int units = batch * heads;
   int rc = dtype == ASRBACK_BF16
-               ? launch<__nv_bfloat16, 64, 1, 1, 4, 64, 4, kWhisperSelf>(p, batch, s)
-               : launch<float, 64, 1, 1, 4, 32, 4, kWhisperSelf>(p, batch, s);
+               ? run<WhisperSelfBf16>(p, batch, units, 1, workspace, workspace_bytes, s)
+               : run<WhisperSelfF32>(p, batch, units, 1, workspace, workspace_bytes, s);
   return rc ? rc : ok();
 }
 
@@ -737,13 +828,11 @@ int asrback_whisper_cross_attention_step(int dtype, int batch, int heads, int he
   p.scale_log2 = scale * 1.4426950408889634f;
   p.groups = heads;
   p.status = status;
-  choose_split(batch * heads, length, whisper_tile(dtype), whisper_ctas_per_sm(), &p.chunk,
-               &p.num_splits);
-  if (int rc = bind_workspace(p, batch * heads, 1, head_dim, workspace, workspace_bytes)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int units = batch * heads;
   int rc = dtype == ASRBACK_BF16
-               ? launch<__nv_bfloat16, 64, 1, 1, 4, 64, 4, kWhisperCross>(p, batch, s)
-               : launch<float, 64, 1, 1, 4, 32, 4, kWhisperCross>(p, batch, s);
+               ? run<WhisperCrossBf16>(p, batch, units, 1, workspace, workspace_bytes, s)
+               : run<WhisperCrossF32>(p, batch, units, 1, workspace, workspace_bytes, s);
   return rc ? rc : ok();
 }
 
@@ -803,18 +892,16 @@ int asrback_qwen3_attention_step(int dtype, int batch, int heads, int kv_heads, 
   p.o_sb = out_stride_batch;
   p.o_sh = head_dim;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.groups = 1;
   p.status = status;
-  choose_split(batch, cache_length, qwen3_tile(dtype), qwen3_ctas_per_sm(), &p.chunk, &p.num_splits);
-  if (int rc = bind_workspace(p, batch, heads, head_dim, workspace, workspace_bytes)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf = dtype == ASRBACK_BF16;
   int rc;
   if (heads == 16)
-    rc = dtype == ASRBACK_BF16 ? launch<__nv_bfloat16, 128, 8, 2, 1, 16, 3, kQwen3>(p, batch, s)
-                               : launch<float, 128, 8, 2, 1, 8, 3, kQwen3>(p, batch, s);
+    rc = bf ? run_qwen3<Qwen3Bf16<2>>(p, batch, workspace, workspace_bytes, s)
+            : run_qwen3<Qwen3F32<2>>(p, batch, workspace, workspace_bytes, s);
   else
-    rc = dtype == ASRBACK_BF16 ? launch<__nv_bfloat16, 128, 8, 1, 1, 16, 3, kQwen3>(p, batch, s)
-                               : launch<float, 128, 8, 1, 1, 8, 3, kQwen3>(p, batch, s);
+    rc = bf ? run_qwen3<Qwen3Bf16<1>>(p, batch, workspace, workspace_bytes, s)
+            : run_qwen3<Qwen3F32<1>>(p, batch, workspace, workspace_bytes, s);
   return rc ? rc : ok();
 }
 
@@ -895,8 +982,10 @@ extern "C" int asrback_whisper_cross_attention_step_noalloc(
   p.scale_log2 = scale * 1.4426950408889634f;
   p.groups = heads;
   p.status = status;
-  choose_split(batch * heads, length, whisper_tile(dtype), whisper_ctas_per_sm(), &p.chunk,
-               &p.num_splits);
+  if (dtype == ASRBACK_BF16)
+    split_for<WhisperCrossBf16>(p, batch * heads);
+  else
+    split_for<WhisperCrossF32>(p, batch * heads);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.num_splits > 1) {
     const int units = batch * heads;
@@ -916,8 +1005,7 @@ extern "C" int asrback_whisper_cross_attention_step_noalloc(
     p.counters = static_cast<int*>(scratch);
     p.partial = reinterpret_cast<float*>(static_cast<char*>(scratch) + kNoallocCounterBytes);
   }
-  int rc = dtype == ASRBACK_BF16
-               ? launch<__nv_bfloat16, 64, 1, 1, 4, 64, 4, kWhisperCross>(p, batch, s)
-               : launch<float, 64, 1, 1, 4, 32, 4, kWhisperCross>(p, batch, s);
+  int rc = dtype == ASRBACK_BF16 ? launch<WhisperCrossBf16>(p, batch, s)
+                                 : launch<WhisperCrossF32>(p, batch, s);
   return rc ? rc : ok();
 }

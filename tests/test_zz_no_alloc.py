@@ -60,13 +60,14 @@ def test_noalloc_matches_workspace_entry_point_twice(dtype, batch, length):
 
 
 def test_noalloc_rejects_splits_beyond_its_scratch(monkeypatch):
-    """Forcing 64-key splits over 5000 (row, head) units needs more than the
-    static scratch: the call is refused on the host, before any launch."""
+    """Forcing 128-key splits of 256 keys over 5000 (row, head) units needs
+    more than the static scratch (any tile size up to 128 keys splits them in
+    two): the call is refused on the host, before any launch."""
     device = torch.device("cuda", 0)
-    monkeypatch.setenv("ASRBACK_SPLIT_CHUNK", "64")
+    monkeypatch.setenv("ASRBACK_SPLIT_CHUNK", "128")
     q = torch.zeros((250, 20, 64), dtype=torch.bfloat16, device=device)
-    kc = torch.zeros((250, 20, 128, 64), dtype=torch.bfloat16, device=device)
+    kc = torch.zeros((250, 20, 256, 64), dtype=torch.bfloat16, device=device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     with pytest.raises(_native.NativeError, match="no-allocation entry point holds"):
         noalloc_cross(q, kc, kc, status)
-    assert os.environ["ASRBACK_SPLIT_CHUNK"] == "64"
+    assert os.environ["ASRBACK_SPLIT_CHUNK"] == "128"
