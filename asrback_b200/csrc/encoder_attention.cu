@@ -1,10 +1,10 @@
 // Whisper encoder self-attention (non-causal), MultiHeadAttention.forward at
 // whisper.py:108-110 calling F.scaled_dot_product_attention unmasked.
 //
-// This translation unit holds the SIMT path: one thread per query row, the
-// block's keys and values staged in shared memory, online softmax in fp32.
-// It serves float32 inputs (the reference's CPU dtype, used for the 1e-4
-// parity check) and is the fallback-free correctness baseline for bf16.
+// bfloat16 runs on the tensor cores (encoder_attention_tc.cu). float32 (the
+// reference's CPU dtype, used for the 1e-4 parity check) runs here on the
+// SIMT path: one thread per query row, the block's keys and values staged in
+// shared memory, online softmax in fp32.
 #include "capi_internal.h"
 #include "common.cuh"
 
@@ -95,6 +95,10 @@ __global__ void __launch_bounds__(kRows) encoder_attention_simt(const __grid_con
 
 }  // namespace
 
+int encoder_attention_tc(int batch, int heads, int length, const void* q, const void* k,
+                         const void* v, void* out, int64_t sb, int64_t sh, int64_t ss, float scale,
+                         int32_t* status, cudaStream_t stream);
+
 }  // namespace asrback
 
 using namespace asrback;
@@ -118,14 +122,18 @@ extern "C" int asrback_whisper_encoder_attention(int dtype, int batch, int heads
   for (int64_t s : {stride_batch, stride_head, stride_seq})
     if (s <= 0 || (s * elem) % 16 != 0)
       return fail(ASRBACK_ERR_ARGUMENT, "strides must be positive multiples of 16 bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == ASRBACK_BF16) {
+    // Tensor cores (tcgen05, TMEM accumulators): encoder_attention_tc.cu.
+    if (int rc = encoder_attention_tc(batch, heads, length, q, k, v, out, stride_batch,
+                                      stride_head, stride_seq, scale, status, s))
+      return rc;
+    return ok();
+  }
   EncoderParams p{q, k, v, out, stride_batch, stride_head, stride_seq, length, heads,
                   scale * 1.4426950408889634f};
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid((length + kRows - 1) / kRows, heads, batch);
-  if (dtype == ASRBACK_BF16)
-    encoder_attention_simt<__nv_bfloat16><<<grid, kRows, 0, s>>>(p);
-  else
-    encoder_attention_simt<float><<<grid, kRows, 0, s>>>(p);
+  encoder_attention_simt<float><<<grid, kRows, 0, s>>>(p);
   if (int rc = check_cuda(cudaGetLastError(), "encoder attention launch")) return rc;
   return ok();
 }
