@@ -59,6 +59,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Non-blocking test: has the phase with `parity` completed?
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Waits for the phase with `parity` to complete, or until `deadline`
 // (%globaltimer ns) has passed. Returns false on a timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline) {
@@ -67,6 +82,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0 && global_timer_ns() > deadline) return false;
+  }
+}
+
+// As mbar_wait, polling with the non-suspending test (for hand-offs between
+// warps of one CTA, where a suspended waiter would add wake-up latency).
+__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, uint64_t deadline) {
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_test(bar, parity)) return true;
+    if ((++spins & 255u) == 0 && global_timer_ns() > deadline) return false;
   }
 }
 

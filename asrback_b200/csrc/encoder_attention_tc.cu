@@ -37,6 +37,7 @@ constexpr int kKeys = 128;  // keys per tile
 constexpr int kDim = 64;
 constexpr int kStages = 4;
 constexpr int kTileBytes = kRows * kDim * 2;  // 16 KB, one Q, K or V tile
+// warp 0 TMA, warp 1 MMA (and TMEM owner), warps 2-3 idle, warps 4-11 softmax.
 constexpr int kThreads = 12 * 32;
 constexpr int kTmemCols = 512;
 // TMEM column of S, O and P for query tile t.
@@ -50,7 +51,8 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = 2 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffBar = kOffV + kStages * kTileBytes;
-// barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2]
+// barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2],
+// o_full[2]
 constexpr int kNumBars = 1 + 3 * kStages + 6;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
@@ -168,6 +170,30 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r);
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st16f(uint32_t taddr, const float* v) {
+  uint32_t r[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(v[i]);
+  tmem_st16(taddr, r);
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -175,6 +201,142 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
+}
+
+// 64 columns of this thread's TMEM lane in one load.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+      "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63"
+      "}, [%64];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
+
+// The 128 columns of one row (this thread's TMEM lane) in one load.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+      "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+      "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, "
+      "%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, "
+      "%80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, "
+      "%96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, "
+      "%112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127"
+      "}, [%128];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]),
+        "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+        "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]),
+        "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]),
+        "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+        "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]),
+        "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]),
+        "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+        "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Packed f32x2 arithmetic (sm_100): two lanes of work per instruction.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// exp2 of two floats on the FMA pipe, to take load off the SFU: 2^x =
+// 2^round(x) * q(f), f = x - round(x) in [-1/2, 1/2], q a cubic fitted here
+// for least maximum relative error over that interval (7.5e-5 in float32
+// Horner form, below the 2^-9 of the bf16 P it feeds). round(x) comes from
+// adding 1.5 * 2^23, whose low mantissa bits then hold it; shifted into the
+// exponent field it scales q. Arguments are clamped at -126 (the results there
+// are ~1e-38, i.e. zero for P).
+constexpr float kPolyC0 = 0.99992805719375610f;
+constexpr float kPolyC1 = 0.69326096773147583f;
+constexpr float kPolyC2 = 0.24261114001274109f;
+constexpr float kPolyC3 = 0.05517166852951050f;
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+__device__ __forceinline__ void exp2_pair_fma(float x0, float x1, float& e0, float& e1) {
+  const uint64_t xx = pack2(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t yy = fadd2(xx, pack2(kRoundMagic, kRoundMagic));
+  const uint64_t rr = fadd2(yy, pack2(-kRoundMagic, -kRoundMagic));
+  const uint64_t ff = ffma2(rr, pack2(-1.f, -1.f), xx);
+  uint64_t pp = ffma2(pack2(kPolyC3, kPolyC3), ff, pack2(kPolyC2, kPolyC2));
+  pp = ffma2(pp, ff, pack2(kPolyC1, kPolyC1));
+  pp = ffma2(pp, ff, pack2(kPolyC0, kPolyC0));
+  float y0, y1, q0, q1;
+  unpack2(yy, y0, y1);
+  unpack2(pp, q0, q1);
+  e0 = __int_as_float(__float_as_int(q0) + (__float_as_int(y0) << 23));
+  e1 = __int_as_float(__float_as_int(q1) + (__float_as_int(y1) << 23));
+}
+
+// One pair in kPolyEvery takes the FMA-pipe exp2 (0: none). Sweeps on B200
+// found the SFU is not the binding limit of this kernel, so it is off.
+#ifndef ASRBACK_ENCODER_POLY_EVERY
+#define ASRBACK_ENCODER_POLY_EVERY 0
+#endif
+constexpr int kPolyEvery = ASRBACK_ENCODER_POLY_EVERY;
+
+// Two floats to a bf16 pair (lo in the low half), round to nearest even.
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
 }
 
 __device__ __forceinline__ void tmem_wait_st() {
@@ -288,6 +450,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ts(tmem + col_o(t), tmem + col_p(t) + k * 8, bd, kIdescPV, (accumulate || k > 0));
         }
       };
+      // Order: per key tile j and query tile t, S_t(j) once the softmax group
+      // of t is done with S_t(j-1) (it has written P_t(j-1), p_full), then
+      // P_t(j-1) V(j-1); the tensor core alternates between the two tiles.
       bool ok = mbar_wait(q_full, 0, deadline);
       for (int j = 0; j < n_k && ok; ++j) {
         const int s = j % kStages;
@@ -343,15 +508,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const int valid = min(kKeys, p.length - j * kKeys);
-      float v[32];
-      float mx = -INFINITY;
+      float v[kKeys];
+      tmem_ld128(tS, v);
+      if (valid < kKeys) {
+        // Keys past the window (the ragged last tile) take no weight.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tS + 32 * c, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c + i < valid) mx = fmaxf(mx, v[i]);
+        for (int i = 0; i < kKeys; ++i)
+          if (i >= valid) v[i] = -INFINITY;
       }
+      // Row max as eight short independent chains.
+      float acc[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
+#pragma unroll
+      for (int i = 16; i < kKeys; i += 16)
+#pragma unroll
+        for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
+      const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
+                             fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
       const float m_tile = mx * p.scale_log2;
       bool o_ready = j == 0;  // P/O of the previous tile no longer in use
       if (m_tile > m_used + kRescaleThreshold) {
@@ -361,13 +535,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           o_ready = true;
           const float alpha = fast_exp2(m_used - m_tile);
-          float o[32];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tO + 32 * c, o);
+          for (int c = 0; c < 4; ++c) {
+            float o[16];
+            tmem_ld16(tO + 16 * c, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tO + 32 * c, o);
+            for (int i = 0; i < 16; ++i) o[i] *= alpha;
+            tmem_st16f(tO + 16 * c, o);
           }
           tmem_wait_st();
           l *= alpha;
@@ -379,22 +553,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
       }
-      const float neg_m = -m_used;
+      const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
+      const uint64_t neg_m2 = pack2(-m_used, -m_used);
+      uint64_t sum2[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tS + 32 * c, v);
-        uint32_t packed[16];
+      for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = 32 * c + 2 * i;
-          const float p0 = col < valid ? fast_exp2(fmaf(v[2 * i], p.scale_log2, neg_m)) : 0.f;
-          const float p1 = col + 1 < valid ? fast_exp2(fmaf(v[2 * i + 1], p.scale_log2, neg_m)) : 0.f;
-          const __nv_bfloat162 pair2 = __floats2bfloat162_rn(p0, p1);
-          l += p0 + p1;
-          packed[i] = *reinterpret_cast<const uint32_t*>(&pair2);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = 64 * half + 2 * i;
+          float x0, x1, p0, p1;
+          unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
+          if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
+            exp2_pair_fma(x0, x1, p0, p1);
+          } else {
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
+          sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
+          packed[i] = bf16x2(p0, p1);
         }
-        tmem_st16(tP + 16 * c, packed);
+        tmem_st32u(tP + 32 * half, packed);
       }
+      float lo0, hi0;
+      unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
+      l += lo0 + hi0;
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -416,12 +601,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 u;
-            uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(o[i + 2 * k] * inv, o[i + 2 * k + 1] * inv);
-              w[k] = *reinterpret_cast<uint32_t*>(&h2);
-            }
+            u.x = bf16x2(o[i] * inv, o[i + 1] * inv);
+            u.y = bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+            u.z = bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+            u.w = bf16x2(o[i + 6] * inv, o[i + 7] * inv);
             *reinterpret_cast<uint4*>(out + 32 * c + i) = u;
           }
         }

@@ -1,22 +1,32 @@
-"""Benchmark of asrback's decoder-step attention on B200 (one replica per GPU).
+"""Benchmarks of asrback's attention hot path on B200 (one replica per GPU).
 
-Workload: Whisper large-v3-turbo decoder attention in
-bf16, 4 decoder layers, 20 heads x 64, batch 64 slots whose self-attention
-lengths start uniform in [1, 448] and grow by one per step (rows that reach
-position 447, the last the cache holds, stay computed as in the reference),
-cross-attention over 1500 encoder frames whose keys/values come from N(0, 1)
-encoder states through the decoder's own k/v projections (seeded weights).
-One step = the attention of one greedy decoder step: per layer, the
-self-attention with its key/value write, then the cross-attention; the 8
-launches of a step replay from one CUDA graph. Unit: decoded tokens (64 per
-step per GPU).
+Default workload (the headline): Whisper large-v3-turbo
+decoder-step attention in bf16 -- 4 decoder layers, 20 heads x 64, batch 64
+slots whose self-attention lengths start uniform in [1, 448] and grow by one
+per step (rows that reach position 447, the last the cache holds, stay
+computed, as in the reference), cross-attention over 1500 encoder frames whose
+keys/values come from N(0, 1) encoder states through the decoder's own k/v
+projections (seeded weights). One step = per layer, the self-attention with its
+key/value write, then the cross-attention; the 8 launches replay from one CUDA
+graph. Unit: decoded tokens (64 per step per GPU).
+
+Other workloads (``--workload``):
+  whisper-encoder  BASELINE config 3: encoder self-attention of 32 layers over
+                   32 windows of 1500 frames (20 x 64, bf16), non-causal; unit:
+                   windows (32 per step);
+  qwen3-decode     BASELINE config 4: Qwen3-1.7B-style decode attention, 28
+                   layers, 16 query / 8 key-value heads x 128, RoPE theta 1e6,
+                   QK-RMSNorm, batch 64 rows whose caches hold the 410-position
+                   prompt (390 audio + 20 text positions), then one position
+                   per step; unit: decoded tokens.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+                    [--workload NAME] [--batch B]
 
 ``--impl reference`` times the reference's CPU path for the same workload (the
-CPU oracle port of its attention, float32, all host threads) on a bounded
-sample of rows. Under torchrun every rank runs its own replica (weak scaling,
-no collective on the data path); rank 0 prints one JSON line.
+CPU oracle port of its attention in float32, all host threads) on a bounded
+sample. Under torchrun every rank runs its own replica (weak scaling, no
+collective on the data path); rank 0 prints one JSON line.
 """
 
 from __future__ import annotations
@@ -26,7 +36,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 from concurrent.futures import ThreadPoolExecutor
@@ -35,11 +44,7 @@ from pathlib import Path
 import numpy as np
 
 ROOT = Path(__file__).resolve().parent
-METRIC = "decoder tokens/s/GPU (batch 64, bf16) at 1/2/4/8 B200; attention HBM GB/s"
-UNIT = "tokens/s"
-
-BATCH, HEADS, HEAD_DIM, LAYERS = 64, 20, 64, 4
-TARGET, SOURCE, WIDTH = 448, 1500, 1280
+DECODE_METRIC = "decoder tokens/s/GPU (batch 64, bf16) at 1/2/4/8 B200; attention HBM GB/s"
 SEED = 1
 
 
@@ -49,42 +54,16 @@ def parse_args():
     parser.add_argument("--steps", type=int, default=128)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
-    parser.add_argument("--cpu-sample-rows", type=int, default=16,
-                        help="rows of the batch the CPU baseline times per step")
+    parser.add_argument("--workload", choices=("whisper-decode", "whisper-encoder", "qwen3-decode"),
+                        default="whisper-decode")
+    parser.add_argument("--batch", type=int, default=None,
+                        help="override the workload's batch (small profiling cases)")
     parser.add_argument("--cpu-seconds", type=float, default=10.0,
                         help="time budget of the CPU baseline sample")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-extras", action="store_true",
+                        help="skip the short runs of the other workloads in the default line")
     return parser.parse_args()
-
-
-def config_dict(n_gpus: int) -> dict:
-    return {
-        "workload": "whisper-large-v3-turbo decoder-step attention (BASELINE config 2)",
-        "model": "whisper-large-v3-turbo decoder attention, random init seed 1",
-        "layers": LAYERS, "heads": HEADS, "head_dim": HEAD_DIM, "batch_per_gpu": BATCH,
-        "global_batch": BATCH * n_gpus, "self_lengths": "U[1,448] at step 0, +1 per step",
-        "cross_frames": SOURCE, "step": "per layer: self-attn with KV append, then cross-attn",
-        "parallelism": f"replicas x{n_gpus} (no collective)",
-        "l2": "inputs larger than L2 (2.26 GB of K/V read per step)",
-    }
-
-
-def initial_lengths(rng: np.random.Generator) -> np.ndarray:
-    return rng.integers(1, TARGET + 1, size=BATCH)
-
-
-def positions_schedule(lengths: np.ndarray, steps: int) -> np.ndarray:
-    """(steps, batch) positions: start at length-1, +1 per step, capped at 447."""
-    start = lengths - 1
-    return np.minimum(start[None, :] + np.arange(steps)[:, None], TARGET - 1).astype(np.int64)
-
-
-def attention_bytes(positions: np.ndarray) -> tuple[float, float]:
-    """Algorithmic K/V bytes of one step: (self, cross), bf16."""
-    row = HEADS * HEAD_DIM * 2 * 2  # K and V, bf16
-    self_bytes = float(LAYERS * (positions.astype(np.float64) + 1).sum() * row)
-    cross_bytes = float(LAYERS * BATCH * SOURCE * row)
-    return self_bytes, cross_bytes
 
 
 # ---------------------------------------------------------------- clocks ----
@@ -113,23 +92,16 @@ class ClockSampler:
                 return handle
         return nvml.nvmlDeviceGetHandleByIndex(0) if count == 1 else None
 
+    def _sample(self):
+        nvml = self._nvml
+        sm = float(nvml.nvmlDeviceGetClockInfo(self._h, nvml.NVML_CLOCK_SM))
+        reasons = int(nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+        self.samples.append((sm, self._max_sm, reasons))
+
     def _run(self):
-        import threading  # noqa: F401
-
         try:
-            import pynvml as nvml
-
-            nvml.nvmlInit()
-            handle = self._handle(nvml)
-            if handle is None:
-                self.error = "no NVML device matches this GPU"
-                return
-            max_sm = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
-            while not self._stop.is_set():
-                sm = float(nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM))
-                reasons = int(nvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
-                self.samples.append((sm, max_sm, reasons))
-                self._stop.wait(0.005)
+            while not self._stop.wait(0.005):
+                self._sample()
         except Exception as exc:  # pragma: no cover - depends on the driver
             self.error = repr(exc)
 
@@ -137,18 +109,41 @@ class ClockSampler:
         import threading
 
         self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            self._nvml = nvml
+            self._h = self._handle(nvml)
+            if self._h is None:
+                self.error = "no NVML device matches this GPU"
+                return self
+            self._max_sm = float(nvml.nvmlDeviceGetMaxClockInfo(self._h, nvml.NVML_CLOCK_SM))
+        except Exception as exc:  # pragma: no cover - depends on the driver
+            self.error = repr(exc)
+            return self
+        # NVML is ready before the timed region starts; sampling runs beside it.
         self._thread = threading.Thread(target=self._run, daemon=True)
         self._thread.start()
         return self
 
+    def mark(self):
+        """Takes one sample now (called inside the timed region)."""
+        if self._thread is not None:
+            try:
+                self._sample()
+            except Exception as exc:  # pragma: no cover
+                self.error = repr(exc)
+
     def __exit__(self, *exc):
         self._stop.set()
-        self._thread.join(timeout=5)
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
-    def summary(self) -> dict | None:
+    def summary(self) -> dict:
         if not self.samples:
             return {"error": self.error or "no samples"}
-        # Samples taken while the GPU was busy (the timed region is all busy).
         reasons = sorted({name for _, _, bits in self.samples
                           for bit, name in self.REASONS.items() if bits & bit})
         return {"sm_mhz": statistics.median(s[0] for s in self.samples),
@@ -156,95 +151,28 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-# ------------------------------------------------------------- CPU oracle ----
-
-def cpu_oracle_rate(seed: int, rows: int, budget_s: float, threads: int) -> dict:
-    """Tokens/s of the CPU oracle (float32, the reference's CPU dtype) over
-    ``rows`` rows of the workload, stepping until ``budget_s`` seconds have
-    passed (at least one step): per step and layer, the self-attention with its
-    in-place cache write and the cross-attention, rows spread over ``threads``
-    threads (numpy's BLAS kept to one thread each)."""
-    steps = 64
-    sys.path.insert(0, str(ROOT))
-    from oracle import attention as oracle
-
+def measured_peaks() -> dict:
     try:
-        from threadpoolctl import threadpool_limits
-    except ImportError:  # pragma: no cover
-        threadpool_limits = None
-    rng = np.random.default_rng(seed)
-    lengths = initial_lengths(rng)[:rows]
-    positions = np.minimum(lengths[None, :] - 1 + np.arange(steps)[:, None], TARGET - 1)
-    self_k = rng.standard_normal((LAYERS, rows, HEADS, TARGET, HEAD_DIM), dtype=np.float32)
-    self_v = rng.standard_normal((LAYERS, rows, HEADS, TARGET, HEAD_DIM), dtype=np.float32)
-    cross_k = rng.standard_normal((LAYERS, rows, HEADS, SOURCE, HEAD_DIM), dtype=np.float32)
-    cross_v = rng.standard_normal((LAYERS, rows, HEADS, SOURCE, HEAD_DIM), dtype=np.float32)
-    q = rng.standard_normal((steps, LAYERS, 4, rows, HEADS, HEAD_DIM), dtype=np.float32)
-
-    def one_row(args):
-        t, layer, b = args
-        pos = positions[t, b:b + 1]
-        oracle.whisper_self_attention_step(
-            q[t, layer, 0, b:b + 1], q[t, layer, 1, b:b + 1], q[t, layer, 2, b:b + 1],
-            self_k[layer, b:b + 1], self_v[layer, b:b + 1], pos, compute=np.float32, copy=False)
-        oracle.whisper_cross_attention(q[t, layer, 3, b:b + 1], cross_k[layer, b:b + 1],
-                                       cross_v[layer, b:b + 1], compute=np.float32)
-
-    limit = threadpool_limits(1) if threadpool_limits else None
-    try:
-        with ThreadPoolExecutor(max_workers=threads) as pool:
-            start = time.perf_counter()
-            done = 0
-            while done < steps:
-                for layer in range(LAYERS):
-                    list(pool.map(one_row, [(done, layer, b) for b in range(rows)]))
-                done += 1
-                if time.perf_counter() - start >= budget_s:
-                    break
-            elapsed = time.perf_counter() - start
-    finally:
-        if limit is not None and hasattr(limit, "unregister"):
-            limit.unregister()
-    return {"value": rows * done / elapsed, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{rows} of {BATCH} rows x {done} steps x {LAYERS} layers "
-                      f"(self with in-place append + cross over {SOURCE}), float32 numpy "
-                      f"oracle, {elapsed:.1f} s"}
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        return {}
 
 
-def run_reference(args, rank: int, world: int) -> None:
-    """The reference arm: rank 0 times the CPU path; other ranks exit."""
-    if rank != 0:
-        return
-    threads = os.cpu_count() or 1
-    result = cpu_oracle_rate(SEED, args.cpu_sample_rows, args.cpu_seconds, threads)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": result["value"], "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": BATCH / result["value"] * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_dict(args.gpus), "cpu_baseline": result,
-        "e2e": {"value": result["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-        "note": "reference CPU path = CPU oracle port of the reference's attention "
-                "(the Python reference is not present on the GPU box)",
-    }
-    print(json.dumps(line), flush=True)
-
-
-# ----------------------------------------------------------------- native ----
-
-def measured_peak() -> tuple[float, str]:
-    path = ROOT / "MEASURED_PEAKS.json"
-    try:
-        peaks = json.loads(path.read_text())
-        return float(peaks["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
-    except (OSError, KeyError, ValueError):
+def peak_for(bound: str) -> tuple[float, str]:
+    peaks = measured_peaks()
+    if bound == "hbm":
+        if "hbm_gbs" in peaks:
+            return float(peaks["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy)"
         return 6650.0, "fallback 6.65 TB/s"
+    if "bf16_tflops" in peaks:
+        return float(peaks["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    return 1590.0, "fallback 1.59 PFLOP/s"
 
 
-def profiled_traffic() -> float | None:
-    """DRAM bytes per cross-attention launch from the committed ncu summary."""
-    path = ROOT / "profiles" / "whisper_cross_decode_b64_bf16.md"
+def profiled_traffic(name: str) -> float | None:
+    """DRAM bytes per launch of the dominant kernel, from its committed ncu
+    summary under profiles/ (a line ``traffic_bytes_per_launch: N``)."""
+    path = ROOT / "profiles" / name
     try:
         for line in path.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
@@ -254,76 +182,529 @@ def profiled_traffic() -> float | None:
     return None
 
 
-def run_native(args, rank: int, world: int, local_rank: int) -> None:
-    import torch
-    import torch.distributed as dist
+def run_cpu(fn, rows, budget_s: float, threads: int):
+    """Runs fn(step, row) over rows (a list) per step on `threads` threads until
+    `budget_s` seconds have passed (at least one step); returns (steps, seconds)."""
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = None
+    limit = threadpool_limits(1) if threadpool_limits else None
+    try:
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            start = time.perf_counter()
+            done = 0
+            while True:
+                list(pool.map(lambda r: fn(done, r), rows))
+                done += 1
+                if time.perf_counter() - start >= budget_s or done >= 1024:
+                    break
+            elapsed = time.perf_counter() - start
+    finally:
+        if limit is not None and hasattr(limit, "unregister"):
+            limit.unregister()
+    return done, elapsed
 
+
+# -------------------------------------------------------------- workloads ----
+
+class WhisperDecode:
+    """Whisper large-v3-turbo decoder-step attention."""
+
+    name = "whisper-decode"
+    metric = DECODE_METRIC
+    unit = "tokens/s"
+    bound = "hbm"
+    reference_in_graph = True
+    layers, heads, head_dim, target, source, width = 4, 20, 64, 448, 1500, 1280
+    profile = "whisper_cross_decode_b64_bf16.md"
+
+    def __init__(self, batch: int | None):
+        self.batch = batch or 64
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": "whisper-large-v3-turbo decoder-step attention (BASELINE config 2)",
+            "model": "whisper-large-v3-turbo decoder attention, random init seed 1",
+            "layers": self.layers, "heads": self.heads, "head_dim": self.head_dim,
+            "batch_per_gpu": self.batch, "global_batch": self.batch * world,
+            "self_lengths": "U[1,448] at step 0, +1 per step (capped at 447)",
+            "cross_frames": self.source,
+            "step": "per layer: self-attn with KV append, then cross-attn",
+            "parallelism": f"replicas x{world} (no collective)",
+            "l2": "inputs larger than L2 (about 2.26 GB of K/V read per step)",
+        }
+
+    def units_per_step(self) -> int:
+        return self.batch
+
+    def lengths(self, rng) -> np.ndarray:
+        return rng.integers(1, self.target + 1, size=self.batch)
+
+    def setup(self, torch, device, seed: int, total: int) -> None:
+        from asrback_b200 import whisper
+        from asrback_b200.synthetic import seeded_parameters
+
+        dtype = torch.bfloat16
+        rng = np.random.default_rng(seed)
+        lengths = self.lengths(rng)
+        start = lengths - 1
+        self.schedule = np.minimum(start[None, :] + np.arange(total)[:, None],
+                                   self.target - 1).astype(np.int64)
+        config = whisper.large_v3_turbo_config()
+        model = whisper.WhisperForConditionalGeneration(config, encoder=False)
+        seeded_parameters(model.model.decoder, SEED)
+        model = model.to(device, dtype).eval()
+        self.cache = model.allocate_cache(self.batch)
+        gen = torch.Generator(device=device).manual_seed(seed)
+        with torch.no_grad():
+            for b0 in range(0, self.batch, 16):
+                b1 = min(self.batch, b0 + 16)
+                states = torch.randn((b1 - b0, self.source, self.width), generator=gen,
+                                     device=device, dtype=dtype)
+                model.set_encoder_output(self.cache.rows(b0, b1), states)
+            for layer in range(self.layers):
+                for b in range(self.batch):
+                    p = int(lengths[b]) - 1
+                    if p > 0:
+                        self.cache.self_keys[layer, b, :, :p].normal_(generator=gen)
+                        self.cache.self_values[layer, b, :, :p].normal_(generator=gen)
+        del model
+        shape = (self.layers, 4, self.batch, self.heads, self.head_dim)
+        self.inputs = torch.randn((total,) + shape, generator=gen, device=device, dtype=dtype)
+        self.positions_all = torch.from_numpy(self.schedule).to(device)
+        self.step_in = torch.empty(shape, device=device, dtype=dtype)
+        self.pos = torch.empty((self.batch,), device=device, dtype=torch.int64)
+        self.outputs: list = [None] * (2 * self.layers)
+
+    def step(self) -> None:
+        from asrback_b200 import attention
+
+        c = self.cache
+        for layer in range(self.layers):
+            x = self.step_in[layer]
+            self.outputs[2 * layer] = attention.whisper_self_attention_step(
+                x[0], x[1], x[2], c.self_keys[layer], c.self_values[layer], self.pos)
+            self.outputs[2 * layer + 1] = attention.whisper_cross_attention_step(
+                x[3], c.cross_keys[layer], c.cross_values[layer])
+
+    def launches_per_step(self) -> int:
+        return 2 * self.layers
+
+    def refresh(self, t: int) -> None:
+        self.step_in.copy_(self.inputs[t])
+        self.pos.copy_(self.positions_all[t])
+
+    def host_step_inputs(self, torch, first: int, count: int):
+        """Pinned host copies of steps first..first+count and their device targets."""
+        host_in = torch.empty((count,) + tuple(self.step_in.shape), dtype=self.step_in.dtype,
+                              pin_memory=True)
+        host_in.copy_(self.inputs[first:first + count].cpu())
+        host_pos = torch.from_numpy(self.schedule[first:first + count].copy()).pin_memory()
+        return [(host_in, self.step_in), (host_pos, self.pos)]
+
+    def row_bytes(self) -> int:
+        return self.heads * self.head_dim * 2 * 2  # K and V, bf16
+
+    def kernels(self, t: int):
+        """(name, launch function, algorithmic bytes of one launch) per kernel."""
+        from asrback_b200 import attention
+
+        c, x, pos = self.cache, self.inputs, self.positions_all
+        self_bytes = float((self.schedule[t] + 1).sum()) * self.row_bytes()
+        cross_bytes = float(self.batch * self.source * self.row_bytes())
+        return [
+            ("cross", lambda layer: attention.whisper_cross_attention_step(
+                x[t, layer, 3], c.cross_keys[layer], c.cross_values[layer]), cross_bytes),
+            ("self", lambda layer: attention.whisper_self_attention_step(
+                x[t, layer, 0], x[t, layer, 1], x[t, layer, 2], c.self_keys[layer],
+                c.self_values[layer], pos[t]), self_bytes),
+        ]
+
+    def step_work(self, first: int, count: int) -> float:
+        """Algorithmic bytes of steps first..first+count."""
+        sched = self.schedule[first:first + count]
+        per_row = self.row_bytes() * self.layers
+        return float(((sched + 1).sum() + count * self.batch * self.source) * per_row)
+
+    def torch_reference_step(self, torch):
+        """The reference's own GPU computation of one step's attention (torch SDPA
+        with its bool step mask and cuDNN-first backend priority, as
+        whisper.py:58-63 and :222-240 run it), for context."""
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        c, x = self.cache, self.step_in
+        key_positions = torch.arange(self.target, device=x.device)
+        backends = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
+                    SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
+        rows = torch.arange(self.batch, device=x.device)
+
+        def run():
+            mask = (key_positions[None, :] <= self.pos[:, None])[:, None, None, :]
+            with sdpa_kernel(backends, set_priority=True):
+                for layer in range(self.layers):
+                    q, k, v, qc = (x[layer, i][:, :, None, :] for i in range(4))
+                    c.self_keys[layer][rows, :, self.pos] = k[:, :, 0]
+                    c.self_values[layer][rows, :, self.pos] = v[:, :, 0]
+                    F.scaled_dot_product_attention(q, c.self_keys[layer], c.self_values[layer],
+                                                   attn_mask=mask)
+                    F.scaled_dot_product_attention(qc, c.cross_keys[layer], c.cross_values[layer])
+        return run
+
+    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+        from oracle import attention as oracle
+
+        rows, steps = 16, 64
+        rng = np.random.default_rng(seed)
+        lengths = self.lengths(rng)[:rows]
+        positions = np.minimum(lengths[None, :] - 1 + np.arange(steps)[:, None], self.target - 1)
+        f32 = np.float32
+        sk = rng.standard_normal((self.layers, rows, self.heads, self.target, self.head_dim), dtype=f32)
+        sv = rng.standard_normal(sk.shape, dtype=f32)
+        ck = rng.standard_normal((self.layers, rows, self.heads, self.source, self.head_dim), dtype=f32)
+        cv = rng.standard_normal(ck.shape, dtype=f32)
+        q = rng.standard_normal((steps, self.layers, 4, rows, self.heads, self.head_dim), dtype=f32)
+
+        def one(t, b):
+            t %= steps
+            for layer in range(self.layers):
+                oracle.whisper_self_attention_step(
+                    q[t, layer, 0, b:b + 1], q[t, layer, 1, b:b + 1], q[t, layer, 2, b:b + 1],
+                    sk[layer, b:b + 1], sv[layer, b:b + 1], positions[t, b:b + 1],
+                    compute=f32, copy=False)
+                oracle.whisper_cross_attention(q[t, layer, 3, b:b + 1], ck[layer, b:b + 1],
+                                               cv[layer, b:b + 1], compute=f32)
+
+        done, elapsed = run_cpu(one, list(range(rows)), budget_s, threads)
+        return {"value": rows * done / elapsed, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{rows} of {self.batch} rows x {done} steps x {self.layers} layers "
+                          f"(self with in-place append + cross over {self.source}), float32 "
+                          f"numpy oracle, {elapsed:.1f} s"}
+
+
+class WhisperEncoder:
+    """the encoder's self-attention prefill."""
+
+    name = "whisper-encoder"
+    metric = "encoder windows/s/GPU (32 windows x 1500 frames, 32 layers, bf16); attention TFLOP/s"
+    unit = "windows/s"
+    bound = "tensor"
+    reference_in_graph = False
+    layers, heads, head_dim, length = 32, 20, 64, 1500
+    profile = "whisper_encoder_attention_b32_bf16.md"
+
+    def __init__(self, batch: int | None):
+        self.batch = batch or 32
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": "whisper-large-v3-turbo encoder self-attention prefill (BASELINE config 3)",
+            "layers": self.layers, "heads": self.heads, "head_dim": self.head_dim,
+            "frames": self.length, "batch_per_gpu": self.batch, "global_batch": self.batch * world,
+            "step": "32 layers of non-causal attention over the batch's windows",
+            "inputs": "N(0,1) bf16 q/k/v per layer in the projections' (B, S, H*D) layout",
+            "parallelism": f"replicas x{world} (no collective)",
+            "l2": "inputs larger than L2 (369 MB of q/k/v per layer)",
+        }
+
+    def units_per_step(self) -> int:
+        return self.batch
+
+    def flops_per_layer(self) -> float:
+        return 4.0 * self.length ** 2 * self.head_dim * self.heads * self.batch
+
+    def setup(self, torch, device, seed: int, total: int) -> None:
+        gen = torch.Generator(device=device).manual_seed(seed)
+        shape = (self.batch, self.length, self.heads * self.head_dim)
+        self.qkv = [[torch.randn(shape, generator=gen, device=device, dtype=torch.bfloat16)
+                     for _ in range(3)] for _ in range(self.layers)]
+        self.outputs: list = [None] * self.layers
+
+    def views(self, layer: int):
+        b, s, h, d = self.batch, self.length, self.heads, self.head_dim
+        return [t.view(b, s, h, d).transpose(1, 2) for t in self.qkv[layer]]
+
+    def step(self) -> None:
+        from asrback_b200 import attention
+
+        for layer in range(self.layers):
+            self.outputs[layer] = attention.whisper_encoder_attention(*self.views(layer))
+
+    def launches_per_step(self) -> int:
+        return self.layers
+
+    def refresh(self, t: int) -> None:
+        pass
+
+    def host_step_inputs(self, torch, first: int, count: int):
+        # One layer's q/k/v in pinned memory, copied into every layer's inputs.
+        host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in self.qkv[0]]
+        for h, d in zip(host, self.qkv[0]):
+            h.copy_(d.cpu())
+        pairs = []
+        for layer in range(self.layers):
+            for i in range(3):
+                pairs.append((host[i][None].expand(count, *host[i].shape), self.qkv[layer][i]))
+        return pairs
+
+    def kernels(self, t: int):
+        from asrback_b200 import attention
+
+        return [("encoder", lambda layer: attention.whisper_encoder_attention(*self.views(layer)),
+                 self.flops_per_layer())]
+
+    def step_work(self, first: int, count: int) -> float:
+        return self.flops_per_layer() * self.layers * count
+
+    def torch_reference_step(self, torch):
+        """torch SDPA on the same tensors (the reference's encoder call, default
+        backend priority), for context."""
+        import torch.nn.functional as F
+
+        def run():
+            for layer in range(self.layers):
+                F.scaled_dot_product_attention(*self.views(layer))
+        return run
+
+    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+        from oracle import attention as oracle
+
+        rng = np.random.default_rng(seed)
+        f32 = np.float32
+        q, k, v = (rng.standard_normal((self.heads, self.length, self.head_dim), dtype=f32)
+                   for _ in range(3))
+
+        def one(_t, h):
+            oracle.sdpa(q[h], k[h], v[h], compute=f32)
+
+        done, elapsed = run_cpu(one, list(range(self.heads)), budget_s, threads)
+        # `done` layer-windows (all heads) in `elapsed`; a window needs 32 layers.
+        rate = done / elapsed / self.layers
+        return {"value": rate, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{done} layer-windows (20 heads x 1500 x 1500 each), float32 numpy "
+                          f"oracle, {elapsed:.1f} s, scaled by 1/32 layers"}
+
+
+class Qwen3Decode:
+    """Qwen3-1.7B-style decode attention."""
+
+    name = "qwen3-decode"
+    metric = "decoder tokens/s/GPU (Qwen3 1.7B-style, batch 64, bf16); attention HBM GB/s"
+    unit = "tokens/s"
+    bound = "hbm"
+    reference_in_graph = True
+    layers, heads, kv_heads, head_dim, cache_length, prompt = 28, 16, 8, 128, 1024, 410
+    profile = "qwen3_decode_b64_bf16.md"
+
+    def __init__(self, batch: int | None):
+        self.batch = batch or 64
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": "Qwen3-ASR-1.7B-style decode attention (BASELINE config 4)",
+            "layers": self.layers, "heads": self.heads, "kv_heads": self.kv_heads,
+            "head_dim": self.head_dim, "rope_theta": 1e6, "qk_rmsnorm": True,
+            "batch_per_gpu": self.batch, "global_batch": self.batch * world,
+            "cache": "(28, batch, 1024, 8, 128) bf16; 410 prompt positions filled with "
+                     "N(0,1) keys/values, then one position per step",
+            "parallelism": f"replicas x{world} (no collective)",
+            "l2": "inputs larger than L2 (about 3.5 GB of K/V read per step)",
+        }
+
+    def units_per_step(self) -> int:
+        return self.batch
+
+    def setup(self, torch, device, seed: int, total: int) -> None:
+        from asrback_b200 import qwen3_asr
+
+        dtype = torch.bfloat16
+        gen = torch.Generator(device=device).manual_seed(seed)
+        config = qwen3_asr.text_config_1_7b()
+        self.cache = qwen3_asr.KVCache.allocate(config, self.batch, self.cache_length,
+                                                device=device, dtype=dtype)
+        self.cache.keys[:, :, :self.prompt].normal_(generator=gen)
+        self.cache.values[:, :, :self.prompt].normal_(generator=gen)
+        self.cos, self.sin = qwen3_asr.rope_tables(1e6, self.head_dim, self.cache_length,
+                                                   device=device, dtype=dtype)
+        self.norms = (1 + 0.1 * torch.randn((self.layers, 2, self.head_dim), generator=gen,
+                                            device=device)).to(dtype)
+        width = (self.heads + 2 * self.kv_heads) * self.head_dim
+        self.inputs = torch.randn((total, self.layers, self.batch, width), generator=gen,
+                                  device=device, dtype=dtype)
+        self.schedule = np.minimum(self.prompt + np.arange(total)[:, None]
+                                   + np.zeros((1, self.batch), np.int64),
+                                   self.cache_length - 1).astype(np.int64)
+        self.positions_all = torch.from_numpy(self.schedule).to(device)
+        self.step_in = torch.empty((self.layers, self.batch, width), device=device, dtype=dtype)
+        self.pos = torch.empty((self.batch,), device=device, dtype=torch.int64)
+        self.outputs: list = [None] * self.layers
+
+    def attend(self, layer, qkv, pos):
+        from asrback_b200 import attention
+
+        return attention.qwen3_attention_step(
+            qkv, self.norms[layer, 0], self.norms[layer, 1], 1e-6, self.cos, self.sin, pos,
+            self.cache.keys[layer], self.cache.values[layer], self.heads, self.kv_heads)
+
+    def step(self) -> None:
+        for layer in range(self.layers):
+            self.outputs[layer] = self.attend(layer, self.step_in[layer], self.pos)
+
+    def launches_per_step(self) -> int:
+        return self.layers
+
+    def refresh(self, t: int) -> None:
+        self.step_in.copy_(self.inputs[t])
+        self.pos.copy_(self.positions_all[t])
+
+    def host_step_inputs(self, torch, first: int, count: int):
+        host_in = torch.empty((count,) + tuple(self.step_in.shape), dtype=self.step_in.dtype,
+                              pin_memory=True)
+        host_in.copy_(self.inputs[first:first + count].cpu())
+        host_pos = torch.from_numpy(self.schedule[first:first + count].copy()).pin_memory()
+        return [(host_in, self.step_in), (host_pos, self.pos)]
+
+    def row_bytes(self) -> int:
+        return self.kv_heads * self.head_dim * 2 * 2
+
+    def kernels(self, t: int):
+        x, pos = self.inputs, self.positions_all
+        bytes_ = float((self.schedule[t] + 1).sum()) * self.row_bytes()
+        return [("qwen3", lambda layer: self.attend(layer, x[t, layer], pos[t]), bytes_)]
+
+    def step_work(self, first: int, count: int) -> float:
+        sched = self.schedule[first:first + count]
+        return float((sched + 1).sum()) * self.row_bytes() * self.layers
+
+    def torch_reference_step(self, torch):
+        """The reference's GPU fallback on torch 2.11 (varlen_attn lacks the
+        kwargs it passes): q/k RMSNorm + RoPE in bf16, cache write, SDPA with
+        the bucket mask over the grouped heads (qwen3_asr.py:366-372, 392-432)."""
+        import torch.nn.functional as F
+
+        h, kvh, d = self.heads, self.kv_heads, self.head_dim
+        rows = torch.arange(self.batch, device=self.pos.device)
+        key_positions = torch.arange(self.cache_length, device=self.pos.device)
+
+        def rotate(x, cos, sin):
+            first, second = x.chunk(2, dim=-1)
+            return x * cos[:, None, :] + torch.cat((-second, first), dim=-1) * sin[:, None, :]
+
+        def run():
+            cos, sin = self.cos[self.pos], self.sin[self.pos]
+            mask = (key_positions[None, :] <= self.pos[:, None])[:, None, None, :]
+            for layer in range(self.layers):
+                q, k, v = self.step_in[layer].split([h * d, kvh * d, kvh * d], dim=-1)
+                q = rotate(F.rms_norm(q.reshape(-1, h, d), (d,), self.norms[layer, 0], 1e-6), cos, sin)
+                k = rotate(F.rms_norm(k.reshape(-1, kvh, d), (d,), self.norms[layer, 1], 1e-6), cos, sin)
+                keys, values = self.cache.keys[layer], self.cache.values[layer]
+                keys[rows, self.pos] = k
+                values[rows, self.pos] = v.reshape(-1, kvh, d)
+                F.scaled_dot_product_attention(q.view(-1, kvh, h // kvh, d), keys.transpose(1, 2),
+                                               values.transpose(1, 2), attn_mask=mask)
+        return run
+
+    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+        from oracle import attention as oracle
+
+        rows = 8
+        rng = np.random.default_rng(seed)
+        f32 = np.float32
+        width = (self.heads + 2 * self.kv_heads) * self.head_dim
+        keys = rng.standard_normal((rows, self.cache_length, self.kv_heads, self.head_dim), dtype=f32)
+        values = rng.standard_normal(keys.shape, dtype=f32)
+        qkv = rng.standard_normal((rows, width), dtype=f32)
+        w = np.ones(self.head_dim, f32)
+        cos, sin = oracle.rope_tables(1e6, self.head_dim, self.cache_length)
+
+        def one(t, b):
+            pos = np.array([min(self.prompt + t, self.cache_length - 1)])
+            for _layer in range(self.layers):
+                oracle.qwen3_decode_attention(qkv[b:b + 1], w, w, 1e-6, cos, sin, pos,
+                                              keys[b:b + 1], values[b:b + 1], self.heads,
+                                              self.kv_heads)
+
+        done, elapsed = run_cpu(one, list(range(rows)), budget_s, threads)
+        return {"value": rows * done / elapsed, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{rows} of {self.batch} rows x {done} steps x {self.layers} layers, "
+                          f"numpy oracle, {elapsed:.1f} s"}
+
+
+WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode)}
+
+
+# ------------------------------------------------------------------ arms ----
+
+def run_reference(args, rank: int) -> None:
+    """The reference arm: rank 0 times the CPU path of the workload."""
+    if rank != 0:
+        return
     sys.path.insert(0, str(ROOT))
-    from asrback_b200 import attention, whisper
-    from asrback_b200.synthetic import seeded_normal, seeded_parameters
+    work = WORKLOADS[args.workload](args.batch)
+    threads = os.cpu_count() or 1
+    result = work.cpu_rate(SEED, args.cpu_seconds, threads)
+    line = {
+        "impl": "reference", "metric": work.metric, "value": result["value"], "unit": work.unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": work.units_per_step() / result["value"] * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": work.config(args.gpus), "cpu_baseline": result,
+        "e2e": {"value": result["value"], "unit": work.unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "reference CPU path = CPU oracle port of the reference's attention in float32 "
+                "(the Python reference is not present on the GPU box)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def graph_time_ms(torch, fn, reps: int, replays: int = 4) -> float:
+    """Average device time of fn() launched `reps` times back to back from a
+    CUDA graph, over `replays` replays (CUDA events on the current stream)."""
     from asrback_b200.transcription import CapturedGraph
 
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    dtype = torch.bfloat16
+    graph = CapturedGraph(lambda: [fn(i) for i in range(reps)], warmup=1)
+    graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(replays):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / (replays * reps)
+
+
+def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, warmup: int,
+            cpu: bool) -> dict:
+    """Runs one workload: graph-replayed timed region, per-kernel timing, e2e."""
+    from asrback_b200 import attention
+    from asrback_b200.transcription import CapturedGraph
+
     seed = SEED + 1000 * rank
-    rng = np.random.default_rng(seed)
-    lengths = initial_lengths(rng)
-    total = args.warmup + args.steps
-    schedule = positions_schedule(lengths, total)
-
-    # Caches and cross K/V through the decoder's own projections (seeded).
-    config = whisper.large_v3_turbo_config()
-    model = whisper.WhisperForConditionalGeneration(config, encoder=False)
-    seeded_parameters(model.model.decoder, SEED)
-    model = model.to(device, dtype).eval()
-    cache = model.allocate_cache(BATCH)
-    gen = torch.Generator(device=device).manual_seed(seed)
-    with torch.no_grad():
-        for start in range(0, BATCH, 16):
-            states = torch.randn((16, SOURCE, WIDTH), generator=gen, device=device, dtype=dtype)
-            part = cache.rows(start, start + 16)
-            model.set_encoder_output(part, states)
-        for layer in range(LAYERS):
-            for b in range(BATCH):
-                p = int(lengths[b]) - 1
-                if p > 0:
-                    cache.self_keys[layer, b, :, :p].normal_(generator=gen)
-                    cache.self_values[layer, b, :, :p].normal_(generator=gen)
-    del model
-    inputs = torch.randn((total, LAYERS, 4, BATCH, HEADS, HEAD_DIM), generator=gen, device=device,
-                         dtype=dtype)
-    positions_all = torch.from_numpy(schedule).to(device)
-    step_in = torch.empty((LAYERS, 4, BATCH, HEADS, HEAD_DIM), device=device, dtype=dtype)
-    pos = torch.empty((BATCH,), device=device, dtype=torch.int64)
-    outputs: dict[int, torch.Tensor] = {}
-
-    def step():
-        for layer in range(LAYERS):
-            outputs[2 * layer] = attention.whisper_self_attention_step(
-                step_in[layer, 0], step_in[layer, 1], step_in[layer, 2],
-                cache.self_keys[layer], cache.self_values[layer], pos)
-            outputs[2 * layer + 1] = attention.whisper_cross_attention_step(
-                step_in[layer, 3], cache.cross_keys[layer], cache.cross_values[layer])
-
-    # Warm-up (eager) and capture, like the reference's CapturedGraph; the
-    # warm-up steps advance positions too (their share of the schedule).
-    step_in.copy_(inputs[0])
-    pos.copy_(positions_all[0])
-    graph = CapturedGraph(step)
-    for t in range(args.warmup):
-        step_in.copy_(inputs[t])
-        pos.copy_(positions_all[t])
+    total = warmup + steps
+    work.setup(torch, device, seed, total)
+    stream = torch.cuda.current_stream()
+    work.refresh(0)
+    graph = CapturedGraph(work.step)
+    for t in range(warmup):
+        work.refresh(t)
         graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
 
-    stream = torch.cuda.current_stream()
     uuid = getattr(torch.cuda.get_device_properties(device), "uuid", None)
-    uuid = f"GPU-{uuid}" if uuid and not str(uuid).startswith("GPU-") else (str(uuid) if uuid else None)
+    uuid = str(uuid) if uuid else None
 
-    # ---- timed region: device-resident inputs, graph replay per step ----
+    def max_over_ranks(ms: float) -> float:
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- timed region: device-resident inputs, one graph replay per step ----
     start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(uuid) as clocks:
         torch.cuda.synchronize()
@@ -331,126 +712,138 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
             dist.barrier()
         torch.cuda.nvtx.range_push("timed")
         start_ev.record(stream)
-        for t in range(args.warmup, total):
-            step_in.copy_(inputs[t])
-            pos.copy_(positions_all[t])
+        for t in range(warmup, total):
+            work.refresh(t)
             graph.replay()
+        clocks.mark()
         end_ev.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-    ms = start_ev.elapsed_time(end_ev)
-    if world > 1:
-        t_max = torch.tensor([ms], device=device)
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-        ms = float(t_max.item())
-    ms_per_step = ms / args.steps
-    value = BATCH * world * args.steps / (ms / 1e3)
+    ms = max_over_ranks(start_ev.elapsed_time(end_ev))
+    ms_per_step = ms / steps
+    value = work.units_per_step() * world * steps / (ms / 1e3)
 
-    # ---- kernel timing: average launch duration of each kernel, launched
-    # back to back from a captured graph (no host launch cost in the way) ----
-    kernel_ms = {}
-    launches = 4 * LAYERS
-    t_kernel = args.warmup
-
-    def cross_only():
-        for i in range(launches):
-            layer = i % LAYERS
-            attention.whisper_cross_attention_step(
-                inputs[t_kernel, layer, 3], cache.cross_keys[layer], cache.cross_values[layer])
-
-    def self_only():
-        for i in range(launches):
-            layer = i % LAYERS
-            attention.whisper_self_attention_step(
-                inputs[t_kernel, layer, 0], inputs[t_kernel, layer, 1], inputs[t_kernel, layer, 2],
-                cache.self_keys[layer], cache.self_values[layer], positions_all[t_kernel])
-
-    for name, fn in (("cross", cross_only), ("self", self_only)):
-        kgraph = CapturedGraph(fn, warmup=1)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        kgraph.replay()
-        torch.cuda.synchronize()
-        a.record(stream)
-        for _ in range(4):
-            kgraph.replay()
-        b.record(stream)
-        torch.cuda.synchronize()
-        kernel_ms[name] = a.elapsed_time(b) / (4 * launches)
-        del kgraph
-    self_bytes, cross_bytes = attention_bytes(schedule[args.warmup:])
-    self_bytes_kernel, _ = attention_bytes(schedule[t_kernel:t_kernel + 1])
-    self_bytes_per_launch = self_bytes_kernel / LAYERS
-    cross_bytes_per_launch = cross_bytes / LAYERS
-    peak, peak_kind = measured_peak()
-    achieved = cross_bytes_per_launch / (kernel_ms["cross"] * 1e-3) / 1e9
-    step_bytes = (self_bytes / args.steps + cross_bytes)
+    # ---- kernel timing: average launch duration, launched from a graph ----
+    kernel = {}
+    layers = work.launches_per_step() if work.name != "whisper-decode" else work.layers
+    for name, fn, amount in work.kernels(warmup):
+        launch_ms = graph_time_ms(torch, lambda i: fn(i % layers), 2 * layers)
+        kernel[name] = {"launch_ms": launch_ms, "work_per_launch": amount}
 
     # ---- e2e: pinned host inputs in, outputs back, every step ----
-    host_in = torch.empty((args.steps,) + tuple(step_in.shape), dtype=dtype, pin_memory=True)
-    host_in.copy_(inputs[args.warmup:total].cpu())
-    host_pos = torch.from_numpy(schedule[args.warmup:]).pin_memory()
-    out_list = [outputs[i] for i in range(2 * LAYERS)]
-    out_bytes = sum(o.numel() * o.element_size() for o in out_list)
-    host_out = torch.empty((args.steps, out_bytes), dtype=torch.uint8, pin_memory=True)
-    in_bytes = step_in.numel() * step_in.element_size() + BATCH * 8
-    # Restore the warm-up state's positions so e2e decodes the same schedule.
+    e2e_steps = min(steps, 4) if work.name == "whisper-encoder" else steps
+    pairs = work.host_step_inputs(torch, warmup, e2e_steps)
+    outs = [o for o in work.outputs]
+    out_bytes = sum(o.numel() * o.element_size() for o in outs)
+    host_out = torch.empty((out_bytes,), dtype=torch.uint8, pin_memory=True)
+    in_bytes = sum(dev.numel() * dev.element_size() for _, dev in pairs)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for i in range(args.steps):
-        step_in.copy_(host_in[i], non_blocking=True)
-        pos.copy_(host_pos[i], non_blocking=True)
+    for i in range(e2e_steps):
+        for host, dev in pairs:
+            dev.copy_(host[i], non_blocking=True)
         graph.replay()
         offset = 0
-        for o in out_list:
+        for o in outs:
             n = o.numel() * o.element_size()
-            host_out[i, offset:offset + n].copy_(o.view(-1).view(torch.uint8), non_blocking=True)
+            host_out[offset:offset + n].copy_(o.reshape(-1).view(torch.uint8), non_blocking=True)
             offset += n
     e_end.record(stream)
     torch.cuda.synchronize()
-    e_ms = e_start.elapsed_time(e_end)
-    if world > 1:
-        t_max = torch.tensor([e_ms], device=device)
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-        e_ms = float(t_max.item())
-    e2e = BATCH * world * args.steps / (e_ms / 1e3)
+    e_ms = max_over_ranks(e_start.elapsed_time(e_end))
+    e2e = work.units_per_step() * world * e2e_steps / (e_ms / 1e3)
 
+    # ---- the reference's GPU computation on the same tensors, for context:
+    # graph-replayed where the reference captures it (decoder steps), eager
+    # where it does not (the encoder) ----
+    ref_fn = work.torch_reference_step(torch)
+    if work.reference_in_graph:
+        ref_graph = CapturedGraph(ref_fn)
+        ref_fn = ref_graph.replay
+    else:
+        for _ in range(3):
+            ref_fn()
+    r_start, r_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    r_start.record(stream)
+    for t in range(warmup, total):
+        work.refresh(t)
+        ref_fn()
+    r_end.record(stream)
+    torch.cuda.synchronize()
+    ref_ms = r_start.elapsed_time(r_end) / steps
+    ref_graph = None
+
+    dominant = work.kernels(warmup)[0]
+    dom = kernel[dominant[0]]
+    peak, peak_kind = peak_for(work.bound)
+    if work.bound == "hbm":
+        achieved = dom["work_per_launch"] / (dom["launch_ms"] * 1e-3) / 1e9
+        unit = "GB/s"
+    else:
+        achieved = dom["work_per_launch"] / (dom["launch_ms"] * 1e-3) / 1e12
+        unit = "TFLOP/s"
+    traffic = profiled_traffic(work.profile)
     status = attention.read_status(device)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        cpu = cpu_oracle_rate(SEED, args.cpu_sample_rows, args.cpu_seconds, threads)
+    result = {
+        "metric": work.metric, "value": value, "unit": work.unit, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": work.config(world),
+        "e2e": {"value": e2e, "unit": work.unit, "h2d_bytes_per_step": in_bytes,
+                "d2h_bytes_per_step": out_bytes, "steps": e2e_steps},
+        "roofline": {"bound": work.bound, "kernel": dominant[0], "achieved": achieved,
+                     "peak": peak, "unit": unit, "frac": achieved / peak, "peak_kind": peak_kind,
+                     "traffic": traffic, "work_per_launch": dom["work_per_launch"],
+                     "launch_ms": dom["launch_ms"]},
+        "kernels": {
+            name: dict(k, rate=(k["work_per_launch"] / (k["launch_ms"] * 1e-3)
+                                / (1e9 if work.bound == "hbm" else 1e12)),
+                       rate_unit=unit)
+            for name, k in kernel.items()},
+        "step_rate": {"value": work.step_work(warmup, steps) / steps / (ms_per_step * 1e-3)
+                      / (1e9 if work.bound == "hbm" else 1e12), "unit": unit},
+        "torch_gpu_reference": {
+            "ms_per_step": ref_ms, "value": work.units_per_step() / (ref_ms * 1e-3),
+            "unit": work.unit,
+            "what": "the reference's attention computation in torch on this GPU (same tensors)"},
+        "gpu_launches": work.launches_per_step() * steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if cpu and rank == 0 and world == 1:
+        result["cpu_baseline"] = work.cpu_rate(SEED, args.cpu_seconds, os.cpu_count() or 1)
+    return result
 
+
+def run_native(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    work = WORKLOADS[args.workload](args.batch)
+    line = measure(args, work, torch, dist, device, rank, world, args.steps, args.warmup,
+                   cpu=not args.no_cpu_baseline)
+    if args.workload == "whisper-decode" and not args.no_extras and args.batch is None:
+        # Short runs of the other two BASELINE workloads, for context.
+        extras = {}
+        for name in ("whisper-encoder", "qwen3-decode"):
+            del work
+            torch.cuda.empty_cache()
+            work = WORKLOADS[name](None)
+            r = measure(args, work, torch, dist, device, rank, world, min(args.steps, 16),
+                        max(3, min(args.warmup, 5)), cpu=False)
+            extras[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "e2e",
+                                              "roofline", "step_rate", "torch_gpu_reference",
+                                              "clocks", "device_status", "config")}
+        line["other_workloads"] = extras
     if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": config_dict(world),
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": in_bytes,
-                    "d2h_bytes_per_step": out_bytes},
-            "roofline": {"bound": "hbm", "kernel": "decode_attention_kernel (cross, Whisper)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": profiled_traffic(),
-                         "algorithmic_bytes_per_launch": cross_bytes_per_launch,
-                         "launch_ms": kernel_ms["cross"]},
-            "kernels": {
-                "self_attention_ms": kernel_ms["self"],
-                "self_attention_gbs": self_bytes_per_launch / (kernel_ms["self"] * 1e-3) / 1e9,
-                "cross_attention_ms": kernel_ms["cross"],
-                "cross_attention_gbs": achieved,
-                "step_attention_gbs": step_bytes / (ms_per_step * 1e-3) / 1e9,
-            },
-            "gpu_launches": 2 * LAYERS * args.steps,
-            "clocks": clocks.summary(),
-            "cpu_baseline": cpu,
-            "device_status": status,
-        }
         print(json.dumps(line), flush=True)
 
 
@@ -463,7 +856,7 @@ def main() -> None:
         print("bench.py: --warmup below 3 is not allowed", file=sys.stderr)
         sys.exit(2)
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        run_reference(args, rank)
         return
     if world > 1:
         import datetime
