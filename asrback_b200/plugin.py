@@ -1,0 +1,129 @@
+"""Drop-in: puts the sm_100a kernels behind the reference's own attention call sites.
+
+``install()`` patches, in place, the classes of the reference's modules
+(``asrback.models.whisper`` and ``asrback.models.qwen3_asr``, or modules with
+the same class names and attributes). Everything around the call sites stays
+the reference's: its Transcriber classes, continuous-batching scheduler,
+caches and ``CapturedGraph`` capture the patched steps unchanged, since the
+kernels read row positions on the device and allocate nothing per call.
+
+Patched call sites (asrback project paths):
+
+- ``whisper.DecoderLayer.forward`` (``src/asrback/models/whisper.py:212-241``):
+  the fixed-shape step branch (``length is None``) runs the self-attention
+  with its key/value write as one kernel and the cross-attention as another;
+  the eager prefix branch (``length`` given) is left to the original method;
+- ``whisper.MultiHeadAttention.forward`` (``whisper.py:108-110``): the
+  encoder's unmasked self-attention;
+- ``qwen3_asr.TextModel.step`` (``src/asrback/models/qwen3_asr.py:494-524``)
+  and ``qwen3_asr.TextAttention.step`` (``qwen3_asr.py:392-432``): the decoder
+  step hands ``qkv_proj``'s output, the full RoPE tables and the positions to
+  one kernel (RMSNorm, RoPE, cache write, grouped-query attention); no mask
+  or varlen triple is built.
+
+The patched methods run the kernels only: tensors on the CPU raise, as every
+op of this package does (there is no fallback).
+"""
+
+from __future__ import annotations
+
+import importlib
+
+import torch.nn.functional as F
+
+from . import attention
+
+__all__ = ["install", "uninstall", "installed"]
+
+_originals: dict[tuple[object, str], object] = {}
+
+
+def _patch(cls, name: str, function) -> None:
+    key = (cls, name)
+    if key not in _originals:
+        _originals[key] = cls.__dict__[name]
+    setattr(cls, name, function)
+
+
+def installed() -> bool:
+    return bool(_originals)
+
+
+def uninstall() -> None:
+    """Restores every patched method."""
+    for (cls, name), function in _originals.items():
+        setattr(cls, name, function)
+    _originals.clear()
+
+
+def _whisper_decoder_layer_forward(original):
+    def forward(self, x, cache, positions, length, mask):
+        if length is not None:
+            return original(self, x, cache, positions, length, mask)
+        self_keys, self_values, cross_keys, cross_values = cache
+        hidden = self.self_attn_layer_norm(x)
+        query = self.self_attn._split_heads(self.self_attn.q_proj(hidden))
+        key, value = self.self_attn.project_key_value(hidden)
+        out = attention.whisper_self_attention_step(query, key, value, self_keys, self_values,
+                                                    positions)
+        x = x + self.self_attn.out_proj(out)
+        hidden = self.encoder_attn_layer_norm(x)
+        query = self.encoder_attn._split_heads(self.encoder_attn.q_proj(hidden))
+        out = attention.whisper_cross_attention_step(query, cross_keys, cross_values)
+        x = x + self.encoder_attn.out_proj(out)
+        return x + self.fc2(F.gelu(self.fc1(self.final_layer_norm(x))))
+
+    forward.__doc__ = original.__doc__
+    return forward
+
+
+def _whisper_encoder_attention_forward(self, x):
+    """Unmasked self-attention on the encoder kernel."""
+    query = self._split_heads(self.q_proj(x))
+    key, value = self.project_key_value(x)
+    return self.out_proj(attention.whisper_encoder_attention(query, key, value))
+
+
+def _qwen3_text_attention_step(self, x, keys, values, positions, mask, cos, sin):
+    """One token per row; ``cos``/``sin`` are the full tables (the patched
+    ``TextModel.step`` passes them ungathered), ``mask`` is unused."""
+    out = attention.qwen3_attention_step(
+        self.qkv_proj(x), self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, cos, sin,
+        positions, keys, values, self.heads, self.kv_heads)
+    return self.o_proj(out)
+
+
+def _qwen3_text_model_step(self, tokens, positions, cache, cos, sin, varlen):
+    """Hidden states for one token per row over a fixed-shape cache view; each
+    row reads only its written keys, whatever ``varlen`` says."""
+    x = self.embed_tokens(tokens)
+    for index, layer in enumerate(self.layers):
+        keys, values = cache.keys[index], cache.values[index]
+        x = layer(x, lambda attn, h, keys=keys, values=values: attn.step(
+            h, keys, values, positions, None, cos, sin))
+    return self.norm(x)
+
+
+def install(whisper_module=None, qwen3_module=None) -> None:
+    """Patches the reference's Whisper and Qwen3-ASR classes (importing
+    ``asrback.models.whisper`` / ``asrback.models.qwen3_asr`` when no module is
+    given; a module that cannot be imported is skipped)."""
+    if whisper_module is None:
+        whisper_module = _try_import("asrback.models.whisper")
+    if qwen3_module is None:
+        qwen3_module = _try_import("asrback.models.qwen3_asr")
+    if whisper_module is not None:
+        layer = whisper_module.DecoderLayer
+        original = _originals.get((layer, "forward"), layer.__dict__["forward"])
+        _patch(layer, "forward", _whisper_decoder_layer_forward(original))
+        _patch(whisper_module.MultiHeadAttention, "forward", _whisper_encoder_attention_forward)
+    if qwen3_module is not None:
+        _patch(qwen3_module.TextAttention, "step", _qwen3_text_attention_step)
+        _patch(qwen3_module.TextModel, "step", _qwen3_text_model_step)
+
+
+def _try_import(name: str):
+    try:
+        return importlib.import_module(name)
+    except ImportError:
+        return None

@@ -1,0 +1,183 @@
+"""The plugin's wiring at the reference's own call sites (CPU, float32).
+
+The reference's modules are imported read-only (skipped where they are not
+mounted). With the plugin installed, the ops of asrback_b200.attention are
+replaced here by CPU stand-ins built on the oracle (test-only; the product
+ops have no CPU path), so the patched reference runs end to end on the host
+and must reproduce the unpatched reference: same hidden states, same cache
+writes. This pins the argument layouts the plugin hands to the kernels.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from asrback_b200 import attention, plugin
+from asrback_b200.synthetic import seeded_normal, seeded_parameters
+from oracle import attention as oracle
+
+REFERENCE = Path("/root/reference/src")
+pytestmark = pytest.mark.skipif(not REFERENCE.is_dir(), reason="reference checkout not mounted")
+
+
+@pytest.fixture(scope="module")
+def reference():
+    from tests.golden.make_golden import install_asrfront_stub
+
+    install_asrfront_stub()
+    sys.path.insert(0, str(REFERENCE))
+    from asrback.models import qwen3_asr, whisper
+
+    return whisper, qwen3_asr
+
+
+@pytest.fixture
+def cpu_ops(monkeypatch):
+    """Oracle-backed CPU stand-ins with the ops' signatures and side effects."""
+
+    def self_step(query, key, value, key_cache, value_cache, positions, scale=None):
+        q, k, v = (t[:, :, 0] if t.dim() == 4 else t for t in (query, key, value))
+        out, kc, vc = oracle.whisper_self_attention_step(
+            q.numpy(), k.numpy(), v.numpy(), key_cache.numpy(), value_cache.numpy(),
+            positions.numpy())
+        key_cache.copy_(torch.from_numpy(kc))
+        value_cache.copy_(torch.from_numpy(vc))
+        b, h, d = q.shape
+        return torch.from_numpy(out).float().reshape(b, 1, h * d)
+
+    def cross_step(query, key_cache, value_cache, scale=None):
+        q = query[:, :, 0] if query.dim() == 4 else query
+        out = oracle.whisper_cross_attention(q.numpy(), key_cache.numpy(), value_cache.numpy())
+        b, h, d = q.shape
+        return torch.from_numpy(out).float().reshape(b, 1, h * d)
+
+    def encoder(q, k, v, scale=None):
+        out = oracle.encoder_attention(q.numpy(), k.numpy(), v.numpy())
+        b, h, s, d = q.shape
+        return torch.from_numpy(out).float().transpose(1, 2).reshape(b, s, h * d)
+
+    def qwen3_step(qkv, qn, kn, eps, cos, sin, positions, keys, values, heads, kv_heads,
+                   scale=None):
+        out, kc, vc = oracle.qwen3_decode_attention(
+            qkv.detach().numpy(), qn.detach().numpy(), kn.detach().numpy(), eps, cos.numpy(),
+            sin.numpy(), positions.numpy(), keys.numpy(), values.numpy(), heads, kv_heads)
+        keys.copy_(torch.from_numpy(kc))
+        values.copy_(torch.from_numpy(vc))
+        return torch.from_numpy(out).float()
+
+    monkeypatch.setattr(attention, "whisper_self_attention_step", self_step)
+    monkeypatch.setattr(attention, "whisper_cross_attention_step", cross_step)
+    monkeypatch.setattr(attention, "whisper_encoder_attention", encoder)
+    monkeypatch.setattr(attention, "qwen3_attention_step", qwen3_step)
+    yield
+    plugin.uninstall()
+
+
+def _whisper(whisper):
+    config = dict(d_model=128, encoder_attention_heads=2, decoder_attention_heads=2,
+                  encoder_layers=1, decoder_layers=2, encoder_ffn_dim=64, decoder_ffn_dim=64,
+                  num_mel_bins=8, max_source_positions=24, max_target_positions=32, vocab_size=50)
+    model = whisper.WhisperForConditionalGeneration(config).eval()
+    seeded_parameters(model, 5)
+    return model
+
+
+@torch.no_grad()
+def test_whisper_decoder_step(reference, cpu_ops):
+    whisper, _ = reference
+    model = _whisper(whisper)
+    positions = torch.tensor([0, 3, 31])
+    tokens = torch.tensor([[1], [7], [49]])
+
+    def run():
+        cache = model.allocate_cache(3)
+        model.set_encoder_output(cache, seeded_normal((3, 24, 128), 1))
+        for layer in range(2):
+            cache.self_keys[layer].copy_(seeded_normal(cache.self_keys[layer].shape, 10 + layer))
+            cache.self_values[layer].copy_(seeded_normal(cache.self_values[layer].shape, 20 + layer))
+        hidden = model.decode(tokens, positions, cache)
+        return hidden, cache
+
+    want, want_cache = run()
+    plugin.install(whisper, None)
+    got, got_cache = run()
+    assert torch.allclose(got, want, atol=1e-4), (got - want).abs().max()
+    # Later layers' keys differ in the last bits (their inputs carry the first
+    # layer's float64-oracle vs float32-SDPA difference).
+    assert torch.allclose(got_cache.self_keys, want_cache.self_keys, atol=1e-5)
+    assert torch.allclose(got_cache.self_values, want_cache.self_values, atol=1e-5)
+
+
+@torch.no_grad()
+def test_whisper_prefix_pass_keeps_reference_path(reference, cpu_ops):
+    """The eager multi-token prefix pass is not the plugin's: it runs the
+    reference's own code (and its results are unchanged)."""
+    whisper, _ = reference
+    model = _whisper(whisper)
+    cache = model.allocate_cache(2)
+    model.set_encoder_output(cache, seeded_normal((2, 24, 128), 1))
+    tokens = torch.tensor([[1, 2, 3], [4, 5, 6]])
+    want = model.decode(tokens, torch.arange(3), cache, length=3)
+    plugin.install(whisper, None)
+    got = model.decode(tokens, torch.arange(3), cache, length=3)
+    assert torch.equal(got, want)
+
+
+@torch.no_grad()
+def test_whisper_encoder_attention(reference, cpu_ops):
+    whisper, _ = reference
+    module = whisper.MultiHeadAttention(128, 2).eval()
+    seeded_parameters(module, 6)
+    x = seeded_normal((2, 40, 128), 2)
+    want = module(x)
+    plugin.install(whisper, None)
+    got = module(x)
+    assert torch.allclose(got, want, atol=1e-4), (got - want).abs().max()
+
+
+@torch.no_grad()
+def test_qwen3_text_model_step(reference, cpu_ops):
+    _, qwen3 = reference
+    config = dict(vocab_size=64, hidden_size=256, num_hidden_layers=2, num_attention_heads=16,
+                  num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6, intermediate_size=64)
+    model = qwen3.TextModel(config).eval()
+    seeded_parameters(model, 7)
+    inverse = 1.0 / (1e6 ** (torch.arange(0, 128, 2).float() / 128))
+    angles = torch.arange(48).float()[:, None] * inverse[None, :]
+    angles = torch.cat((angles, angles), dim=-1)
+    cos, sin = angles.cos(), angles.sin()
+    positions = torch.tensor([0, 17, 47])
+    tokens = torch.tensor([3, 9, 60])
+
+    def run():
+        keys = seeded_normal((2, 3, 48, 8, 128), 30)
+        values = seeded_normal((2, 3, 48, 8, 128), 31)
+        cache = qwen3.KVCache(keys, values)
+        return model.step(tokens, positions, cache, cos, sin, varlen=False), cache
+
+    want, want_cache = run()
+    plugin.install(None, qwen3)
+    got, got_cache = run()
+    assert torch.allclose(got, want, atol=1e-4), (got - want).abs().max()
+    rows = np.arange(3)
+    np.testing.assert_allclose(got_cache.keys.numpy()[:, rows, positions.numpy()],
+                               want_cache.keys.numpy()[:, rows, positions.numpy()], atol=1e-5)
+    assert torch.allclose(got_cache.values, want_cache.values, atol=1e-5)
+
+
+def test_uninstall_restores_reference(reference):
+    whisper, qwen3 = reference
+    before = (whisper.DecoderLayer.forward, whisper.MultiHeadAttention.forward,
+              qwen3.TextAttention.step, qwen3.TextModel.step)
+    plugin.install(whisper, qwen3)
+    assert plugin.installed()
+    assert whisper.DecoderLayer.forward is not before[0]
+    plugin.uninstall()
+    after = (whisper.DecoderLayer.forward, whisper.MultiHeadAttention.forward,
+             qwen3.TextAttention.step, qwen3.TextModel.step)
+    assert after == before
