@@ -459,12 +459,24 @@ class WhisperEncoder:
 
     def torch_reference_step(self, torch):
         """torch SDPA on the same tensors (the reference's encoder call, default
-        backend priority), for context."""
+        backend priority, eager as the reference runs it), for context."""
         import torch.nn.functional as F
 
         def run():
             for layer in range(self.layers):
                 F.scaled_dot_product_attention(*self.views(layer))
+        return run
+
+    def torch_cudnn_step(self, torch):
+        """The same with torch's cuDNN attention backend forced (the fastest
+        torch kernel for this shape on B200)."""
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        def run():
+            with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                for layer in range(self.layers):
+                    F.scaled_dot_product_attention(*self.views(layer))
         return run
 
     def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
@@ -697,12 +709,7 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     uuid = getattr(torch.cuda.get_device_properties(device), "uuid", None)
     uuid = str(uuid) if uuid else None
 
-    def max_over_ranks(ms: float) -> float:
-        if world == 1:
-            return ms
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    from asrback_b200.replicas import max_over_ranks
 
     # ---- timed region: device-resident inputs, one graph replay per step ----
     start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -778,6 +785,20 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     torch.cuda.synchronize()
     ref_ms = r_start.elapsed_time(r_end) / steps
     ref_graph = None
+    cudnn = None
+    if hasattr(work, "torch_cudnn_step"):
+        fn = work.torch_cudnn_step(torch)
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        r_start.record(stream)
+        for _ in range(steps):
+            fn()
+        r_end.record(stream)
+        torch.cuda.synchronize()
+        c_ms = r_start.elapsed_time(r_end) / steps
+        cudnn = {"ms_per_step": c_ms, "value": work.units_per_step() / (c_ms * 1e-3),
+                 "unit": work.unit, "what": "torch SDPA with the cuDNN backend forced, eager"}
 
     dominant = work.kernels(warmup)[0]
     dom = kernel[dominant[0]]
@@ -811,6 +832,7 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
             "ms_per_step": ref_ms, "value": work.units_per_step() / (ref_ms * 1e-3),
             "unit": work.unit,
             "what": "the reference's attention computation in torch on this GPU (same tensors)"},
+        "torch_gpu_cudnn": cudnn,
         "gpu_launches": work.launches_per_step() * steps,
         "clocks": clocks.summary(),
         "device_status": status,
@@ -841,7 +863,8 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
                         max(3, min(args.warmup, 5)), cpu=False)
             extras[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "e2e",
                                               "roofline", "step_rate", "torch_gpu_reference",
-                                              "clocks", "device_status", "config")}
+                                              "torch_gpu_cudnn", "clocks", "device_status",
+                                              "config")}
         line["other_workloads"] = extras
     if rank == 0:
         print(json.dumps(line), flush=True)
