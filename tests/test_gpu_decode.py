@@ -232,6 +232,41 @@ def test_position_outside_cache_sets_status_and_skips_row():
     assert torch.count_nonzero(out[0]) > 0
 
 
+@pytest.mark.parametrize("tag", ["bf16", "fp32"])
+def test_ragged_rows_share_ctas_and_rearm(tag):
+    """Rows of very different lengths, rows outside the view and a row at
+    position 0 in one call: the long row is split over many CTAs while short
+    rows take one. Three calls on the same workspace must each match the
+    reference (the split-merge counters re-arm themselves)."""
+    dtype = DTYPES[tag]
+    gen = torch.Generator().manual_seed(11)
+    dim, kv_heads, heads, bucket = 128, 8, 16, 1024
+    qkv, qn, kn, cos, sin, k_store, v_store, _ = _qwen3_inputs(gen, 4, bucket, heads, dtype)
+    kd, vd = k_store.to(DEV), v_store.to(DEV)
+    for positions in ([bucket - 1, 0, bucket + 5, 3], [-1, 700, 1, bucket - 1], [17, 16, 15, 0]):
+        positions = torch.tensor(positions)
+        k_before, v_before = host(kd), host(vd)
+        out = attention.qwen3_attention_step(qkv.to(DEV), qn.to(DEV), kn.to(DEV), 1e-6,
+                                             cos.to(DEV), sin.to(DEV), positions.to(DEV),
+                                             kd[:4, :bucket], vd[:4, :bucket], heads, kv_heads)
+        valid = ((positions >= 0) & (positions < bucket)).numpy()
+        safe = torch.where(torch.from_numpy(valid), positions, torch.zeros_like(positions))
+        want, k_after, _ = oracle.qwen3_decode_attention(
+            qkv.float().numpy(), qn.float().numpy(), kn.float().numpy(), 1e-6,
+            cos.float().numpy(), sin.float().numpy(), safe.numpy(), k_before[:4, :bucket],
+            v_before[:4, :bucket], heads, kv_heads, bf16=dtype == torch.bfloat16)
+        got = host(out)
+        np.testing.assert_allclose(got[valid], want[valid], atol=TOL[dtype], rtol=0)
+        assert not got[~valid].any()
+        got_k = host(kd)
+        np.testing.assert_allclose(got_k[:4][valid, :bucket], k_after[valid], atol=TOL[dtype],
+                                   rtol=0)
+        np.testing.assert_array_equal(got_k[:4][~valid], k_before[:4][~valid])
+        status = attention.read_status()
+        assert bool(status & _native.STATUS_POSITION) == (not valid.all())
+        assert not status & _native.STATUS_TIMEOUT
+
+
 def test_graph_capture_replays_with_new_positions():
     from asrback_b200.transcription import CapturedGraph
 
