@@ -429,26 +429,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
       constexpr uint32_t kIdescPV = idesc_bf16(kRows, kDim, true);
-      const uint32_t q_addr = smem_addr(smem + kOffQ);
-      const uint32_t k_addr = smem_addr(smem + kOffK);
-      const uint32_t v_addr = smem_addr(smem + kOffV);
+      // Descriptors are built once; a step moves the start-address field
+      // (address >> 4): 32 bytes along K inside a swizzled row (Q, K), two
+      // 8-row swizzle atoms of V (2048 bytes), one tile (kTileBytes). This lane
+      // shares its sub-partition's issue slots with softmax warps, so its
+      // per-MMA work is an add and the MMA.
+      const uint64_t q_desc = sw128_desc(smem_addr(smem + kOffQ), 16, 1024);
+      const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
+      const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
+      constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4, kTile = kTileBytes >> 4;
       auto issue_qk = [&](int t, int s) {
-        // K = 64 in four steps of 16 elements (32 bytes inside the swizzled row).
+        // K = 64 in four steps of 16 elements.
 #pragma unroll
-        for (int k = 0; k < kDim / 16; ++k) {
-          const uint64_t a = sw128_desc(q_addr + t * kTileBytes + k * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(k_addr + s * kTileBytes + k * 32, 16, 1024);
-          mma_ss(tmem + col_s(t), a, bd, kIdescQK, k > 0);
-        }
+        for (int k = 0; k < kDim / 16; ++k)
+          mma_ss(tmem + col_s(t), q_desc + t * kTile + k * kStepK, k_desc + s * kTile + k * kStepK,
+                 kIdescQK, k > 0);
       };
       auto issue_pv = [&](int t, int s, bool accumulate) {
         // K = 128 keys in eight steps of 16: P advances 8 TMEM columns (bf16
-        // pairs), V two 8-row swizzle atoms (2048 bytes).
+        // pairs), V two 8-row swizzle atoms.
 #pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k) {
-          const uint64_t bd = sw128_desc(v_addr + s * kTileBytes + k * 2048, kTileBytes, 1024);
-          mma_ts(tmem + col_o(t), tmem + col_p(t) + k * 8, bd, kIdescPV, (accumulate || k > 0));
-        }
+        for (int k = 0; k < kKeys / 16; ++k)
+          mma_ts(tmem + col_o(t), tmem + col_p(t) + k * 8, v_desc + s * kTile + k * kStepV,
+                 kIdescPV, (accumulate || k > 0));
       };
       // Order: per key tile j and query tile t, S_t(j) once the softmax group
       // of t is done with S_t(j-1) (it has written P_t(j-1), p_full), then
