@@ -10,16 +10,25 @@
 //               (batch, length, heads, 64) layout, 128-byte swizzle; rows past
 //               the window read as zeros);
 //   warp 1      allocates the 512 TMEM columns; one lane issues every MMA:
-//               S_t = Q_t K^T (SS: both operands from shared memory) and
-//               O_t += P_t V (TS: P from TMEM, V from shared memory);
+//               S = Q_t K^T (SS: both operands from shared memory) and
+//               O_t += P V (TS: P from TMEM, V from shared memory);
 //   warps 4-7   softmax of query tile 0 (thread = TMEM lane = query row);
 //   warps 8-11  softmax of query tile 1.
-// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
-//               P0 [384,448) P1 [448,512) (P as packed bf16 pairs).
-// The two softmax groups ping-pong: while one turns S into P, the tensor core
-// computes the other's S or P V. The running max is rescaled lazily: P uses a
-// stale max m until a tile's max exceeds it by more than 8 (log2 units), and
-// only then are O (in TMEM) and the row sum rescaled, so P stays <= 2^8.
+// TMEM columns: three S buffers [0,128) [128,256) [256,384), O0 [384,448),
+// O1 [448,512). The k-th S (tile t, key tile j, k = 2j + t) goes to buffer
+// k % 3; its softmax writes P (packed bf16 pairs) over the buffer's first 64
+// columns, and the next S into that buffer is issued right after that P V
+// (the tensor core runs one thread's MMAs in order). So S_1(j+1) follows
+// P_0(j) V and S_0(j+2) follows P_1(j) V: each tile's next S is computed
+// while the other tile's softmax runs, and a softmax goes from one key tile
+// to the next without waiting for the tensor core.
+// Barriers that can run ahead of their waiters come in copies so that no
+// waiter ever sees one complete twice: one S barrier per buffer, two P
+// barriers per tile (alternating), and O's last P V commits to a barrier of
+// its own.
+// The running max is rescaled lazily: P uses a stale max m until a tile's max
+// exceeds it by more than 8 (log2 units), and only then are O (in TMEM, once
+// its previous P V is done) and the row sum rescaled, so P stays <= 2^8.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -41,9 +50,12 @@ constexpr int kTileBytes = kRows * kDim * 2;  // 16 KB, one Q, K or V tile
 constexpr int kThreads = 12 * 32;
 constexpr int kTmemCols = 512;
 // TMEM column of S, O and P for query tile t.
-__host__ __device__ constexpr int col_s(int t) { return 128 * t; }
-__host__ __device__ constexpr int col_o(int t) { return 256 + 64 * t; }
-__host__ __device__ constexpr int col_p(int t) { return 384 + 64 * t; }
+// Three S buffers of 128 columns rotate over the two query tiles: the k-th
+// S (k = 2j + t) goes to buffer k % 3, and P overwrites the first 64 columns
+// of its own S buffer.
+__host__ __device__ constexpr int col_buf(int b) { return 128 * b; }
+__host__ __device__ constexpr int buf_of(int t, int j) { return (2 * j + t) % 3; }
+__host__ __device__ constexpr int col_o(int t) { return 384 + 64 * t; }
 // Lazy rescale threshold (log2 units): P <= 2^8 between rescales.
 constexpr float kRescaleThreshold = 8.0f;
 
@@ -51,9 +63,9 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = 2 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffBar = kOffV + kStages * kTileBytes;
-// barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2],
-// o_full[2]
-constexpr int kNumBars = 1 + 3 * kStages + 6;
+// barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[3] (one per S
+// buffer), p_full[2][2] (per tile, alternating), o_full[2], o_final[2]
+constexpr int kNumBars = 1 + 3 * kStages + 3 + 4 + 2 + 2;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
 
@@ -371,9 +383,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + kStages;
   uint64_t* kv_empty = v_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_full = p_full + 2;
+  uint64_t* s_full = kv_empty + kStages;  // [buffer]
+  uint64_t* p_full = s_full + 3;          // [2 * t + (j & 1)]
+  uint64_t* o_full = p_full + 4;
+  uint64_t* o_final = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -389,10 +402,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
+    for (int b = 0; b < 3; ++b) mbar_init(&s_full[b], 1);
+    for (int t = 0; t < 4; ++t) mbar_init(&p_full[t], 4);  // one arrival per softmax warp
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
       mbar_init(&o_full[t], 1);
+      mbar_init(&o_final[t], 1);
     }
     fence_barrier_init();
   }
@@ -438,60 +452,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
       const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
       constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4, kTile = kTileBytes >> 4;
-      auto issue_qk = [&](int t, int s) {
+      auto issue_qk = [&](int t, int s, int buf) {
         // K = 64 in four steps of 16 elements.
 #pragma unroll
         for (int k = 0; k < kDim / 16; ++k)
-          mma_ss(tmem + col_s(t), q_desc + t * kTile + k * kStepK, k_desc + s * kTile + k * kStepK,
-                 kIdescQK, k > 0);
+          mma_ss(tmem + col_buf(buf), q_desc + t * kTile + k * kStepK,
+                 k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
       };
-      auto issue_pv = [&](int t, int s, bool accumulate) {
+      auto issue_pv = [&](int t, int s, int buf, bool accumulate) {
         // K = 128 keys in eight steps of 16: P advances 8 TMEM columns (bf16
         // pairs), V two 8-row swizzle atoms.
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k)
-          mma_ts(tmem + col_o(t), tmem + col_p(t) + k * 8, v_desc + s * kTile + k * kStepV,
+          mma_ts(tmem + col_o(t), tmem + col_buf(buf) + k * 8, v_desc + s * kTile + k * kStepV,
                  kIdescPV, (accumulate || k > 0));
       };
-      // Order: per key tile j and query tile t, S_t(j) once the softmax group
-      // of t is done with S_t(j-1) (it has written P_t(j-1), p_full), then
-      // P_t(j-1) V(j-1); the tensor core alternates between the two tiles.
-      bool ok = mbar_wait(q_full, 0, deadline);
+      // P_t(j) V(j) as soon as tile t's softmax has written P_t(j); right
+      // after it, the S that reuses that buffer: S_1(j+1) after P_0(j) V,
+      // S_0(j+2) after P_1(j) V. Each tile's next S is thus computed while
+      // the other tile's softmax runs.
+      bool ok = mbar_wait(q_full, 0, deadline) && mbar_wait(&k_full[0], 0, deadline);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0, buf_of(0, 0));
+        mma_commit(&s_full[buf_of(0, 0)]);
+        issue_qk(1, 0, buf_of(1, 0));
+        mma_commit(&s_full[buf_of(1, 0)]);
+      }
+      if (ok && n_k > 1) {
+        ok = mbar_wait(&k_full[1 % kStages], (1 / kStages) & 1, deadline);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(0, 1 % kStages, buf_of(0, 1));
+          mma_commit(&s_full[buf_of(0, 1)]);
+        }
+      }
       for (int j = 0; j < n_k && ok; ++j) {
-        const int s = j % kStages;
-        ok = mbar_wait(&k_full[s], (j / kStages) & 1, deadline);
+        const int sp = j % kStages;
+        ok = mbar_wait(&v_full[sp], (j / kStages) & 1, deadline);
+        if (ok) ok = mbar_wait(&p_full[0 + (j & 1)], (j >> 1) & 1, deadline);
         if (!ok) break;
         tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j > 0) {
-            ok = mbar_wait(&p_full[t], (j - 1) & 1, deadline);
-            if (!ok) break;
-            tc_fence_after();
-          }
-          issue_qk(t, s);
-          mma_commit(&s_full[t]);
-          if (j > 0) {
-            const int sp = (j - 1) % kStages;
-            if (t == 0) {
-              ok = mbar_wait(&v_full[sp], ((j - 1) / kStages) & 1, deadline);
-              if (!ok) break;
-            }
-            issue_pv(t, sp, j - 1 > 0);
-            mma_commit(&o_full[t]);
-          }
-        }
-        if (ok && j > 0 && (j - 1) + kStages < n_k) mma_commit(&kv_empty[(j - 1) % kStages]);
-      }
-      if (ok) {
-        const int sp = (n_k - 1) % kStages;
-        ok = mbar_wait(&v_full[sp], ((n_k - 1) / kStages) & 1, deadline);
-        for (int t = 0; t < 2 && ok; ++t) {
-          ok = mbar_wait(&p_full[t], (n_k - 1) & 1, deadline);
+        issue_pv(0, sp, buf_of(0, j), j > 0);
+        mma_commit(j + 1 < n_k ? &o_full[0] : &o_final[0]);
+        if (j + 1 < n_k) {
+          const int s1 = (j + 1) % kStages;
+          ok = mbar_wait(&k_full[s1], ((j + 1) / kStages) & 1, deadline);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(t, sp, n_k - 1 > 0);
-          mma_commit(&o_full[t]);
+          issue_qk(1, s1, buf_of(1, j + 1));
+          mma_commit(&s_full[buf_of(1, j + 1)]);
         }
+        ok = mbar_wait(&p_full[2 + (j & 1)], (j >> 1) & 1, deadline);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(1, sp, buf_of(1, j), j > 0);
+        mma_commit(j + 1 < n_k ? &o_full[1] : &o_final[1]);
+        if (j + 2 < n_k) {
+          const int s2 = (j + 2) % kStages;
+          ok = mbar_wait(&k_full[s2], ((j + 2) / kStages) & 1, deadline);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk(0, s2, buf_of(0, j + 2));
+          mma_commit(&s_full[buf_of(0, j + 2)]);
+        }
+        if (j + kStages < n_k) mma_commit(&kv_empty[sp]);
       }
       timed_out = !ok;
     }
@@ -501,13 +526,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_bits + col_s(t);
     const uint32_t tO = tmem + lane_bits + col_o(t);
-    const uint32_t tP = tmem + lane_bits + col_p(t);
+    int buf = buf_of(t, 0);
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_k && ok; ++j) {
-      ok = mbar_wait(&s_full[t], j & 1, deadline);
+      // This tile's S is the k-th (k = 2j + t): buffer k % 3, the
+      // (k / 3)-th completion of that buffer's barrier.
+      const uint32_t tS = tmem + lane_bits + col_buf(buf);
+      ok = mbar_wait(&s_full[buf], ((2 * j + t) / 3) & 1, deadline);
+      buf = buf >= 1 ? buf - 1 : 2;  // buf_of(t, j + 1) = (buf + 2) % 3
       if (!ok) break;
       tc_fence_after();
       const int valid = min(kKeys, p.length - j * kKeys);
@@ -530,13 +558,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
                              fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
       const float m_tile = mx * p.scale_log2;
-      bool o_ready = j == 0;  // P/O of the previous tile no longer in use
       if (m_tile > m_used + kRescaleThreshold) {
         if (j > 0) {
+          // O_t must be idle: P_t(j-1) V done. (P_t(j-2) V is: S_t(j), just
+          // completed, was issued after it.)
           ok = mbar_wait(&o_full[t], (j - 1) & 1, deadline);
           if (!ok) break;
           tc_fence_after();
-          o_ready = true;
           const float alpha = fast_exp2(m_used - m_tile);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -550,11 +578,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           l *= alpha;
         }
         m_used = m_tile;
-      }
-      if (!o_ready) {
-        ok = mbar_wait(&o_full[t], (j - 1) & 1, deadline);
-        if (!ok) break;
-        tc_fence_after();
       }
       const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
       const uint64_t neg_m2 = pack2(-m_used, -m_used);
@@ -578,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
           packed[i] = bf16x2(p0, p1);
         }
-        tmem_st32u(tP + 32 * half, packed);
+        tmem_st32u(tS + 32 * half, packed);
       }
       float lo0, hi0;
       unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
@@ -586,9 +609,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0) mbar_arrive(&p_full[2 * t + (j & 1)]);
     }
-    if (ok) ok = mbar_wait(&o_full[t], (n_k - 1) & 1, deadline);
+    // O_t is final after P_t(n_k - 1) V, whose commit has a barrier of its own.
+    if (ok) ok = mbar_wait(&o_final[t], 0, deadline);
     timed_out = !ok;
     if (ok) {
       tc_fence_after();
