@@ -24,6 +24,7 @@ ERR_WORKSPACE = 3
 
 STATUS_POSITION = 1
 STATUS_TIMEOUT = 2
+STATUS_SEGMENT = 4
 
 ABI_MAJOR = 1
 
@@ -82,6 +83,15 @@ SIGNATURES: dict[str, tuple[list, object]] = {
         [_c_int, _c_int, _c_int, _c_int, _c_int,
          _c_p, _c_p, _c_p, _c_p,
          _c_i64, _c_i64, _c_i64,
+         _c_f, _c_p, _c_p],
+        _c_int,
+    ),
+    "asrback_varlen_attention": (
+        [_c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_p, _c_i64, _c_i64,
+         _c_p, _c_p, _c_i64, _c_i64,
+         _c_p, _c_int, _c_int, _c_int,
+         _c_p, _c_i64, _c_i64,
          _c_f, _c_p, _c_p],
         _c_int,
     ),

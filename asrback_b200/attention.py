@@ -32,6 +32,7 @@ __all__ = [
     "whisper_cross_attention_step",
     "qwen3_attention_step",
     "whisper_encoder_attention",
+    "varlen_attention",
     "reserve_workspace",
     "read_status",
     "DeviceStatusError",
@@ -301,6 +302,46 @@ def whisper_encoder_attention(q: Tensor, k: Tensor, v: Tensor, scale: float | No
         dtype, batch, heads, head_dim, length,
         q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
         q.stride(0), q.stride(1), q.stride(2),
+        scale if scale is not None else 1.0 / math.sqrt(head_dim),
+        state.status.data_ptr(), _stream(q.device),
+    )
+    return out
+
+
+def varlen_attention(q: Tensor, k: Tensor, v: Tensor, starts: Tensor, longest: int, causal: bool,
+                     scale: float | None = None) -> Tensor:
+    """Attention within each segment of packed ``(tokens, heads, head_dim)``
+    tensors: the reference's ``attend(q, k, v, segments, causal)``
+    (``qwen3_asr.py:152-181``) with ``segments.starts`` and
+    ``segments.longest``. ``k``/``v`` may have fewer heads than ``q`` (query
+    head ``h`` reads key/value head ``h // (heads / kv_heads)``); ``causal``
+    lets token ``i`` of a segment see tokens ``0..i`` of it. ``starts`` is
+    ``(segments + 1,)`` int32 on the tensors' device. Returns ``(tokens,
+    heads, head_dim)``."""
+    dtype = _dtype_code(q, k, v)
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise ValueError("asrback_b200: q, k, v must be (tokens, heads, head_dim)")
+    tokens, heads, head_dim = q.shape
+    kv_heads = k.shape[1]
+    if k.shape != (tokens, kv_heads, head_dim) or v.shape != k.shape:
+        raise ValueError(f"asrback_b200: k {tuple(k.shape)} / v {tuple(v.shape)} do not match q {tuple(q.shape)}")
+    if k.stride() != v.stride():
+        raise ValueError("asrback_b200: k and v must share strides")
+    if q.stride(2) != 1 or k.stride(2) != 1:
+        raise ValueError("asrback_b200: head_dim must have unit stride")
+    if starts.dtype != torch.int32 or starts.dim() != 1 or starts.device != q.device:
+        raise ValueError("asrback_b200: starts must be (segments + 1,) int32 on the tensors' device")
+    starts = starts.contiguous()
+    segments = starts.shape[0] - 1
+    out = torch.empty((tokens, heads, head_dim), dtype=q.dtype, device=q.device)
+    state = _state(q.device)
+    _native.call(
+        "asrback_varlen_attention",
+        dtype, tokens, heads, kv_heads, head_dim,
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+        starts.data_ptr(), segments, int(longest), 1 if causal else 0,
+        out.data_ptr(), out.stride(0), out.stride(1),
         scale if scale is not None else 1.0 / math.sqrt(head_dim),
         state.status.data_ptr(), _stream(q.device),
     )

@@ -49,7 +49,7 @@ int sm_count() {
 
 extern "C" {
 
-int asrback_abi_version(void) { return (1 << 16) | 0; }
+int asrback_abi_version(void) { return (1 << 16) | 1; }
 
 const char* asrback_last_error(void) { return asrback::g_last_error; }
 

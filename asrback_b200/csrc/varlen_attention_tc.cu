@@ -1,0 +1,414 @@
+// Attention within the segments of packed (tokens, heads, head_dim) tensors on
+// the 5th-generation tensor cores (tcgen05, accumulators in tensor memory),
+// bf16, head_dim 64 or 128, causal or not, grouped-query heads.
+//
+// Replaces asrback's `attend(q, k, v, segments, causal)` (qwen3_asr.py:152-181):
+//   - Qwen3 prompt prefill, TextAttention.prefill (qwen3_asr.py:374-390):
+//     causal, 16 query heads over 8 key/value heads, head_dim 128;
+//   - Qwen3 audio encoder, AudioAttention.forward (qwen3_asr.py:214-219):
+//     non-causal windows.
+// Segment s holds the tokens cu[s] .. cu[s+1]-1 (the reference's `starts`).
+//
+// One CTA owns one (segment, query head, pair of 128-row query tiles). Roles:
+//   warp 0      TMA: both Q tiles, then K/V tiles of 128 keys of the query
+//               head's key/value head into a STAGES-deep ring. A tile is
+//               head_dim / 64 column blocks of 128 bytes (128-byte swizzle);
+//               rows past the segment belong to the next one and are masked,
+//               rows past the tensor read as zeros;
+//   warp 1      allocates the 512 TMEM columns; one lane issues every MMA:
+//               S_t = Q_t K^T (SS) and O_t += P_t V (TS: P from TMEM);
+//   warps 4-11  softmax of query tile 0 and 1 (thread = TMEM lane = row).
+// TMEM of query tile t: S_t [256t, 256t+128), the softmax writing P_t (packed
+// bf16 pairs) over its first 64 columns, and O_t [256t+128, 256t+128+D).
+// Per key tile j the MMA lane issues P_t(j-1) V, then S_t(j) into the same
+// columns (the tensor core runs one thread's MMAs in order), so S_t(j)'s
+// completion also means O_t is idle: the lazy rescale (P uses a stale max
+// until a tile's max exceeds it by more than 8 in log2 units) needs no wait.
+// Causal: query row r reads keys 0..r of its segment, so a query tile stops
+// at the key tile of its own rows and only that diagonal tile is masked.
+#include "tcgen05.cuh"
+
+namespace asrback {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kRows = 128;  // query rows per tile (= TMEM lanes)
+constexpr int kKeys = 128;  // keys per tile
+constexpr int kThreads = 12 * 32;
+constexpr int kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;
+
+template <int D>
+struct VarlenShape {
+  static constexpr int kAtoms = D / 64;         // 128-byte column blocks per row
+  static constexpr int kAtomBytes = kRows * 128;  // one column block of a tile
+  static constexpr int kTileBytes = kAtoms * kAtomBytes;
+  static constexpr int kStages = D == 128 ? 2 : 4;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = 2 * kTileBytes;
+  static constexpr int kOffV = kOffK + kStages * kTileBytes;
+  static constexpr int kOffBar = kOffV + kStages * kTileBytes;
+  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2],
+  // o_full[2]
+  static constexpr int kNumBars = 1 + 3 * kStages + 6;
+  static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory exceeds a CTA's 227 KB");
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+};
+__host__ __device__ constexpr int col_s(int t) { return 256 * t; }
+__host__ __device__ constexpr int col_o(int t) { return 256 * t + 128; }
+
+struct VarlenParams {
+  void* out;
+  int64_t os_tok, os_head;  // output strides (elements)
+  const int32_t* cu;        // segment starts, segments + 1 entries
+  int tokens;
+  int max_length;
+  int group;                // query heads per key/value head
+  int causal;
+  float scale_log2;
+  int32_t* status;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    varlen_attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
+                               const __grid_constant__ CUtensorMap map_k,
+                               const __grid_constant__ CUtensorMap map_v,
+                               const __grid_constant__ VarlenParams p) {
+  using Sh = VarlenShape<D>;
+  const int pair = blockIdx.x, h = blockIdx.y, seg = blockIdx.z;
+  const int start = p.cu[seg];
+  const int len = p.cu[seg + 1] - start;
+  // A segment outside the tensor or longer than the launch covers is skipped
+  // (its output rows untouched) and reported; nothing is read or written
+  // out of bounds.
+  if (start < 0 || len < 0 || start + len > p.tokens || len > p.max_length) {
+    if (pair == 0 && h == 0 && threadIdx.x == 0 && p.status)
+      atomicOr(p.status, ASRBACK_STATUS_SEGMENT);
+    return;
+  }
+  const int r0 = pair * 2 * kRows;
+  if (r0 >= len) return;  // the whole CTA: this segment is shorter
+  const int kvh = h / p.group;
+  const int n_seg = (len + kKeys - 1) / kKeys;
+  // Key tiles of query tile t (0: the tile lies past the segment).
+  int n_k[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int first_row = r0 + t * kRows;
+    n_k[t] = first_row >= len ? 0 : (p.causal ? min(n_seg, first_row / kKeys + 1) : n_seg);
+  }
+  const int n_max = max(n_k[0], n_k[1]);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + Sh::kStages;
+  uint64_t* kv_empty = v_full + Sh::kStages;
+  uint64_t* s_full = kv_empty + Sh::kStages;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Sh::kOffTmemSlot);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint64_t deadline = global_timer_ns() + kWaitBudgetNs;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < Sh::kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
+      mbar_init(&o_full[t], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool timed_out = false;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&map_q);
+      prefetch_tensormap(&map_k);
+      prefetch_tensormap(&map_v);
+      const int q_tiles = n_k[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, q_tiles * Sh::kTileBytes);
+      for (int t = 0; t < q_tiles; ++t)
+#pragma unroll
+        for (int a = 0; a < Sh::kAtoms; ++a)
+          tma_load_3d(smem + Sh::kOffQ + t * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q, 64 * a,
+                      h, start + r0 + t * kRows, q_full);
+      for (int j = 0; j < n_max; ++j) {
+        const int s = j % Sh::kStages;
+        if (j >= Sh::kStages &&
+            !mbar_wait(&kv_empty[s], ((j / Sh::kStages) - 1) & 1, deadline)) {
+          timed_out = true;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[s], Sh::kTileBytes);
+#pragma unroll
+        for (int a = 0; a < Sh::kAtoms; ++a)
+          tma_load_3d(smem + Sh::kOffK + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_k, 64 * a,
+                      kvh, start + j * kKeys, &k_full[s]);
+        mbar_arrive_expect_tx(&v_full[s], Sh::kTileBytes);
+#pragma unroll
+        for (int a = 0; a < Sh::kAtoms; ++a)
+          tma_load_3d(smem + Sh::kOffV + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_v, 64 * a,
+                      kvh, start + j * kKeys, &v_full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
+      constexpr uint32_t kIdescPV = idesc_bf16(kRows, 64, true);
+      // Descriptors are built once and stepped by adds of address >> 4:
+      // 32 bytes per 16 elements along K inside a 128-byte block, one block
+      // (kAtomBytes) per 64 elements, 2048 bytes per 16 rows of V.
+      const uint64_t q_desc = sw128_desc(smem_addr(smem + Sh::kOffQ), 16, 1024);
+      const uint64_t k_desc = sw128_desc(smem_addr(smem + Sh::kOffK), 16, 1024);
+      const uint64_t v_desc = sw128_desc(smem_addr(smem + Sh::kOffV), Sh::kAtomBytes, 1024);
+      constexpr uint64_t kTile = Sh::kTileBytes >> 4, kAtom = Sh::kAtomBytes >> 4;
+      auto issue_qk = [&](int t, int s) {
+        // K = head_dim in steps of 16: four per 128-byte block.
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t off = (k / 4) * kAtom + (k % 4) * (32 >> 4);
+          mma_ss(tmem + col_s(t), q_desc + t * kTile + off, k_desc + s * kTile + off, kIdescQK,
+                 k > 0);
+        }
+      };
+      auto issue_pv = [&](int t, int s, bool accumulate) {
+        // N = head_dim as 64-column blocks of V; K = 128 keys in steps of 16:
+        // P advances 8 TMEM columns (bf16 pairs), V 16 rows (2048 bytes).
+#pragma unroll
+        for (int a = 0; a < Sh::kAtoms; ++a)
+#pragma unroll
+          for (int k = 0; k < kKeys / 16; ++k)
+            mma_ts(tmem + col_o(t) + 64 * a, tmem + col_s(t) + k * 8,
+                   v_desc + s * kTile + a * kAtom + k * (2048 >> 4), kIdescPV,
+                   accumulate || k > 0);
+      };
+      bool ok = mbar_wait(q_full, 0, deadline);
+      // Step j: for each query tile still reading keys, P_t(j-1) V(j-1) once
+      // its softmax has written P_t(j-1), then S_t(j) over the same columns
+      // (or, after its last key tile, the commit that O_t is final).
+      for (int j = 0; j <= n_max && ok; ++j) {
+        if (j < n_max) ok = mbar_wait(&k_full[j % Sh::kStages], (j / Sh::kStages) & 1, deadline);
+        if (ok && j > 0)
+          ok = mbar_wait(&v_full[(j - 1) % Sh::kStages], ((j - 1) / Sh::kStages) & 1, deadline);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (n_k[t] == 0 || j > n_k[t]) continue;
+          if (j > 0) {
+            ok = mbar_wait(&p_full[t], (j - 1) & 1, deadline);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(t, (j - 1) % Sh::kStages, j > 1);
+          }
+          if (j < n_k[t]) {
+            issue_qk(t, j % Sh::kStages);
+            mma_commit(&s_full[t]);
+          } else {
+            mma_commit(&o_full[t]);
+          }
+        }
+        if (ok && j > 0 && (j - 1) + Sh::kStages < n_max)
+          mma_commit(&kv_empty[(j - 1) % Sh::kStages]);
+      }
+      timed_out = !ok;
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax (one query row per thread) ----------------
+    const int t = (warp - 4) >> 2;
+    const int quarter = warp & 3;
+    const int row = r0 + t * kRows + quarter * 32 + lane;  // within the segment
+    const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_bits + col_s(t);
+    const uint32_t tO = tmem + lane_bits + col_o(t);
+    // Keys this row may read: its segment, and (causal) up to itself.
+    const int limit = p.causal ? min(len, row + 1) : len;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_k[t] && ok; ++j) {
+      ok = mbar_wait(&s_full[t], j & 1, deadline);
+      if (!ok) break;
+      tc_fence_after();
+      const int valid = limit - j * kKeys;
+      float v[kKeys];
+      tmem_ld128(tS, v);
+      if (valid < kKeys) {
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i)
+          if (i >= valid) v[i] = -INFINITY;
+      }
+      float acc[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
+#pragma unroll
+      for (int i = 16; i < kKeys; i += 16)
+#pragma unroll
+        for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
+      const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
+                             fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
+      const float m_tile = mx * p.scale_log2;
+      if (m_tile > m_used + kRescaleThreshold) {
+        if (j > 0) {
+          // O_t is idle: P_t(j-1) V was issued before S_t(j), which is done.
+          const float alpha = fast_exp2(m_used - m_tile);
+#pragma unroll
+          for (int c = 0; c < D / 16; ++c) {
+            float o[16];
+            tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] *= alpha;
+            tmem_st16f(tO + 16 * c, o);
+          }
+          l *= alpha;
+        }
+        m_used = m_tile;
+      }
+      const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
+      const uint64_t neg_m2 = pack2(-m_used, -m_used);
+      uint64_t sum2[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = 64 * half + 2 * i;
+          float x0, x1;
+          unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
+          packed[i] = bf16x2(p0, p1);
+        }
+        tmem_st32u(tS + 32 * half, packed);
+      }
+      float lo0, hi0;
+      unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
+      l += lo0 + hi0;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (n_k[t] > 0) {
+      if (ok) ok = mbar_wait(&o_full[t], 0, deadline);
+      timed_out = !ok;
+      if (ok) {
+        tc_fence_after();
+        const float inv = 1.f / l;
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
+                             static_cast<int64_t>(start + row) * p.os_tok + h * p.os_head;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(tO + 32 * c, o);
+          if (row < len) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 u;
+              u.x = bf16x2(o[i] * inv, o[i + 1] * inv);
+              u.y = bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+              u.z = bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+              u.w = bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+              *reinterpret_cast<uint4*>(out + 32 * c + i) = u;
+            }
+          }
+        }
+      }
+    }
+  }
+  if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// (tokens, heads, head_dim) bf16 view with the given element strides as a
+// 3-D tensor map {d, head, token}; 64 x 1 x 128 boxes (one 128-byte column
+// block of 128 rows), 128-byte swizzle, zero fill past the tensor.
+int make_map_3d(CUtensorMap* map, const void* base, int tokens, int heads, int head_dim,
+                int64_t s_tok, int64_t s_head) {
+  int rc = ASRBACK_OK;
+  auto encode = tensor_map_encoder(&rc);
+  if (!encode) return rc;
+  cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)heads, (cuuint64_t)tokens};
+  cuuint64_t strides[2] = {(cuuint64_t)s_head * 2, (cuuint64_t)s_tok * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)kRows};
+  cuuint32_t elem_strides[3] = {1, 1, 1};
+  CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                        strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS)
+    return fail(ASRBACK_ERR_ARGUMENT,
+                "cuTensorMapEncodeTiled rejected the layout (error %d): strides (%lld, %lld)",
+                (int)res, (long long)s_tok, (long long)s_head);
+  return ASRBACK_OK;
+}
+
+template <int D>
+int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+           const VarlenParams& p, int segments, int heads, int max_length, cudaStream_t stream) {
+  using Sh = VarlenShape<D>;
+  auto kernel = varlen_attention_tc_kernel<D>;
+  static thread_local int prepared_device = -1;
+  int device = 0;
+  if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
+  if (prepared_device != device) {
+    if (int rc = check_cuda(
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmemBytes),
+            "cudaFuncSetAttribute(varlen attention)"))
+      return rc;
+    prepared_device = device;
+  }
+  dim3 grid((max_length + 2 * kRows - 1) / (2 * kRows), heads, segments);
+  kernel<<<grid, kThreads, Sh::kSmemBytes, stream>>>(mq, mk, mv, p);
+  return check_cuda(cudaGetLastError(), "varlen attention (tensor core) launch");
+}
+
+}  // namespace
+
+// Launches the tensor-core varlen attention; arguments already validated
+// (bf16, head_dim 64 or 128, 16-byte aligned pointers and strides).
+int varlen_attention_tc(int tokens, int heads, int kv_heads, int head_dim, const void* q,
+                        int64_t q_tok, int64_t q_head, const void* k, const void* v,
+                        int64_t kv_tok, int64_t kv_head, const int32_t* cu, int segments,
+                        int max_length, int causal, void* out, int64_t o_tok, int64_t o_head,
+                        float scale, int32_t* status, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv;
+  if (int rc = make_map_3d(&mq, q, tokens, heads, head_dim, q_tok, q_head)) return rc;
+  if (int rc = make_map_3d(&mk, k, tokens, kv_heads, head_dim, kv_tok, kv_head)) return rc;
+  if (int rc = make_map_3d(&mv, v, tokens, kv_heads, head_dim, kv_tok, kv_head)) return rc;
+  VarlenParams p{out,   o_tok,          o_head,     cu, tokens, max_length, heads / kv_heads,
+                 causal ? 1 : 0, scale * 1.4426950408889634f, status};
+  return head_dim == 128 ? launch<128>(mq, mk, mv, p, segments, heads, max_length, stream)
+                         : launch<64>(mq, mk, mv, p, segments, heads, max_length, stream);
+}
+
+}  // namespace asrback

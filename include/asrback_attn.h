@@ -27,7 +27,12 @@
  *     RoPE) and the cache write (qwen3_asr.py:409-411) fused in;
  *   - asrback_whisper_encoder_attention replaces the unmasked SDPA call of
  *     MultiHeadAttention.forward, whisper.py:108-110 (via attend, :102-104),
- *     in the encoder layers (whisper.py:123-125).
+ *     in the encoder layers (whisper.py:123-125);
+ *   - asrback_varlen_attention replaces attend(q, k, v, segments, causal),
+ *     src/asrback/models/qwen3_asr.py:152-181 (torch varlen_attn with equal
+ *     query/key segments), called by TextAttention.prefill (qwen3_asr.py:
+ *     374-390, causal) and AudioAttention.forward (qwen3_asr.py:214-219,
+ *     non-causal windows).
  */
 #ifndef ASRBACK_ATTN_H_
 #define ASRBACK_ATTN_H_
@@ -58,6 +63,8 @@ extern "C" {
 /* Bits of the device-side status word. */
 #define ASRBACK_STATUS_POSITION 1 /* a row's position was < 0 or >= cache length */
 #define ASRBACK_STATUS_TIMEOUT 2  /* a bounded wait inside a kernel gave up */
+#define ASRBACK_STATUS_SEGMENT 4  /* a segment of cu_seqlens lay outside the tensor or
+                                     exceeded max_length (asrback_varlen_attention) */
 
 /* Version of this ABI: (major << 16) | minor. */
 ASRBACK_API int asrback_abi_version(void);
@@ -184,6 +191,32 @@ ASRBACK_API int asrback_whisper_encoder_attention(
     int dtype, int batch, int heads, int head_dim, int length,
     const void* q, const void* k, const void* v, void* out,
     int64_t stride_batch, int64_t stride_head, int64_t stride_seq,
+    float scale, int32_t* status, void* stream);
+
+/*
+ * Attention within segments of packed tokens: asrback's attend(q, k, v,
+ * segments, causal) (qwen3_asr.py:152-181), i.e. varlen_attn(q, k, v,
+ * cu_seqlens, cu_seqlens, max_length, max_length, window_size=(-1, 0) if
+ * causal else (-1, -1), enable_gqa) with the same segments for queries and
+ * keys.
+ *
+ * q, out        (tokens, heads, head_dim) at [t*stride_token + h*stride_head + d];
+ * key, value    (tokens, kv_heads, head_dim) with kv_stride_token/_head;
+ *               query head h reads key/value head h / (heads / kv_heads);
+ * cu_seqlens    device int32, segments + 1 entries: segment s is tokens
+ *               cu_seqlens[s] .. cu_seqlens[s+1]-1 (the reference's
+ *               Segments.starts); every segment at most max_length tokens;
+ * causal        nonzero: token i of a segment attends to tokens 0..i of it.
+ * head_dim 64 or 128; dtype ASRBACK_BF16 (tensor cores) or ASRBACK_F32.
+ * A segment outside [0, tokens) or longer than max_length is skipped (its
+ * output rows are not written) and sets ASRBACK_STATUS_SEGMENT.
+ */
+ASRBACK_API int asrback_varlen_attention(
+    int dtype, int tokens, int heads, int kv_heads, int head_dim,
+    const void* q, int64_t q_stride_token, int64_t q_stride_head,
+    const void* key, const void* value, int64_t kv_stride_token, int64_t kv_stride_head,
+    const int32_t* cu_seqlens, int segments, int max_length, int causal,
+    void* out, int64_t out_stride_token, int64_t out_stride_head,
     float scale, int32_t* status, void* stream);
 
 #ifdef __cplusplus

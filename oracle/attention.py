@@ -38,6 +38,7 @@ __all__ = [
     "rotate",
     "qwen3_project",
     "qwen3_decode_attention",
+    "varlen_attention",
 ]
 
 
@@ -204,3 +205,34 @@ def qwen3_decode_attention(qkv, q_norm_weight, k_norm_weight, eps, cos, sin, pos
     values = np.asarray(value_cache, dtype=np.float64).transpose(0, 2, 1, 3)
     out = sdpa(grouped, keys, values, mask)
     return out.reshape(batch, heads * head_dim), key_cache, value_cache
+
+
+def varlen_attention(q, k, v, starts, causal, scale=None, compute=np.float64):
+    """Attention within each segment of packed ``(tokens, heads, head_dim)``
+    tensors: ``attend(q, k, v, segments, causal)`` (``qwen3_asr.py:152-181``).
+
+    Segment ``s`` is tokens ``starts[s] .. starts[s+1]-1`` (the reference's
+    ``Segments.starts``, ``:136-149``). Within it, token ``i`` attends to all
+    tokens of the segment, or (``causal``) to tokens ``0..i`` of it: the padded
+    path's ``valid`` mask and ``tril`` (``:163-175``), the varlen path's
+    ``window_size=(-1, 0)`` (``:155-165``). ``k``/``v`` may have fewer heads:
+    query head ``h`` reads key/value head ``h // (heads / kv_heads)``
+    (``enable_gqa``). Returns ``(tokens, heads, head_dim)``.
+    """
+    q = np.asarray(q, dtype=compute)
+    k = np.asarray(k, dtype=compute)
+    v = np.asarray(v, dtype=compute)
+    starts = np.asarray(starts, dtype=np.int64)
+    tokens, heads, head_dim = q.shape
+    group = heads // k.shape[1]
+    out = np.zeros((tokens, heads, head_dim), dtype=compute)
+    for s in range(len(starts) - 1):
+        a, b = int(starts[s]), int(starts[s + 1])
+        if b <= a:
+            continue
+        qs = q[a:b].transpose(1, 0, 2)                                 # (heads, L, D)
+        ks = np.repeat(k[a:b].transpose(1, 0, 2), group, axis=0)       # (heads, L, D)
+        vs = np.repeat(v[a:b].transpose(1, 0, 2), group, axis=0)
+        mask = np.tril(np.ones((b - a, b - a), dtype=bool)) if causal else None
+        out[a:b] = sdpa(qs, ks, vs, mask, scale, compute).transpose(1, 0, 2)
+    return out

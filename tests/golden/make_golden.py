@@ -197,6 +197,34 @@ def encoder_attention(whisper, dtype: torch.dtype, tag: str) -> None:
          q=f32(call["q"]), k=f32(call["k"]), v=f32(call["v"]), out=f32(call["out"]))
 
 
+def qwen3_varlen(qwen3, dtype: torch.dtype, tag: str) -> None:
+    """``attend(q, k, v, segments, causal)`` (qwen3_asr.py:152-181) on its
+    padded-SDPA path (``Segments.from_lengths(..., varlen=False)``) for the two
+    call sites: causal grouped-query prefill (TextAttention.prefill: heads of
+    128, two query heads per key-value head as in 16/8, kept to 2/1 here for
+    size) and non-causal audio windows (AudioAttention, heads of 64). Ragged
+    segments, one longer than two 128-row tiles."""
+    cases = {
+        "prefill": dict(lengths=[37, 130, 1, 290], heads=2, kv_heads=1, head_dim=128, causal=True,
+                        seed=500),
+        "audio": dict(lengths=[104, 104, 57], heads=2, kv_heads=2, head_dim=64, causal=False,
+                      seed=510),
+    }
+    arrays = {}
+    for name, case in cases.items():
+        tokens = sum(case["lengths"])
+        q = seeded_normal((tokens, case["heads"], case["head_dim"]), case["seed"]).to(dtype)
+        k = seeded_normal((tokens, case["kv_heads"], case["head_dim"]), case["seed"] + 1).to(dtype)
+        v = seeded_normal((tokens, case["kv_heads"], case["head_dim"]), case["seed"] + 2).to(dtype)
+        segments = qwen3.Segments.from_lengths(case["lengths"], torch.device("cpu"), False)
+        with torch.no_grad():
+            out = qwen3.attend(q, k, v, segments, case["causal"])
+        arrays.update({f"{name}_q": f32(q), f"{name}_k": f32(k), f"{name}_v": f32(v),
+                       f"{name}_starts": segments.starts.numpy(), f"{name}_out": f32(out)})
+    save(f"qwen3_varlen_{tag}",
+         dict(dtype=str(dtype), site="qwen3_asr.py:152-181", cases=cases), **arrays)
+
+
 WHISPER_PREFIX = [50258, 50259, 50359, 50363]  # SOT, <|en|>, <|transcribe|>, <|notimestamps|>
 
 
@@ -304,6 +332,7 @@ def main() -> None:
         whisper_step(whisper, dtype, tag)
         qwen3_step(qwen3, dtype, tag)
         encoder_attention(whisper, dtype, tag)
+        qwen3_varlen(qwen3, dtype, tag)
     whisper_tiny_decode(whisper)
     qwen3_small_decode(qwen3)
 

@@ -91,6 +91,31 @@ def test_qwen3_shape_limits(lib):
     assert "8 key/value heads" in lib.asrback_last_error().decode()
 
 
+def _varlen_call(lib, **overrides):
+    args = dict(dtype=_native.BF16, tokens=512, heads=16, kv_heads=8, head_dim=128, q=16, k=16,
+                v=16, cu=16, segments=2, max_length=256, out=16, q_tok=2048)
+    args.update(overrides)
+    return lib.asrback_varlen_attention(
+        args["dtype"], args["tokens"], args["heads"], args["kv_heads"], args["head_dim"],
+        args["q"], args["q_tok"], 128, args["k"], args["v"], 1024, 128,
+        args["cu"], args["segments"], args["max_length"], 1,
+        args["out"], 2048, 128, 0.088, None, None)
+
+
+@pytest.mark.parametrize("overrides,fragment", [
+    (dict(head_dim=96), "head_dim must be 64 or 128"),
+    (dict(heads=12), "multiple of kv_heads"),
+    (dict(segments=0), "positive"),
+    (dict(cu=0), "null"),
+    (dict(k=8), "aligned"),
+    (dict(q_tok=1000), "do not hold"),
+])
+def test_varlen_invalid_arguments_are_rejected_on_the_host(lib, overrides, fragment):
+    rc = _varlen_call(lib, **overrides)
+    assert rc == _native.ERR_ARGUMENT
+    assert fragment in lib.asrback_last_error().decode()
+
+
 def test_ops_refuse_cpu_tensors():
     """No CPU fallback: the product path raises on host tensors."""
     import torch

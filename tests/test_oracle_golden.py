@@ -97,6 +97,30 @@ def test_qwen3_decode_attention(tag, tol):
     np.testing.assert_array_equal(v_after[rows, g["positions"]], g["v_new"])
 
 
+@pytest.mark.parametrize("case", ["prefill", "audio"])
+@pytest.mark.parametrize("tag,tol", [("fp32", F32_TOL), ("bf16", BF16_TOL)])
+def test_varlen_attention(tag, tol, case):
+    """attend() over packed segments (qwen3_asr.py:152-181): causal GQA
+    prefill and non-causal audio windows."""
+    g = load(f"qwen3_varlen_{tag}")
+    meta = g["meta"]["cases"][case]
+    starts = g[f"{case}_starts"]
+    np.testing.assert_array_equal(np.diff(starts), meta["lengths"])
+    out = oracle.varlen_attention(g[f"{case}_q"], g[f"{case}_k"], g[f"{case}_v"], starts,
+                                  meta["causal"])
+    np.testing.assert_allclose(out, g[f"{case}_out"], atol=tol, rtol=0)
+
+
+def test_varlen_attention_causal_first_token_is_its_value():
+    """A segment's first token sees only itself: its output is its value."""
+    g = load("qwen3_varlen_fp32")
+    starts = g["prefill_starts"]
+    out = oracle.varlen_attention(g["prefill_q"], g["prefill_k"], g["prefill_v"], starts, True)
+    group = g["prefill_q"].shape[1] // g["prefill_k"].shape[1]
+    for a in starts[:-1]:
+        np.testing.assert_allclose(out[a], np.repeat(g["prefill_v"][a], group, axis=0), atol=1e-12)
+
+
 def test_bf16_round_is_nearest_even():
     x = np.array([1.0, 1.00390625, 1.005859375, -2.5e-3, 3.0e38, np.inf], np.float32)
     r = oracle.bf16_round(x)
