@@ -89,12 +89,14 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "asrback_varlen_attention": (
         [_c_int, _c_int, _c_int, _c_int, _c_int,
          _c_p, _c_i64, _c_i64,
-         _c_p, _c_p, _c_i64, _c_i64,
+         _c_p, _c_i64, _c_i64,
+         _c_p, _c_i64, _c_i64,
          _c_p, _c_int, _c_int, _c_int,
          _c_p, _c_i64, _c_i64,
          _c_f, _c_p, _c_p],
         _c_int,
     ),
+    "asrback_selftest_bounded_wait": ([_c_i64, _c_p, _c_p], _c_int),
 }
 
 _lock = threading.Lock()

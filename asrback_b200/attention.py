@@ -325,9 +325,7 @@ def varlen_attention(q: Tensor, k: Tensor, v: Tensor, starts: Tensor, longest: i
     kv_heads = k.shape[1]
     if k.shape != (tokens, kv_heads, head_dim) or v.shape != k.shape:
         raise ValueError(f"asrback_b200: k {tuple(k.shape)} / v {tuple(v.shape)} do not match q {tuple(q.shape)}")
-    if k.stride() != v.stride():
-        raise ValueError("asrback_b200: k and v must share strides")
-    if q.stride(2) != 1 or k.stride(2) != 1:
+    if q.stride(2) != 1 or k.stride(2) != 1 or v.stride(2) != 1:
         raise ValueError("asrback_b200: head_dim must have unit stride")
     if starts.dtype != torch.int32 or starts.dim() != 1 or starts.device != q.device:
         raise ValueError("asrback_b200: starts must be (segments + 1,) int32 on the tensors' device")
@@ -339,7 +337,8 @@ def varlen_attention(q: Tensor, k: Tensor, v: Tensor, starts: Tensor, longest: i
         "asrback_varlen_attention",
         dtype, tokens, heads, kv_heads, head_dim,
         q.data_ptr(), q.stride(0), q.stride(1),
-        k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+        k.data_ptr(), k.stride(0), k.stride(1),
+        v.data_ptr(), v.stride(0), v.stride(1),
         starts.data_ptr(), segments, int(longest), 1 if causal else 0,
         out.data_ptr(), out.stride(0), out.stride(1),
         scale if scale is not None else 1.0 / math.sqrt(head_dim),

@@ -5,6 +5,7 @@
 
 #include "../../include/asrback_attn.h"
 #include "capi_internal.h"
+#include "common.cuh"
 
 namespace asrback {
 
@@ -45,9 +46,36 @@ int sm_count() {
   return counts[device];
 }
 
+namespace {
+
+// Waits on an mbarrier that nothing arrives at, with the same bounded wait the
+// attention kernels use, given up after `budget_ns`: the wait must return
+// false, and the kernel reports ASRBACK_STATUS_TIMEOUT and exits normally.
+__global__ void bounded_wait_selftest(uint64_t budget_ns, int32_t* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  const uint64_t deadline = global_timer_ns() + budget_ns;
+  if (!mbar_wait(&bar, 0, deadline)) atomicOr(status, ASRBACK_STATUS_TIMEOUT);
+}
+
+}  // namespace
+
 }  // namespace asrback
 
 extern "C" {
+
+int asrback_selftest_bounded_wait(int64_t budget_ns, int32_t* status, void* stream) {
+  using namespace asrback;
+  if (budget_ns <= 0 || budget_ns > 1000000000LL || status == nullptr)
+    return fail(ASRBACK_ERR_ARGUMENT, "budget_ns must be in (0, 1e9] and status non-null");
+  bounded_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint64_t>(budget_ns), status);
+  if (int rc = check_cuda(cudaGetLastError(), "bounded wait self-test launch")) return rc;
+  return ok();
+}
+
 
 int asrback_abi_version(void) { return (1 << 16) | 1; }
 

@@ -11,8 +11,9 @@
 namespace asrback {
 
 int varlen_attention_tc(int tokens, int heads, int kv_heads, int head_dim, const void* q,
-                        int64_t q_tok, int64_t q_head, const void* k, const void* v,
-                        int64_t kv_tok, int64_t kv_head, const int32_t* cu, int segments,
+                        int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                        int64_t k_head, const void* v, int64_t v_tok, int64_t v_head,
+                        const int32_t* cu, int segments,
                         int max_length, int causal, void* out, int64_t o_tok, int64_t o_head,
                         float scale, int32_t* status, cudaStream_t stream);
 
@@ -26,7 +27,7 @@ struct SimtParams {
   const float* k;
   const float* v;
   float* out;
-  int64_t q_tok, q_head, kv_tok, kv_head, o_tok, o_head;
+  int64_t q_tok, q_head, k_tok, k_head, v_tok, v_head, o_tok, o_head;
   const int32_t* cu;
   int tokens;
   int max_length;
@@ -69,8 +70,8 @@ __global__ void __launch_bounds__(kRowsS) varlen_attention_simt(const __grid_con
     for (int i = threadIdx.x; i < kKeysS * D; i += kRowsS) {
       const int r = i / D, d = i % D;
       const int64_t tok = start + k0 + r;
-      ks[r][d] = r < n ? p.k[tok * p.kv_tok + kvh * p.kv_head + d] : 0.f;
-      vs[r][d] = r < n ? p.v[tok * p.kv_tok + kvh * p.kv_head + d] : 0.f;
+      ks[r][d] = r < n ? p.k[tok * p.k_tok + kvh * p.k_head + d] : 0.f;
+      vs[r][d] = r < n ? p.v[tok * p.v_tok + kvh * p.v_head + d] : 0.f;
     }
     __syncthreads();
     float s[kKeysS];
@@ -112,9 +113,10 @@ using namespace asrback;
 
 extern "C" int asrback_varlen_attention(int dtype, int tokens, int heads, int kv_heads,
                                         int head_dim, const void* q, int64_t q_stride_token,
-                                        int64_t q_stride_head, const void* key, const void* value,
-                                        int64_t kv_stride_token, int64_t kv_stride_head,
-                                        const int32_t* cu_seqlens, int segments, int max_length,
+                                        int64_t q_stride_head, const void* key,
+                                        int64_t k_stride_token, int64_t k_stride_head,
+                                        const void* value, int64_t v_stride_token,
+                                        int64_t v_stride_head, const int32_t* cu_seqlens, int segments, int max_length,
                                         int causal, void* out, int64_t out_stride_token,
                                         int64_t out_stride_head, float scale, int32_t* status,
                                         void* stream) {
@@ -136,26 +138,28 @@ extern "C" int asrback_varlen_attention(int dtype, int tokens, int heads, int kv
   if (!aligned16(q) || !aligned16(key) || !aligned16(value) || !aligned16(out))
     return fail(ASRBACK_ERR_ARGUMENT, "tensor pointers must be 16-byte aligned");
   const int64_t elem = dtype == ASRBACK_BF16 ? 2 : 4;
-  for (int64_t s : {q_stride_token, q_stride_head, kv_stride_token, kv_stride_head,
-                    out_stride_token, out_stride_head})
+  for (int64_t s : {q_stride_token, q_stride_head, k_stride_token, k_stride_head, v_stride_token,
+                    v_stride_head, out_stride_token, out_stride_head})
     if (s <= 0 || (s * elem) % 16 != 0)
       return fail(ASRBACK_ERR_ARGUMENT, "strides must be positive multiples of 16 bytes");
-  if (q_stride_head < head_dim || kv_stride_head < head_dim || out_stride_head < head_dim ||
-      q_stride_token < (int64_t)heads * head_dim || kv_stride_token < (int64_t)kv_heads * head_dim ||
+  if (q_stride_head < head_dim || k_stride_head < head_dim || v_stride_head < head_dim ||
+      out_stride_head < head_dim || q_stride_token < (int64_t)heads * head_dim ||
+      k_stride_token < (int64_t)kv_heads * head_dim || v_stride_token < (int64_t)kv_heads * head_dim ||
       out_stride_token < (int64_t)heads * head_dim)
     return fail(ASRBACK_ERR_ARGUMENT, "strides do not hold (tokens, heads, head_dim) rows");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == ASRBACK_BF16) {
     if (int rc = varlen_attention_tc(tokens, heads, kv_heads, head_dim, q, q_stride_token,
-                                     q_stride_head, key, value, kv_stride_token, kv_stride_head,
-                                     cu_seqlens, segments, max_length, causal, out,
+                                     q_stride_head, key, k_stride_token, k_stride_head, value,
+                                     v_stride_token, v_stride_head, cu_seqlens, segments, max_length, causal, out,
                                      out_stride_token, out_stride_head, scale, status, s))
       return rc;
     return ok();
   }
   SimtParams p{static_cast<const float*>(q), static_cast<const float*>(key),
                static_cast<const float*>(value), static_cast<float*>(out), q_stride_token,
-               q_stride_head, kv_stride_token, kv_stride_head, out_stride_token, out_stride_head,
+               q_stride_head, k_stride_token, k_stride_head, v_stride_token, v_stride_head,
+               out_stride_token, out_stride_head,
                cu_seqlens, tokens, max_length, heads / kv_heads, causal ? 1 : 0,
                scale * 1.4426950408889634f, status};
   dim3 grid((max_length + kRowsS - 1) / kRowsS, heads, segments);

@@ -9,7 +9,8 @@
 //     non-causal windows.
 // Segment s holds the tokens cu[s] .. cu[s+1]-1 (the reference's `starts`).
 //
-// One CTA owns one (segment, query head, pair of 128-row query tiles). Roles:
+// One CTA owns one (segment, query head) and two adjacent 128-row query tiles
+// of the segment, which share every key/value tile they read. Roles:
 //   warp 0      TMA: both Q tiles, then K/V tiles of 128 keys of the query
 //               head's key/value head into a STAGES-deep ring. A tile is
 //               head_dim / 64 column blocks of 128 bytes (128-byte swizzle);
@@ -91,16 +92,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicOr(p.status, ASRBACK_STATUS_SEGMENT);
     return;
   }
-  const int r0 = pair * 2 * kRows;
-  if (r0 >= len) return;  // the whole CTA: this segment is shorter
+  if (pair * 2 * kRows >= len) return;  // the whole CTA: this segment is shorter
   const int kvh = h / p.group;
   const int n_seg = (len + kKeys - 1) / kKeys;
-  // Key tiles of query tile t (0: the tile lies past the segment).
-  int n_k[2];
+  // Query tiles 2*pair and 2*pair+1 (the second absent past the segment's
+  // end), and the key tiles each reads. (Pairing tile p with tile n-1-p to
+  // even out causal work measured slower: it streams more key tiles.)
+  int first_row[2], n_k[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int first_row = r0 + t * kRows;
-    n_k[t] = first_row >= len ? 0 : (p.causal ? min(n_seg, first_row / kKeys + 1) : n_seg);
+    first_row[t] = (2 * pair + t) * kRows;
+    n_k[t] = first_row[t] >= len ? 0 : (p.causal ? min(n_seg, first_row[t] / kKeys + 1) : n_seg);
   }
   const int n_max = max(n_k[0], n_k[1]);
 
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int a = 0; a < Sh::kAtoms; ++a)
           tma_load_3d(smem + Sh::kOffQ + t * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q, 64 * a,
-                      h, start + r0 + t * kRows, q_full);
+                      h, start + first_row[t], q_full);
       for (int j = 0; j < n_max; ++j) {
         const int s = j % Sh::kStages;
         if (j >= Sh::kStages &&
@@ -240,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- softmax (one query row per thread) ----------------
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
-    const int row = r0 + t * kRows + quarter * 32 + lane;  // within the segment
+    const int row = first_row[t] + quarter * 32 + lane;  // within the segment
     const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_bits + col_s(t);
     const uint32_t tO = tmem + lane_bits + col_o(t);
@@ -397,14 +399,15 @@ int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
 // Launches the tensor-core varlen attention; arguments already validated
 // (bf16, head_dim 64 or 128, 16-byte aligned pointers and strides).
 int varlen_attention_tc(int tokens, int heads, int kv_heads, int head_dim, const void* q,
-                        int64_t q_tok, int64_t q_head, const void* k, const void* v,
-                        int64_t kv_tok, int64_t kv_head, const int32_t* cu, int segments,
+                        int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                        int64_t k_head, const void* v, int64_t v_tok, int64_t v_head,
+                        const int32_t* cu, int segments,
                         int max_length, int causal, void* out, int64_t o_tok, int64_t o_head,
                         float scale, int32_t* status, cudaStream_t stream) {
   CUtensorMap mq, mk, mv;
   if (int rc = make_map_3d(&mq, q, tokens, heads, head_dim, q_tok, q_head)) return rc;
-  if (int rc = make_map_3d(&mk, k, tokens, kv_heads, head_dim, kv_tok, kv_head)) return rc;
-  if (int rc = make_map_3d(&mv, v, tokens, kv_heads, head_dim, kv_tok, kv_head)) return rc;
+  if (int rc = make_map_3d(&mk, k, tokens, kv_heads, head_dim, k_tok, k_head)) return rc;
+  if (int rc = make_map_3d(&mv, v, tokens, kv_heads, head_dim, v_tok, v_head)) return rc;
   VarlenParams p{out,   o_tok,          o_head,     cu, tokens, max_length, heads / kv_heads,
                  causal ? 1 : 0, scale * 1.4426950408889634f, status};
   return head_dim == 128 ? launch<128>(mq, mk, mv, p, segments, heads, max_length, stream)

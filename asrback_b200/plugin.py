@@ -19,7 +19,12 @@ Patched call sites (asrback project paths):
   and ``qwen3_asr.TextAttention.step`` (``qwen3_asr.py:392-432``): the decoder
   step hands ``qkv_proj``'s output, the full RoPE tables and the positions to
   one kernel (RMSNorm, RoPE, cache write, grouped-query attention); no mask
-  or varlen triple is built.
+  or varlen triple is built;
+- ``qwen3_asr.attend`` (``qwen3_asr.py:152-181``), the module function that
+  ``TextAttention.prefill`` (causal prompt prefill, ``:374-390``) and
+  ``AudioAttention.forward`` (non-causal audio windows, ``:214-219``) call:
+  attention within the packed segments runs on the varlen kernel, whichever
+  path (``varlen_attn`` or padded SDPA) the segments were built for.
 
 The patched methods run the kernels only: tensors on the CPU raise, as every
 op of this package does (there is no fallback).
@@ -93,6 +98,13 @@ def _qwen3_text_attention_step(self, x, keys, values, positions, mask, cos, sin)
     return self.o_proj(out)
 
 
+def _qwen3_attend(q, k, v, segments, causal):
+    """Attention within each segment of packed ``(tokens, heads, head_dim)``
+    tensors on the varlen kernel (``segments.starts`` is already on the
+    device)."""
+    return attention.varlen_attention(q, k, v, segments.starts, segments.longest, causal)
+
+
 def _qwen3_text_model_step(self, tokens, positions, cache, cos, sin, varlen):
     """Hidden states for one token per row over a fixed-shape cache view; each
     row reads only its written keys, whatever ``varlen`` says."""
@@ -120,6 +132,7 @@ def install(whisper_module=None, qwen3_module=None) -> None:
     if qwen3_module is not None:
         _patch(qwen3_module.TextAttention, "step", _qwen3_text_attention_step)
         _patch(qwen3_module.TextModel, "step", _qwen3_text_model_step)
+        _patch(qwen3_module, "attend", _qwen3_attend)
 
 
 def _try_import(name: str):

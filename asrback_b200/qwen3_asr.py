@@ -9,14 +9,13 @@ kv_heads, head_dim)``, ``:333-347``), ``TextAttention`` with the fused
 per-head q/k RMSNorm, the RoPE rotation, the cache write and the grouped-query
 attention over each row's written keys (the reference does these in
 ``_project``, ``:366-372``, and ``step``, ``:392-432``). The packed causal
-prefill (``:374-390``) is not part of this build; rows are filled one position
-per step (:meth:`TextModel.step_embeddings` takes embeddings directly, as the
-audio positions of a prompt need).
+prompt prefill (``TextAttention.prefill``, ``:374-390``; ``TextModel.prefill``,
+``:471-490``) runs ``attend`` (``:152-181``) on the varlen kernel, with
+``Segments`` holding the packed prompts' starts (``:122-149``).
 """
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import torch
@@ -27,6 +26,9 @@ from . import attention as ops
 
 __all__ = [
     "CACHE_LENGTH",
+    "Segments",
+    "attend",
+    "rotate",
     "RMSNorm",
     "KVCache",
     "TextAttention",
@@ -95,6 +97,36 @@ class KVCache:
         return KVCache(self.keys[:, :batch_size, :length], self.values[:, :batch_size, :length])
 
 
+@dataclass
+class Segments:
+    """Boundaries of the sequences laid out back to back in a packed tensor:
+    ``starts`` ``(sequences + 1,)`` int32 cumulative lengths on the device and
+    the longest length (the reference's ``Segments``, ``qwen3_asr.py:122-149``)."""
+
+    starts: Tensor
+    longest: int
+
+    @classmethod
+    def from_lengths(cls, lengths: list[int], device: torch.device) -> "Segments":
+        sizes = torch.tensor(lengths, dtype=torch.int64)
+        starts = F.pad(sizes.cumsum(0), (1, 0)).to(torch.int32)
+        return cls(starts.to(device), max(lengths))
+
+
+def attend(q: Tensor, k: Tensor, v: Tensor, segments: Segments, causal: bool) -> Tensor:
+    """Attention within each segment of packed ``(tokens, heads, head_dim)``
+    tensors; ``k`` and ``v`` may have fewer heads than ``q`` (grouped-query)."""
+    return ops.varlen_attention(q, k, v, segments.starts, segments.longest, causal)
+
+
+def rotate(x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
+    """Rotary embedding (rotate-half) of ``(tokens, heads, head_dim)`` with
+    ``cos``/``sin`` ``(tokens, head_dim)`` (``qwen3_asr.py:326-330``)."""
+    half = x.shape[-1] // 2
+    rotated = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return x * cos[:, None] + rotated * sin[:, None]
+
+
 class TextAttention(nn.Module):
     def __init__(self, config: dict) -> None:
         super().__init__()
@@ -118,6 +150,25 @@ class TextAttention(nn.Module):
             cos, sin, positions, keys, values, self.heads, self.kv_heads,
         )
         return self.o_proj(out)
+
+    def _project(self, x: Tensor, cos: Tensor, sin: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+        """``(tokens, heads, head_dim)`` queries, keys and values for
+        ``(tokens, width)``: q/k RMSNorm, then RoPE with each token's
+        ``cos``/``sin`` rows."""
+        shape = (len(x), -1, self.head_dim)
+        q, k, v = self.qkv_proj(x).split(self.sizes, dim=-1)
+        q = rotate(self.q_norm(q.reshape(shape)), cos, sin)
+        k = rotate(self.k_norm(k.reshape(shape)), cos, sin)
+        return q, k, v.reshape(shape)
+
+    def prefill(self, x: Tensor, keys: Tensor, values: Tensor, rows: Tensor, positions: Tensor,
+                segments: Segments, cos: Tensor, sin: Tensor) -> Tensor:
+        """Causal attention within each packed prompt; every token's key and
+        value go to its row and position of the cache."""
+        q, k, v = self._project(x, cos, sin)
+        keys[rows, positions] = k
+        values[rows, positions] = v
+        return self.o_proj(attend(q, k, v, segments, causal=True).flatten(1))
 
 
 class TextMLP(nn.Module):
@@ -145,6 +196,12 @@ class DecoderLayer(nn.Module):
         x = x + self.self_attn.step(self.input_layernorm(x), keys, values, positions, cos, sin)
         return x + self.mlp(self.post_attention_layernorm(x))
 
+    def prefill(self, x: Tensor, keys: Tensor, values: Tensor, rows: Tensor, positions: Tensor,
+                segments: Segments, cos: Tensor, sin: Tensor) -> Tensor:
+        x = x + self.self_attn.prefill(self.input_layernorm(x), keys, values, rows, positions,
+                                       segments, cos, sin)
+        return x + self.mlp(self.post_attention_layernorm(x))
+
 
 class TextModel(nn.Module):
     def __init__(self, config: dict) -> None:
@@ -167,6 +224,12 @@ class TextModel(nn.Module):
             x = layer(x, cache.keys[index], cache.values[index], positions, cos, sin)
         return self.norm(x)
 
-
-def default_scale(head_dim: int) -> float:
-    return 1.0 / math.sqrt(head_dim)
+    def prefill(self, x: Tensor, cache: KVCache, rows: Tensor, positions: Tensor,
+                segments: Segments, cos: Tensor, sin: Tensor) -> Tensor:
+        """Hidden states of packed prompts ``x`` ``(tokens, width)``; token ``i``
+        is at ``positions[i]`` of cache row ``rows[i]``; ``cos``/``sin`` are the
+        tokens' rows of the tables."""
+        for index, layer in enumerate(self.layers):
+            x = layer.prefill(x, cache.keys[index], cache.values[index], rows, positions, segments,
+                              cos, sin)
+        return self.norm(x)

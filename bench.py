@@ -54,7 +54,8 @@ def parse_args():
     parser.add_argument("--steps", type=int, default=128)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
-    parser.add_argument("--workload", choices=("whisper-decode", "whisper-encoder", "qwen3-decode"),
+    parser.add_argument("--workload", choices=("whisper-decode", "whisper-encoder", "qwen3-decode",
+                                               "qwen3-prefill"),
                         default="whisper-decode")
     parser.add_argument("--batch", type=int, default=None,
                         help="override the workload's batch (small profiling cases)")
@@ -643,7 +644,137 @@ class Qwen3Decode:
                           f"numpy oracle, {elapsed:.1f} s"}
 
 
-WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode)}
+class Qwen3Prefill:
+    """Admission prefill of BASELINE config 4's prompts: causal grouped-query
+    attention within the packed prompts (TextAttention.prefill's `attend`)."""
+
+    name = "qwen3-prefill"
+    metric = ("prefill tokens/s/GPU (Qwen3 1.7B-style, 64 packed prompts x 410 tokens, 28 layers, "
+              "bf16); attention TFLOP/s")
+    unit = "tokens/s"
+    bound = "tensor"
+    reference_in_graph = False
+    layers, heads, kv_heads, head_dim, prompt = 28, 16, 8, 128, 410
+    profile = "qwen3_prefill_b64_bf16.md"
+
+    def __init__(self, batch: int | None):
+        self.batch = batch or 64
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": "Qwen3-ASR-1.7B-style packed prompt prefill attention (BASELINE config 4 "
+                        "admission: 390 audio + 20 prompt positions per row)",
+            "layers": self.layers, "heads": self.heads, "kv_heads": self.kv_heads,
+            "head_dim": self.head_dim, "causal": True, "prompts_per_gpu": self.batch,
+            "prompt_tokens": self.prompt, "global_batch": self.batch * world,
+            "step": "28 layers of causal varlen attention over the packed prompts",
+            "inputs": "N(0,1) bf16 q (tokens, 16, 128), k/v (tokens, 8, 128) per layer",
+            "parallelism": f"replicas x{world} (no collective)",
+            "l2": "inputs larger than L2 (215 MB of q/k/v per layer)",
+        }
+
+    def units_per_step(self) -> int:
+        return self.batch * self.prompt
+
+    def flops_per_layer(self) -> float:
+        # Causal: query i reads i + 1 keys; 2 flops per multiply-add, QK and PV.
+        pairs = self.prompt * (self.prompt + 1) / 2
+        return 4.0 * pairs * self.head_dim * self.heads * self.batch
+
+    def setup(self, torch, device, seed: int, total: int) -> None:
+        gen = torch.Generator(device=device).manual_seed(seed)
+        tokens = self.batch * self.prompt
+        dtype = torch.bfloat16
+        self.q = [torch.randn((tokens, self.heads, self.head_dim), generator=gen, device=device,
+                              dtype=dtype) for _ in range(self.layers)]
+        self.k = [torch.randn((tokens, self.kv_heads, self.head_dim), generator=gen, device=device,
+                              dtype=dtype) for _ in range(self.layers)]
+        self.v = [torch.randn((tokens, self.kv_heads, self.head_dim), generator=gen, device=device,
+                              dtype=dtype) for _ in range(self.layers)]
+        self.starts = (torch.arange(self.batch + 1, device=device) * self.prompt).to(torch.int32)
+        self.outputs: list = [None] * self.layers
+
+    def attend(self, layer):
+        from asrback_b200 import attention
+
+        return attention.varlen_attention(self.q[layer], self.k[layer], self.v[layer],
+                                          self.starts, self.prompt, True)
+
+    def step(self) -> None:
+        for layer in range(self.layers):
+            self.outputs[layer] = self.attend(layer)
+
+    def launches_per_step(self) -> int:
+        return self.layers
+
+    def refresh(self, t: int) -> None:
+        pass
+
+    def host_step_inputs(self, torch, first: int, count: int):
+        # One layer's q/k/v in pinned memory, copied into every layer's inputs.
+        host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                for t in (self.q[0], self.k[0], self.v[0])]
+        for h, d in zip(host, (self.q[0], self.k[0], self.v[0])):
+            h.copy_(d.cpu())
+        pairs = []
+        for layer in range(self.layers):
+            for h, d in zip(host, (self.q[layer], self.k[layer], self.v[layer])):
+                pairs.append((h[None].expand(count, *h.shape), d))
+        return pairs
+
+    def kernels(self, t: int):
+        return [("varlen", self.attend, self.flops_per_layer())]
+
+    def step_work(self, first: int, count: int) -> float:
+        return self.flops_per_layer() * self.layers * count
+
+    def torch_reference_step(self, torch):
+        """The reference's `attend` on its GPU path under torch 2.11 (varlen_attn
+        lacks the kwargs it passes, so the padded batch): gather the prompts,
+        SDPA with the valid & causal mask and grouped heads, keep the valid
+        rows (qwen3_asr.py:136-149, 166-181), on the same tensors."""
+        import torch.nn.functional as F
+
+        device = self.starts.device
+        offsets = torch.arange(self.prompt, device=device)
+        sizes = self.starts[1:] - self.starts[:-1]
+        valid = offsets[None, :] < sizes[:, None]
+        last = (self.starts[1:] - 1)[:, None]
+        gather = torch.minimum(self.starts[:-1, None] + offsets, last)
+        causal = torch.ones((self.prompt, self.prompt), dtype=torch.bool, device=device).tril()
+        mask = valid[:, None, None, :] & causal
+
+        def run():
+            for layer in range(self.layers):
+                out = F.scaled_dot_product_attention(
+                    *(t[gather].transpose(1, 2) for t in (self.q[layer], self.k[layer], self.v[layer])),
+                    attn_mask=mask, enable_gqa=True)
+                out.transpose(1, 2)[valid]
+        return run
+
+    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+        from oracle import attention as oracle
+
+        rng = np.random.default_rng(seed)
+        f32 = np.float32
+        q = rng.standard_normal((self.prompt, self.heads, self.head_dim), dtype=f32)
+        k = rng.standard_normal((self.prompt, self.kv_heads, self.head_dim), dtype=f32)
+        v = rng.standard_normal((self.prompt, self.kv_heads, self.head_dim), dtype=f32)
+        starts = np.array([0, self.prompt])
+
+        def one(_t, _p):
+            oracle.varlen_attention(q, k, v, starts, True, compute=f32)
+
+        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
+        # `done` rounds of `threads` prompt-layers in `elapsed`; a prompt needs 28 layers.
+        layers_done = done * threads
+        rate = layers_done / elapsed / self.layers * self.prompt
+        return {"value": rate, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{layers_done} prompt-layers (16 heads x 410 x 410 causal each), float32 "
+                          f"numpy oracle, {elapsed:.1f} s, scaled by 1/28 layers"}
+
+
+WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode, Qwen3Prefill)}
 
 
 # ------------------------------------------------------------------ arms ----
@@ -853,9 +984,9 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     line = measure(args, work, torch, dist, device, rank, world, args.steps, args.warmup,
                    cpu=not args.no_cpu_baseline)
     if args.workload == "whisper-decode" and not args.no_extras and args.batch is None:
-        # Short runs of the other two BASELINE workloads, for context.
+        # Short runs of the other workloads, for context.
         extras = {}
-        for name in ("whisper-encoder", "qwen3-decode"):
+        for name in ("whisper-encoder", "qwen3-decode", "qwen3-prefill"):
             del work
             torch.cuda.empty_cache()
             work = WORKLOADS[name](None)

@@ -201,7 +201,9 @@ ASRBACK_API int asrback_whisper_encoder_attention(
  * keys.
  *
  * q, out        (tokens, heads, head_dim) at [t*stride_token + h*stride_head + d];
- * key, value    (tokens, kv_heads, head_dim) with kv_stride_token/_head;
+ * key, value    (tokens, kv_heads, head_dim), each with its own strides (the
+ *               reference hands attend a rotated, contiguous key and the value
+ *               as a view of the fused projection);
  *               query head h reads key/value head h / (heads / kv_heads);
  * cu_seqlens    device int32, segments + 1 entries: segment s is tokens
  *               cu_seqlens[s] .. cu_seqlens[s+1]-1 (the reference's
@@ -214,10 +216,19 @@ ASRBACK_API int asrback_whisper_encoder_attention(
 ASRBACK_API int asrback_varlen_attention(
     int dtype, int tokens, int heads, int kv_heads, int head_dim,
     const void* q, int64_t q_stride_token, int64_t q_stride_head,
-    const void* key, const void* value, int64_t kv_stride_token, int64_t kv_stride_head,
+    const void* key, int64_t k_stride_token, int64_t k_stride_head,
+    const void* value, int64_t v_stride_token, int64_t v_stride_head,
     const int32_t* cu_seqlens, int segments, int max_length, int causal,
     void* out, int64_t out_stride_token, int64_t out_stride_head,
     float scale, int32_t* status, void* stream);
+
+/*
+ * Self-test of the kernels' bounded waits: one CTA waits on an mbarrier that
+ * nothing completes, gives up after budget_ns (at most 1 s) of %globaltimer,
+ * sets ASRBACK_STATUS_TIMEOUT in `status` and exits; the context stays usable.
+ * Lets a host check the timeout path on its own GPU without faulting it.
+ */
+ASRBACK_API int asrback_selftest_bounded_wait(int64_t budget_ns, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

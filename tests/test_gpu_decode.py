@@ -359,3 +359,42 @@ def test_qwen3_small_greedy_steps_match_reference():
             same.append(host(choice) == g["argmax"][:, t])
     assert max(hidden_err) < 1e-3, max(hidden_err)
     assert np.mean(same) >= 0.99, np.mean(same)
+
+
+def test_qwen3_small_packed_prefill_then_steps_match_reference():
+    """The prompts filled by one packed causal prefill (TextModel.prefill on
+    the varlen kernel) instead of one position per step, then the same greedy
+    steps: the same hidden states and tokens as the reference."""
+    from asrback_b200 import qwen3_asr
+    from asrback_b200.synthetic import seeded_parameters
+
+    g = load("qwen3_small_decode")
+    meta = g["meta"]
+    config = dict(meta["config"], rope_theta=meta["rope_theta"])
+    model = qwen3_asr.TextModel(config)
+    lm_head = torch.nn.Linear(config["hidden_size"], config["vocab_size"], bias=False)
+    seeded_parameters(model, meta["seed"])
+    seeded_parameters(lm_head, meta["lm_head_seed"])
+    model, lm_head = model.to(DEV).eval(), lm_head.to(DEV)
+    cos, sin = qwen3_asr.rope_tables(meta["rope_theta"], 128, 1024, device=DEV)
+    batch = len(meta["prompts"])
+    cache = qwen3_asr.KVCache.allocate(config, batch, 1024, device=DEV, dtype=torch.float32)
+    prompts = [prompt[:-1] for prompt in meta["prompts"]]
+    lengths = [len(prompt) for prompt in prompts]
+    tokens = torch.tensor([t for prompt in prompts for t in prompt], device=DEV)
+    rows = torch.tensor([b for b, n in enumerate(lengths) for _ in range(n)], device=DEV)
+    positions = torch.cat([torch.arange(n) for n in lengths]).to(DEV)
+    segments = qwen3_asr.Segments.from_lengths(lengths, torch.device(DEV))
+    with torch.no_grad():
+        model.prefill(model.embed_tokens(tokens), cache, rows, positions, segments,
+                      cos[positions], sin[positions])
+        hidden_err, same = [], []
+        for t in range(meta["steps"]):
+            hidden = model.step(dev(g["tokens"][:, t], torch.int64),
+                                dev(g["positions"][:, t], torch.int64), cache, cos, sin)
+            choice = lm_head(hidden).argmax(dim=-1)
+            hidden_err.append(np.abs(host(hidden) - g["hidden"][:, t]).max())
+            same.append(host(choice) == g["argmax"][:, t])
+    assert attention.read_status() == 0
+    assert max(hidden_err) < 1e-3, max(hidden_err)
+    assert np.mean(same) >= 0.99, np.mean(same)

@@ -76,9 +76,12 @@ def test_varlen_random(tag, lengths, heads, kv_heads, head_dim, causal):
     assert attention.read_status() == 0
 
 
-def test_varlen_strided_views_of_a_fused_projection():
+@pytest.mark.parametrize("contiguous_k", [False, True])
+def test_varlen_strided_views_of_a_fused_projection(contiguous_k):
     """q, k, v as views into one (tokens, (16 + 8 + 8) * 128) projection, the
-    layout TextAttention._project splits (qwen3_asr.py:366-372)."""
+    layout TextAttention._project splits (qwen3_asr.py:366-372); with
+    `contiguous_k`, q and k are new tensors (as after RMSNorm and RoPE) while v
+    stays a view, so k and v have different strides."""
     gen = torch.Generator().manual_seed(3)
     lengths = [200, 61, 390]
     tokens = sum(lengths)
@@ -86,6 +89,9 @@ def test_varlen_strided_views_of_a_fused_projection():
     q = qkv[:, : 16 * 128].view(tokens, 16, 128)
     k = qkv[:, 16 * 128 : 24 * 128].view(tokens, 8, 128)
     v = qkv[:, 24 * 128 :].view(tokens, 8, 128)
+    if contiguous_k:
+        q, k = q.contiguous(), k.contiguous()
+        assert k.stride() != v.stride()
     starts = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
     out = attention.varlen_attention(q, k, v, torch.from_numpy(starts).to(DEV), max(lengths), True)
     want = oracle.varlen_attention(host(q), host(k), host(v), starts, True)

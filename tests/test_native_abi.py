@@ -97,7 +97,7 @@ def _varlen_call(lib, **overrides):
     args.update(overrides)
     return lib.asrback_varlen_attention(
         args["dtype"], args["tokens"], args["heads"], args["kv_heads"], args["head_dim"],
-        args["q"], args["q_tok"], 128, args["k"], args["v"], 1024, 128,
+        args["q"], args["q_tok"], 128, args["k"], 1024, 128, args["v"], 4096, 128,
         args["cu"], args["segments"], args["max_length"], 1,
         args["out"], 2048, 128, 0.088, None, None)
 
@@ -114,6 +114,12 @@ def test_varlen_invalid_arguments_are_rejected_on_the_host(lib, overrides, fragm
     rc = _varlen_call(lib, **overrides)
     assert rc == _native.ERR_ARGUMENT
     assert fragment in lib.asrback_last_error().decode()
+
+
+def test_bounded_wait_selftest_checks_its_budget(lib):
+    assert lib.asrback_selftest_bounded_wait(0, 16, None) == _native.ERR_ARGUMENT
+    assert lib.asrback_selftest_bounded_wait(2_000_000_000, 16, None) == _native.ERR_ARGUMENT
+    assert lib.asrback_selftest_bounded_wait(1000, None, None) == _native.ERR_ARGUMENT
 
 
 def test_ops_refuse_cpu_tensors():

@@ -70,6 +70,12 @@ def cpu_ops(monkeypatch):
         values.copy_(torch.from_numpy(vc))
         return torch.from_numpy(out).float()
 
+    def varlen(q, k, v, starts, longest, causal, scale=None):
+        out = oracle.varlen_attention(q.detach().numpy(), k.detach().numpy(), v.detach().numpy(),
+                                      starts.numpy(), causal)
+        return torch.from_numpy(out).float()
+
+    monkeypatch.setattr(attention, "varlen_attention", varlen)
     monkeypatch.setattr(attention, "whisper_self_attention_step", self_step)
     monkeypatch.setattr(attention, "whisper_cross_attention_step", cross_step)
     monkeypatch.setattr(attention, "whisper_encoder_attention", encoder)
@@ -170,14 +176,52 @@ def test_qwen3_text_model_step(reference, cpu_ops):
     assert torch.allclose(got_cache.values, want_cache.values, atol=1e-5)
 
 
+@torch.no_grad()
+def test_qwen3_prefill_and_audio_attention(reference, cpu_ops):
+    """TextAttention.prefill (causal, grouped-query, cache writes) and
+    AudioAttention.forward (non-causal windows) through the patched attend."""
+    _, qwen3 = reference
+    config = dict(vocab_size=64, hidden_size=256, num_hidden_layers=1, num_attention_heads=16,
+                  num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6, intermediate_size=64)
+    text = qwen3.TextAttention(config).eval()
+    seeded_parameters(text, 8)
+    audio = qwen3.AudioAttention(128, 2).eval()
+    seeded_parameters(audio, 9)
+    lengths = [5, 17, 1]
+    tokens = sum(lengths)
+    rows = torch.tensor([0] * 5 + [1] * 17 + [2])
+    positions = torch.cat([torch.arange(n) for n in lengths])
+    inverse = 1.0 / (1e6 ** (torch.arange(0, 128, 2).float() / 128))
+    angles = positions.float()[:, None] * inverse[None, :]
+    angles = torch.cat((angles, angles), dim=-1)
+    cos, sin = angles.cos(), angles.sin()
+    x = seeded_normal((tokens, 256), 40)
+    xa = seeded_normal((tokens, 128), 41)
+
+    def run():
+        keys = torch.zeros((3, 20, 8, 128))
+        values = torch.zeros_like(keys)
+        segments = qwen3.Segments.from_lengths(lengths, torch.device("cpu"), False)
+        out = text.prefill(x, keys, values, rows, positions, segments, cos, sin)
+        return out, keys, values, audio(xa, segments)
+
+    want = run()
+    plugin.install(None, qwen3)
+    assert qwen3.attend is not None and qwen3.attend.__name__ == "_qwen3_attend"
+    got = run()
+    for a, b in zip(got, want):
+        assert torch.allclose(a, b, atol=1e-4), (a - b).abs().max()
+
+
 def test_uninstall_restores_reference(reference):
     whisper, qwen3 = reference
     before = (whisper.DecoderLayer.forward, whisper.MultiHeadAttention.forward,
-              qwen3.TextAttention.step, qwen3.TextModel.step)
+              qwen3.TextAttention.step, qwen3.TextModel.step, qwen3.attend)
     plugin.install(whisper, qwen3)
     assert plugin.installed()
     assert whisper.DecoderLayer.forward is not before[0]
+    assert qwen3.attend is not before[4]
     plugin.uninstall()
     after = (whisper.DecoderLayer.forward, whisper.MultiHeadAttention.forward,
-             qwen3.TextAttention.step, qwen3.TextModel.step)
+             qwen3.TextAttention.step, qwen3.TextModel.step, qwen3.attend)
     assert after == before
