@@ -55,7 +55,7 @@ def parse_args():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--workload", choices=("whisper-decode", "whisper-encoder", "qwen3-decode",
-                                               "qwen3-prefill"),
+                                               "qwen3-prefill", "qwen3-audio"),
                         default="whisper-decode")
     parser.add_argument("--batch", type=int, default=None,
                         help="override the workload's batch (small profiling cases)")
@@ -774,7 +774,98 @@ class Qwen3Prefill:
                           f"numpy oracle, {elapsed:.1f} s, scaled by 1/28 layers"}
 
 
-WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode, Qwen3Prefill)}
+class Qwen3AudioWindows(Qwen3Prefill):
+    """Qwen3-ASR audio encoder attention: non-causal attention within 104-token
+    windows of packed audio tokens (AudioAttention.forward's `attend`)."""
+
+    name = "qwen3-audio"
+    metric = ("audio tokens/s/GPU (Qwen3-ASR-style audio encoder attention, 64 x 30 s requests "
+              "in 104-token windows, bf16); attention TFLOP/s")
+    unit = "tokens/s"
+    bound = "tensor"
+    # 30 s of audio = 30 chunks of 13 tokens = 390 tokens per request: windows
+    # of 104 tokens (8 chunks) and a last window of 78.
+    layers, heads, kv_heads, head_dim, prompt = 24, 16, 16, 64, 390
+    window = 104
+    profile = "qwen3_audio_b64_bf16.md"
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": "Qwen3-ASR-style audio encoder window attention (SURVEY 8(f) rank 3 row)",
+            "layers": self.layers, "heads": self.heads, "head_dim": self.head_dim,
+            "causal": False, "requests_per_gpu": self.batch, "tokens_per_request": self.prompt,
+            "window_tokens": self.window, "global_batch": self.batch * world,
+            "assumed": "24 layers, 16 heads of 64 (d_model 1024); the checkpoint's audio config "
+                       "is not available here",
+            "step": "24 layers of non-causal varlen attention over the packed windows",
+            "inputs": "N(0,1) bf16 q/k/v (tokens, 16, 64) per layer",
+            "parallelism": f"replicas x{world} (no collective)",
+        }
+
+    def lengths(self) -> list[int]:
+        per = [self.window] * (self.prompt // self.window)
+        if self.prompt % self.window:
+            per.append(self.prompt % self.window)
+        return per * self.batch
+
+    def flops_per_layer(self) -> float:
+        return float(sum(4.0 * n * n * self.head_dim * self.heads for n in self.lengths()))
+
+    def setup(self, torch, device, seed: int, total: int) -> None:
+        super().setup(torch, device, seed, total)
+        lengths = torch.tensor(self.lengths())
+        self.starts = torch.nn.functional.pad(lengths.cumsum(0), (1, 0)).to(torch.int32).to(device)
+
+    def attend(self, layer):
+        from asrback_b200 import attention
+
+        return attention.varlen_attention(self.q[layer], self.k[layer], self.v[layer],
+                                          self.starts, self.window, False)
+
+    def torch_reference_step(self, torch):
+        """The reference's padded path for the windows: gather, SDPA with the
+        valid mask (no causal part), keep the valid rows."""
+        import torch.nn.functional as F
+
+        device = self.starts.device
+        offsets = torch.arange(self.window, device=device)
+        sizes = self.starts[1:] - self.starts[:-1]
+        valid = offsets[None, :] < sizes[:, None]
+        last = (self.starts[1:] - 1)[:, None]
+        gather = torch.minimum(self.starts[:-1, None] + offsets, last)
+        mask = valid[:, None, None, :]
+
+        def run():
+            for layer in range(self.layers):
+                out = F.scaled_dot_product_attention(
+                    *(t[gather].transpose(1, 2) for t in (self.q[layer], self.k[layer], self.v[layer])),
+                    attn_mask=mask)
+                out.transpose(1, 2)[valid]
+        return run
+
+    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+        from oracle import attention as oracle
+
+        rng = np.random.default_rng(seed)
+        f32 = np.float32
+        q = rng.standard_normal((self.prompt, self.heads, self.head_dim), dtype=f32)
+        k = rng.standard_normal(q.shape, dtype=f32)
+        v = rng.standard_normal(q.shape, dtype=f32)
+        starts = np.concatenate([[0], np.cumsum(self.lengths()[: len(self.lengths()) // self.batch])])
+
+        def one(_t, _p):
+            oracle.varlen_attention(q, k, v, starts, False, compute=f32)
+
+        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
+        layers_done = done * threads
+        rate = layers_done / elapsed / self.layers * self.prompt
+        return {"value": rate, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{layers_done} request-layers (16 heads x windows of 104), float32 numpy "
+                          f"oracle, {elapsed:.1f} s, scaled by 1/24 layers"}
+
+
+WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode, Qwen3Prefill,
+                                       Qwen3AudioWindows)}
 
 
 # ------------------------------------------------------------------ arms ----
@@ -986,7 +1077,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     if args.workload == "whisper-decode" and not args.no_extras and args.batch is None:
         # Short runs of the other workloads, for context.
         extras = {}
-        for name in ("whisper-encoder", "qwen3-decode", "qwen3-prefill"):
+        for name in ("whisper-encoder", "qwen3-decode", "qwen3-prefill", "qwen3-audio"):
             del work
             torch.cuda.empty_cache()
             work = WORKLOADS[name](None)
