@@ -9,8 +9,12 @@
 //     non-causal windows.
 // Segment s holds the tokens cu[s] .. cu[s+1]-1 (the reference's `starts`).
 //
-// One CTA owns one (segment, query head) and two adjacent 128-row query tiles
-// of the segment, which share every key/value tile they read. Roles:
+// Work item: one (segment, query head) and two adjacent 128-row query tiles
+// of the segment, which share every key/value tile they read. The kernel is
+// persistent: one CTA per SM takes items blockIdx.x, + gridDim.x, ...; its
+// TMA warp loads the next item's Q (once the current item's last S is done)
+// and K/V while the current item finishes, and the next item's first P V
+// waits only until the current item's epilogue has read O. Roles:
 //   warp 0      TMA: both Q tiles, then K/V tiles of 128 keys of the query
 //               head's key/value head into a STAGES-deep ring. A tile is
 //               head_dim / 64 column blocks of 128 bytes (128-byte swizzle);
@@ -27,6 +31,8 @@
 // until a tile's max exceeds it by more than 8 in log2 units) needs no wait.
 // Causal: query row r reads keys 0..r of its segment, so a query tile stops
 // at the key tile of its own rows and only that diagonal tile is masked.
+#include <algorithm>
+
 #include "tcgen05.cuh"
 
 namespace asrback {
@@ -51,9 +57,9 @@ struct VarlenShape {
   static constexpr int kOffK = 2 * kTileBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
   static constexpr int kOffBar = kOffV + kStages * kTileBytes;
-  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2],
-  // o_full[2]
-  static constexpr int kNumBars = 1 + 3 * kStages + 6;
+  // barriers: q_full, q_empty, k_full[S], v_full[S], kv_empty[S], s_full[2],
+  // p_full[2], o_full[2], o_free[2]
+  static constexpr int kNumBars = 2 + 3 * kStages + 8;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
   static_assert(kSmemBytes <= 227 * 1024, "shared memory exceeds a CTA's 227 KB");
@@ -66,6 +72,9 @@ struct VarlenParams {
   void* out;
   int64_t os_tok, os_head;  // output strides (elements)
   const int32_t* cu;        // segment starts, segments + 1 entries
+  int segments;
+  int heads;
+  int pairs;                // query-tile pairs per segment at max_length
   int tokens;
   int max_length;
   int group;                // query heads per key/value head
@@ -74,6 +83,54 @@ struct VarlenParams {
   int32_t* status;
 };
 
+// One work item: a (segment, query head, pair of adjacent 128-row query tiles).
+struct Item {
+  bool active;      // the pair holds rows of a valid segment
+  int start, len;   // the segment's first token and length
+  int h, kvh;       // query head, its key/value head
+  int first_row[2]; // first row of each query tile within the segment
+  int n_k[2];       // key tiles each query tile reads (0: the tile is absent)
+  int n_max;
+};
+
+// Items are numbered head fastest (the query heads of one key/value head run
+// together), then segment, then pair. With the pair slowest, the CTAs' strided
+// shares each hold every pair index in proportion: under the causal mask a
+// later pair costs more, and a CTA count that is a multiple of the pairs per
+// segment would otherwise hand each CTA pairs of one cost only.
+__device__ __forceinline__ Item item_at(const VarlenParams& p, int index, int pairs, int heads,
+                                        bool report) {
+  Item it;
+  it.h = index % heads;
+  const int seg = (index / heads) % p.segments;
+  const int pair = index / (heads * p.segments);
+  it.start = p.cu[seg];
+  it.len = p.cu[seg + 1] - it.start;
+  it.kvh = it.h / p.group;
+  it.active = false;
+  it.n_k[0] = it.n_k[1] = it.n_max = 0;
+  it.first_row[0] = it.first_row[1] = 0;
+  // A segment outside the tensor or longer than the launch covers is skipped
+  // (its output rows untouched) and reported once; nothing is read or written
+  // out of bounds.
+  if (it.start < 0 || it.len < 0 || it.start + it.len > p.tokens || it.len > p.max_length) {
+    if (report && pair == 0 && it.h == 0 && p.status) atomicOr(p.status, ASRBACK_STATUS_SEGMENT);
+    return it;
+  }
+  if (pair * 2 * kRows >= it.len) return it;  // the segment is shorter
+  it.active = true;
+  const int n_seg = (it.len + kKeys - 1) / kKeys;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    it.first_row[t] = (2 * pair + t) * kRows;
+    it.n_k[t] = it.first_row[t] >= it.len
+                    ? 0
+                    : (p.causal ? min(n_seg, it.first_row[t] / kKeys + 1) : n_seg);
+  }
+  it.n_max = max(it.n_k[0], it.n_k[1]);
+  return it;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     varlen_attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -81,50 +138,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                                const __grid_constant__ CUtensorMap map_v,
                                const __grid_constant__ VarlenParams p) {
   using Sh = VarlenShape<D>;
-  const int pair = blockIdx.x, h = blockIdx.y, seg = blockIdx.z;
-  const int start = p.cu[seg];
-  const int len = p.cu[seg + 1] - start;
-  // A segment outside the tensor or longer than the launch covers is skipped
-  // (its output rows untouched) and reported; nothing is read or written
-  // out of bounds.
-  if (start < 0 || len < 0 || start + len > p.tokens || len > p.max_length) {
-    if (pair == 0 && h == 0 && threadIdx.x == 0 && p.status)
-      atomicOr(p.status, ASRBACK_STATUS_SEGMENT);
-    return;
-  }
-  if (pair * 2 * kRows >= len) return;  // the whole CTA: this segment is shorter
-  const int kvh = h / p.group;
-  const int n_seg = (len + kKeys - 1) / kKeys;
-  // Query tiles 2*pair and 2*pair+1 (the second absent past the segment's
-  // end), and the key tiles each reads. (Pairing tile p with tile n-1-p to
-  // even out causal work measured slower: it streams more key tiles.)
-  int first_row[2], n_k[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    first_row[t] = (2 * pair + t) * kRows;
-    n_k[t] = first_row[t] >= len ? 0 : (p.causal ? min(n_seg, first_row[t] / kKeys + 1) : n_seg);
-  }
-  const int n_max = max(n_k[0], n_k[1]);
-
+  constexpr int S = Sh::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBar);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + Sh::kStages;
-  uint64_t* kv_empty = v_full + Sh::kStages;
-  uint64_t* s_full = kv_empty + Sh::kStages;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;
+  uint64_t* v_full = k_full + S;
+  uint64_t* kv_empty = v_full + S;
+  uint64_t* s_full = kv_empty + S;
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
+  uint64_t* o_free = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Sh::kOffTmemSlot);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint64_t deadline = global_timer_ns() + kWaitBudgetNs;
+  // Waits give up kWaitBudgetNs after the start of the item they belong to.
+  uint64_t deadline = global_timer_ns() + kWaitBudgetNs;
+  const int pairs = p.pairs, heads = p.heads;
+  const int items = p.segments * heads * pairs;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < Sh::kStages; ++s) {
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < S; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -133,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);  // one arrival per softmax warp
       mbar_init(&o_full[t], 1);
+      mbar_init(&o_free[t], 4);
     }
     fence_barrier_init();
   }
@@ -149,30 +189,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      const int q_tiles = n_k[1] > 0 ? 2 : 1;
-      mbar_arrive_expect_tx(q_full, q_tiles * Sh::kTileBytes);
-      for (int t = 0; t < q_tiles; ++t)
-#pragma unroll
-        for (int a = 0; a < Sh::kAtoms; ++a)
-          tma_load_3d(smem + Sh::kOffQ + t * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q, 64 * a,
-                      h, start + first_row[t], q_full);
-      for (int j = 0; j < n_max; ++j) {
-        const int s = j % Sh::kStages;
-        if (j >= Sh::kStages &&
-            !mbar_wait(&kv_empty[s], ((j / Sh::kStages) - 1) & 1, deadline)) {
+      int q_loads = 0;  // items whose Q this lane has loaded
+      int g = 0;        // K/V tiles loaded, over all items
+      for (int index = blockIdx.x; index < items && !timed_out; index += gridDim.x) {
+        const Item it = item_at(p, index, pairs, heads, true);
+        if (!it.active) continue;
+        deadline = global_timer_ns() + kWaitBudgetNs;
+        // Q of the previous item is in use until its last S is done.
+        if (q_loads > 0 && !mbar_wait(q_empty, (q_loads - 1) & 1, deadline)) {
           timed_out = true;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[s], Sh::kTileBytes);
+        const int q_tiles = it.n_k[1] > 0 ? 2 : 1;
+        mbar_arrive_expect_tx(q_full, q_tiles * Sh::kTileBytes);
+        for (int t = 0; t < q_tiles; ++t)
 #pragma unroll
-        for (int a = 0; a < Sh::kAtoms; ++a)
-          tma_load_3d(smem + Sh::kOffK + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_k, 64 * a,
-                      kvh, start + j * kKeys, &k_full[s]);
-        mbar_arrive_expect_tx(&v_full[s], Sh::kTileBytes);
+          for (int a = 0; a < Sh::kAtoms; ++a)
+            tma_load_3d(smem + Sh::kOffQ + t * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q,
+                        64 * a, it.h, it.start + it.first_row[t], q_full);
+        ++q_loads;
+        for (int j = 0; j < it.n_max; ++j, ++g) {
+          const int s = g % S;
+          if (g >= S && !mbar_wait(&kv_empty[s], ((g / S) - 1) & 1, deadline)) {
+            timed_out = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[s], Sh::kTileBytes);
 #pragma unroll
-        for (int a = 0; a < Sh::kAtoms; ++a)
-          tma_load_3d(smem + Sh::kOffV + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_v, 64 * a,
-                      kvh, start + j * kKeys, &v_full[s]);
+          for (int a = 0; a < Sh::kAtoms; ++a)
+            tma_load_3d(smem + Sh::kOffK + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_k,
+                        64 * a, it.kvh, it.start + j * kKeys, &k_full[s]);
+          mbar_arrive_expect_tx(&v_full[s], Sh::kTileBytes);
+#pragma unroll
+          for (int a = 0; a < Sh::kAtoms; ++a)
+            tma_load_3d(smem + Sh::kOffV + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_v,
+                        64 * a, it.kvh, it.start + j * kKeys, &v_full[s]);
+        }
       }
     }
   } else if (warp == 1) {
@@ -207,34 +259,53 @@ __global__ void __launch_bounds__(kThreads, 1)
                    v_desc + s * kTile + a * kAtom + k * (2048 >> 4), kIdescPV,
                    accumulate || k > 0);
       };
-      bool ok = mbar_wait(q_full, 0, deadline);
-      // Step j: for each query tile still reading keys, P_t(j-1) V(j-1) once
-      // its softmax has written P_t(j-1), then S_t(j) over the same columns
-      // (or, after its last key tile, the commit that O_t is final).
-      for (int j = 0; j <= n_max && ok; ++j) {
-        if (j < n_max) ok = mbar_wait(&k_full[j % Sh::kStages], (j / Sh::kStages) & 1, deadline);
-        if (ok && j > 0)
-          ok = mbar_wait(&v_full[(j - 1) % Sh::kStages], ((j - 1) / Sh::kStages) & 1, deadline);
-        if (!ok) break;
-        tc_fence_after();
+      bool ok = true;
+      int q_items = 0;                // items whose Q this lane has used
+      int base = 0;                   // global index of the item's first K/V tile
+      int p_seen[2] = {0, 0};         // p_full completions consumed, per query tile
+      int o_done[2] = {0, 0};         // items whose O_t is final (o_full commits)
+      for (int index = blockIdx.x; index < items && ok; index += gridDim.x) {
+        const Item it = item_at(p, index, pairs, heads, false);
+        if (!it.active) continue;
+        deadline = global_timer_ns() + kWaitBudgetNs;
+        ok = mbar_wait(q_full, q_items & 1, deadline);
+        ++q_items;
+        // Step j: for each query tile still reading keys, P_t(j-1) V(j-1) once
+        // its softmax has written P_t(j-1) (the first of an item also once
+        // the previous item's epilogue has read O_t), then S_t(j) over the
+        // same columns (or, after its last key tile, the commit that O_t is
+        // final). After the item's last S its Q buffer is released.
+        for (int j = 0; j <= it.n_max && ok; ++j) {
+          const int g = base + j;
+          if (j < it.n_max) ok = mbar_wait(&k_full[g % S], (g / S) & 1, deadline);
+          if (ok && j > 0) ok = mbar_wait(&v_full[(g - 1) % S], ((g - 1) / S) & 1, deadline);
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (n_k[t] == 0 || j > n_k[t]) continue;
-          if (j > 0) {
-            ok = mbar_wait(&p_full[t], (j - 1) & 1, deadline);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv(t, (j - 1) % Sh::kStages, j > 1);
+          for (int t = 0; t < 2; ++t) {
+            if (it.n_k[t] == 0 || j > it.n_k[t]) continue;
+            if (j > 0) {
+              ok = mbar_wait(&p_full[t], p_seen[t] & 1, deadline);
+              ++p_seen[t];
+              if (ok && j == 1 && o_done[t] > 0)
+                ok = mbar_wait(&o_free[t], (o_done[t] - 1) & 1, deadline);
+              if (!ok) break;
+              tc_fence_after();
+              issue_pv(t, (g - 1) % S, j > 1);
+            }
+            if (j < it.n_k[t]) {
+              issue_qk(t, g % S);
+              mma_commit(&s_full[t]);
+            } else {
+              mma_commit(&o_full[t]);
+              ++o_done[t];
+            }
           }
-          if (j < n_k[t]) {
-            issue_qk(t, j % Sh::kStages);
-            mma_commit(&s_full[t]);
-          } else {
-            mma_commit(&o_full[t]);
-          }
+          if (!ok) break;
+          if (j == it.n_max - 1) mma_commit(q_empty);
+          if (j > 0) mma_commit(&kv_empty[(g - 1) % S]);
         }
-        if (ok && j > 0 && (j - 1) + Sh::kStages < n_max)
-          mma_commit(&kv_empty[(j - 1) % Sh::kStages]);
+        base += it.n_max;
       }
       timed_out = !ok;
     }
@@ -242,105 +313,115 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- softmax (one query row per thread) ----------------
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
-    const int row = first_row[t] + quarter * 32 + lane;  // within the segment
     const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_bits + col_s(t);
     const uint32_t tO = tmem + lane_bits + col_o(t);
-    // Keys this row may read: its segment, and (causal) up to itself.
-    const int limit = p.causal ? min(len, row + 1) : len;
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_k[t] && ok; ++j) {
-      ok = mbar_wait(&s_full[t], j & 1, deadline);
+    int s_seen = 0, o_seen = 0;  // s_full / o_full completions consumed
+    for (int index = blockIdx.x; index < items && ok; index += gridDim.x) {
+      const Item it = item_at(p, index, pairs, heads, false);
+      if (!it.active || it.n_k[t] == 0) continue;
+      deadline = global_timer_ns() + kWaitBudgetNs;
+      const int row = it.first_row[t] + quarter * 32 + lane;  // within the segment
+      // Keys this row may read: its segment, and (causal) up to itself.
+      const int limit = p.causal ? min(it.len, row + 1) : it.len;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.n_k[t] && ok; ++j) {
+        ok = mbar_wait(&s_full[t], s_seen & 1, deadline);
+        ++s_seen;
+        if (!ok) break;
+        tc_fence_after();
+        const int valid = limit - j * kKeys;
+        float v[kKeys];
+        tmem_ld128(tS, v);
+        if (valid < kKeys) {
+#pragma unroll
+          for (int i = 0; i < kKeys; ++i)
+            if (i >= valid) v[i] = -INFINITY;
+        }
+        float acc[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
+#pragma unroll
+        for (int i = 16; i < kKeys; i += 16)
+#pragma unroll
+          for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
+        const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
+                               fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
+        const float m_tile = mx * p.scale_log2;
+        if (m_tile > m_used + kRescaleThreshold) {
+          if (j > 0) {
+            // O_t is idle: P_t(j-1) V was issued before S_t(j), which is done.
+            const float alpha = fast_exp2(m_used - m_tile);
+#pragma unroll
+            for (int c = 0; c < D / 16; ++c) {
+              float o[16];
+              tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] *= alpha;
+              tmem_st16f(tO + 16 * c, o);
+            }
+            l *= alpha;
+          }
+          m_used = m_tile;
+        }
+        const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
+        const uint64_t neg_m2 = pack2(-m_used, -m_used);
+        uint64_t sum2[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t packed[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = 64 * half + 2 * i;
+            float x0, x1;
+            unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
+            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+            sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
+            packed[i] = bf16x2(p0, p1);
+          }
+          tmem_st32u(tS + 32 * half, packed);
+        }
+        float lo0, hi0;
+        unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
+        l += lo0 + hi0;
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (!ok) break;
+      ok = mbar_wait(&o_full[t], o_seen & 1, deadline);
+      ++o_seen;
       if (!ok) break;
       tc_fence_after();
-      const int valid = limit - j * kKeys;
-      float v[kKeys];
-      tmem_ld128(tS, v);
-      if (valid < kKeys) {
+      const float inv = 1.f / l;
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
+                           static_cast<int64_t>(it.start + row) * p.os_tok + it.h * p.os_head;
 #pragma unroll
-        for (int i = 0; i < kKeys; ++i)
-          if (i >= valid) v[i] = -INFINITY;
-      }
-      float acc[8];
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        tmem_ld32(tO + 32 * c, o);
+        if (row < it.len) {
 #pragma unroll
-      for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
-#pragma unroll
-      for (int i = 16; i < kKeys; i += 16)
-#pragma unroll
-        for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
-      const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
-                             fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
-      const float m_tile = mx * p.scale_log2;
-      if (m_tile > m_used + kRescaleThreshold) {
-        if (j > 0) {
-          // O_t is idle: P_t(j-1) V was issued before S_t(j), which is done.
-          const float alpha = fast_exp2(m_used - m_tile);
-#pragma unroll
-          for (int c = 0; c < D / 16; ++c) {
-            float o[16];
-            tmem_ld16(tO + 16 * c, o);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] *= alpha;
-            tmem_st16f(tO + 16 * c, o);
+          for (int i = 0; i < 32; i += 8) {
+            uint4 u;
+            u.x = bf16x2(o[i] * inv, o[i + 1] * inv);
+            u.y = bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+            u.z = bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+            u.w = bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+            *reinterpret_cast<uint4*>(out + 32 * c + i) = u;
           }
-          l *= alpha;
         }
-        m_used = m_tile;
       }
-      const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
-      const uint64_t neg_m2 = pack2(-m_used, -m_used);
-      uint64_t sum2[4];
-#pragma unroll
-      for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t packed[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = 64 * half + 2 * i;
-          float x0, x1;
-          unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
-          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-          sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
-          packed[i] = bf16x2(p0, p1);
-        }
-        tmem_st32u(tS + 32 * half, packed);
-      }
-      float lo0, hi0;
-      unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
-      l += lo0 + hi0;
-      tmem_wait_st();
+      // O_t has been read: the next item's first P V may overwrite it.
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0) mbar_arrive(&o_free[t]);
     }
-    if (n_k[t] > 0) {
-      if (ok) ok = mbar_wait(&o_full[t], 0, deadline);
-      timed_out = !ok;
-      if (ok) {
-        tc_fence_after();
-        const float inv = 1.f / l;
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
-                             static_cast<int64_t>(start + row) * p.os_tok + h * p.os_head;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float o[32];
-          tmem_ld32(tO + 32 * c, o);
-          if (row < len) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 u;
-              u.x = bf16x2(o[i] * inv, o[i + 1] * inv);
-              u.y = bf16x2(o[i + 2] * inv, o[i + 3] * inv);
-              u.z = bf16x2(o[i + 4] * inv, o[i + 5] * inv);
-              u.w = bf16x2(o[i + 6] * inv, o[i + 7] * inv);
-              *reinterpret_cast<uint4*>(out + 32 * c + i) = u;
-            }
-          }
-        }
-      }
-    }
+    timed_out = !ok;
   }
   if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
   tc_fence_before();
@@ -389,8 +470,10 @@ int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
       return rc;
     prepared_device = device;
   }
-  dim3 grid((max_length + 2 * kRows - 1) / (2 * kRows), heads, segments);
-  kernel<<<grid, kThreads, Sh::kSmemBytes, stream>>>(mq, mk, mv, p);
+  // Persistent: one CTA per SM (512 TMEM columns each), at most one per item.
+  const long long items = (long long)p.segments * p.heads * p.pairs;
+  const int ctas = static_cast<int>(std::min<long long>(items, sm_count()));
+  kernel<<<ctas, kThreads, Sh::kSmemBytes, stream>>>(mq, mk, mv, p);
   return check_cuda(cudaGetLastError(), "varlen attention (tensor core) launch");
 }
 
@@ -408,8 +491,19 @@ int varlen_attention_tc(int tokens, int heads, int kv_heads, int head_dim, const
   if (int rc = make_map_3d(&mq, q, tokens, heads, head_dim, q_tok, q_head)) return rc;
   if (int rc = make_map_3d(&mk, k, tokens, kv_heads, head_dim, k_tok, k_head)) return rc;
   if (int rc = make_map_3d(&mv, v, tokens, kv_heads, head_dim, v_tok, v_head)) return rc;
-  VarlenParams p{out,   o_tok,          o_head,     cu, tokens, max_length, heads / kv_heads,
-                 causal ? 1 : 0, scale * 1.4426950408889634f, status};
+  VarlenParams p{out,
+                 o_tok,
+                 o_head,
+                 cu,
+                 segments,
+                 heads,
+                 (max_length + 2 * kRows - 1) / (2 * kRows),
+                 tokens,
+                 max_length,
+                 heads / kv_heads,
+                 causal ? 1 : 0,
+                 scale * 1.4426950408889634f,
+                 status};
   return head_dim == 128 ? launch<128>(mq, mk, mv, p, segments, heads, max_length, stream)
                          : launch<64>(mq, mk, mv, p, segments, heads, max_length, stream);
 }
