@@ -85,6 +85,42 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// As mbar_wait, with a budget of kWaitBudgetNs counted from the wait's own
+// first slow poll: a wait that is already satisfied, or soon is, reads no
+// timer (a %globaltimer read costs more than a satisfied try_wait).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t deadline = 0;
+  for (uint32_t spins = 1;; ++spins) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spins & 63u) == 0) {
+      const uint64_t now = global_timer_ns();
+      if (deadline == 0) {
+        deadline = now + kWaitBudgetNs;
+      } else if (now > deadline) {
+        return false;
+      }
+    }
+  }
+}
+
+// As mbar_wait_bounded, polling with the non-suspending test (a hand-off
+// between warps of one CTA, where a suspended waiter wakes late).
+__device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, uint32_t parity) {
+  uint64_t deadline = 0;
+  for (uint32_t spins = 1;; ++spins) {
+    if (mbar_test(bar, parity)) return true;
+    if ((spins & 255u) == 0) {
+      const uint64_t now = global_timer_ns();
+      if (deadline == 0) {
+        deadline = now + kWaitBudgetNs;
+      } else if (now > deadline) {
+        return false;
+      }
+    }
+  }
+}
+
 // As mbar_wait, polling with the non-suspending test (for hand-offs between
 // warps of one CTA, where a suspended waiter would add wake-up latency).
 __device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, uint64_t deadline) {

@@ -11,26 +11,38 @@
 //
 // Work item: one (segment, query head) and two adjacent 128-row query tiles
 // of the segment, which share every key/value tile they read. The kernel is
-// persistent: one CTA per SM takes items blockIdx.x, + gridDim.x, ...; its
-// TMA warp loads the next item's Q (once the current item's last S is done)
-// and K/V while the current item finishes, and the next item's first P V
-// waits only until the current item's epilogue has read O. Roles:
+// persistent: one CTA per SM takes items blockIdx.x, + gridDim.x, ... Roles:
 //   warp 0      TMA: both Q tiles, then K/V tiles of 128 keys of the query
 //               head's key/value head into a STAGES-deep ring. A tile is
 //               head_dim / 64 column blocks of 128 bytes (128-byte swizzle);
 //               rows past the segment belong to the next one and are masked,
-//               rows past the tensor read as zeros;
+//               rows past the tensor read as zeros. The next item's Q loads
+//               once the current item's last S is done;
 //   warp 1      allocates the 512 TMEM columns; one lane issues every MMA:
-//               S_t = Q_t K^T (SS) and O_t += P_t V (TS: P from TMEM);
-//   warps 4-11  softmax of query tile 0 and 1 (thread = TMEM lane = row).
+//               S = Q K^T (SS) and O += P V (TS: P from TMEM);
+//   warp 2      the item list: 32 lanes look up 32 of the CTA's items at a
+//               time (the segment bounds are global loads) and publish the
+//               valid ones, in order, into an 8-entry shared-memory ring
+//               that the other roles read;
+//   warps 4-11  softmax of query tile 0 and 1 (thread = TMEM lane = row), and
+//               the epilogue: O / l as bf16, staged per warp in shared memory
+//               so that each store instruction writes whole 128-byte rows.
 // TMEM of query tile t: S_t [256t, 256t+128), the softmax writing P_t (packed
 // bf16 pairs) over its first 64 columns, and O_t [256t+128, 256t+128+D).
 // Per key tile j the MMA lane issues P_t(j-1) V, then S_t(j) into the same
 // columns (the tensor core runs one thread's MMAs in order), so S_t(j)'s
 // completion also means O_t is idle: the lazy rescale (P uses a stale max
 // until a tile's max exceeds it by more than 8 in log2 units) needs no wait.
-// Causal: query row r reads keys 0..r of its segment, so a query tile stops
-// at the key tile of its own rows and only that diagonal tile is masked.
+// The next item's first P V waits until the current item's epilogue has read
+// O_t. Causal: query row r reads keys 0..r of its segment, so a query tile
+// stops at the key tile of its own rows and only that diagonal tile is masked.
+//
+// Single-tile mode (every segment at most 128 tokens, e.g. the audio windows):
+// an item is one (segment, query head), one query tile and one key tile. Item
+// k uses Q buffer, TMEM S/O columns and softmax warpgroup k & 1 (those of
+// query tile t = k & 1 above), and the MMA lane issues S(k + 1) before
+// P(k) V(k), so item k+1's S runs under item k's softmax and item k's
+// epilogue under item k+1's softmax.
 #include <algorithm>
 
 #include "tcgen05.cuh"
@@ -46,27 +58,40 @@ constexpr int kKeys = 128;  // keys per tile
 constexpr int kThreads = 12 * 32;
 constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;
+constexpr int kItemSlots = 8;        // entries of the shared-memory item ring
+constexpr int kItemReaders = 2 + 8;  // TMA lane, MMA lane, 8 softmax warps
+constexpr int kStageRowBytes = 128;  // epilogue staging: 64 bf16 columns per row
+constexpr int kStageWarpBytes = 32 * kStageRowBytes;
+
+// One work item: a (segment, query head, pair of adjacent 128-row query tiles).
+struct Item {
+  int start, len;    // the segment's first token and length
+  int h, kvh;        // query head, its key/value head
+  int first_row[2];  // first row of each query tile within the segment
+  int n_k[2];        // key tiles each query tile reads (0: the tile is absent)
+  int n_max;         // 0: no work (a skipped item, or the end of the list)
+};
 
 template <int D>
 struct VarlenShape {
-  static constexpr int kAtoms = D / 64;         // 128-byte column blocks per row
+  static constexpr int kAtoms = D / 64;           // 128-byte column blocks per row
   static constexpr int kAtomBytes = kRows * 128;  // one column block of a tile
   static constexpr int kTileBytes = kAtoms * kAtomBytes;
   static constexpr int kStages = D == 128 ? 2 : 4;
-  static constexpr int kOffQ = 0;
+  static constexpr int kOffQ = 0;  // two Q tiles
   static constexpr int kOffK = 2 * kTileBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
-  static constexpr int kOffBar = kOffV + kStages * kTileBytes;
-  // barriers: q_full, q_empty, k_full[S], v_full[S], kv_empty[S], s_full[2],
-  // p_full[2], o_full[2], o_free[2]
-  static constexpr int kNumBars = 2 + 3 * kStages + 8;
-  static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+  static constexpr int kOffStage = kOffV + kStages * kTileBytes;  // 8 warps x 32 rows
+  static constexpr int kOffBar = kOffStage + 8 * kStageWarpBytes;
+  // barriers: q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S],
+  // s_full[2], p_full[2], o_full[2], o_free[2], item_full[R], item_empty[R]
+  static constexpr int kNumBars = 2 + 2 + 3 * kStages + 2 + 2 + 2 + 2 + 2 * kItemSlots;
+  static constexpr int kOffItems = kOffBar + kNumBars * 8;
+  static constexpr int kOffTmemSlot = kOffItems + kItemSlots * static_cast<int>(sizeof(Item));
   static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
   static_assert(kSmemBytes <= 227 * 1024, "shared memory exceeds a CTA's 227 KB");
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
 };
-__host__ __device__ constexpr int col_s(int t) { return 256 * t; }
-__host__ __device__ constexpr int col_o(int t) { return 256 * t + 128; }
 
 struct VarlenParams {
   void* out;
@@ -83,42 +108,29 @@ struct VarlenParams {
   int32_t* status;
 };
 
-// One work item: a (segment, query head, pair of adjacent 128-row query tiles).
-struct Item {
-  bool active;      // the pair holds rows of a valid segment
-  int start, len;   // the segment's first token and length
-  int h, kvh;       // query head, its key/value head
-  int first_row[2]; // first row of each query tile within the segment
-  int n_k[2];       // key tiles each query tile reads (0: the tile is absent)
-  int n_max;
-};
-
 // Items are numbered head fastest (the query heads of one key/value head run
 // together), then segment, then pair. With the pair slowest, the CTAs' strided
 // shares each hold every pair index in proportion: under the causal mask a
 // later pair costs more, and a CTA count that is a multiple of the pairs per
 // segment would otherwise hand each CTA pairs of one cost only.
-__device__ __forceinline__ Item item_at(const VarlenParams& p, int index, int pairs, int heads,
-                                        bool report) {
+__device__ __forceinline__ Item item_at(const VarlenParams& p, int index) {
   Item it;
-  it.h = index % heads;
-  const int seg = (index / heads) % p.segments;
-  const int pair = index / (heads * p.segments);
+  it.h = index % p.heads;
+  const int seg = (index / p.heads) % p.segments;
+  const int pair = index / (p.heads * p.segments);
   it.start = p.cu[seg];
   it.len = p.cu[seg + 1] - it.start;
   it.kvh = it.h / p.group;
-  it.active = false;
   it.n_k[0] = it.n_k[1] = it.n_max = 0;
   it.first_row[0] = it.first_row[1] = 0;
   // A segment outside the tensor or longer than the launch covers is skipped
   // (its output rows untouched) and reported once; nothing is read or written
   // out of bounds.
   if (it.start < 0 || it.len < 0 || it.start + it.len > p.tokens || it.len > p.max_length) {
-    if (report && pair == 0 && it.h == 0 && p.status) atomicOr(p.status, ASRBACK_STATUS_SEGMENT);
+    if (pair == 0 && it.h == 0 && p.status) atomicOr(p.status, ASRBACK_STATUS_SEGMENT);
     return it;
   }
   if (pair * 2 * kRows >= it.len) return it;  // the segment is shorter
-  it.active = true;
   const int n_seg = (it.len + kKeys - 1) / kKeys;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
@@ -131,7 +143,7 @@ __device__ __forceinline__ Item item_at(const VarlenParams& p, int index, int pa
   return it;
 }
 
-template <int D>
+template <int D, bool kSingle>
 __global__ void __launch_bounds__(kThreads, 1)
     varlen_attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                const __grid_constant__ CUtensorMap map_k,
@@ -143,36 +155,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBar);
-  uint64_t* q_full = bars;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;
+  uint64_t* q_full = bars;  // [2]: per Q buffer (pair mode: [0] only)
+  uint64_t* q_empty = q_full + 2;
+  uint64_t* k_full = q_empty + 2;
   uint64_t* v_full = k_full + S;
   uint64_t* kv_empty = v_full + S;
-  uint64_t* s_full = kv_empty + S;
+  uint64_t* s_full = kv_empty + S;  // [2]: per query tile (single-tile mode: per item parity)
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
   uint64_t* o_free = o_full + 2;
+  uint64_t* item_full = o_free + 2;
+  uint64_t* item_empty = item_full + kItemSlots;
+  Item* ring = reinterpret_cast<Item*>(smem + Sh::kOffItems);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Sh::kOffTmemSlot);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Waits give up kWaitBudgetNs after the start of the item they belong to.
-  uint64_t deadline = global_timer_ns() + kWaitBudgetNs;
-  const int pairs = p.pairs, heads = p.heads;
-  const int items = p.segments * heads * pairs;
+  // TMEM columns of query tile t's S and O.
+  auto s_col = [](int t) { return 256 * t; };
+  auto o_col = [](int t) { return 256 * t + 128; };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&q_full[t], 1);
+      mbar_init(&q_empty[t], 1);
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
+      mbar_init(&o_full[t], 1);
+      mbar_init(&o_free[t], 4);
+    }
     for (int s = 0; s < S; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
-      mbar_init(&o_full[t], 1);
-      mbar_init(&o_free[t], 4);
+    for (int e = 0; e < kItemSlots; ++e) {
+      mbar_init(&item_full[e], 1);
+      mbar_init(&item_empty[e], kItemReaders);
     }
     fence_barrier_init();
   }
@@ -183,47 +201,80 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool timed_out = false;
 
+  // Entry n of the CTA's item list, for a role run by one lane (`warp_wide`
+  // false) or a whole warp; false if the wait ran out. Every reader releases
+  // every entry, the end-of-list entry (n_max 0) included.
+  auto read_item = [&](int n, Item& it, bool warp_wide) {
+    const int e = n % kItemSlots;
+    if (!mbar_wait_bounded(&item_full[e], (n / kItemSlots) & 1)) return false;
+    it = ring[e];
+    if (warp_wide) __syncwarp();
+    if (!warp_wide || lane == 0) mbar_arrive(&item_empty[e]);
+    return true;
+  };
+
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      int q_loads = 0;  // items whose Q this lane has loaded
-      int g = 0;        // K/V tiles loaded, over all items
-      for (int index = blockIdx.x; index < items && !timed_out; index += gridDim.x) {
-        const Item it = item_at(p, index, pairs, heads, true);
-        if (!it.active) continue;
-        deadline = global_timer_ns() + kWaitBudgetNs;
-        // Q of the previous item is in use until its last S is done.
-        if (q_loads > 0 && !mbar_wait(q_empty, (q_loads - 1) & 1, deadline)) {
+      int g = 0;  // K/V tiles loaded, over all items
+      auto load_kv = [&](const Item& it, int j) {
+        const int s = g % S;
+        if (g >= S && !mbar_wait_bounded(&kv_empty[s], ((g / S) - 1) & 1)) return false;
+        mbar_arrive_expect_tx(&k_full[s], Sh::kTileBytes);
+#pragma unroll
+        for (int a = 0; a < Sh::kAtoms; ++a)
+          tma_load_3d(smem + Sh::kOffK + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_k,
+                      64 * a, it.kvh, it.start + j * kKeys, &k_full[s]);
+        mbar_arrive_expect_tx(&v_full[s], Sh::kTileBytes);
+#pragma unroll
+        for (int a = 0; a < Sh::kAtoms; ++a)
+          tma_load_3d(smem + Sh::kOffV + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_v,
+                      64 * a, it.kvh, it.start + j * kKeys, &v_full[s]);
+        ++g;
+        return true;
+      };
+      for (int n = 0;; ++n) {
+        Item it;
+        if (!read_item(n, it, false)) {
           timed_out = true;
           break;
         }
-        const int q_tiles = it.n_k[1] > 0 ? 2 : 1;
-        mbar_arrive_expect_tx(q_full, q_tiles * Sh::kTileBytes);
-        for (int t = 0; t < q_tiles; ++t)
-#pragma unroll
-          for (int a = 0; a < Sh::kAtoms; ++a)
-            tma_load_3d(smem + Sh::kOffQ + t * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q,
-                        64 * a, it.h, it.start + it.first_row[t], q_full);
-        ++q_loads;
-        for (int j = 0; j < it.n_max; ++j, ++g) {
-          const int s = g % S;
-          if (g >= S && !mbar_wait(&kv_empty[s], ((g / S) - 1) & 1, deadline)) {
+        if (it.n_max == 0) break;
+        if constexpr (kSingle) {
+          // Item n: Q into buffer n & 1 once item n-2's S is done, then its
+          // one key/value tile.
+          const int b = n & 1;
+          if (n >= 2 && !mbar_wait_bounded(&q_empty[b], ((n >> 1) - 1) & 1)) {
             timed_out = true;
             break;
           }
-          mbar_arrive_expect_tx(&k_full[s], Sh::kTileBytes);
+          mbar_arrive_expect_tx(&q_full[b], Sh::kTileBytes);
 #pragma unroll
           for (int a = 0; a < Sh::kAtoms; ++a)
-            tma_load_3d(smem + Sh::kOffK + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_k,
-                        64 * a, it.kvh, it.start + j * kKeys, &k_full[s]);
-          mbar_arrive_expect_tx(&v_full[s], Sh::kTileBytes);
+            tma_load_3d(smem + Sh::kOffQ + b * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q,
+                        64 * a, it.h, it.start, &q_full[b]);
+          if (!load_kv(it, 0)) {
+            timed_out = true;
+            break;
+          }
+        } else {
+          // Q of the previous item is in use until its last S is done.
+          if (n > 0 && !mbar_wait_bounded(q_empty, (n - 1) & 1)) {
+            timed_out = true;
+            break;
+          }
+          const int q_tiles = it.n_k[1] > 0 ? 2 : 1;
+          mbar_arrive_expect_tx(q_full, q_tiles * Sh::kTileBytes);
+          for (int t = 0; t < q_tiles; ++t)
 #pragma unroll
-          for (int a = 0; a < Sh::kAtoms; ++a)
-            tma_load_3d(smem + Sh::kOffV + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_v,
-                        64 * a, it.kvh, it.start + j * kKeys, &v_full[s]);
+            for (int a = 0; a < Sh::kAtoms; ++a)
+              tma_load_3d(smem + Sh::kOffQ + t * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q,
+                          64 * a, it.h, it.start + it.first_row[t], q_full);
+          for (int j = 0; j < it.n_max && !timed_out; ++j) timed_out = !load_kv(it, j);
+          if (timed_out) break;
         }
       }
     }
@@ -239,15 +290,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t k_desc = sw128_desc(smem_addr(smem + Sh::kOffK), 16, 1024);
       const uint64_t v_desc = sw128_desc(smem_addr(smem + Sh::kOffV), Sh::kAtomBytes, 1024);
       constexpr uint64_t kTile = Sh::kTileBytes >> 4, kAtom = Sh::kAtomBytes >> 4;
+      // S_t = Q buffer t . K tile of ring slot s.
       auto issue_qk = [&](int t, int s) {
         // K = head_dim in steps of 16: four per 128-byte block.
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint64_t off = (k / 4) * kAtom + (k % 4) * (32 >> 4);
-          mma_ss(tmem + col_s(t), q_desc + t * kTile + off, k_desc + s * kTile + off, kIdescQK,
+          mma_ss(tmem + s_col(t), q_desc + t * kTile + off, k_desc + s * kTile + off, kIdescQK,
                  k > 0);
         }
       };
+      // O_t (+)= P_t . V tile of ring slot s.
       auto issue_pv = [&](int t, int s, bool accumulate) {
         // N = head_dim as 64-column blocks of V; K = 128 keys in steps of 16:
         // P advances 8 TMEM columns (bf16 pairs), V 16 rows (2048 bytes).
@@ -255,79 +308,208 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int a = 0; a < Sh::kAtoms; ++a)
 #pragma unroll
           for (int k = 0; k < kKeys / 16; ++k)
-            mma_ts(tmem + col_o(t) + 64 * a, tmem + col_s(t) + k * 8,
+            mma_ts(tmem + o_col(t) + 64 * a, tmem + s_col(t) + k * 8,
                    v_desc + s * kTile + a * kAtom + k * (2048 >> 4), kIdescPV,
                    accumulate || k > 0);
       };
       bool ok = true;
-      int q_items = 0;                // items whose Q this lane has used
-      int base = 0;                   // global index of the item's first K/V tile
-      int p_seen[2] = {0, 0};         // p_full completions consumed, per query tile
-      int o_done[2] = {0, 0};         // items whose O_t is final (o_full commits)
-      for (int index = blockIdx.x; index < items && ok; index += gridDim.x) {
-        const Item it = item_at(p, index, pairs, heads, false);
-        if (!it.active) continue;
-        deadline = global_timer_ns() + kWaitBudgetNs;
-        ok = mbar_wait(q_full, q_items & 1, deadline);
-        ++q_items;
-        // Step j: for each query tile still reading keys, P_t(j-1) V(j-1) once
-        // its softmax has written P_t(j-1) (the first of an item also once
-        // the previous item's epilogue has read O_t), then S_t(j) over the
-        // same columns (or, after its last key tile, the commit that O_t is
-        // final). After the item's last S its Q buffer is released.
-        for (int j = 0; j <= it.n_max && ok; ++j) {
-          const int g = base + j;
-          if (j < it.n_max) ok = mbar_wait(&k_full[g % S], (g / S) & 1, deadline);
-          if (ok && j > 0) ok = mbar_wait(&v_full[(g - 1) % S], ((g - 1) / S) & 1, deadline);
+      if constexpr (kSingle) {
+        // Before P(k) V(k), S is issued for items up to k + 1: S(m)
+        // overwrites P(m - 2), whose P V is already issued. P V(k) overwrites
+        // O_{k & 1} once item k-2's epilogue has read it.
+        int k_s = 0;  // items whose S is issued
+        bool more = true;
+        for (int k = 0; ok; ++k) {
+          while (more && k_s < k + 2) {
+            Item it;
+            ok = read_item(k_s, it, false);
+            if (!ok) break;
+            if (it.n_max == 0) {
+              more = false;
+              break;
+            }
+            const int t = k_s & 1;
+            ok = mbar_wait_bounded(&q_full[t], (k_s >> 1) & 1) &&
+                 mbar_wait_bounded(&k_full[k_s % S], (k_s / S) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            issue_qk(t, k_s % S);
+            mma_commit(&s_full[t]);
+            mma_commit(&q_empty[t]);
+            ++k_s;
+          }
+          if (!ok || k >= k_s) break;
+          const int t = k & 1;
+          ok = mbar_wait_bounded(&p_full[t], (k >> 1) & 1);
+          if (ok && k >= 2) ok = mbar_wait_bounded(&o_free[t], ((k >> 1) - 1) & 1);
+          if (ok) ok = mbar_wait_bounded(&v_full[k % S], (k / S) & 1);
           if (!ok) break;
           tc_fence_after();
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (it.n_k[t] == 0 || j > it.n_k[t]) continue;
-            if (j > 0) {
-              ok = mbar_wait(&p_full[t], p_seen[t] & 1, deadline);
-              ++p_seen[t];
-              if (ok && j == 1 && o_done[t] > 0)
-                ok = mbar_wait(&o_free[t], (o_done[t] - 1) & 1, deadline);
-              if (!ok) break;
-              tc_fence_after();
-              issue_pv(t, (g - 1) % S, j > 1);
-            }
-            if (j < it.n_k[t]) {
-              issue_qk(t, g % S);
-              mma_commit(&s_full[t]);
-            } else {
-              mma_commit(&o_full[t]);
-              ++o_done[t];
-            }
-          }
-          if (!ok) break;
-          if (j == it.n_max - 1) mma_commit(q_empty);
-          if (j > 0) mma_commit(&kv_empty[(g - 1) % S]);
+          issue_pv(t, k % S, false);
+          mma_commit(&o_full[t]);
+          mma_commit(&kv_empty[k % S]);
         }
-        base += it.n_max;
+      } else {
+        int base = 0;            // global index of the item's first K/V tile
+        int p_seen[2] = {0, 0};  // p_full completions consumed, per query tile
+        int o_done[2] = {0, 0};  // items whose O_t is final (o_full commits)
+        for (int n = 0; ok; ++n) {
+          Item it;
+          ok = read_item(n, it, false);
+          if (!ok || it.n_max == 0) break;
+          ok = mbar_wait_bounded(q_full, n & 1);
+          // Step j: for each query tile still reading keys, P_t(j-1) V(j-1)
+          // once its softmax has written P_t(j-1) (the first of an item also
+          // once the previous item's epilogue has read O_t), then S_t(j) over
+          // the same columns (or, after its last key tile, the commit that
+          // O_t is final). After the item's last S its Q buffer is released.
+          for (int j = 0; j <= it.n_max && ok; ++j) {
+            const int g = base + j;
+            if (j < it.n_max) ok = mbar_wait_bounded(&k_full[g % S], (g / S) & 1);
+            if (ok && j > 0) ok = mbar_wait_bounded(&v_full[(g - 1) % S], ((g - 1) / S) & 1);
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              if (it.n_k[t] == 0 || j > it.n_k[t]) continue;
+              if (j > 0) {
+                ok = mbar_wait_bounded(&p_full[t], p_seen[t] & 1);
+                ++p_seen[t];
+                if (ok && j == 1 && o_done[t] > 0)
+                  ok = mbar_wait_bounded(&o_free[t], (o_done[t] - 1) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(t, (g - 1) % S, j > 1);
+              }
+              if (j < it.n_k[t]) {
+                issue_qk(t, g % S);
+                mma_commit(&s_full[t]);
+              } else {
+                mma_commit(&o_full[t]);
+                ++o_done[t];
+              }
+            }
+            if (!ok) break;
+            if (j == it.n_max - 1) mma_commit(q_empty);
+            if (j > 0) mma_commit(&kv_empty[(g - 1) % S]);
+          }
+          base += it.n_max;
+        }
       }
       timed_out = !ok;
     }
+  } else if (warp == 2) {
+    // ---------------- item list ----------------
+    // Lane i looks up item base + i * gridDim.x; the valid ones are published
+    // in order, at most kItemSlots per round so that no lane waits on an
+    // entry another lane of this warp has yet to write.
+    const int items = p.segments * p.heads * p.pairs;
+    int n = 0;  // entries published
+    for (int base = blockIdx.x; base < items && !timed_out; base += 32 * gridDim.x) {
+      const int index = base + lane * gridDim.x;
+      Item it;
+      if (index < items) {
+        it = item_at(p, index);
+      } else {
+        it.n_max = 0;
+      }
+      const uint32_t valid = __ballot_sync(0xffffffffu, it.n_max > 0);
+      const int rank = __popc(valid & ((1u << lane) - 1u));
+      for (int round = 0; round < __popc(valid); round += kItemSlots) {
+        if (it.n_max > 0 && rank >= round && rank < round + kItemSlots) {
+          const int m = n + rank;
+          const int e = m % kItemSlots;
+          if (m >= kItemSlots && !mbar_wait_bounded(&item_empty[e], ((m / kItemSlots) - 1) & 1)) {
+            timed_out = true;
+          } else {
+            ring[e] = it;
+            mbar_arrive(&item_full[e]);
+          }
+        }
+        if (__any_sync(0xffffffffu, timed_out)) {
+          timed_out = true;
+          break;
+        }
+      }
+      n += __popc(valid);
+    }
+    // The end of the list.
+    if (!timed_out && lane == 0) {
+      const int e = n % kItemSlots;
+      if (n >= kItemSlots && !mbar_wait_bounded(&item_empty[e], ((n / kItemSlots) - 1) & 1)) {
+        timed_out = true;
+      } else {
+        ring[e].n_max = 0;
+        mbar_arrive(&item_full[e]);
+      }
+    }
   } else if (warp >= 4) {
-    // ---------------- softmax (one query row per thread) ----------------
+    // ---------------- softmax and epilogue (one query row per thread) ----------------
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_bits + col_s(t);
-    const uint32_t tO = tmem + lane_bits + col_o(t);
+    const uint32_t tS = tmem + lane_bits + s_col(t);
+    const uint32_t tO = tmem + lane_bits + o_col(t);
+    uint8_t* stage = smem + Sh::kOffStage + (warp - 4) * kStageWarpBytes;
     bool ok = true;
-    int s_seen = 0, o_seen = 0;  // s_full / o_full completions consumed
-    for (int index = blockIdx.x; index < items && ok; index += gridDim.x) {
-      const Item it = item_at(p, index, pairs, heads, false);
-      if (!it.active || it.n_k[t] == 0) continue;
-      deadline = global_timer_ns() + kWaitBudgetNs;
-      const int row = it.first_row[t] + quarter * 32 + lane;  // within the segment
+    int s_seen = 0, o_seen = 0;  // s_full[t] / o_full[t] completions consumed
+
+    // Output rows of this warp for the item whose O_t is final: O / l as bf16. Each lane writes its row into the staging rows
+    // (16-byte chunk c at position c ^ (row & 7), so that eight rows' chunks
+    // fall in distinct banks); then each store instruction writes four rows'
+    // 128 contiguous bytes.
+    auto epilogue = [&](int start, int len, int h, int first_row, float l) {
+      ok = mbar_spin_bounded(&o_full[t], o_seen & 1);
+      ++o_seen;
+      if (!ok) return;
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const int row0 = first_row + quarter * 32;  // the warp's first row in the segment
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
+                           static_cast<int64_t>(start + row0) * p.os_tok + h * p.os_head;
+#pragma unroll
+      for (int half = 0; half < D / 64; ++half) {
+        float o[64];
+        tmem_ld64(tO + 64 * half, o);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 u;
+          u.x = bf16x2(o[8 * c] * inv, o[8 * c + 1] * inv);
+          u.y = bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+          u.z = bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+          u.w = bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+          *reinterpret_cast<uint4*>(stage + lane * kStageRowBytes + ((c ^ (lane & 7)) << 4)) = u;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = 4 * i + (lane >> 3), c = lane & 7;
+          if (row0 + r < len) {
+            const uint4 u =
+                *reinterpret_cast<const uint4*>(stage + r * kStageRowBytes + ((c ^ (r & 7)) << 4));
+            *reinterpret_cast<uint4*>(out + r * p.os_tok + 64 * half + 8 * c) = u;
+          }
+        }
+        __syncwarp();
+      }
+      // O_t has been read: the next item's P V may overwrite it.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[t]);
+    };
+
+    for (int n = 0; ok; ++n) {
+      Item it;
+      ok = read_item(n, it, true);
+      if (!ok || it.n_max == 0) break;
+      if (kSingle ? ((n & 1) != t) : it.n_k[t] == 0) continue;
+      const int tile = kSingle ? 0 : t;
+      const int row = it.first_row[tile] + quarter * 32 + lane;  // within the segment
       // Keys this row may read: its segment, and (causal) up to itself.
       const int limit = p.causal ? min(it.len, row + 1) : it.len;
       float m_used = -INFINITY, l = 0.f;
-      for (int j = 0; j < it.n_k[t] && ok; ++j) {
-        ok = mbar_wait(&s_full[t], s_seen & 1, deadline);
+      for (int j = 0; j < it.n_k[tile] && ok; ++j) {
+        ok = mbar_spin_bounded(&s_full[t], s_seen & 1);
         ++s_seen;
         if (!ok) break;
         tc_fence_after();
@@ -393,33 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
-      ok = mbar_wait(&o_full[t], o_seen & 1, deadline);
-      ++o_seen;
-      if (!ok) break;
-      tc_fence_after();
-      const float inv = 1.f / l;
-      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
-                           static_cast<int64_t>(it.start + row) * p.os_tok + it.h * p.os_head;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        tmem_ld32(tO + 32 * c, o);
-        if (row < it.len) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 u;
-            u.x = bf16x2(o[i] * inv, o[i + 1] * inv);
-            u.y = bf16x2(o[i + 2] * inv, o[i + 3] * inv);
-            u.z = bf16x2(o[i + 4] * inv, o[i + 5] * inv);
-            u.w = bf16x2(o[i + 6] * inv, o[i + 7] * inv);
-            *reinterpret_cast<uint4*>(out + 32 * c + i) = u;
-          }
-        }
-      }
-      // O_t has been read: the next item's first P V may overwrite it.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[t]);
+      epilogue(it.start, it.len, it.h, it.first_row[tile], l);
     }
     timed_out = !ok;
   }
@@ -455,11 +611,11 @@ int make_map_3d(CUtensorMap* map, const void* base, int tokens, int heads, int h
   return ASRBACK_OK;
 }
 
-template <int D>
+template <int D, bool kSingle>
 int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-           const VarlenParams& p, int segments, int heads, int max_length, cudaStream_t stream) {
+           const VarlenParams& p, cudaStream_t stream) {
   using Sh = VarlenShape<D>;
-  auto kernel = varlen_attention_tc_kernel<D>;
+  auto kernel = varlen_attention_tc_kernel<D, kSingle>;
   static thread_local int prepared_device = -1;
   int device = 0;
   if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
@@ -504,8 +660,12 @@ int varlen_attention_tc(int tokens, int heads, int kv_heads, int head_dim, const
                  causal ? 1 : 0,
                  scale * 1.4426950408889634f,
                  status};
-  return head_dim == 128 ? launch<128>(mq, mk, mv, p, segments, heads, max_length, stream)
-                         : launch<64>(mq, mk, mv, p, segments, heads, max_length, stream);
+  // Segments of at most one query tile run two items per CTA at a time.
+  const bool single = max_length <= kRows;
+  if (head_dim == 128)
+    return single ? launch<128, true>(mq, mk, mv, p, stream)
+                  : launch<128, false>(mq, mk, mv, p, stream);
+  return single ? launch<64, true>(mq, mk, mv, p, stream) : launch<64, false>(mq, mk, mv, p, stream);
 }
 
 }  // namespace asrback

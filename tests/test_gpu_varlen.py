@@ -59,6 +59,10 @@ def _rand(gen, shape, dtype):
     ([104, 104, 104, 57, 1], 16, 16, 64, False),                       # audio windows
     ([600, 33], 4, 1, 128, False),
     ([300, 5, 700], 8, 2, 64, True),
+    # segments of at most one 128-row tile: two items per CTA in flight
+    ([128, 1, 77, 128, 100, 0, 3], 16, 8, 128, True),
+    ([104] * 60 + [57, 0, 1, 128, 90], 16, 16, 64, False),   # ~8 items per CTA
+    ([100, 0, 0, 128, 5] * 12, 8, 2, 128, True),
 ])
 def test_varlen_random(tag, lengths, heads, kv_heads, head_dim, causal):
     dtype = DTYPES[tag]
@@ -98,10 +102,12 @@ def test_varlen_strided_views_of_a_fused_projection(contiguous_k):
     np.testing.assert_allclose(host(out), want, atol=2e-2, rtol=0)
 
 
-def test_bad_segments_are_skipped_and_reported():
+@pytest.mark.parametrize("longest", [150, 100])
+def test_bad_segments_are_skipped_and_reported(longest):
     """A segment past the tensor, or longer than max_length, is not computed
     (its rows keep what the output held) and sets STATUS_SEGMENT; the other
-    segments are still right."""
+    segments are still right. `longest` 100 takes the one-tile-per-segment
+    schedule."""
     gen = torch.Generator().manual_seed(4)
     tokens = 300
     q = _rand(gen, (tokens, 4, 128), torch.bfloat16).to(DEV)
@@ -109,7 +115,7 @@ def test_bad_segments_are_skipped_and_reported():
     v = _rand(gen, (tokens, 2, 128), torch.bfloat16).to(DEV)
     for starts in ([0, 100, 400], [0, 100, 300]):
         cu = torch.tensor(starts, dtype=torch.int32, device=DEV)
-        longest = 150  # the second segment (200 tokens) is longer
+        # the second segment (200 tokens) is longer than `longest`
         out = attention.varlen_attention(q, k, v, cu, longest, True)
         want = oracle.varlen_attention(host(q)[:100], host(k)[:100], host(v)[:100], [0, 100], True)
         np.testing.assert_allclose(host(out)[:100], want, atol=2e-2, rtol=0)
