@@ -96,6 +96,20 @@ SIGNATURES: dict[str, tuple[list, object]] = {
          _c_f, _c_p, _c_p],
         _c_int,
     ),
+    "asrback_greedy_step_workspace_bytes": ([_c_int], _c_size),
+    "asrback_greedy_step": (
+        [_c_int, _c_int, _c_int, _c_int,
+         _c_p, _c_i64,
+         _c_p, _c_i64,
+         _c_p,
+         _c_p, _c_p,
+         _c_p, _c_i64, _c_p, _c_p,
+         _c_p, _c_p,
+         _c_p, _c_i64, _c_i64,
+         _c_p, _c_int,
+         _c_p, _c_size, _c_p, _c_p],
+        _c_int,
+    ),
     "asrback_selftest_bounded_wait": ([_c_i64, _c_p, _c_p], _c_int),
 }
 

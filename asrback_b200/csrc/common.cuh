@@ -138,6 +138,13 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return policy;
 }
 
+// L2 policy for data every CTA re-reads (a small operand): evict last.
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
 // Bulk copy (TMA engine, untiled) of `bytes` from global to this CTA's shared
 // memory, completing `bytes` of transaction count on `bar`. Both addresses
 // 16-byte aligned, `bytes` a multiple of 16.

@@ -24,7 +24,12 @@ Patched call sites (asrback project paths):
   ``TextAttention.prefill`` (causal prompt prefill, ``:374-390``) and
   ``AudioAttention.forward`` (non-causal audio windows, ``:214-219``) call:
   attention within the packed segments runs on the varlen kernel, whichever
-  path (``varlen_attn`` or padded SDPA) the segments were built for.
+  path (``varlen_attn`` or padded SDPA) the segments were built for;
+- ``whisper.Transcriber._step`` (``whisper.py:942-960``) and
+  ``qwen3_asr.Qwen3ASRTranscriber._step`` (``qwen3_asr.py:1180-1201``): after
+  the decoder, a greedy step (``temperatures`` None) runs the logits,
+  ``_choose`` and the state update as one kernel; a step that samples goes to
+  the original method.
 
 The patched methods run the kernels only: tensors on the CPU raise, as every
 op of this package does (there is no fallback).
@@ -36,7 +41,7 @@ import importlib
 
 import torch.nn.functional as F
 
-from . import attention
+from . import attention, step
 
 __all__ = ["install", "uninstall", "installed"]
 
@@ -116,6 +121,38 @@ def _qwen3_text_model_step(self, tokens, positions, cache, cos, sin, varlen):
     return self.norm(x)
 
 
+def _whisper_transcriber_step(original):
+    def _step(self, state, cache, temperatures=None):
+        if temperatures is not None:
+            return original(self, state, cache, temperatures)
+        hidden = self.model.decode(state.tokens, state.position, cache)
+        # `logits` (whisper.py:337-342) multiplies by the tied embedding.
+        step.greedy_step(hidden[:, -1], self.model.model.decoder.embed_tokens.weight,
+                         state.tokens, state.position, state.end, state.finished,
+                         state.sum_logprobs, state.generated, (self._eos,), self._suppress)
+
+    _step.__doc__ = original.__doc__
+    return _step
+
+
+def _qwen3_transcriber_step(original):
+    def _step(self, state, cache, temperatures=None):
+        if temperatures is not None:
+            return original(self, state, cache, temperatures)
+        hidden = self._text.step(state.tokens, state.position, cache, self._cos, self._sin,
+                                 self._varlen)
+        # The EOS ids live on the device; a host copy is taken on the first
+        # (eager, uncaptured) step and kept.
+        eos = self.__dict__.get("_asrback_eos_ids")
+        if eos is None:
+            eos = self._asrback_eos_ids = tuple(int(e) for e in self._eos_ids.reshape(-1).tolist())
+        step.greedy_step(hidden, self._lm_head.weight, state.tokens, state.position, state.end,
+                         state.finished, state.sum_logprobs, state.generated, eos)
+
+    _step.__doc__ = original.__doc__
+    return _step
+
+
 def install(whisper_module=None, qwen3_module=None) -> None:
     """Patches the reference's Whisper and Qwen3-ASR classes (importing
     ``asrback.models.whisper`` / ``asrback.models.qwen3_asr`` when no module is
@@ -129,10 +166,18 @@ def install(whisper_module=None, qwen3_module=None) -> None:
         original = _originals.get((layer, "forward"), layer.__dict__["forward"])
         _patch(layer, "forward", _whisper_decoder_layer_forward(original))
         _patch(whisper_module.MultiHeadAttention, "forward", _whisper_encoder_attention_forward)
+        if hasattr(whisper_module, "Transcriber"):
+            transcriber = whisper_module.Transcriber
+            original = _originals.get((transcriber, "_step"), transcriber.__dict__["_step"])
+            _patch(transcriber, "_step", _whisper_transcriber_step(original))
     if qwen3_module is not None:
         _patch(qwen3_module.TextAttention, "step", _qwen3_text_attention_step)
         _patch(qwen3_module.TextModel, "step", _qwen3_text_model_step)
         _patch(qwen3_module, "attend", _qwen3_attend)
+        if hasattr(qwen3_module, "Qwen3ASRTranscriber"):
+            transcriber = qwen3_module.Qwen3ASRTranscriber
+            original = _originals.get((transcriber, "_step"), transcriber.__dict__["_step"])
+            _patch(transcriber, "_step", _qwen3_transcriber_step(original))
 
 
 def _try_import(name: str):

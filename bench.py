@@ -18,7 +18,14 @@ Other workloads (``--workload``):
                    layers, 16 query / 8 key-value heads x 128, RoPE theta 1e6,
                    QK-RMSNorm, batch 64 rows whose caches hold the 410-position
                    prompt (390 audio + 20 text positions), then one position
-                   per step; unit: decoded tokens.
+                   per step; unit: decoded tokens;
+  qwen3-prefill    causal grouped-query attention within 64 packed 410-token
+                   prompts, 28 layers; unit: prompt tokens;
+  qwen3-audio      non-causal attention within 104-token audio-encoder
+                   windows, 64 requests of 390 tokens, 24 layers;
+  whisper-step,    the greedy step epilogue after the decoder (logits against
+  qwen3-step       the 51866 x 1280 tied embedding / the 151936 x 2048 lm_head,
+                   argmax, log-softmax, state update) for 64 rows; unit: tokens.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
                     [--workload NAME] [--batch B]
@@ -55,7 +62,8 @@ def parse_args():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--workload", choices=("whisper-decode", "whisper-encoder", "qwen3-decode",
-                                               "qwen3-prefill", "qwen3-audio"),
+                                               "qwen3-prefill", "qwen3-audio", "whisper-step",
+                                               "qwen3-step"),
                         default="whisper-decode")
     parser.add_argument("--batch", type=int, default=None,
                         help="override the workload's batch (small profiling cases)")
@@ -864,8 +872,166 @@ class Qwen3AudioWindows(Qwen3Prefill):
                           f"oracle, {elapsed:.1f} s, scaled by 1/24 layers"}
 
 
+class WhisperGreedyStep:
+    """The step epilogue after the decoder: logits against
+    the tied embedding, greedy `_choose` with the suppress mask and the state
+    update (whisper.py:949-975), BASELINE config 2 widths, 64 rows."""
+
+    name = "whisper-step"
+    family = "whisper"
+    metric = ("greedy step epilogue tokens/s/GPU (Whisper large-v3-turbo: logits 51866 x 1280 + "
+              "argmax/log-softmax + state update, 64 rows, bf16); weight-read GB/s")
+    unit = "tokens/s"
+    bound = "hbm"
+    reference_in_graph = True
+    vocab, width, length, eos = 51866, 1280, 448, (50257,)
+    copies = 4  # weight copies, rotated so that no launch finds its weights in L2
+    profile = "greedy_step_whisper_b64_bf16.md"
+
+    def __init__(self, batch: int | None):
+        self.batch = batch or 64
+        self.layers = self.copies
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": f"{self.family} greedy step epilogue (logits GEMM + _choose + state "
+                        "update; SURVEY 8(f) rank 4 row)",
+            "vocab": self.vocab, "hidden": self.width, "rows_per_gpu": self.batch,
+            "global_batch": self.batch * world, "suppress": self.family == "whisper",
+            "eos_ids": list(self.eos), "steps_per_replay": self.copies,
+            "step": f"{self.copies} greedy steps per graph replay, each over its own weight copy",
+            "inputs": "weight N(0, 0.02) bf16, hidden N(0, 1) bf16",
+            "parallelism": f"replicas x{world} (no collective)",
+            "l2": f"{self.copies} weight copies of {self.weight_bytes() / 1e6:.0f} MB rotate "
+                  "(larger than L2)",
+        }
+
+    def weight_bytes(self) -> int:
+        return self.vocab * self.width * 2
+
+    def bytes_per_launch(self) -> float:
+        # The weight once, the hidden rows, the suppress flags, the state.
+        return float(self.weight_bytes() + self.batch * self.width * 2
+                     + (self.vocab if self.family == "whisper" else 0) + self.batch * 40)
+
+    def units_per_step(self) -> int:
+        return self.batch * self.copies
+
+    def setup(self, torch, device, seed: int, total: int) -> None:
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.weights = [(torch.randn((self.vocab, self.width), generator=gen, device=device)
+                         * 0.02).to(torch.bfloat16) for _ in range(self.copies)]
+        self.hidden = [torch.randn((self.batch, self.width), generator=gen, device=device)
+                       .to(torch.bfloat16) for _ in range(self.copies)]
+        self.suppress = None
+        if self.family == "whisper":
+            self.suppress = torch.zeros(self.vocab, dtype=torch.bool, device=device)
+            self.suppress[50364:] = True  # timestamp tokens
+        b = self.batch
+        self.tokens = torch.zeros(b, dtype=torch.int64, device=device)
+        self.position = torch.randint(0, 100, (b,), generator=gen, device=device)
+        self.end = torch.full((b,), self.length - 1, dtype=torch.int64, device=device)
+        self.finished = torch.zeros(b, dtype=torch.bool, device=device)
+        self.sum_logprobs = torch.zeros(b, device=device)
+        self.generated = torch.zeros((b, self.length), dtype=torch.int64, device=device)
+        self.outputs = [self.tokens]
+
+    def attend(self, i: int) -> None:
+        from asrback_b200 import step
+
+        step.greedy_step(self.hidden[i], self.weights[i], self.tokens, self.position, self.end,
+                         self.finished, self.sum_logprobs, self.generated, self.eos,
+                         self.suppress)
+
+    def step(self) -> None:
+        for i in range(self.copies):
+            self.attend(i)
+
+    def launches_per_step(self) -> int:
+        return self.copies
+
+    def refresh(self, t: int) -> None:
+        pass
+
+    def host_step_inputs(self, torch, first: int, count: int):
+        pairs = []
+        for h in self.hidden:
+            host = torch.empty(h.shape, dtype=h.dtype, pin_memory=True)
+            host.copy_(h.cpu())
+            pairs.append((host[None].expand(count, *host.shape), h))
+        return pairs
+
+    def kernels(self, t: int):
+        return [("greedy_step", self.attend, self.bytes_per_launch())]
+
+    def step_work(self, first: int, count: int) -> float:
+        return self.bytes_per_launch() * self.copies * count
+
+    def torch_reference_step(self, torch):
+        """The reference's `_step` after `decode` on its GPU path (graph-captured
+        by the reference): logits, `_choose` without sampling, the state update
+        (whisper.py:949-975 / qwen3_asr.py:1189-1213), on the same tensors."""
+        import torch.nn.functional as F
+
+        eos = torch.tensor(self.eos, device=self.tokens.device)
+        tokens = self.tokens.clone()
+        position, finished = self.position.clone(), self.finished.clone()
+        sums, generated = self.sum_logprobs.clone(), self.generated.clone()
+
+        def run():
+            for i in range(self.copies):
+                logits = (self.weights[i] @ self.hidden[i].T).T.float()
+                if self.suppress is not None:
+                    logits.masked_fill_(self.suppress, -float("inf"))
+                token = logits.argmax(dim=-1)
+                logprob = F.log_softmax(logits, dim=-1).gather(1, token[:, None]).squeeze(1)
+                active = ~finished
+                pos = position + active
+                token = torch.where(active, token, tokens)
+                sums.add_(logprob.masked_fill(finished, 0.0))
+                generated.scatter_(1, pos[:, None], token[:, None])
+                finished.logical_or_(torch.isin(token, eos) | (pos >= self.end))
+                position.copy_(pos)
+                tokens.copy_(token)
+        return run
+
+    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+        from oracle import step as oracle_step
+
+        rng = np.random.default_rng(seed)
+        weight = (rng.standard_normal((self.vocab, self.width), dtype=np.float32) * 0.02)
+        hidden = rng.standard_normal((threads, 1, self.width), dtype=np.float32)
+        suppress = None
+        if self.family == "whisper":
+            suppress = np.zeros(self.vocab, bool)
+            suppress[50364:] = True
+
+        def one(_t, row):
+            oracle_step.choose(oracle_step.logits(weight, hidden[row], False, np.float32),
+                               suppress)
+
+        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
+        return {"value": threads * done / elapsed, "unit": self.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{threads * done} rows (logits over {self.vocab} x {self.width} + "
+                          f"_choose), float32 numpy oracle, {elapsed:.1f} s"}
+
+
+class Qwen3GreedyStep(WhisperGreedyStep):
+    """The Qwen3-ASR-1.7B step epilogue: `lm_head` (151936 x 2048), `_choose`,
+    the state update with two EOS ids (qwen3_asr.py:1189-1213), 64 rows."""
+
+    name = "qwen3-step"
+    family = "qwen3"
+    metric = ("greedy step epilogue tokens/s/GPU (Qwen3-ASR-1.7B-style: lm_head 151936 x 2048 + "
+              "argmax/log-softmax + state update, 64 rows, bf16); weight-read GB/s")
+    vocab, width, length, eos = 151936, 2048, 1024, (151643, 151645)
+    copies = 2
+    profile = "greedy_step_qwen3_b64_bf16.md"
+
+
 WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode, Qwen3Prefill,
-                                       Qwen3AudioWindows)}
+                                       Qwen3AudioWindows, WhisperGreedyStep, Qwen3GreedyStep)}
 
 
 # ------------------------------------------------------------------ arms ----
@@ -1077,7 +1243,8 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     if args.workload == "whisper-decode" and not args.no_extras and args.batch is None:
         # Short runs of the other workloads, for context.
         extras = {}
-        for name in ("whisper-encoder", "qwen3-decode", "qwen3-prefill", "qwen3-audio"):
+        for name in ("whisper-encoder", "qwen3-decode", "qwen3-prefill", "qwen3-audio",
+                     "whisper-step", "qwen3-step"):
             del work
             torch.cuda.empty_cache()
             work = WORKLOADS[name](None)

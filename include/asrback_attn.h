@@ -32,7 +32,12 @@
  *     src/asrback/models/qwen3_asr.py:152-181 (torch varlen_attn with equal
  *     query/key segments), called by TextAttention.prefill (qwen3_asr.py:
  *     374-390, causal) and AudioAttention.forward (qwen3_asr.py:214-219,
- *     non-causal windows).
+ *     non-causal windows);
+ *   - asrback_greedy_step replaces what a greedy step does after the decoder:
+ *     the logits (whisper.py:337-342, qwen3_asr.py:1189 lm_head), _choose
+ *     without sampling (whisper.py:962-975 with the suppress mask,
+ *     qwen3_asr.py:1203-1213) and the decode-state update of _step
+ *     (whisper.py:951-960, qwen3_asr.py:1190-1201).
  */
 #ifndef ASRBACK_ATTN_H_
 #define ASRBACK_ATTN_H_
@@ -221,6 +226,47 @@ ASRBACK_API int asrback_varlen_attention(
     const int32_t* cu_seqlens, int segments, int max_length, int causal,
     void* out, int64_t out_stride_token, int64_t out_stride_head,
     float scale, int32_t* status, void* stream);
+
+/*
+ * Workspace of asrback_greedy_step for up to `batch` rows: a ticket counter
+ * (zero before the first call; every call leaves it zero) and per-CTA
+ * partials. 16-byte aligned; reusable by consecutive calls on one stream.
+ */
+ASRBACK_API size_t asrback_greedy_step_workspace_bytes(int batch);
+
+/*
+ * One greedy step after the decoder, for `batch` rows:
+ *   logits[b][v] = hidden[b] . weight[v]  (bf16: fp32 sums rounded to bf16,
+ *                  as the reference's bf16 matmul returns them; f32: fp32);
+ *   suppressed tokens (suppress[v] != 0, or suppress null: none) get -inf;
+ *   token[b]   = first index of the row's maximum (torch argmax);
+ *   logprob[b] = log_softmax(logits[b])[token[b]] = -ln(sum_v exp(x - max)).
+ * hidden (batch, hidden_dim) rows at hidden_stride; weight (vocab, hidden_dim)
+ * rows at weight_stride (Whisper's tied embedding, Qwen3's lm_head.weight).
+ * out_token (int64) / out_logprob (float), if given, receive token / logprob.
+ * If `tokens` is given, the decode state is updated as _step does (int64
+ * tokens at tokens[b * tokens_stride], position, end; uint8 finished; float
+ * sum_logprobs; int64 generated (batch, generated_cols) at generated_stride):
+ *   a finished row keeps its token and position; an active row advances;
+ *   sum_logprobs[b] += logprob (active rows); generated[b][position] = token;
+ *   finished[b] |= token in eos_ids[0..n_eos) or position >= end[b].
+ * eos_ids is a HOST array (at most 8), copied into the launch.
+ * dtype ASRBACK_BF16: batch <= 128, hidden_dim and strides multiples of 8;
+ * ASRBACK_F32: batch <= 64, batch * hidden_dim * 4 <= 200 KB.
+ * A position outside [0, generated_cols) skips the write and sets
+ * ASRBACK_STATUS_POSITION.
+ */
+ASRBACK_API int asrback_greedy_step(
+    int dtype, int batch, int vocab, int hidden_dim,
+    const void* hidden, int64_t hidden_stride,
+    const void* weight, int64_t weight_stride,
+    const uint8_t* suppress,
+    int64_t* out_token, float* out_logprob,
+    int64_t* tokens, int64_t tokens_stride, int64_t* position, const int64_t* end,
+    uint8_t* finished, float* sum_logprobs,
+    int64_t* generated, int64_t generated_stride, int64_t generated_cols,
+    const int64_t* eos_ids, int n_eos,
+    void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
  * Self-test of the kernels' bounded waits: one CTA waits on an mbarrier that

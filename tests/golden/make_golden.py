@@ -317,10 +317,126 @@ def qwen3_small_decode(qwen3) -> None:
          argmax=np.stack(argmax_all, 1), hidden=np.stack(hidden_all, 1))
 
 
+def _run_steps(step, stub, state, hiddens, fields) -> dict:
+    """Runs the reference's ``_step(stub, state, None, None)`` once per hidden
+    state, recording ``_choose``'s token and log-probability and the state
+    fields after each step."""
+    queue = list(hiddens)
+    choose = stub._choose
+    chosen = []
+
+    def recording_choose(*args):
+        token, logprob = choose(*args)
+        chosen.append((token.clone(), logprob.clone()))
+        return token, logprob
+
+    stub._choose = recording_choose
+    stub.next_hidden = lambda *args, **kwargs: queue.pop(0)
+    after = {name: [] for name in fields}
+    with torch.no_grad():
+        for _ in hiddens:
+            step(stub, state, None, None)
+            for name in fields:
+                after[name].append(getattr(state, name).clone().reshape(len(state.position), -1)
+                                   .squeeze(1).numpy())
+    out = {f"after_{name}": np.stack(values) for name, values in after.items()}
+    out["token"] = np.stack([t.numpy() for t, _ in chosen])
+    out["logprob"] = np.stack([lp.float().numpy() for _, lp in chosen])
+    out["generated"] = state.generated.numpy()
+    return out
+
+
+def step_epilogue(whisper, qwen3, dtype: torch.dtype, tag: str) -> None:
+    """Greedy ``_step`` calls of the reference's Transcriber classes
+    (``whisper.py:942-960``, ``qwen3_asr.py:1180-1201``) on a stub engine whose
+    decoder returns given hidden states: the logits, ``_choose`` and the state
+    update are the reference's own. Weights come from ``seeded_parameters``
+    (the embedding / ``lm_head`` seeds are in ``meta``), so the tests rebuild
+    them without the reference."""
+    import types as _types
+
+    fields = ("tokens", "position", "finished", "sum_logprobs")
+    arrays = {}
+    # Whisper-tiny widths (config 1): tied embedding (51865, 384).
+    config = dict(d_model=384, encoder_attention_heads=6, decoder_attention_heads=6,
+                  encoder_layers=1, decoder_layers=1, encoder_ffn_dim=64, decoder_ffn_dim=64,
+                  num_mel_bins=80, max_source_positions=40, max_target_positions=448,
+                  vocab_size=51865)
+    model = whisper.WhisperForConditionalGeneration(config)
+    seeded_parameters(model.model.decoder, 7)
+    model = model.to(dtype)
+    batch, eos = 8, 50257
+    weight = model.model.decoder.embed_tokens.weight
+    suppress = torch.zeros(51865, dtype=torch.bool)
+    suppress[50364:] = True                      # every timestamp token
+    suppress[[1, 2, 7, 8, 9, 10, 14, 25, 26, 27, 28, 29, 31, 58, 59, 60, 61, 62, 63, 90, 91,
+              92, 93, 220, 359, 503, 522, 542, 873, 893, 902, 918, 922, 931, 1350, 1853, 1982,
+              2460, 2627, 3246, 3253, 3268, 3536, 3846, 3961, 4183, 4667, 6585, 6647, 7273,
+              9061, 9383, 10428, 10929, 11938, 12033, 12331, 12562, 13793, 14157, 14635, 15265,
+              15618, 16553, 16604, 18362, 18956, 20075, 21675, 22520, 26130, 26161, 26435,
+              28279, 29464, 31650, 32302, 32470, 36865, 42863, 47425, 49870, 50254, 50258,
+              50358, 50359, 50360, 50361, 50362]] = True
+    hiddens = [seeded_normal((batch, 1, 384), 600 + i).to(dtype) for i in range(3)]
+    # Row 3 is steered onto EOS at the first step.
+    hiddens[0][3, 0] = (weight[eos].float() * 40.0).to(dtype)
+    state = whisper._DecodeState.allocate(batch, 448, torch.device("cpu"))
+    state.tokens[:, 0] = torch.tensor([50258, 11, 400, 7000, 13, 50363, 0, 220])
+    state.position[:] = torch.tensor([3, 10, 50, 100, 200, 446, 0, 30])
+    state.end[:] = torch.tensor([447, 447, 447, 447, 447, 447, 0, 31])
+    state.finished[:] = torch.tensor([False] * 6 + [True, False])
+    state.sum_logprobs[:] = seeded_normal((batch,), 610).abs().neg()
+    state.generated[:, :4] = torch.tensor([50258, 50259, 50360, 50364])
+    for name in fields + ("end",):
+        arrays[f"whisper_{name}0"] = getattr(state, name).clone().reshape(batch, -1)[:, 0].numpy()
+    arrays["whisper_generated0"] = state.generated.numpy().copy()
+    stub = _types.SimpleNamespace(_suppress=suppress, _eos=eos)
+    stub.model = _types.SimpleNamespace(
+        decode=lambda tokens, position, cache: stub.next_hidden(), logits=model.logits)
+    stub._choose = _types.MethodType(whisper.Transcriber._choose, stub)
+    out = _run_steps(whisper.Transcriber._step, stub, state, hiddens, fields)
+    arrays.update({f"whisper_{key}": value for key, value in out.items()})
+    arrays["whisper_hidden"] = np.stack([f32(h[:, 0]) for h in hiddens])
+    arrays["whisper_suppress"] = suppress.numpy()
+
+    # Qwen3: lm_head (8192, 1024), several EOS ids, CACHE_LENGTH-wide generated.
+    vocab, width, batch, eos_ids = 8192, 1024, 6, [8000, 8001]
+    lm_head = torch.nn.Linear(width, vocab, bias=False)
+    seeded_parameters(lm_head, 8)
+    lm_head = lm_head.to(dtype)
+    hiddens = [seeded_normal((batch, width), 620 + i).to(dtype) for i in range(3)]
+    hiddens[1][1] = (lm_head.weight[8001].float() * 12.0).to(dtype)
+    state = qwen3._DecodeState.allocate(batch, torch.device("cpu"))
+    state.tokens[:] = torch.tensor([151, 9, 4000, 77, 1, 0])
+    state.position[:] = torch.tensor([19, 100, 409, 1022, 5, 0])
+    state.end[:] = torch.tensor([1023, 1023, 1023, 1023, 7, 0])
+    state.finished[:] = torch.tensor([False] * 5 + [True])
+    state.sum_logprobs[:] = seeded_normal((batch,), 630).abs().neg()
+    for name in fields + ("end",):
+        arrays[f"qwen3_{name}0"] = getattr(state, name).clone().numpy()
+    arrays["qwen3_generated0"] = state.generated.numpy().copy()
+    stub = _types.SimpleNamespace(_lm_head=lm_head, _eos_ids=torch.tensor(eos_ids), _cos=None,
+                                  _sin=None, _varlen=False)
+    stub._text = _types.SimpleNamespace(step=lambda *args: stub.next_hidden())
+    stub._choose = _types.MethodType(qwen3.Qwen3ASRTranscriber._choose, stub)
+    out = _run_steps(qwen3.Qwen3ASRTranscriber._step, stub, state, hiddens, fields)
+    arrays.update({f"qwen3_{key}": value for key, value in out.items()})
+    arrays["qwen3_hidden"] = np.stack([f32(h) for h in hiddens])
+    save(f"step_epilogue_{tag}",
+         dict(dtype=str(dtype), steps=3,
+              whisper=dict(vocab=51865, width=384, batch=8, eos=[eos], seed=7,
+                           weight="decoder embed_tokens.weight, N(0, 0.02)",
+                           site="whisper.py:942-975"),
+              qwen3=dict(vocab=vocab, width=width, batch=batch, eos=eos_ids, seed=8,
+                         weight="lm_head weight, N(0, 1/width)", site="qwen3_asr.py:1180-1213")),
+         **arrays)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--reference", default="/root/reference",
                         help="checkout of sjjeong94/asrback (read-only)")
+    parser.add_argument("--only", default=None, help="generate only the fixtures whose "
+                        "generator function has this name")
     args = parser.parse_args()
     install_asrfront_stub()
     sys.path.insert(0, str(Path(args.reference) / "src"))
@@ -328,13 +444,17 @@ def main() -> None:
     from asrback.models import whisper  # noqa: E402
 
     torch.set_num_threads(8)
+    per_dtype = (whisper_step, qwen3_step, encoder_attention, qwen3_varlen)
     for dtype, tag in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
-        whisper_step(whisper, dtype, tag)
-        qwen3_step(qwen3, dtype, tag)
-        encoder_attention(whisper, dtype, tag)
-        qwen3_varlen(qwen3, dtype, tag)
-    whisper_tiny_decode(whisper)
-    qwen3_small_decode(qwen3)
+        for make in per_dtype:
+            if args.only in (None, make.__name__):
+                make(qwen3 if make.__name__.startswith("qwen3") else whisper, dtype, tag)
+        if args.only in (None, "step_epilogue"):
+            step_epilogue(whisper, qwen3, dtype, tag)
+    if args.only in (None, "whisper_tiny_decode"):
+        whisper_tiny_decode(whisper)
+    if args.only in (None, "qwen3_small_decode"):
+        qwen3_small_decode(qwen3)
 
 
 if __name__ == "__main__":

@@ -149,3 +149,43 @@ def test_ctypes_signatures_cover_argument_counts(lib):
         params = [p for p in match.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(argtypes), name
         assert isinstance(getattr(lib, name), ctypes._CFuncPtr)
+
+
+def _greedy_call(lib, **overrides):
+    args = dict(dtype=_native.BF16, batch=64, vocab=51866, width=1280, hidden=16, h_stride=1280,
+                weight=16, w_stride=1280, tokens=None, position=16, generated_cols=448,
+                n_eos=1, workspace=16, workspace_bytes=1 << 20)
+    args.update(overrides)
+    eos = (ctypes.c_int64 * 1)(50257)
+    return lib.asrback_greedy_step(
+        args["dtype"], args["batch"], args["vocab"], args["width"], args["hidden"],
+        args["h_stride"], args["weight"], args["w_stride"], None, None, None,
+        args["tokens"], 1, args["position"], 16, 16, 16, 16, 448, args["generated_cols"],
+        eos, args["n_eos"], args["workspace"], args["workspace_bytes"], None, None)
+
+
+@pytest.mark.parametrize("overrides,fragment", [
+    (dict(batch=0), "batch must be in [1, 128]"),
+    (dict(batch=129), "batch must be in [1, 128]"),
+    (dict(dtype=_native.F32, batch=65), "batch must be in [1, 64]"),
+    (dict(width=1000, h_stride=1000, w_stride=1001), "16-byte boundaries"),
+    (dict(weight=8), "16-byte boundaries"),
+    (dict(h_stride=100), "at least hidden_dim"),
+    (dict(n_eos=9), "n_eos"),
+    (dict(tokens=16, position=None), "state update needs"),
+    (dict(tokens=16, generated_cols=0), "state update needs"),
+    (dict(workspace=None), "null workspace"),
+    (dict(dtype=_native.F32, batch=1, width=65536, h_stride=65536, w_stride=65536), "200 KB"),
+])
+def test_greedy_step_invalid_arguments_are_rejected_on_the_host(lib, overrides, fragment):
+    rc = _greedy_call(lib, **overrides)
+    assert rc == _native.ERR_ARGUMENT
+    assert fragment in lib.asrback_last_error().decode()
+
+
+def test_greedy_step_workspace(lib):
+    need = lib.asrback_greedy_step_workspace_bytes(64)
+    assert need >= 256 + 64 * 16
+    assert lib.asrback_greedy_step_workspace_bytes(128) > need
+    assert lib.asrback_greedy_step_workspace_bytes(0) == 0
+    assert _greedy_call(lib, workspace_bytes=need - 1) == _native.ERR_WORKSPACE

@@ -140,3 +140,37 @@ def test_model_fixtures_are_consistent():
         assert len(np.unique(g["positions"][:, 0])) == g["positions"].shape[0]
         assert len(np.unique(g["argmax"])) > 20
         np.testing.assert_array_equal(g["tokens"][:, 1:], g["argmax"][:, :-1])
+
+
+@pytest.mark.parametrize("tag", ["fp32", "bf16"])
+@pytest.mark.parametrize("family", ["whisper", "qwen3"])
+def test_step_epilogue(family, tag):
+    """Three greedy ``_step`` calls of the reference's Transcriber: the oracle's
+    logits, ``_choose`` and state update give the same tokens, log-probabilities
+    and state."""
+    from oracle import step as oracle_step
+    from tests.step_fixtures import initial_state, step_weight
+
+    g = load(f"step_epilogue_{tag}")
+    info = g["meta"][family]
+    bf16 = tag == "bf16"
+    weight = step_weight(family, g["meta"], bf16).float().numpy()
+    suppress = g.get(f"{family}_suppress")
+    state = initial_state(g, family)
+    for step in range(g["meta"]["steps"]):
+        logits = oracle_step.logits(weight, g[f"{family}_hidden"][step], bf16)
+        token, logprob = oracle_step.choose(logits, suppress)
+        np.testing.assert_array_equal(token, g[f"{family}_token"][step])
+        np.testing.assert_allclose(logprob, g[f"{family}_logprob"][step], atol=1e-4, rtol=0)
+        state = oracle_step.update_state(state, token, logprob, info["eos"])
+        for name in ("tokens", "position", "finished"):
+            np.testing.assert_array_equal(state[name], g[f"{family}_after_{name}"][step])
+        np.testing.assert_allclose(state["sum_logprobs"], g[f"{family}_after_sum_logprobs"][step],
+                                   atol=1e-4, rtol=0)
+    np.testing.assert_array_equal(state["generated"], g[f"{family}_generated"])
+    # The fixture reaches every branch: an EOS, a row at its end, a free row.
+    assert np.isin(g[f"{family}_token"], info["eos"]).any()
+    finished = g[f"{family}_after_finished"]
+    assert finished[-1].sum() > g[f"{family}_finished0"].sum() + 1
+    assert (g[f"{family}_after_position"][-1] == g[f"{family}_position0"])[
+        g[f"{family}_finished0"]].all()

@@ -213,15 +213,133 @@ def test_qwen3_prefill_and_audio_attention(reference, cpu_ops):
         assert torch.allclose(a, b, atol=1e-4), (a - b).abs().max()
 
 
+@pytest.fixture
+def cpu_step(monkeypatch):
+    """Oracle-backed stand-in for ``step.greedy_step`` (same signature and
+    in-place state update)."""
+    from asrback_b200 import step
+    from oracle import step as oracle_step
+
+    calls = []
+
+    def greedy_step(hidden, weight, tokens, position, end, finished, sum_logprobs, generated,
+                    eos_ids, suppress=None):
+        calls.append(tuple(hidden.shape))
+        logits = oracle_step.logits(weight.detach().float().numpy(),
+                                    hidden.detach().float().numpy(),
+                                    hidden.dtype == torch.bfloat16)
+        token, logprob = oracle_step.choose(logits, None if suppress is None else suppress.numpy())
+        new = oracle_step.update_state(
+            dict(tokens=tokens.reshape(-1).numpy(), position=position.numpy(), end=end.numpy(),
+                 finished=finished.numpy(), sum_logprobs=sum_logprobs.numpy(),
+                 generated=generated.numpy()), token, logprob, eos_ids)
+        tokens.copy_(torch.from_numpy(new["tokens"]).reshape(tokens.shape))
+        position.copy_(torch.from_numpy(new["position"]))
+        finished.copy_(torch.from_numpy(new["finished"]))
+        sum_logprobs.copy_(torch.from_numpy(new["sum_logprobs"]))
+        generated.copy_(torch.from_numpy(new["generated"]))
+
+    monkeypatch.setattr(step, "greedy_step", greedy_step)
+    return calls
+
+
+def _whisper_engine(whisper, hiddens):
+    """A Transcriber stand-in: the reference's ``logits`` over a seeded
+    embedding, its ``_choose``, and a decoder returning ``hiddens`` in turn."""
+    import types
+
+    config = dict(d_model=64, encoder_attention_heads=2, decoder_attention_heads=2,
+                  encoder_layers=1, decoder_layers=1, encoder_ffn_dim=32, decoder_ffn_dim=32,
+                  num_mel_bins=80, max_source_positions=40, max_target_positions=48,
+                  vocab_size=3000)
+    model = whisper.WhisperForConditionalGeneration(config)
+    seeded_parameters(model.model.decoder, 21)
+    queue = list(hiddens)
+    engine = types.SimpleNamespace(_eos=2999, _suppress=torch.arange(3000) % 7 == 3)
+    engine.model = types.SimpleNamespace(decode=lambda *args: queue.pop(0), logits=model.logits,
+                                         model=model.model)
+    engine._choose = types.MethodType(whisper.Transcriber._choose, engine)
+    state = whisper._DecodeState.allocate(5, 48, torch.device("cpu"))
+    state.tokens[:, 0] = torch.tensor([5, 6, 7, 8, 9])
+    state.position[:] = torch.tensor([3, 10, 46, 0, 20])
+    state.end[:] = torch.tensor([47, 47, 47, 0, 47])
+    state.finished[:] = torch.tensor([False, False, False, True, False])
+    return engine, state
+
+
+def _qwen3_engine(qwen3, hiddens):
+    import types
+
+    lm_head = torch.nn.Linear(64, 2000, bias=False)
+    seeded_parameters(lm_head, 22)
+    queue = list(hiddens)
+    engine = types.SimpleNamespace(_lm_head=lm_head, _eos_ids=torch.tensor([1990, 1999]),
+                                   _cos=None, _sin=None, _varlen=False)
+    engine._text = types.SimpleNamespace(step=lambda *args: queue.pop(0))
+    engine._choose = types.MethodType(qwen3.Qwen3ASRTranscriber._choose, engine)
+    state = qwen3._DecodeState.allocate(4, torch.device("cpu"))
+    state.tokens[:] = torch.tensor([1, 2, 3, 4])
+    state.position[:] = torch.tensor([0, 500, 1022, 7])
+    state.end[:] = torch.tensor([1023, 1023, 1023, 1023])
+    state.finished[:] = torch.tensor([False, False, False, True])
+    return engine, state
+
+
+@pytest.mark.parametrize("family", ["whisper", "qwen3"])
+def test_transcriber_greedy_step(reference, cpu_step, family):
+    """The patched ``_step`` hands the decoder's last hidden state, the logits
+    weight, the suppress mask and the EOS ids to the fused step and leaves the
+    same decode state as the reference's own ``_step``."""
+    whisper, qwen3 = reference
+    module = whisper if family == "whisper" else qwen3
+    cls = whisper.Transcriber if family == "whisper" else qwen3.Qwen3ASRTranscriber
+    make = _whisper_engine if family == "whisper" else _qwen3_engine
+    shape = (5, 1, 64) if family == "whisper" else (4, 64)
+    hiddens = [seeded_normal(shape, 700 + i) * 3 for i in range(4)]
+    engine, want = make(module, [h.clone() for h in hiddens])
+    with torch.no_grad():
+        for _ in hiddens:
+            cls._step(engine, want, None, None)
+    plugin.install(whisper, qwen3)
+    try:
+        engine, got = make(module, [h.clone() for h in hiddens])
+        with torch.no_grad():
+            for _ in hiddens:
+                cls._step(engine, got, None, None)
+    finally:
+        plugin.uninstall()
+    assert len(cpu_step) == len(hiddens)
+    for name in ("tokens", "position", "finished", "generated"):
+        assert torch.equal(getattr(got, name), getattr(want, name)), name
+    torch.testing.assert_close(got.sum_logprobs, want.sum_logprobs, atol=1e-5, rtol=0)
+    assert want.finished.sum() > 1  # an EOS or an end was reached
+
+
+def test_transcriber_sampling_step_keeps_reference_path(reference, cpu_step):
+    """A step with temperatures goes to the reference's own ``_step``."""
+    whisper, qwen3 = reference
+    engine, state = _whisper_engine(whisper, [seeded_normal((5, 1, 64), 710)])
+    plugin.install(whisper, qwen3)
+    try:
+        torch.manual_seed(0)
+        with torch.no_grad():
+            whisper.Transcriber._step(engine, state, None, torch.full((5,), 0.7))
+    finally:
+        plugin.uninstall()
+    assert cpu_step == []
+
+
 def test_uninstall_restores_reference(reference):
     whisper, qwen3 = reference
     before = (whisper.DecoderLayer.forward, whisper.MultiHeadAttention.forward,
-              qwen3.TextAttention.step, qwen3.TextModel.step, qwen3.attend)
+              qwen3.TextAttention.step, qwen3.TextModel.step, qwen3.attend,
+              whisper.Transcriber._step, qwen3.Qwen3ASRTranscriber._step)
     plugin.install(whisper, qwen3)
     assert plugin.installed()
     assert whisper.DecoderLayer.forward is not before[0]
     assert qwen3.attend is not before[4]
     plugin.uninstall()
     after = (whisper.DecoderLayer.forward, whisper.MultiHeadAttention.forward,
-             qwen3.TextAttention.step, qwen3.TextModel.step, qwen3.attend)
+             qwen3.TextAttention.step, qwen3.TextModel.step, qwen3.attend,
+             whisper.Transcriber._step, qwen3.Qwen3ASRTranscriber._step)
     assert after == before
