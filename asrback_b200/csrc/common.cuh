@@ -1,6 +1,7 @@
 // Device helpers shared by the asrback sm_100a kernels: mbarrier and bulk-copy
-// (TMA engine) wrappers in inline PTX, bounded waits, and bf16/f32 vector
-// unpacking. Host helpers for the C ABI's error reporting live in capi.cu.
+// (TMA engine) wrappers in inline PTX, bounded waits, programmatic dependent
+// launch, packed f32x2 arithmetic, and bf16/f32 vector unpacking. Host helpers
+// for the C ABI's error reporting live in capi.cu.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -131,6 +132,19 @@ __device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// Programmatic dependent launch (a kernel launched with programmatic stream
+// serialization may start before the previous kernel in its stream ends).
+// griddep_wait blocks until that kernel has completed and its writes are
+// visible; griddep_launch_dependents lets the next such kernel start once
+// every CTA of this grid has issued it (or exited). Both are no-ops for a
+// kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // L2 policy for data read once per step (the KV stream): evict first.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;
@@ -157,6 +171,36 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Packed f32 pairs (low element first) and Blackwell's paired f32 FMA / add
+// / multiply.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 // Named barrier among `threads` threads (a multiple of 32), id 1..15.
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

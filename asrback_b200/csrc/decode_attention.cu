@@ -25,10 +25,13 @@
 // at the row's own position (the one this step writes) is taken from
 // registers, so the cache write and the tile reads never overlap.
 //
-// Splits. A row's splits each leave (m, l, o) partials in the workspace; the
-// last CTA of the row to finish (an atomic counter, re-armed to zero by that
-// CTA) merges them and writes the output. A row with a single active split
-// writes its output directly.
+// Splits. The grid has num_splits CTAs per (row, group); a row uses as many
+// as its own key count fills at `chunk` keys or more apiece and cuts its keys
+// evenly between them (whole tiles), so the CTAs of a launch carry similar
+// byte counts whatever the rows' lengths. A row's splits each leave (m, l, o)
+// partials in the workspace; the last CTA of the row to finish (an atomic
+// counter, re-armed to zero by that CTA) merges them and writes the output.
+// A row with a single active split writes its output directly.
 #include <cfloat>
 #include <cstdio>
 #include <cstdlib>
@@ -201,6 +204,13 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  // Launched with programmatic stream serialization: the CTA may be resident
+  // before the previous kernel of the stream has finished, so it reads no
+  // input (positions, caches, queries, workspace) before that kernel is done;
+  // then the next launch may begin to be scheduled.
+  griddep_wait();
+  griddep_launch_dependents();
+
   // Keys of this row: n_cached read from the cache, plus (self/Qwen3) the
   // step's own key at index `pos`.
   int pos = 0, n_cached, n_total;
@@ -223,10 +233,14 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
     n_cached = pos;
     n_total = pos + 1;
   }
-  const int active = (n_total + p.chunk - 1) / p.chunk;
+  // This row's splits: at most p.num_splits, each at least p.chunk keys (but
+  // one), the row's keys cut evenly into whole tiles, none left empty.
+  int active = min(p.num_splits, (n_total + p.chunk - 1) / p.chunk);
+  const int per = ((n_total + active - 1) / active + TP - 1) / TP * TP;
+  active = (n_total + per - 1) / per;
   if (split >= active) return;
-  const int k0 = split * p.chunk;
-  const int k1 = min(k0 + p.chunk, n_cached);
+  const int k0 = split * per;
+  const int k1 = min(k0 + per, n_cached);
   const int n_tiles = k1 > k0 ? (k1 - k0 + TP - 1) / TP : 0;
   const bool has_own_key = MODE != kWhisperCross && split == active - 1;
   const uint64_t deadline = global_timer_ns() + kWaitBudgetNs;
@@ -579,30 +593,30 @@ int chunk_override() {
   return env ? std::atoi(env) : 0;
 }
 
-// Keys per split for `units` independent (row, group) units of at most
-// `max_keys` keys: about two CTAs per SM in all, whole tiles (rounded up to
-// `granule_tiles`) per split, at most kMaxSplits splits.
-void choose_split(int units, int max_keys, int tile, int granule_tiles, int* chunk, int* splits) {
+// Splits for `units` independent (row, group) units of at most `max_keys`
+// keys: as many CTAs per unit as fill the GPU's resident slots once
+// (`ctas_per_sm` per SM; a second partial wave would leave the first wave's
+// SMs idle at the end), at most one per tile and kMaxSplits. `chunk` is the
+// fewest keys a split takes (whole tiles, at least `granule_tiles`); the
+// kernel cuts each row's own keys evenly between the splits it uses.
+void choose_split(int units, int max_keys, int tile, int granule_tiles, int ctas_per_sm,
+                  int* chunk, int* splits) {
   const int tiles = (max_keys + tile - 1) / tile;
   int want = 1;
+  int chunk_tiles = granule_tiles;
   const int override_keys = chunk_override();
   if (override_keys > 0) {
-    int c = (override_keys + tile - 1) / tile;
-    want = (tiles + c - 1) / c;
+    chunk_tiles = (override_keys + tile - 1) / tile;
+    want = (tiles + chunk_tiles - 1) / chunk_tiles;
   } else {
-    // About two CTAs per SM: enough to fill the GPU, few enough that each
-    // split keeps a pipeline's worth of tiles (sweeps on B200).
-    const int target = sm_count() * 2;
-    want = (target + units - 1) / units;
+    want = sm_count() * ctas_per_sm / units;
   }
   want = want < 1 ? 1 : want;
   want = want > tiles ? tiles : want;
   want = want > kMaxSplits ? kMaxSplits : want;
-  int chunk_tiles = (tiles + want - 1) / want;
-  if (override_keys <= 0 && granule_tiles > 1)
-    chunk_tiles = (chunk_tiles + granule_tiles - 1) / granule_tiles * granule_tiles;
+  chunk_tiles = chunk_tiles < 1 ? 1 : chunk_tiles;
   *chunk = chunk_tiles * tile;
-  *splits = (tiles + chunk_tiles - 1) / chunk_tiles;
+  *splits = want;
 }
 
 // Kernel shape per call site and dtype: warps per key/value head, key
@@ -640,9 +654,9 @@ template <int QPK>
 using Qwen3F32 = DecodeConfig<float, 128, ASRBACK_QWEN3_GROUP, QPK, ASRBACK_SHAPE_QWEN3_F32, kQwen3>;
 
 // Splits `units` (row, group) units of at most p.length keys for config C.
-// Splits are whole tiles; Qwen3 rounds them to 64 positions, which on
-// bucket-length views (1024) gives the 256-position splits its rows of
-// ~410-540 positions stream fastest with (sweeps on B200).
+// A Qwen3 split takes at least 64 positions (four 16-position tiles), so
+// that a short row is not cut into splits whose merge costs more than their
+// streaming saves.
 template <class C>
 constexpr int split_granule_tiles() {
   return C::MODE == kQwen3 ? (64 + C::TP - 1) / C::TP : 1;
@@ -650,14 +664,15 @@ constexpr int split_granule_tiles() {
 
 template <class C>
 void split_for(DecodeParams& p, int units) {
-  choose_split(units, p.length, C::TP, split_granule_tiles<C>(), &p.chunk, &p.num_splits);
+  choose_split(units, p.length, C::TP, split_granule_tiles<C>(), C::MIN_BLOCKS, &p.chunk,
+               &p.num_splits);
 }
 
 // Workspace bytes config C needs for `units` units of `qh` query heads.
 template <class C>
 size_t workspace_for(int units, int qh, int max_keys) {
   int chunk, splits;
-  choose_split(units, max_keys, C::TP, split_granule_tiles<C>(), &chunk, &splits);
+  choose_split(units, max_keys, C::TP, split_granule_tiles<C>(), C::MIN_BLOCKS, &chunk, &splits);
   return workspace_bytes_for(units, qh, C::D, splits);
 }
 
@@ -674,9 +689,8 @@ int launch(const DecodeParams& p, int batch, cudaStream_t stream) {
       return rc;
     prepared_device = device;
   }
-  dim3 grid(p.num_splits, p.groups, batch);
-  kernel<<<grid, C::THREADS, C::SMEM, stream>>>(p);
-  return check_cuda(cudaGetLastError(), "decode attention launch");
+  return launch_pdl(kernel, dim3(p.num_splits, p.groups, batch), dim3(C::THREADS), C::SMEM, stream,
+                    "decode attention launch", p);
 }
 
 // Splits, binds the workspace and launches config C.

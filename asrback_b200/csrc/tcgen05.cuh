@@ -1,7 +1,7 @@
 // tcgen05 / TMA / TMEM building blocks shared by the sm_100a tensor-core
 // kernels: inline-PTX wrappers for tensor-memory allocation, loads and stores,
-// tcgen05.mma (SS and TS forms) and commits, tiled TMA loads, packed f32x2
-// arithmetic, shared-memory matrix descriptors (128-byte swizzle), and the
+// tcgen05.mma (SS and TS forms) and commits, tiled TMA loads, shared-memory
+// matrix descriptors (128-byte swizzle), and the
 // driver entry point that encodes TMA tensor maps.
 #pragma once
 
@@ -244,29 +244,6 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* r) {
 }
 
 // Packed f32x2 arithmetic (sm_100): two lanes of work per instruction.
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void unpack2(uint64_t r, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
 // Two floats to a bf16 pair (lo in the low half), round to nearest even.
 __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
   uint32_t d;
