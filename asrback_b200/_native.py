@@ -96,6 +96,15 @@ SIGNATURES: dict[str, tuple[list, object]] = {
          _c_f, _c_p, _c_p],
         _c_int,
     ),
+    "asrback_whisper_cross_kv_projection": (
+        [_c_int, _c_int, _c_int, _c_int,
+         _c_p, _c_i64, _c_i64,
+         _c_p, _c_p, _c_i64, _c_p,
+         _c_p, _c_p,
+         _c_i64, _c_i64, _c_i64,
+         _c_p, _c_p],
+        _c_int,
+    ),
     "asrback_greedy_step_workspace_bytes": ([_c_int], _c_size),
     "asrback_greedy_step": (
         [_c_int, _c_int, _c_int, _c_int,

@@ -14,7 +14,10 @@ Reference call sites (asrback project paths):
 - :func:`qwen3_attention_step`: ``TextAttention.step``,
   ``src/asrback/models/qwen3_asr.py:392-432`` with ``_project`` (``:366-372``);
 - :func:`whisper_encoder_attention`: ``MultiHeadAttention.forward``,
-  ``whisper.py:108-110``.
+  ``whisper.py:108-110``;
+- :func:`whisper_cross_kv_projection`: ``set_encoder_output``,
+  ``whisper.py:313-319`` (``project_key_value``, ``:88-91``, and the copy into
+  the cross-attention cache), one decoder layer per call.
 """
 
 from __future__ import annotations
@@ -32,6 +35,7 @@ __all__ = [
     "whisper_cross_attention_step",
     "qwen3_attention_step",
     "whisper_encoder_attention",
+    "whisper_cross_kv_projection",
     "varlen_attention",
     "reserve_workspace",
     "read_status",
@@ -306,6 +310,44 @@ def whisper_encoder_attention(q: Tensor, k: Tensor, v: Tensor, scale: float | No
         state.status.data_ptr(), _stream(q.device),
     )
     return out
+
+
+def whisper_cross_kv_projection(encoder_output: Tensor, k_weight: Tensor, v_weight: Tensor,
+                                v_bias: Tensor | None, keys: Tensor, values: Tensor) -> None:
+    """One decoder layer's cross-attention keys and values, written into its
+    cache rows: ``keys[:, h, :S] = (x @ k_weight.T)`` split into heads of 64,
+    ``values`` likewise with ``v_bias`` (``encoder_output`` ``(B, S, W)``;
+    ``keys``/``values`` the ``(B, H, L >= S, 64)`` views
+    ``cross_keys[layer, :B]`` / ``cross_values[layer, :B]``)."""
+    dtype = _dtype_code(encoder_output, k_weight, v_weight, keys, values)
+    if v_bias is not None:
+        _dtype_code(encoder_output, v_bias)
+    if encoder_output.dim() != 3 or encoder_output.stride(2) != 1:
+        raise ValueError("asrback_b200: encoder_output must be (batch, tokens, width) with "
+                         "contiguous rows")
+    batch, tokens, width = encoder_output.shape
+    for name, w in (("k_weight", k_weight), ("v_weight", v_weight)):
+        if w.shape != (width, width) or w.stride(1) != 1 or w.stride(0) != k_weight.stride(0):
+            raise ValueError(f"asrback_b200: {name} must be ({width}, {width}) with contiguous "
+                             "rows, both weights with one stride")
+    if v_bias is not None and (v_bias.shape != (width,) or v_bias.stride(0) != 1):
+        raise ValueError(f"asrback_b200: v_bias must be a contiguous ({width},) tensor")
+    for name, c in (("keys", keys), ("values", values)):
+        if c.dim() != 4 or c.shape[0] != batch or c.shape[1] * c.shape[3] != width \
+                or c.shape[3] != 64 or c.shape[2] < tokens or c.stride(3) != 1:
+            raise ValueError(f"asrback_b200: {name} must be a (batch, heads, length >= tokens, 64) "
+                             "cache view with contiguous rows")
+    if keys.stride() != values.stride():
+        raise ValueError("asrback_b200: keys and values must share strides")
+    state = _state(encoder_output.device)
+    _native.call(
+        "asrback_whisper_cross_kv_projection", dtype, batch, tokens, width,
+        encoder_output.data_ptr(), encoder_output.stride(0), encoder_output.stride(1),
+        k_weight.data_ptr(), v_weight.data_ptr(), k_weight.stride(0),
+        None if v_bias is None else v_bias.data_ptr(),
+        keys.data_ptr(), values.data_ptr(), keys.stride(0), keys.stride(1), keys.stride(2),
+        state.status.data_ptr(), _stream(encoder_output.device),
+    )
 
 
 def varlen_attention(q: Tensor, k: Tensor, v: Tensor, starts: Tensor, longest: int, causal: bool,

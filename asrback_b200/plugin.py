@@ -15,6 +15,9 @@ Patched call sites (asrback project paths):
   the eager prefix branch (``length`` given) is left to the original method;
 - ``whisper.MultiHeadAttention.forward`` (``whisper.py:108-110``): the
   encoder's unmasked self-attention;
+- ``whisper.WhisperForConditionalGeneration.set_encoder_output``
+  (``whisper.py:313-319``): each decoder layer's cross-attention keys and
+  values are projected and written into the cache by one kernel;
 - ``qwen3_asr.TextModel.step`` (``src/asrback/models/qwen3_asr.py:494-524``)
   and ``qwen3_asr.TextAttention.step`` (``qwen3_asr.py:392-432``): the decoder
   step hands ``qkv_proj``'s output, the full RoPE tables and the positions to
@@ -94,6 +97,17 @@ def _whisper_encoder_attention_forward(self, x):
     return self.out_proj(attention.whisper_encoder_attention(query, key, value))
 
 
+def _whisper_set_encoder_output(self, cache, encoder_output):
+    """Fills the first ``len(encoder_output)`` rows' cross keys/values, one
+    projection kernel per decoder layer."""
+    batch_size = encoder_output.shape[0]
+    for index, layer in enumerate(self.model.decoder.layers):
+        attn = layer.encoder_attn
+        attention.whisper_cross_kv_projection(
+            encoder_output, attn.k_proj.weight, attn.v_proj.weight, attn.v_proj.bias,
+            cache.cross_keys[index, :batch_size], cache.cross_values[index, :batch_size])
+
+
 def _qwen3_text_attention_step(self, x, keys, values, positions, mask, cos, sin):
     """One token per row; ``cos``/``sin`` are the full tables (the patched
     ``TextModel.step`` passes them ungathered), ``mask`` is unused."""
@@ -166,6 +180,8 @@ def install(whisper_module=None, qwen3_module=None) -> None:
         original = _originals.get((layer, "forward"), layer.__dict__["forward"])
         _patch(layer, "forward", _whisper_decoder_layer_forward(original))
         _patch(whisper_module.MultiHeadAttention, "forward", _whisper_encoder_attention_forward)
+        _patch(whisper_module.WhisperForConditionalGeneration, "set_encoder_output",
+               _whisper_set_encoder_output)
         if hasattr(whisper_module, "Transcriber"):
             transcriber = whisper_module.Transcriber
             original = _originals.get((transcriber, "_step"), transcriber.__dict__["_step"])

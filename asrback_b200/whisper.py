@@ -262,12 +262,15 @@ class WhisperForConditionalGeneration(nn.Module):
         return DecoderCache(zeros(target), zeros(target), zeros(source), zeros(source))
 
     def set_encoder_output(self, cache: DecoderCache, encoder_output: Tensor) -> None:
-        """Fills the first ``len(encoder_output)`` rows' cross keys/values."""
+        """Fills the first ``len(encoder_output)`` rows' cross keys/values
+        (``whisper.py:313-319``): each layer's projections are written into
+        the cache by one kernel."""
         batch_size = encoder_output.shape[0]
         for index, layer in enumerate(self.model.decoder.layers):
-            key, value = layer.encoder_attn.project_key_value(encoder_output)
-            cache.cross_keys[index, :batch_size] = key
-            cache.cross_values[index, :batch_size] = value
+            attn = layer.encoder_attn
+            ops.whisper_cross_kv_projection(
+                encoder_output, attn.k_proj.weight, attn.v_proj.weight, attn.v_proj.bias,
+                cache.cross_keys[index, :batch_size], cache.cross_values[index, :batch_size])
 
     def decode(self, tokens: Tensor, positions: Tensor, cache: DecoderCache,
                length: int | None = None) -> Tensor:

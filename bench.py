@@ -25,7 +25,10 @@ Other workloads (``--workload``):
                    windows, 64 requests of 390 tokens, 24 layers;
   whisper-step,    the greedy step epilogue after the decoder (logits against
   qwen3-step       the 51866 x 1280 tied embedding / the 151936 x 2048 lm_head,
-                   argmax, log-softmax, state update) for 64 rows; unit: tokens.
+                   argmax, log-softmax, state update) for 64 rows; unit: tokens;
+  whisper-cross-kv set_encoder_output for 32 windows: the 4 decoder layers'
+                   cross-attention keys/values projected into the cache; unit:
+                   windows.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
                     [--workload NAME] [--batch B]
@@ -63,7 +66,7 @@ def parse_args():
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--workload", choices=("whisper-decode", "whisper-encoder", "qwen3-decode",
                                                "qwen3-prefill", "qwen3-audio", "whisper-step",
-                                               "qwen3-step"),
+                                               "qwen3-step", "whisper-cross-kv"),
                         default="whisper-decode")
     parser.add_argument("--batch", type=int, default=None,
                         help="override the workload's batch (small profiling cases)")
@@ -872,6 +875,123 @@ class Qwen3AudioWindows(Qwen3Prefill):
                           f"oracle, {elapsed:.1f} s, scaled by 1/24 layers"}
 
 
+class WhisperCrossKV:
+    """Admission of BASELINE config 3's windows into the decoder (SURVEY 8(f)
+    rank 2): `set_encoder_output` (whisper.py:313-319), each of the 4 decoder
+    layers' cross-attention keys/values projected from the encoder output and
+    written into the cache."""
+
+    name = "whisper-cross-kv"
+    metric = ("cross-attention K/V fill windows/s/GPU (Whisper large-v3-turbo set_encoder_output: "
+              "32 windows x 1500 frames, 4 decoder layers, bf16); projection TFLOP/s")
+    unit = "windows/s"
+    bound = "tensor"
+    reference_in_graph = False
+    layers, width, tokens, heads = 4, 1280, 1500, 20
+    profile = "cross_kv_projection_b32_bf16.md"
+
+    def __init__(self, batch: int | None):
+        self.batch = batch or 32
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": "Whisper large-v3-turbo set_encoder_output: k_proj/v_proj of the encoder "
+                        "output into the cross-attention cache (SURVEY 8(f) rank 2 row)",
+            "layers": self.layers, "width": self.width, "heads": self.heads,
+            "frames": self.tokens, "windows_per_gpu": self.batch,
+            "global_batch": self.batch * world,
+            "step": "4 decoder layers' projections into the cache",
+            "inputs": "encoder output N(0, 1) bf16, weights N(0, 1/width), v_proj bias N(0, 0.02)",
+            "parallelism": f"replicas x{world} (no collective)",
+        }
+
+    def units_per_step(self) -> int:
+        return self.batch
+
+    def flops_per_layer(self) -> float:
+        return 2.0 * self.batch * self.tokens * 2 * self.width * self.width
+
+    def setup(self, torch, device, seed: int, total: int) -> None:
+        gen = torch.Generator(device=device).manual_seed(seed)
+        w, dtype = self.width, torch.bfloat16
+        self.x = torch.randn((self.batch, self.tokens, w), generator=gen, device=device).to(dtype)
+        self.wk = [(torch.randn((w, w), generator=gen, device=device) / w ** 0.5).to(dtype)
+                   for _ in range(self.layers)]
+        self.wv = [(torch.randn((w, w), generator=gen, device=device) / w ** 0.5).to(dtype)
+                   for _ in range(self.layers)]
+        self.bv = [(torch.randn((w,), generator=gen, device=device) * 0.02).to(dtype)
+                   for _ in range(self.layers)]
+        shape = (self.layers, self.batch, self.heads, self.tokens, w // self.heads)
+        self.keys = torch.zeros(shape, device=device, dtype=dtype)
+        self.values = torch.zeros(shape, device=device, dtype=dtype)
+        self.outputs = [self.keys[layer, 0, 0, 0] for layer in range(self.layers)]
+
+    def attend(self, layer: int) -> None:
+        from asrback_b200 import attention
+
+        attention.whisper_cross_kv_projection(self.x, self.wk[layer], self.wv[layer],
+                                              self.bv[layer], self.keys[layer],
+                                              self.values[layer])
+
+    def step(self) -> None:
+        for layer in range(self.layers):
+            self.attend(layer)
+
+    def launches_per_step(self) -> int:
+        return self.layers
+
+    def refresh(self, t: int) -> None:
+        pass
+
+    def host_step_inputs(self, torch, first: int, count: int):
+        host = torch.empty(self.x.shape, dtype=self.x.dtype, pin_memory=True)
+        host.copy_(self.x.cpu())
+        return [(host[None].expand(count, *host.shape), self.x)]
+
+    def kernels(self, t: int):
+        return [("cross_kv", self.attend, self.flops_per_layer())]
+
+    def step_work(self, first: int, count: int) -> float:
+        return self.flops_per_layer() * self.layers * count
+
+    def torch_reference_step(self, torch):
+        """The reference's set_encoder_output on the same tensors: per layer,
+        project_key_value (two F.linear, _split_heads) and the copy into the
+        cache rows (whisper.py:313-319, :85-91)."""
+        import torch.nn.functional as F
+
+        def split(t):
+            b, s, w = t.shape
+            return t.view(b, s, self.heads, w // self.heads).transpose(1, 2)
+
+        def run():
+            for layer in range(self.layers):
+                self.keys[layer, :self.batch] = split(F.linear(self.x, self.wk[layer]))
+                self.values[layer, :self.batch] = split(
+                    F.linear(self.x, self.wv[layer], self.bv[layer]))
+        return run
+
+    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+        from oracle import attention as oracle
+
+        rng = np.random.default_rng(seed)
+        w = self.width
+        x = rng.standard_normal((1, self.tokens, w), dtype=np.float32)
+        wk = rng.standard_normal((w, w), dtype=np.float32) / w ** 0.5
+        wv = rng.standard_normal((w, w), dtype=np.float32) / w ** 0.5
+        bv = rng.standard_normal((w,), dtype=np.float32) * 0.02
+
+        def one(_t, _p):
+            oracle.cross_kv_projection(x, wk, wv, bv, compute=np.float32)
+
+        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
+        layers_done = done * threads
+        return {"value": layers_done / elapsed / self.layers, "unit": self.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{layers_done} window-layers (1500 x 1280 @ 1280 x 2560), float32 "
+                          f"numpy oracle, {elapsed:.1f} s, scaled by 1/4 layers"}
+
+
 class WhisperGreedyStep:
     """The step epilogue after the decoder: logits against
     the tied embedding, greedy `_choose` with the suppress mask and the state
@@ -1031,7 +1151,8 @@ class Qwen3GreedyStep(WhisperGreedyStep):
 
 
 WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode, Qwen3Prefill,
-                                       Qwen3AudioWindows, WhisperGreedyStep, Qwen3GreedyStep)}
+                                       Qwen3AudioWindows, WhisperGreedyStep, Qwen3GreedyStep,
+                                       WhisperCrossKV)}
 
 
 # ------------------------------------------------------------------ arms ----
@@ -1244,7 +1365,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         # Short runs of the other workloads, for context.
         extras = {}
         for name in ("whisper-encoder", "qwen3-decode", "qwen3-prefill", "qwen3-audio",
-                     "whisper-step", "qwen3-step"):
+                     "whisper-step", "qwen3-step", "whisper-cross-kv"):
             del work
             torch.cuda.empty_cache()
             work = WORKLOADS[name](None)

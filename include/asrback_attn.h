@@ -33,6 +33,10 @@
  *     query/key segments), called by TextAttention.prefill (qwen3_asr.py:
  *     374-390, causal) and AudioAttention.forward (qwen3_asr.py:214-219,
  *     non-causal windows);
+ *   - asrback_whisper_cross_kv_projection replaces set_encoder_output's work
+ *     per decoder layer (whisper.py:313-319): k_proj / v_proj of the encoder
+ *     states (project_key_value, whisper.py:88-91) written into the
+ *     cross-attention cache without the copy pass;
  *   - asrback_greedy_step replaces what a greedy step does after the decoder:
  *     the logits (whisper.py:337-342, qwen3_asr.py:1189 lm_head), _choose
  *     without sampling (whisper.py:962-975 with the suppress mask,
@@ -226,6 +230,31 @@ ASRBACK_API int asrback_varlen_attention(
     const int32_t* cu_seqlens, int segments, int max_length, int causal,
     void* out, int64_t out_stride_token, int64_t out_stride_head,
     float scale, int32_t* status, void* stream);
+
+/*
+ * Cross-attention keys and values of one Whisper decoder layer, written into
+ * the cache layout:
+ *   keys[b][h][t][d]   = sum_k x[b][t][k] * k_weight[h*64 + d][k]
+ *   values[b][h][t][d] = sum_k x[b][t][k] * v_weight[h*64 + d][k] + v_bias[h*64 + d]
+ * for b < batch, t < tokens, heads = width / 64, d < 64.
+ * x            (batch, tokens, width) at [b*x_stride_batch + t*x_stride_token + k]
+ *              (the encoder output);
+ * k_weight, v_weight (width, width) rows at w_stride (nn.Linear weights:
+ *              out_features x in_features); v_bias (width,) or null;
+ * keys, values (batch, heads, length >= tokens, 64) cache views at
+ *              [b*c_stride_batch + h*c_stride_head + t*c_stride_token + d]
+ *              (cross_keys[layer, :batch] / cross_values[layer, :batch]).
+ * width a multiple of 128. dtype ASRBACK_BF16 (tensor cores; fp32 sums, the
+ * bias added in fp32, one rounding to bf16 as nn.Linear returns it) or
+ * ASRBACK_F32.
+ */
+ASRBACK_API int asrback_whisper_cross_kv_projection(
+    int dtype, int batch, int tokens, int width,
+    const void* x, int64_t x_stride_batch, int64_t x_stride_token,
+    const void* k_weight, const void* v_weight, int64_t w_stride, const void* v_bias,
+    void* keys, void* values,
+    int64_t c_stride_batch, int64_t c_stride_head, int64_t c_stride_token,
+    int32_t* status, void* stream);
 
 /*
  * Workspace of asrback_greedy_step for up to `batch` rows: a ticket counter

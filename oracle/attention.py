@@ -39,6 +39,7 @@ __all__ = [
     "qwen3_project",
     "qwen3_decode_attention",
     "varlen_attention",
+    "cross_kv_projection",
 ]
 
 
@@ -236,3 +237,24 @@ def varlen_attention(q, k, v, starts, causal, scale=None, compute=np.float64):
         mask = np.tril(np.ones((b - a, b - a), dtype=bool)) if causal else None
         out[a:b] = sdpa(qs, ks, vs, mask, scale, compute).transpose(1, 0, 2)
     return out
+
+
+def cross_kv_projection(x, k_weight, v_weight, v_bias, bf16: bool = False, compute=np.float64):
+    """One decoder layer of ``set_encoder_output`` (``whisper.py:313-319``):
+    ``project_key_value`` (``:88-91``: ``k_proj`` without bias, ``v_proj`` with
+    it, ``_split_heads`` into heads of 64) of ``x`` ``(B, S, W)``. Returns
+    ``(keys, values)``, each ``(B, W / 64, S, 64)``. ``nn.Linear`` in bf16
+    rounds each output once (after the bias), which ``bf16=True`` replays."""
+    x = np.asarray(x, compute)
+    k = x @ np.asarray(k_weight, compute).T
+    v = x @ np.asarray(v_weight, compute).T
+    if v_bias is not None:
+        v = v + np.asarray(v_bias, compute)
+    out = []
+    for t in (k, v):
+        t = t.astype(np.float32)
+        if bf16:
+            t = bf16_round(t)
+        b, s, w = t.shape
+        out.append(t.reshape(b, s, w // 64, 64).transpose(0, 2, 1, 3))
+    return out[0], out[1]

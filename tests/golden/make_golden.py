@@ -317,6 +317,25 @@ def qwen3_small_decode(qwen3) -> None:
          argmax=np.stack(argmax_all, 1), hidden=np.stack(hidden_all, 1))
 
 
+def cross_kv(whisper, dtype: torch.dtype, tag: str) -> None:
+    """``set_encoder_output`` (``whisper.py:313-319``) of a 2-layer decoder,
+    384 wide (6 heads), for 2 windows of 40 encoder frames into a 3-row cache
+    (the third row stays as allocated)."""
+    config = dict(d_model=384, encoder_attention_heads=6, decoder_attention_heads=6,
+                  encoder_layers=1, decoder_layers=2, encoder_ffn_dim=64, decoder_ffn_dim=64,
+                  num_mel_bins=80, max_source_positions=40, max_target_positions=48,
+                  vocab_size=128)
+    model = whisper.WhisperForConditionalGeneration(config)
+    seeded_parameters(model.model.decoder, 9)
+    model = model.to(dtype)
+    cache = model.allocate_cache(3)
+    states = seeded_normal((2, 40, 384), 13).to(dtype)
+    with torch.no_grad():
+        model.set_encoder_output(cache, states)
+    save(f"cross_kv_{tag}", dict(config=config, dtype=str(dtype), seed=9, site="whisper.py:313-319"),
+         states=f32(states), cross_keys=f32(cache.cross_keys), cross_values=f32(cache.cross_values))
+
+
 def _run_steps(step, stub, state, hiddens, fields) -> dict:
     """Runs the reference's ``_step(stub, state, None, None)`` once per hidden
     state, recording ``_choose``'s token and log-probability and the state
@@ -451,6 +470,8 @@ def main() -> None:
                 make(qwen3 if make.__name__.startswith("qwen3") else whisper, dtype, tag)
         if args.only in (None, "step_epilogue"):
             step_epilogue(whisper, qwen3, dtype, tag)
+        if args.only in (None, "cross_kv"):
+            cross_kv(whisper, dtype, tag)
     if args.only in (None, "whisper_tiny_decode"):
         whisper_tiny_decode(whisper)
     if args.only in (None, "qwen3_small_decode"):

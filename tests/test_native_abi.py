@@ -189,3 +189,27 @@ def test_greedy_step_workspace(lib):
     assert lib.asrback_greedy_step_workspace_bytes(128) > need
     assert lib.asrback_greedy_step_workspace_bytes(0) == 0
     assert _greedy_call(lib, workspace_bytes=need - 1) == _native.ERR_WORKSPACE
+
+
+def _cross_kv_call(lib, **overrides):
+    args = dict(dtype=_native.BF16, batch=32, tokens=1500, width=1280, x=16, x_sb=1500 * 1280,
+                x_st=1280, wk=16, wv=16, w_stride=1280, keys=16, c_st=64)
+    args.update(overrides)
+    return lib.asrback_whisper_cross_kv_projection(
+        args["dtype"], args["batch"], args["tokens"], args["width"], args["x"], args["x_sb"],
+        args["x_st"], args["wk"], args["wv"], args["w_stride"], None, args["keys"], 16,
+        20 * 1500 * 64, 1500 * 64, args["c_st"], None, None)
+
+
+@pytest.mark.parametrize("overrides,fragment", [
+    (dict(width=1000), "multiple of 128"),
+    (dict(batch=0), "positive"),
+    (dict(wk=None), "null"),
+    (dict(x_st=1000), "(batch, tokens, width)"),
+    (dict(c_st=32), "views with contiguous rows"),
+    (dict(x=8), "16-byte aligned"),
+])
+def test_cross_kv_invalid_arguments_are_rejected_on_the_host(lib, overrides, fragment):
+    rc = _cross_kv_call(lib, **overrides)
+    assert rc == _native.ERR_ARGUMENT
+    assert fragment in lib.asrback_last_error().decode()

@@ -174,3 +174,32 @@ def test_step_epilogue(family, tag):
     assert finished[-1].sum() > g[f"{family}_finished0"].sum() + 1
     assert (g[f"{family}_after_position"][-1] == g[f"{family}_position0"])[
         g[f"{family}_finished0"]].all()
+
+
+@pytest.mark.parametrize("tag,tol", [("fp32", F32_TOL), ("bf16", BF16_TOL)])
+def test_cross_kv_projection(tag, tol):
+    """``set_encoder_output`` of the reference: each layer's k/v projections,
+    split into heads, in the cache rows of the windows given; other rows as
+    allocated."""
+    import torch
+
+    from asrback_b200.synthetic import seeded_parameters
+    from asrback_b200.whisper import WhisperForConditionalGeneration
+
+    g = load(f"cross_kv_{tag}")
+    model = WhisperForConditionalGeneration(g["meta"]["config"], encoder=False)
+    seeded_parameters(model.model.decoder, g["meta"]["seed"])
+    if tag == "bf16":
+        model = model.to(torch.bfloat16)
+    batch = g["states"].shape[0]
+    for index, layer in enumerate(model.model.decoder.layers):
+        attn = layer.encoder_attn
+        keys, values = oracle.cross_kv_projection(
+            g["states"], attn.k_proj.weight.float().detach().numpy(),
+            attn.v_proj.weight.float().detach().numpy(), attn.v_proj.bias.float().detach().numpy(),
+            bf16=tag == "bf16")
+        length = keys.shape[2]
+        np.testing.assert_allclose(keys, g["cross_keys"][index, :batch, :, :length], atol=tol, rtol=0)
+        np.testing.assert_allclose(values, g["cross_values"][index, :batch, :, :length], atol=tol,
+                                   rtol=0)
+        assert not g["cross_keys"][index, batch:].any()

@@ -75,6 +75,15 @@ def cpu_ops(monkeypatch):
                                       starts.numpy(), causal)
         return torch.from_numpy(out).float()
 
+    def cross_kv(x, wk, wv, bv, keys, values):
+        k, v = oracle.cross_kv_projection(
+            x.detach().float().numpy(), wk.detach().float().numpy(), wv.detach().float().numpy(),
+            None if bv is None else bv.detach().float().numpy())
+        tokens = x.shape[1]
+        keys[:, :, :tokens].copy_(torch.from_numpy(k))
+        values[:, :, :tokens].copy_(torch.from_numpy(v))
+
+    monkeypatch.setattr(attention, "whisper_cross_kv_projection", cross_kv)
     monkeypatch.setattr(attention, "varlen_attention", varlen)
     monkeypatch.setattr(attention, "whisper_self_attention_step", self_step)
     monkeypatch.setattr(attention, "whisper_cross_attention_step", cross_step)
@@ -333,7 +342,8 @@ def test_uninstall_restores_reference(reference):
     whisper, qwen3 = reference
     before = (whisper.DecoderLayer.forward, whisper.MultiHeadAttention.forward,
               qwen3.TextAttention.step, qwen3.TextModel.step, qwen3.attend,
-              whisper.Transcriber._step, qwen3.Qwen3ASRTranscriber._step)
+              whisper.Transcriber._step, qwen3.Qwen3ASRTranscriber._step,
+              whisper.WhisperForConditionalGeneration.set_encoder_output)
     plugin.install(whisper, qwen3)
     assert plugin.installed()
     assert whisper.DecoderLayer.forward is not before[0]
@@ -341,5 +351,6 @@ def test_uninstall_restores_reference(reference):
     plugin.uninstall()
     after = (whisper.DecoderLayer.forward, whisper.MultiHeadAttention.forward,
              qwen3.TextAttention.step, qwen3.TextModel.step, qwen3.attend,
-             whisper.Transcriber._step, qwen3.Qwen3ASRTranscriber._step)
+             whisper.Transcriber._step, qwen3.Qwen3ASRTranscriber._step,
+             whisper.WhisperForConditionalGeneration.set_encoder_output)
     assert after == before
