@@ -4,24 +4,32 @@
 // Replaces F.scaled_dot_product_attention in MultiHeadAttention.forward
 // (whisper.py:108-110, via attend :102-104) for the encoder layers.
 //
-// One CTA owns one (window b, head h) and two 128-row query tiles. Warp roles:
-//   warp 0      TMA producer: both Q tiles once, then K/V tiles of 128 keys
-//               into a STAGES-deep ring (4-D tensor maps over the projections'
-//               (batch, length, heads, 64) layout, 128-byte swizzle; rows past
-//               the window read as zeros);
+// A work item is one (window b, head h) and two 128-row query tiles; the
+// kernel is persistent (one CTA per SM takes items blockIdx.x, + gridDim.x,
+// ..., the pair index fastest so that CTAs running together share each
+// (window, head)'s keys and values in L2). Warp roles:
+//   warp 0      TMA producer: each item's two Q tiles into one of two Q
+//               buffers (once the item two before has issued its last S), and
+//               its K/V tiles of 128 keys into a STAGES-deep ring that runs on
+//               across items (4-D tensor maps over the projections' (batch,
+//               length, heads, 64) layout, 128-byte swizzle; rows past the
+//               window read as zeros);
 //   warp 1      allocates the 512 TMEM columns; one lane issues every MMA:
 //               S = Q_t K^T (SS: both operands from shared memory) and
 //               O_t += P V (TS: P from TMEM, V from shared memory);
 //   warps 4-7   softmax of query tile 0 (thread = TMEM lane = query row);
 //   warps 8-11  softmax of query tile 1.
 // TMEM columns: three S buffers [0,128) [128,256) [256,384), O0 [384,448),
-// O1 [448,512). The k-th S (tile t, key tile j, k = 2j + t) goes to buffer
+// O1 [448,512). Key tiles are numbered J over all of a CTA's items (item i,
+// tile j: J = i * n_k + j). The k-th S (tile t, k = 2J + t) goes to buffer
 // k % 3; its softmax writes P (packed bf16 pairs) over the buffer's first 64
 // columns, and the next S into that buffer is issued right after that P V
-// (the tensor core runs one thread's MMAs in order). So S_1(j+1) follows
-// P_0(j) V and S_0(j+2) follows P_1(j) V: each tile's next S is computed
+// (the tensor core runs one thread's MMAs in order). So S_1(J+1) follows
+// P_0(J) V and S_0(J+2) follows P_1(J) V: each tile's next S is computed
 // while the other tile's softmax runs, and a softmax goes from one key tile
-// to the next without waiting for the tensor core.
+// to the next without waiting for the tensor core, across item boundaries
+// too; an item's first P V into O_t waits only until the previous item's
+// epilogue has read O_t.
 // Barriers that can run ahead of their waiters come in copies so that no
 // waiter ever sees one complete twice: one S barrier per buffer, two P
 // barriers per tile (alternating), and O's last P V commits to a barrier of
@@ -55,13 +63,14 @@ __host__ __device__ constexpr int col_o(int t) { return 384 + 64 * t; }
 // Lazy rescale threshold (log2 units): P <= 2^8 between rescales.
 constexpr float kRescaleThreshold = 8.0f;
 
-constexpr int kOffQ = 0;
-constexpr int kOffK = 2 * kTileBytes;
+constexpr int kOffQ = 0;  // two Q buffers of two tiles
+constexpr int kOffK = 4 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffBar = kOffV + kStages * kTileBytes;
-// barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[3] (one per S
-// buffer), p_full[2][2] (per tile, alternating), o_full[2], o_final[2]
-constexpr int kNumBars = 1 + 3 * kStages + 3 + 4 + 2 + 2;
+// barriers: q_full[2], q_empty[2] (per Q buffer), k_full[S], v_full[S],
+// kv_empty[S], s_full[3] (one per S buffer), p_full[2][2] (per tile,
+// alternating), o_full[2], o_final[2], o_free[2]
+constexpr int kNumBars = 2 + 2 + 3 * kStages + 3 + 4 + 2 + 2 + 2;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
 
@@ -70,6 +79,8 @@ struct TcParams {
   int64_t sb, sh, ss;  // output strides (elements)
   int length;
   int q_pairs;
+  int heads;
+  int items;  // q_pairs * heads * batch
   float scale_log2;
   int32_t* status;
 };
@@ -118,24 +129,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint64_t* q_full = bars;  // [Q buffer]
+  uint64_t* q_empty = q_full + 2;
+  uint64_t* k_full = q_empty + 2;
   uint64_t* v_full = k_full + kStages;
   uint64_t* kv_empty = v_full + kStages;
   uint64_t* s_full = kv_empty + kStages;  // [buffer]
-  uint64_t* p_full = s_full + 3;          // [2 * t + (j & 1)]
+  uint64_t* p_full = s_full + 3;          // [2 * t + (J & 1)]
   uint64_t* o_full = p_full + 4;
   uint64_t* o_final = o_full + 2;
+  uint64_t* o_free = o_final + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int pair = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int n_k = (p.length + kKeys - 1) / kKeys;
-  const uint64_t deadline = global_timer_ns() + kWaitBudgetNs;
+  // This CTA's items: blockIdx.x, + gridDim.x, ...
+  const int n_items = p.items > (int)blockIdx.x
+                          ? (p.items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                          : 0;
+  const int total = n_items * n_k;  // key tiles over all items
+  auto item_index = [&](int li) { return (int)blockIdx.x + li * (int)gridDim.x; };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&q_full[q], 1);
+      mbar_init(&q_empty[q], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
@@ -146,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&o_full[t], 1);
       mbar_init(&o_final[t], 1);
+      mbar_init(&o_free[t], 4);
     }
     fence_barrier_init();
   }
@@ -154,6 +175,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
   bool timed_out = false;
 
   if (warp == 0) {
@@ -162,24 +185,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
-      tma_load_4d(smem + kOffQ, &map_q, 0, h, (2 * pair) * kRows, b, q_full);
-      tma_load_4d(smem + kOffQ + kTileBytes, &map_q, 0, h, (2 * pair + 1) * kRows, b, q_full);
-      for (int j = 0; j < n_k; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, deadline)) {
+      int g = 0;  // key tiles loaded (= J)
+      for (int li = 0; li < n_items && !timed_out; ++li) {
+        const int index = item_index(li);
+        const int pair = index % p.q_pairs, h = (index / p.q_pairs) % p.heads;
+        const int b = index / (p.q_pairs * p.heads);
+        const int qb = li & 1;
+        if (li >= 2 && !mbar_wait_bounded(&q_empty[qb], ((li >> 1) - 1) & 1)) {
           timed_out = true;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-        tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, b, &k_full[s]);
-        mbar_arrive_expect_tx(&v_full[s], kTileBytes);
-        tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, b, &v_full[s]);
+        uint8_t* qdst = smem + kOffQ + qb * 2 * kTileBytes;
+        mbar_arrive_expect_tx(&q_full[qb], 2 * kTileBytes);
+        tma_load_4d(qdst, &map_q, 0, h, (2 * pair) * kRows, b, &q_full[qb]);
+        tma_load_4d(qdst + kTileBytes, &map_q, 0, h, (2 * pair + 1) * kRows, b, &q_full[qb]);
+        for (int j = 0; j < n_k; ++j, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages && !mbar_wait_bounded(&kv_empty[s], ((g / kStages) - 1) & 1)) {
+            timed_out = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+          tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, b, &k_full[s]);
+          mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+          tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, b, &v_full[s]);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    if (lane == 0 && total > 0) {
       constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
       constexpr uint32_t kIdescPV = idesc_bf16(kRows, kDim, true);
       // Descriptors are built once; a step moves the start-address field
@@ -191,170 +226,183 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
       const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
       constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4, kTile = kTileBytes >> 4;
-      auto issue_qk = [&](int t, int s, int buf) {
+      bool ok = true;
+      // Position of key tile X in the sequence: item li (Q buffer li & 1), tile
+      // j within it, ring slot s, ring lap, S buffer of tile 0. Kept as running
+      // counters (one per tile stream below) so the lane divides nothing.
+      struct Cursor {
+        int X, li, j, s, lap, buf0;
+        __device__ void next(int n_k) {
+          ++X;
+          if (++j == n_k) {
+            j = 0;
+            ++li;
+          }
+          if (++s == kStages) {
+            s = 0;
+            ++lap;
+          }
+          buf0 = buf0 == 0 ? 2 : buf0 - 1;  // (2X) % 3 steps by 2 mod 3
+        }
+      };
+      // S_t(X): query tile t of item li against key tile X. The item's first S
+      // (t = 0, j == 0) waits for its Q; after its last S (t = 1, j == n_k - 1)
+      // the Q buffer is free.
+      auto issue_qk = [&](int t, const Cursor& c) {
+        const int qb = c.li & 1;
+        if (t == 0 && c.j == 0) ok = ok && mbar_wait_bounded(&q_full[qb], (c.li >> 1) & 1);
+        ok = ok && mbar_wait_bounded(&k_full[c.s], c.lap & 1);
+        if (!ok) return;
+        tc_fence_after();
+        const int s = c.s;
+        const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
         // K = 64 in four steps of 16 elements.
 #pragma unroll
         for (int k = 0; k < kDim / 16; ++k)
-          mma_ss(tmem + col_buf(buf), q_desc + t * kTile + k * kStepK,
+          mma_ss(tmem + col_buf(buf), q_desc + (2 * qb + t) * kTile + k * kStepK,
                  k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
+        mma_commit(&s_full[buf]);
+        if (t == 1 && c.j == n_k - 1) mma_commit(&q_empty[qb]);
       };
-      auto issue_pv = [&](int t, int s, int buf, bool accumulate) {
+      // O_t (+)= P_t(J) V(J); an item's first one waits until the previous
+      // item's epilogue has read O_t; the item's last one commits o_final.
+      auto issue_pv = [&](int t, const Cursor& c) {
+        const int J = c.X, li = c.li, j = c.j, s = c.s;
+        if (t == 0) ok = ok && mbar_wait_bounded(&v_full[s], c.lap & 1);
+        ok = ok && mbar_wait_bounded(&p_full[2 * t + (J & 1)], (J >> 1) & 1);
+        if (j == 0 && li > 0) ok = ok && mbar_wait_bounded(&o_free[t], (li - 1) & 1);
+        if (!ok) return;
+        tc_fence_after();
+        const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
         // K = 128 keys in eight steps of 16: P advances 8 TMEM columns (bf16
         // pairs), V two 8-row swizzle atoms.
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k)
           mma_ts(tmem + col_o(t), tmem + col_buf(buf) + k * 8, v_desc + s * kTile + k * kStepV,
-                 kIdescPV, (accumulate || k > 0));
+                 kIdescPV, (j > 0 || k > 0));
+        mma_commit(j + 1 < n_k ? &o_full[t] : &o_final[t]);
       };
-      // P_t(j) V(j) as soon as tile t's softmax has written P_t(j); right
-      // after it, the S that reuses that buffer: S_1(j+1) after P_0(j) V,
-      // S_0(j+2) after P_1(j) V. Each tile's next S is thus computed while
-      // the other tile's softmax runs.
-      bool ok = mbar_wait(q_full, 0, deadline) && mbar_wait(&k_full[0], 0, deadline);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(0, 0, buf_of(0, 0));
-        mma_commit(&s_full[buf_of(0, 0)]);
-        issue_qk(1, 0, buf_of(1, 0));
-        mma_commit(&s_full[buf_of(1, 0)]);
-      }
-      if (ok && n_k > 1) {
-        ok = mbar_wait(&k_full[1 % kStages], (1 / kStages) & 1, deadline);
-        if (ok) {
-          tc_fence_after();
-          issue_qk(0, 1 % kStages, buf_of(0, 1));
-          mma_commit(&s_full[buf_of(0, 1)]);
-        }
-      }
-      for (int j = 0; j < n_k && ok; ++j) {
-        const int sp = j % kStages;
-        ok = mbar_wait(&v_full[sp], (j / kStages) & 1, deadline);
-        if (ok) ok = mbar_wait(&p_full[0 + (j & 1)], (j >> 1) & 1, deadline);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(0, sp, buf_of(0, j), j > 0);
-        mma_commit(j + 1 < n_k ? &o_full[0] : &o_final[0]);
-        if (j + 1 < n_k) {
-          const int s1 = (j + 1) % kStages;
-          ok = mbar_wait(&k_full[s1], ((j + 1) / kStages) & 1, deadline);
-          if (!ok) break;
-          tc_fence_after();
-          issue_qk(1, s1, buf_of(1, j + 1));
-          mma_commit(&s_full[buf_of(1, j + 1)]);
-        }
-        ok = mbar_wait(&p_full[2 + (j & 1)], (j >> 1) & 1, deadline);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(1, sp, buf_of(1, j), j > 0);
-        mma_commit(j + 1 < n_k ? &o_full[1] : &o_final[1]);
-        if (j + 2 < n_k) {
-          const int s2 = (j + 2) % kStages;
-          ok = mbar_wait(&k_full[s2], ((j + 2) / kStages) & 1, deadline);
-          if (!ok) break;
-          tc_fence_after();
-          issue_qk(0, s2, buf_of(0, j + 2));
-          mma_commit(&s_full[buf_of(0, j + 2)]);
-        }
-        if (j + kStages < n_k) mma_commit(&kv_empty[sp]);
+      // Three cursors: the P V tile J, and the S tiles J + 1 and J + 2.
+      Cursor c0{0, 0, 0, 0, 0, 0};
+      Cursor c1 = c0, c2 = c0;
+      issue_qk(0, c0);
+      issue_qk(1, c0);
+      c1.next(n_k);
+      c2.next(n_k);
+      c2.next(n_k);
+      if (total > 1) issue_qk(0, c1);
+      for (int J = 0; J < total && ok; ++J) {
+        issue_pv(0, c0);
+        if (ok && J + 1 < total) issue_qk(1, c1);
+        if (ok) issue_pv(1, c0);
+        if (ok && J + 2 < total) issue_qk(0, c2);
+        if (ok && J + kStages < total) mma_commit(&kv_empty[c0.s]);
+        c0.next(n_k);
+        c1.next(n_k);
+        c2.next(n_k);
       }
       timed_out = !ok;
     }
   } else if (warp >= 4) {
-    // ---------------- softmax (one query row per thread) ----------------
+    // ---------------- softmax and epilogue (one query row per thread) ----------------
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tO = tmem + lane_bits + col_o(t);
-    int buf = buf_of(t, 0);
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_k && ok; ++j) {
-      // This tile's S is the k-th (k = 2j + t): buffer k % 3, the
-      // (k / 3)-th completion of that buffer's barrier.
-      const uint32_t tS = tmem + lane_bits + col_buf(buf);
-      ok = mbar_wait(&s_full[buf], ((2 * j + t) / 3) & 1, deadline);
-      buf = buf >= 1 ? buf - 1 : 2;  // buf_of(t, j + 1) = (buf + 2) % 3
+    for (int li = 0; li < n_items && ok; ++li) {
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_k && ok; ++j) {
+        const int J = li * n_k + j;
+        // This tile's S is the k-th (k = 2J + t): buffer k % 3, the
+        // (k / 3)-th completion of that buffer's barrier.
+        const int buf = buf_of(t, J);
+        const uint32_t tS = tmem + lane_bits + col_buf(buf);
+        ok = mbar_wait_bounded(&s_full[buf], ((2 * J + t) / 3) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const int valid = min(kKeys, p.length - j * kKeys);
+        float v[kKeys];
+        tmem_ld128(tS, v);
+        if (valid < kKeys) {
+          // Keys past the window (the ragged last tile) take no weight.
+#pragma unroll
+          for (int i = 0; i < kKeys; ++i)
+            if (i >= valid) v[i] = -INFINITY;
+        }
+        // Row max as eight short independent chains.
+        float acc[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
+#pragma unroll
+        for (int i = 16; i < kKeys; i += 16)
+#pragma unroll
+          for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
+        const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
+                               fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
+        const float m_tile = mx * p.scale_log2;
+        if (m_tile > m_used + kRescaleThreshold) {
+          if (j > 0) {
+            // O_t must be idle: P_t(j-1) V done. (P_t(j-2) V is: S_t(j), just
+            // completed, was issued after it.)
+            ok = mbar_wait_bounded(&o_full[t], (li * (n_k - 1) + j - 1) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            const float alpha = fast_exp2(m_used - m_tile);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float o[16];
+              tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] *= alpha;
+              tmem_st16f(tO + 16 * c, o);
+            }
+            tmem_wait_st();
+            l *= alpha;
+          }
+          m_used = m_tile;
+        }
+        const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
+        const uint64_t neg_m2 = pack2(-m_used, -m_used);
+        uint64_t sum2[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t packed[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = 64 * half + 2 * i;
+            float x0, x1, p0, p1;
+            unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
+            if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
+              exp2_pair_fma(x0, x1, p0, p1);
+            } else {
+              p0 = fast_exp2(x0);
+              p1 = fast_exp2(x1);
+            }
+            sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
+            packed[i] = bf16x2(p0, p1);
+          }
+          tmem_st32u(tS + 32 * half, packed);
+        }
+        float lo0, hi0;
+        unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
+        l += lo0 + hi0;
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[2 * t + (J & 1)]);
+      }
+      if (!ok) break;
+      // O_t is final after P_t(n_k - 1) V, whose commit has a barrier of its own.
+      ok = mbar_wait_bounded(&o_final[t], li & 1);
       if (!ok) break;
       tc_fence_after();
-      const int valid = min(kKeys, p.length - j * kKeys);
-      float v[kKeys];
-      tmem_ld128(tS, v);
-      if (valid < kKeys) {
-        // Keys past the window (the ragged last tile) take no weight.
-#pragma unroll
-        for (int i = 0; i < kKeys; ++i)
-          if (i >= valid) v[i] = -INFINITY;
-      }
-      // Row max as eight short independent chains.
-      float acc[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
-#pragma unroll
-      for (int i = 16; i < kKeys; i += 16)
-#pragma unroll
-        for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
-      const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
-                             fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
-      const float m_tile = mx * p.scale_log2;
-      if (m_tile > m_used + kRescaleThreshold) {
-        if (j > 0) {
-          // O_t must be idle: P_t(j-1) V done. (P_t(j-2) V is: S_t(j), just
-          // completed, was issued after it.)
-          ok = mbar_wait(&o_full[t], (j - 1) & 1, deadline);
-          if (!ok) break;
-          tc_fence_after();
-          const float alpha = fast_exp2(m_used - m_tile);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float o[16];
-            tmem_ld16(tO + 16 * c, o);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] *= alpha;
-            tmem_st16f(tO + 16 * c, o);
-          }
-          tmem_wait_st();
-          l *= alpha;
-        }
-        m_used = m_tile;
-      }
-      const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
-      const uint64_t neg_m2 = pack2(-m_used, -m_used);
-      uint64_t sum2[4];
-#pragma unroll
-      for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t packed[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = 64 * half + 2 * i;
-          float x0, x1, p0, p1;
-          unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
-          if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
-            exp2_pair_fma(x0, x1, p0, p1);
-          } else {
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
-          }
-          sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
-          packed[i] = bf16x2(p0, p1);
-        }
-        tmem_st32u(tS + 32 * half, packed);
-      }
-      float lo0, hi0;
-      unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
-      l += lo0 + hi0;
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[2 * t + (j & 1)]);
-    }
-    // O_t is final after P_t(n_k - 1) V, whose commit has a barrier of its own.
-    if (ok) ok = mbar_wait(&o_final[t], 0, deadline);
-    timed_out = !ok;
-    if (ok) {
-      tc_fence_after();
+      const int index = item_index(li);
+      const int pair = index % p.q_pairs, h = (index / p.q_pairs) % p.heads;
+      const int b = index / (p.q_pairs * p.heads);
       const int row = (2 * pair + t) * kRows + row_in_tile;
       const float inv = 1.f / l;
       __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + b * p.sb + h * p.sh +
@@ -375,7 +423,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // O_t has been read: the next item's first P V may overwrite it.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[t]);
     }
+    timed_out = !ok;
   }
   if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
   tc_fence_before();
@@ -433,11 +486,13 @@ int encoder_attention_tc(int batch, int heads, int length, const void* q, const 
       return rc;
     prepared_device = device;
   }
-  TcParams p{out, sb, sh, ss, length, (length + 2 * kRows - 1) / (2 * kRows),
+  const int q_pairs = (length + 2 * kRows - 1) / (2 * kRows);
+  TcParams p{out, sb, sh, ss, length, q_pairs, heads, q_pairs * heads * batch,
              scale * 1.4426950408889634f, status};
-  dim3 grid(p.q_pairs, heads, batch);
-  encoder_attention_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, p);
-  return check_cuda(cudaGetLastError(), "encoder attention (tensor core) launch");
+  // Persistent: one CTA per SM (512 TMEM columns each), at most one per item.
+  const int ctas = p.items < sm_count() ? p.items : sm_count();
+  return launch_pdl(encoder_attention_tc_kernel, dim3(ctas), dim3(kThreads), kSmemBytes, stream,
+                    "encoder attention (tensor core) launch", mq, mk, mv, p);
 }
 
 }  // namespace asrback
