@@ -60,6 +60,22 @@ SIGNATURES: dict[str, tuple[list, object]] = {
          _c_f, _c_p, _c_size, _c_p, _c_p],
         _c_int,
     ),
+    "asrback_whisper_self_attention_prefix": (
+        [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_p, _c_i64, _c_i64,
+         _c_p, _c_p, _c_i64, _c_i64,
+         _c_p, _c_i64, _c_i64,
+         _c_f, _c_p, _c_size, _c_p, _c_p],
+        _c_int,
+    ),
+    "asrback_whisper_cross_attention_prefix": (
+        [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_p, _c_i64, _c_i64,
+         _c_p, _c_p, _c_i64, _c_i64,
+         _c_p, _c_i64, _c_i64,
+         _c_f, _c_p, _c_size, _c_p, _c_p],
+        _c_int,
+    ),
     "asrback_whisper_cross_attention_step_noalloc": (
         [_c_int, _c_int, _c_int, _c_int, _c_int,
          _c_p, _c_i64, _c_i64,

@@ -11,6 +11,10 @@ Reference call sites (asrback project paths):
 - :func:`whisper_self_attention_step`: ``DecoderLayer.forward`` step branch,
   ``src/asrback/models/whisper.py:222-237`` (``scatter_`` then masked attend);
 - :func:`whisper_cross_attention_step`: ``whisper.py:239-240``;
+- :func:`whisper_self_attention_prefix` and
+  :func:`whisper_cross_attention_prefix`: the same two calls in the eager
+  branch (``whisper.py:228-236``, ``:239-240``) for a prompt pass of P tokens
+  per window with ``length == P``;
 - :func:`qwen3_attention_step`: ``TextAttention.step``,
   ``src/asrback/models/qwen3_asr.py:392-432`` with ``_project`` (``:366-372``);
 - :func:`whisper_encoder_attention`: ``MultiHeadAttention.forward``,
@@ -230,6 +234,72 @@ def whisper_cross_attention_step(query: Tensor, key_cache: Tensor, value_cache: 
         ws, ws_bytes, state.status.data_ptr(), _stream(query.device),
     )
     return out
+
+
+def _prefix_query(t: Tensor, name: str) -> tuple[Tensor, int]:
+    """A ``(B, H, P, D)`` query view and its token stride, with the (window,
+    token) rows evenly spaced (row ``b*P + t`` at ``(b*P + t) * stride``), as
+    ``_split_heads`` of a ``(B, P, W)`` projection lays them out. Other
+    layouts are copied into that one first."""
+    if t.dim() != 4 or t.stride(-1) != 1:
+        raise ValueError(f"asrback_b200: {name} must be (batch, heads, tokens, head_dim) with unit last stride")
+    batch, _, tokens, _ = t.shape
+    stride = t.stride(2) if tokens > 1 else t.stride(0)
+    if batch > 1 and tokens > 1 and t.stride(0) != tokens * stride:
+        t = t.transpose(1, 2).contiguous().transpose(1, 2)
+        stride = t.stride(2)
+    return t, stride
+
+
+def _prefix_call(name: str, query: Tensor, key_cache: Tensor, value_cache: Tensor, length: int,
+                 max_keys: int, scale: float | None) -> Tensor:
+    query, token_stride = _prefix_query(query, "query")
+    key_cache, value_cache = _cache(key_cache, "key_cache"), _cache(value_cache, "value_cache")
+    dtype = _dtype_code(query, key_cache, value_cache)
+    batch, heads, tokens, head_dim = query.shape
+    if key_cache.shape[:2] != (batch, heads) or key_cache.shape[3] != head_dim:
+        raise ValueError(f"asrback_b200: cache {tuple(key_cache.shape)} does not match query {tuple(query.shape)}")
+    if value_cache.shape != key_cache.shape or value_cache.stride() != key_cache.stride():
+        raise ValueError("asrback_b200: key and value caches differ in shape or strides")
+    out = torch.empty((batch, tokens, heads * head_dim), dtype=query.dtype, device=query.device)
+    state = _state(query.device)
+    ws, ws_bytes = _workspace(state, batch * tokens, heads, head_dim, max_keys)
+    _native.call(
+        name,
+        dtype, batch, tokens, heads, head_dim, length,
+        query.data_ptr(), token_stride, query.stride(1),
+        key_cache.data_ptr(), value_cache.data_ptr(), key_cache.stride(0), key_cache.stride(1),
+        out.data_ptr(), heads * head_dim, head_dim,
+        scale if scale is not None else 1.0 / math.sqrt(head_dim),
+        ws, ws_bytes, state.status.data_ptr(), _stream(query.device),
+    )
+    return out
+
+
+def whisper_self_attention_prefix(query: Tensor, key_cache: Tensor, value_cache: Tensor,
+                                  scale: float | None = None) -> Tensor:
+    """Causal self-attention of a prompt pass: token ``t`` of each window
+    attends to cache keys ``0..t``, which the caller has written (the
+    reference's ``index_copy_``, ``whisper.py:231-232``); the caches are read
+    only.
+
+    ``query`` ``(B, H, P, D)`` (the ``_split_heads`` view); caches
+    ``(B, H, L, D)`` with ``L >= P``. Returns ``(B, P, H*D)``, the layout
+    ``attend`` hands to ``out_proj``.
+    """
+    tokens = query.shape[2] if query.dim() == 4 else 0
+    return _prefix_call("asrback_whisper_self_attention_prefix", query, key_cache, value_cache,
+                        key_cache.shape[2], tokens, scale)
+
+
+def whisper_cross_attention_prefix(query: Tensor, key_cache: Tensor, value_cache: Tensor,
+                                   scale: float | None = None) -> Tensor:
+    """Unmasked attention of every prompt token over its window's encoder
+    keys. ``query`` ``(B, H, P, D)``; caches ``(B, H, S, D)``. Returns
+    ``(B, P, H*D)``."""
+    length = key_cache.shape[2] if key_cache.dim() == 4 else 0
+    return _prefix_call("asrback_whisper_cross_attention_prefix", query, key_cache, value_cache,
+                        length, length, scale)
 
 
 def qwen3_attention_step(qkv: Tensor, q_norm_weight: Tensor, k_norm_weight: Tensor, eps: float,

@@ -77,7 +77,7 @@ int asrback_selftest_bounded_wait(int64_t budget_ns, int32_t* status, void* stre
 }
 
 
-int asrback_abi_version(void) { return (1 << 16) | 2; }
+int asrback_abi_version(void) { return (1 << 16) | 3; }
 
 const char* asrback_last_error(void) { return asrback::g_last_error; }
 

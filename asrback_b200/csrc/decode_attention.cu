@@ -9,6 +9,11 @@
 //                   rotate-half RoPE (qwen3_asr.py:366-372) in the prologue,
 //                   the key/value write (:409-411), then grouped-query
 //                   attention, query head h reading key/value head h / QPK.
+// The Whisper modes also serve the eager prompt pass (whisper.py:228-240 with
+// length == P, from _prefill and _detect_languages): each of a window's P
+// tokens is a query row of its own that reads the window's cache row; self
+// attention then reads keys 0..t for token t and writes nothing (the caller
+// has already written the pass's keys/values).
 //
 // Work split. A CTA owns one row b, one group of G key/value heads and one
 // chunk of key positions (a "split"). Its keys stream through shared memory
@@ -59,6 +64,12 @@ struct DecodeParams {
   void* v_cache;
   int64_t c_sb, c_sh, c_sp;
   const int64_t* positions;  // (batch,) or null for a fixed key count
+  // Prefix calls (Whisper eager branch), tokens_per_row > 0: query row r is
+  // token t = r % tokens_per_row of cache row r / tokens_per_row. Self
+  // attention then reads the cache's keys 0..t (all of them written before
+  // the launch) and writes none; positions and k_new/v_new are unused.
+  // Zero: one query row per cache row (the step calls).
+  int tokens_per_row;
   int length;                // cross: key count; self/Qwen3: cache view length
   void* out;                 // (b, q head h, d) at out[b*o_sb + h*o_sh + d]
   int64_t o_sb, o_sh;
@@ -200,7 +211,9 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
 
   const int split = blockIdx.x;
   const int grp = blockIdx.y;
-  const int b = blockIdx.z;
+  const int b = blockIdx.z;  // query row
+  const bool prefix = p.tokens_per_row > 0;
+  const int cb = prefix ? b / p.tokens_per_row : b;  // cache row
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -211,11 +224,13 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   griddep_wait();
   griddep_launch_dependents();
 
-  // Keys of this row: n_cached read from the cache, plus (self/Qwen3) the
-  // step's own key at index `pos`.
+  // Keys of this row: n_cached read from the cache, plus (self/Qwen3 steps)
+  // the step's own key at index `pos`.
   int pos = 0, n_cached, n_total;
   if constexpr (MODE == kWhisperCross) {
     n_cached = n_total = p.length;
+  } else if (MODE == kWhisperSelf && prefix) {
+    n_cached = n_total = b % p.tokens_per_row + 1;
   } else {
     const int64_t given = p.positions[b];
     if (given < 0 || given >= p.length) {
@@ -242,7 +257,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   const int k0 = split * per;
   const int k1 = min(k0 + per, n_cached);
   const int n_tiles = k1 > k0 ? (k1 - k0 + TP - 1) / TP : 0;
-  const bool has_own_key = MODE != kWhisperCross && split == active - 1;
+  const bool has_own_key = MODE != kWhisperCross && !prefix && split == active - 1;
   const uint64_t deadline = global_timer_ns() + kWaitBudgetNs;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -259,8 +274,8 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   __syncthreads();
 
   const int64_t head0 = (int64_t)grp * G;
-  const T* kbase = static_cast<const T*>(p.k_cache) + b * p.c_sb + head0 * p.c_sh;
-  const T* vbase = static_cast<const T*>(p.v_cache) + b * p.c_sb + head0 * p.c_sh;
+  const T* kbase = static_cast<const T*>(p.k_cache) + cb * p.c_sb + head0 * p.c_sh;
+  const T* vbase = static_cast<const T*>(p.v_cache) + cb * p.c_sb + head0 * p.c_sh;
 
   if (warp == C::CWARPS) {
     // Producer warp. When a tile's rows are contiguous in the cache (each
@@ -353,7 +368,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   if constexpr (MODE != kWhisperCross) {
     if (has_own_key) {
       if (owner) {
-        const int64_t off = b * p.c_sb + (int64_t)kv_head * p.c_sh + (int64_t)pos * p.c_sp;
+        const int64_t off = cb * p.c_sb + (int64_t)kv_head * p.c_sh + (int64_t)pos * p.c_sp;
         S::store(static_cast<T*>(p.k_cache) + off, c, own_k);
         S::store(static_cast<T*>(p.v_cache) + off, c, own_v);
       }
@@ -811,6 +826,87 @@ int asrback_whisper_self_attention_step(
   int rc = dtype == ASRBACK_BF16
                ? run<WhisperSelfBf16>(p, batch, units, 1, workspace, workspace_bytes, s)
                : run<WhisperSelfF32>(p, batch, units, 1, workspace, workspace_bytes, s);
+  return rc ? rc : ok();
+}
+
+int asrback_whisper_self_attention_prefix(
+    int dtype, int windows, int tokens, int heads, int head_dim, int cache_length,
+    const void* query, int64_t q_stride_token, int64_t q_stride_head, const void* key_cache,
+    const void* value_cache, int64_t cache_stride_batch, int64_t cache_stride_head, void* out,
+    int64_t out_stride_token, int64_t out_stride_head, float scale, void* workspace,
+    size_t workspace_bytes, int32_t* status, void* stream) {
+  if (windows < 1 || tokens < 1 || (int64_t)windows * tokens > 65535)
+    return fail(ASRBACK_ERR_ARGUMENT, "windows (%d) x tokens (%d) must be in [1, 65535]", windows,
+                tokens);
+  if (tokens > cache_length)
+    return fail(ASRBACK_ERR_ARGUMENT, "tokens (%d) exceed the cache length (%d)", tokens,
+                cache_length);
+  if (int rc = whisper_common(dtype, windows, heads, head_dim, cache_length, query, q_stride_token,
+                              q_stride_head, key_cache, value_cache, cache_stride_batch,
+                              cache_stride_head, out, out_stride_token, out_stride_head))
+    return rc;
+  DecodeParams p{};
+  p.q = query;
+  p.q_sb = q_stride_token;
+  p.q_sh = q_stride_head;
+  p.k_cache = const_cast<void*>(key_cache);
+  p.v_cache = const_cast<void*>(value_cache);
+  p.c_sb = cache_stride_batch;
+  p.c_sh = cache_stride_head;
+  p.c_sp = head_dim;
+  p.tokens_per_row = tokens;
+  p.length = tokens;
+  p.out = out;
+  p.o_sb = out_stride_token;
+  p.o_sh = out_stride_head;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.groups = heads;
+  p.status = status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rows = windows * tokens;
+  const int units = rows * heads;
+  int rc = dtype == ASRBACK_BF16
+               ? run<WhisperSelfBf16>(p, rows, units, 1, workspace, workspace_bytes, s)
+               : run<WhisperSelfF32>(p, rows, units, 1, workspace, workspace_bytes, s);
+  return rc ? rc : ok();
+}
+
+int asrback_whisper_cross_attention_prefix(
+    int dtype, int windows, int tokens, int heads, int head_dim, int length, const void* query,
+    int64_t q_stride_token, int64_t q_stride_head, const void* key_cache, const void* value_cache,
+    int64_t cache_stride_batch, int64_t cache_stride_head, void* out, int64_t out_stride_token,
+    int64_t out_stride_head, float scale, void* workspace, size_t workspace_bytes,
+    int32_t* status, void* stream) {
+  if (windows < 1 || tokens < 1 || (int64_t)windows * tokens > 65535)
+    return fail(ASRBACK_ERR_ARGUMENT, "windows (%d) x tokens (%d) must be in [1, 65535]", windows,
+                tokens);
+  if (int rc = whisper_common(dtype, windows, heads, head_dim, length, query, q_stride_token,
+                              q_stride_head, key_cache, value_cache, cache_stride_batch,
+                              cache_stride_head, out, out_stride_token, out_stride_head))
+    return rc;
+  DecodeParams p{};
+  p.q = query;
+  p.q_sb = q_stride_token;
+  p.q_sh = q_stride_head;
+  p.k_cache = const_cast<void*>(key_cache);
+  p.v_cache = const_cast<void*>(value_cache);
+  p.c_sb = cache_stride_batch;
+  p.c_sh = cache_stride_head;
+  p.c_sp = head_dim;
+  p.tokens_per_row = tokens;
+  p.length = length;
+  p.out = out;
+  p.o_sb = out_stride_token;
+  p.o_sh = out_stride_head;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.groups = heads;
+  p.status = status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rows = windows * tokens;
+  const int units = rows * heads;
+  int rc = dtype == ASRBACK_BF16
+               ? run<WhisperCrossBf16>(p, rows, units, 1, workspace, workspace_bytes, s)
+               : run<WhisperCrossF32>(p, rows, units, 1, workspace, workspace_bytes, s);
   return rc ? rc : ok();
 }
 

@@ -12,7 +12,11 @@ Patched call sites (asrback project paths):
 - ``whisper.DecoderLayer.forward`` (``src/asrback/models/whisper.py:212-241``):
   the fixed-shape step branch (``length is None``) runs the self-attention
   with its key/value write as one kernel and the cross-attention as another;
-  the eager prefix branch (``length`` given) is left to the original method;
+  the eager branch (``length`` given) with ``length`` equal to its token count
+  (the prompt pass and language detection, ``whisper.py:847-849``,
+  ``:979-981``) keeps the reference's ``index_copy_`` and runs causal
+  self-attention and cross-attention for every prompt token on the same
+  kernels; any other eager call goes to the original method;
 - ``whisper.MultiHeadAttention.forward`` (``whisper.py:108-110``): the
   encoder's unmasked self-attention;
 - ``whisper.WhisperForConditionalGeneration.set_encoder_output``
@@ -71,18 +75,31 @@ def uninstall() -> None:
 
 def _whisper_decoder_layer_forward(original):
     def forward(self, x, cache, positions, length, mask):
-        if length is not None:
+        prefix = length is not None
+        if prefix and (length != x.shape[1] or mask is not None):
             return original(self, x, cache, positions, length, mask)
         self_keys, self_values, cross_keys, cross_values = cache
         hidden = self.self_attn_layer_norm(x)
         query = self.self_attn._split_heads(self.self_attn.q_proj(hidden))
         key, value = self.self_attn.project_key_value(hidden)
-        out = attention.whisper_self_attention_step(query, key, value, self_keys, self_values,
-                                                    positions)
+        if prefix:
+            # whisper.py:229-233: the tokens' keys/values at the shared
+            # positions; token t then attends to keys 0..t of the first
+            # `length` positions (is_causal).
+            self_keys.index_copy_(2, positions, key)
+            self_values.index_copy_(2, positions, value)
+            out = attention.whisper_self_attention_prefix(
+                query, self_keys[:, :, :length], self_values[:, :, :length])
+        else:
+            out = attention.whisper_self_attention_step(query, key, value, self_keys, self_values,
+                                                        positions)
         x = x + self.self_attn.out_proj(out)
         hidden = self.encoder_attn_layer_norm(x)
         query = self.encoder_attn._split_heads(self.encoder_attn.q_proj(hidden))
-        out = attention.whisper_cross_attention_step(query, cross_keys, cross_values)
+        if prefix:
+            out = attention.whisper_cross_attention_prefix(query, cross_keys, cross_values)
+        else:
+            out = attention.whisper_cross_attention_step(query, cross_keys, cross_values)
         x = x + self.encoder_attn.out_proj(out)
         return x + self.fc2(F.gelu(self.fc1(self.final_layer_norm(x))))
 

@@ -9,11 +9,13 @@ reference state dict loads unchanged), the same cache layout
 What differs is what runs: the fixed-shape step's self-attention (key/value
 write plus masked attention, ``whisper.py:222-237``) is one kernel that reads
 only each row's written positions, the cross-attention (``:239-240``) another,
-and the encoder's attention (``:108-110``) a third. Linear layers, norms and
-embeddings stay torch (cuBLAS), as in the reference.
-
-The eager multi-token prefix pass (``decode(..., length=n)``) and language
-detection are not part of this build; a prefix is fed one token per step.
+and the encoder's attention (``:108-110``) a third. The eager prompt pass
+(``decode(tokens, positions[:P], cache, length=P)``, used by the prefill and
+by language detection) writes its keys/values with ``index_copy_`` as the
+reference does (``whisper.py:229-233``) and runs causal self-attention and
+cross-attention for all P tokens of each window on the same kernel, one
+query row per (window, token). Linear layers, norms and embeddings stay
+torch (cuBLAS), as in the reference.
 """
 
 from __future__ import annotations
@@ -97,6 +99,27 @@ class MultiHeadAttention(nn.Module):
         """One decoder step of cross-attention over the window's encoder keys."""
         query = self._split_heads(self.q_proj(x))
         return self.out_proj(ops.whisper_cross_attention_step(query, key_cache, value_cache))
+
+    def prefix_self(self, x: Tensor, key_cache: Tensor, value_cache: Tensor,
+                    positions: Tensor) -> Tensor:
+        """Self-attention of a prompt pass, ``x`` ``(B, P, W)``: the tokens'
+        keys/values go into the caches at ``positions`` (``index_copy_``,
+        ``whisper.py:231-232``) and token ``t`` attends causally to keys
+        ``0..t`` of the first P positions (``is_causal`` over
+        ``cache[:, :, :P]``)."""
+        query = self._split_heads(self.q_proj(x))
+        key, value = self.project_key_value(x)
+        key_cache.index_copy_(2, positions, key)
+        value_cache.index_copy_(2, positions, value)
+        tokens = x.shape[1]
+        out = ops.whisper_self_attention_prefix(query, key_cache[:, :, :tokens],
+                                                value_cache[:, :, :tokens])
+        return self.out_proj(out)
+
+    def prefix_cross(self, x: Tensor, key_cache: Tensor, value_cache: Tensor) -> Tensor:
+        """Cross-attention of a prompt pass over the window's encoder keys."""
+        query = self._split_heads(self.q_proj(x))
+        return self.out_proj(ops.whisper_cross_attention_prefix(query, key_cache, value_cache))
 
 
 class EncoderLayer(nn.Module):
@@ -194,13 +217,27 @@ class DecoderLayer(nn.Module):
         self.final_layer_norm = nn.LayerNorm(width)
 
     def forward(self, x: Tensor, cache: tuple[Tensor, Tensor, Tensor, Tensor],
-                positions: Tensor) -> Tensor:
-        """One token per row (``x`` ``(B, 1, W)``) at ``positions`` ``(B,)``."""
+                positions: Tensor, length: int | None = None) -> Tensor:
+        """The step (``length`` None): one token per row (``x`` ``(B, 1, W)``)
+        at ``positions`` ``(B,)``. The prompt pass: P tokens per row at
+        ``positions`` ``(P,)`` with ``length == P``."""
         self_keys, self_values, cross_keys, cross_values = cache
-        x = x + self.self_attn.step_self(self.self_attn_layer_norm(x), self_keys, self_values,
-                                         positions)
-        x = x + self.encoder_attn.step_cross(self.encoder_attn_layer_norm(x), cross_keys,
-                                             cross_values)
+        if length is None:
+            x = x + self.self_attn.step_self(self.self_attn_layer_norm(x), self_keys,
+                                             self_values, positions)
+            x = x + self.encoder_attn.step_cross(self.encoder_attn_layer_norm(x), cross_keys,
+                                                 cross_values)
+        else:
+            if length != x.shape[1]:
+                raise NotImplementedError(
+                    f"asrback_b200 runs the eager pass with length == tokens (the form the "
+                    f"prompt pass and language detection use); got length {length} for "
+                    f"{x.shape[1]} tokens"
+                )
+            x = x + self.self_attn.prefix_self(self.self_attn_layer_norm(x), self_keys,
+                                               self_values, positions)
+            x = x + self.encoder_attn.prefix_cross(self.encoder_attn_layer_norm(x), cross_keys,
+                                                   cross_values)
         return x + self.fc2(F.gelu(self.fc1(self.final_layer_norm(x))))
 
 
@@ -215,18 +252,18 @@ class WhisperDecoder(nn.Module):
 
     def forward(self, tokens: Tensor, positions: Tensor, cache: DecoderCache,
                 length: int | None = None) -> Tensor:
-        """Hidden states for ``tokens`` ``(B, 1)`` at ``positions`` ``(B,)``.
-        Keys past each row's position are never read, so no mask is built."""
-        if length is not None:
-            raise NotImplementedError(
-                "asrback_b200 runs the fixed-shape decoder step only; feed a prefix one "
-                "token per step"
-            )
-        x = self.embed_tokens(tokens) + self.embed_positions(positions)[:, None]
+        """Hidden states for ``tokens`` ``(B, 1)`` at ``positions`` ``(B,)``
+        (the step; keys past each row's position are never read, so no mask is
+        built), or, with ``length`` given, for ``tokens`` ``(B, P)`` at the
+        shared ``positions`` ``(P,)`` (the prompt pass, ``whisper.py:265-266``)."""
+        if length is None:
+            x = self.embed_tokens(tokens) + self.embed_positions(positions)[:, None]
+        else:
+            x = self.embed_tokens(tokens) + self.embed_positions(positions)
         for index, layer in enumerate(self.layers):
             layer_cache = (cache.self_keys[index], cache.self_values[index],
                            cache.cross_keys[index], cache.cross_values[index])
-            x = layer(x, layer_cache, positions)
+            x = layer(x, layer_cache, positions, length)
         return self.layer_norm(x)
 
 

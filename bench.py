@@ -28,7 +28,10 @@ Other workloads (``--workload``):
                    argmax, log-softmax, state update) for 64 rows; unit: tokens;
   whisper-cross-kv set_encoder_output for 32 windows: the 4 decoder layers'
                    cross-attention keys/values projected into the cache; unit:
-                   windows.
+                   windows;
+  whisper-prefix   the prompt pass's attention for 32 windows of 4 prompt
+                   tokens (decode with length=P): causal self-attention and
+                   cross-attention over 1500 frames, 4 layers; unit: windows.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
                     [--workload NAME] [--batch B]
@@ -66,7 +69,8 @@ def parse_args():
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--workload", choices=("whisper-decode", "whisper-encoder", "qwen3-decode",
                                                "qwen3-prefill", "qwen3-audio", "whisper-step",
-                                               "qwen3-step", "whisper-cross-kv"),
+                                               "qwen3-step", "whisper-cross-kv",
+                                               "whisper-prefix"),
                         default="whisper-decode")
     parser.add_argument("--batch", type=int, default=None,
                         help="override the workload's batch (small profiling cases)")
@@ -992,6 +996,153 @@ class WhisperCrossKV:
                           f"numpy oracle, {elapsed:.1f} s, scaled by 1/4 layers"}
 
 
+class WhisperPrefix:
+    """The prompt pass of BASELINE config 3's windows at admission (SURVEY
+    8(f) rank 2): `decode(tokens, positions[:P], cache, length=P)`
+    (whisper.py:847-849) for 32 windows sharing the 4-token start sequence
+    (windows queued together share a prefix length), the attention of its 4
+    decoder layers: causal self-attention over the P written keys
+    (whisper.py:228-236) and cross-attention of every prompt token over the
+    window's 1500 encoder keys (:239-240)."""
+
+    name = "whisper-prefix"
+    metric = ("prompt-pass attention windows/s/GPU (Whisper large-v3-turbo decoder, 32 windows x "
+              "4 prompt tokens, self + cross over 1500 frames, 4 layers, bf16); cross-attention "
+              "GB/s")
+    unit = "windows/s"
+    bound = "hbm"
+    reference_in_graph = False
+    layers, heads, dim, frames, bucket = 4, 20, 64, 1500, 448
+    profile = "whisper_prefix_b32_bf16.md"
+
+    def __init__(self, batch: int | None, tokens: int = 4):
+        self.batch = batch or 32
+        self.tokens = tokens
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": "Whisper large-v3-turbo prompt pass attention (decode with length=P, "
+                        "SURVEY 8(f) rank 2 row)",
+            "layers": self.layers, "heads": self.heads, "head_dim": self.dim,
+            "prompt_tokens": self.tokens, "frames": self.frames,
+            "windows_per_gpu": self.batch, "global_batch": self.batch * world,
+            "step": "per layer: causal self-attention of P tokens + cross-attention of P tokens",
+            "inputs": "queries and caches N(0, 1) bf16; cross caches 4 x 246 MB (> L2)",
+            "parallelism": f"replicas x{world} (no collective)",
+        }
+
+    def units_per_step(self) -> int:
+        return self.batch
+
+    def cross_bytes(self) -> float:
+        kv = 2.0 * self.batch * self.heads * self.frames * self.dim * 2
+        rows = 2.0 * self.batch * self.tokens * self.heads * self.dim * 2
+        return kv + rows
+
+    def self_bytes(self) -> float:
+        return 4.0 * self.batch * self.tokens * self.heads * self.dim * 2
+
+    def setup(self, torch, device, seed: int, total: int) -> None:
+        gen = torch.Generator(device=device).manual_seed(seed)
+        dtype, b, h, p, d = torch.bfloat16, self.batch, self.heads, self.tokens, self.dim
+
+        def rand(*shape):
+            return torch.randn(shape, generator=gen, device=device).to(dtype)
+
+        self.self_q = rand(b, p, h * d)
+        self.cross_q = rand(b, p, h * d)
+        self.self_k = rand(self.layers, b, h, self.bucket, d)
+        self.self_v = rand(self.layers, b, h, self.bucket, d)
+        self.cross_k = rand(self.layers, b, h, self.frames, d)
+        self.cross_v = rand(self.layers, b, h, self.frames, d)
+        self.outputs: list = [None] * (2 * self.layers)
+
+    def _query(self, x):
+        b, p, _ = x.shape
+        return x.view(b, p, self.heads, self.dim).transpose(1, 2)
+
+    def attend_self(self, layer: int):
+        from asrback_b200 import attention
+
+        layer %= self.layers
+        p = self.tokens
+        return attention.whisper_self_attention_prefix(
+            self._query(self.self_q), self.self_k[layer][:, :, :p], self.self_v[layer][:, :, :p])
+
+    def attend_cross(self, layer: int):
+        from asrback_b200 import attention
+
+        layer %= self.layers
+        return attention.whisper_cross_attention_prefix(
+            self._query(self.cross_q), self.cross_k[layer], self.cross_v[layer])
+
+    def step(self) -> None:
+        for layer in range(self.layers):
+            self.outputs[2 * layer] = self.attend_self(layer)
+            self.outputs[2 * layer + 1] = self.attend_cross(layer)
+
+    def launches_per_step(self) -> int:
+        return 2 * self.layers
+
+    def refresh(self, t: int) -> None:
+        pass
+
+    def host_step_inputs(self, torch, first: int, count: int):
+        pairs = []
+        for dev in (self.self_q, self.cross_q):
+            host = torch.empty(dev.shape, dtype=dev.dtype, pin_memory=True)
+            host.copy_(dev.cpu())
+            pairs.append((host[None].expand(count, *host.shape), dev))
+        return pairs
+
+    def kernels(self, t: int):
+        return [("cross_prefix", self.attend_cross, self.cross_bytes()),
+                ("self_prefix", self.attend_self, self.self_bytes())]
+
+    def step_work(self, first: int, count: int) -> float:
+        return (self.cross_bytes() + self.self_bytes()) * self.layers * count
+
+    def torch_reference_step(self, torch):
+        """The reference's eager branch calls on the same tensors:
+        `attend`'s SDPA with is_causal over the first P cache positions, then
+        SDPA over the cross cache (whisper.py:233-240, :102-104)."""
+        import torch.nn.functional as F
+
+        p = self.tokens
+
+        def run():
+            for layer in range(self.layers):
+                F.scaled_dot_product_attention(
+                    self._query(self.self_q), self.self_k[layer][:, :, :p],
+                    self.self_v[layer][:, :, :p], is_causal=p > 1)
+                F.scaled_dot_product_attention(
+                    self._query(self.cross_q), self.cross_k[layer], self.cross_v[layer])
+        return run
+
+    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+        from oracle import attention as oracle
+
+        rng = np.random.default_rng(seed)
+        h, p, d = self.heads, self.tokens, self.dim
+        q = rng.standard_normal((1, h, p, d), dtype=np.float32)
+        k = rng.standard_normal((1, h, p, d), dtype=np.float32)
+        ck = rng.standard_normal((1, h, self.frames, d), dtype=np.float32)
+        cv = rng.standard_normal((1, h, self.frames, d), dtype=np.float32)
+        mask = np.arange(p)[None, :] <= np.arange(p)[:, None]
+
+        def one(_t, _p):
+            oracle.sdpa(q, k, k, mask, compute=np.float32)
+            oracle.whisper_cross_attention_prefix(q, ck, cv, compute=np.float32)
+
+        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
+        layers_done = done * threads
+        return {"value": layers_done / elapsed / self.layers, "unit": self.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{layers_done} window-layers (20 heads, {p} prompt tokens, self + cross "
+                          f"over 1500 frames), float32 numpy oracle, {elapsed:.1f} s, scaled by "
+                          f"1/4 layers"}
+
+
 class WhisperGreedyStep:
     """The step epilogue after the decoder: logits against
     the tied embedding, greedy `_choose` with the suppress mask and the state
@@ -1152,7 +1303,7 @@ class Qwen3GreedyStep(WhisperGreedyStep):
 
 WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode, Qwen3Prefill,
                                        Qwen3AudioWindows, WhisperGreedyStep, Qwen3GreedyStep,
-                                       WhisperCrossKV)}
+                                       WhisperCrossKV, WhisperPrefix)}
 
 
 # ------------------------------------------------------------------ arms ----
@@ -1365,7 +1516,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         # Short runs of the other workloads, for context.
         extras = {}
         for name in ("whisper-encoder", "qwen3-decode", "qwen3-prefill", "qwen3-audio",
-                     "whisper-step", "qwen3-step", "whisper-cross-kv"):
+                     "whisper-step", "qwen3-step", "whisper-cross-kv", "whisper-prefix"):
             del work
             torch.cuda.empty_cache()
             work = WORKLOADS[name](None)

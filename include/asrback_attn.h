@@ -21,6 +21,12 @@
  *     MultiHeadAttention.attend with the step mask of whisper.py:262-264);
  *   - asrback_whisper_cross_attention_step replaces the cross-attention call
  *     whisper.py:239-240 (attend over the window's encoder keys, no mask);
+ *   - asrback_whisper_self_attention_prefix and
+ *     asrback_whisper_cross_attention_prefix replace the same two calls in
+ *     DecoderLayer.forward's eager branch (whisper.py:228-236, 239-240) as
+ *     the prompt pass (_prefill, whisper.py:847-849) and language detection
+ *     (_detect_languages, whisper.py:979-981) use it: P tokens per window at
+ *     positions 0..P-1, length == P, causal self-attention;
  *   - asrback_qwen3_attention_step replaces TextAttention.step between
  *     qkv_proj and o_proj, src/asrback/models/qwen3_asr.py:392-432, with
  *     _project (qwen3_asr.py:366-372: per-head RMSNorm of q and k, rotate-half
@@ -131,6 +137,48 @@ ASRBACK_API int asrback_whisper_cross_attention_step(
     const void* key_cache, const void* value_cache,
     int64_t cache_stride_batch, int64_t cache_stride_head,
     void* out, int64_t out_stride_batch, int64_t out_stride_head,
+    float scale, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Whisper decoder self-attention for a prompt pass: `tokens` (P) query tokens
+ * per window, token t attending causally to cache keys 0..t. This is the
+ * eager branch of DecoderLayer.forward (whisper.py:228-236) with length == P
+ * and positions 0..P-1, the only form its callers use: the caller has already
+ * written the pass's keys/values into the cache at positions 0..P-1
+ * (index_copy_, whisper.py:231-232); this call reads them and writes nothing
+ * to the cache.
+ *
+ * query       (windows*tokens, heads, head_dim): window w's token t at row
+ *             r = w*tokens + t, query[r*q_stride_token + h*q_stride_head + d]
+ * key_cache,  (windows, heads, cache_length, head_dim) as for the step, with
+ * value_cache   cache_length >= tokens
+ * out         (windows*tokens, heads, head_dim), strides out_stride_*
+ * workspace   asrback_decode_workspace_bytes(windows*tokens, heads, head_dim,
+ *             tokens) bytes
+ * windows*tokens <= 65535; other conditions as for the step.
+ */
+ASRBACK_API int asrback_whisper_self_attention_prefix(
+    int dtype, int windows, int tokens, int heads, int head_dim, int cache_length,
+    const void* query, int64_t q_stride_token, int64_t q_stride_head,
+    const void* key_cache, const void* value_cache,
+    int64_t cache_stride_batch, int64_t cache_stride_head,
+    void* out, int64_t out_stride_token, int64_t out_stride_head,
+    float scale, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Whisper decoder cross-attention for a prompt pass (whisper.py:239-240 in
+ * the eager branch): each of a window's `tokens` query rows attends, without
+ * a mask, to all `length` encoder keys of that window. Query and output rows
+ * as in asrback_whisper_self_attention_prefix, caches as in
+ * asrback_whisper_cross_attention_step; workspace
+ * asrback_decode_workspace_bytes(windows*tokens, heads, head_dim, length).
+ */
+ASRBACK_API int asrback_whisper_cross_attention_prefix(
+    int dtype, int windows, int tokens, int heads, int head_dim, int length,
+    const void* query, int64_t q_stride_token, int64_t q_stride_head,
+    const void* key_cache, const void* value_cache,
+    int64_t cache_stride_batch, int64_t cache_stride_head,
+    void* out, int64_t out_stride_token, int64_t out_stride_head,
     float scale, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /*

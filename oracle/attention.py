@@ -32,6 +32,8 @@ __all__ = [
     "sdpa",
     "whisper_self_attention_step",
     "whisper_cross_attention",
+    "whisper_self_attention_prefix",
+    "whisper_cross_attention_prefix",
     "encoder_attention",
     "rope_tables",
     "rms_norm",
@@ -113,6 +115,38 @@ def whisper_cross_attention(query, key_cache, value_cache, compute=np.float64) -
     """
     out = sdpa(np.asarray(query)[:, :, None, :], key_cache, value_cache, compute=compute)
     return out[:, :, 0, :]
+
+
+def whisper_self_attention_prefix(query, key, value, key_cache, value_cache, positions, length,
+                                  compute=np.float64):
+    """Self-attention of the eager branch of ``DecoderLayer.forward``
+    (``whisper.py:228-236``): ``index_copy_`` of the P tokens' keys/values at
+    the shared ``positions``, the cache cut to its first ``length`` positions,
+    then ``attend`` with ``is_causal = P > 1``, which torch aligns to the top
+    left (query ``t`` attends keys ``0..t``).
+
+    ``query``/``key``/``value`` ``(B, H, P, D)``; caches ``(B, H, L, D)``;
+    ``positions`` ``(P,)``. Returns ``(out (B, H, P, D) float64, key_cache,
+    value_cache)`` with the caches as updated copies.
+    """
+    key_cache = np.array(key_cache, copy=True)
+    value_cache = np.array(value_cache, copy=True)
+    positions = np.asarray(positions, dtype=np.int64)
+    key_cache[:, :, positions] = key
+    value_cache[:, :, positions] = value
+    tokens = np.asarray(query).shape[2]
+    mask = None
+    if tokens > 1:
+        mask = np.arange(length)[None, :] <= np.arange(tokens)[:, None]
+    out = sdpa(query, key_cache[:, :, :length], value_cache[:, :, :length], mask, compute=compute)
+    return out, key_cache, value_cache
+
+
+def whisper_cross_attention_prefix(query, key_cache, value_cache, compute=np.float64) -> np.ndarray:
+    """Cross-attention of the eager branch (``whisper.py:239-240``): every one
+    of a window's P query tokens over all its encoder keys. ``query``
+    ``(B, H, P, D)``, caches ``(B, H, S, D)`` -> ``(B, H, P, D)``."""
+    return sdpa(query, key_cache, value_cache, compute=compute)
 
 
 def encoder_attention(q, k, v) -> np.ndarray:

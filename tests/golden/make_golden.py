@@ -136,6 +136,48 @@ def whisper_step(whisper, dtype: torch.dtype, tag: str) -> None:
          cross_v=f32(cross_call["v"]), cross_out=f32(cross_call["out"][:, :, 0]))
 
 
+def whisper_prefix(whisper, dtype: torch.dtype, tag: str) -> None:
+    """The eager prompt pass (``decode(tokens, positions[:P], cache,
+    length=P)``, ``whisper.py:847-849``) and language detection (the same with
+    P = 1, ``whisper.py:979-981``) of a 1-layer decoder: the self call
+    (``index_copy_``, then causal SDPA over the first P positions) and the
+    cross call of each."""
+    config = dict(d_model=384, encoder_attention_heads=6, decoder_attention_heads=6,
+                  encoder_layers=1, decoder_layers=1, encoder_ffn_dim=64, decoder_ffn_dim=64,
+                  num_mel_bins=80, max_source_positions=40, max_target_positions=48,
+                  vocab_size=128)
+    torch.manual_seed(0)
+    model = whisper.WhisperForConditionalGeneration(config)
+    seeded_parameters(model.model.decoder, 1)
+    model = model.to(dtype)
+    batch, tokens = 3, 7
+    cache = model.allocate_cache(batch)
+    states = seeded_normal((batch, 40, 384), 12).to(dtype)
+    positions = torch.arange(48)
+    arrays = {}
+    with torch.no_grad():
+        model.set_encoder_output(cache, states)
+        for name, prompt in (("detect", torch.full((batch, 1), 5)),
+                             ("prompt", torch.arange(batch * tokens).view(batch, tokens) % 128)):
+            length = prompt.shape[1]
+            with SdpaRecorder() as rec:
+                hidden = model.decode(prompt, positions[:length], cache, length=length)
+            self_call, cross_call = rec.calls
+            assert self_call["kwargs"].get("is_causal") == (length > 1)
+            arrays.update({
+                f"{name}_self_q": f32(self_call["q"]), f"{name}_self_k": f32(self_call["k"]),
+                f"{name}_self_v": f32(self_call["v"]), f"{name}_self_out": f32(self_call["out"]),
+                f"{name}_cross_q": f32(cross_call["q"]), f"{name}_cross_out": f32(cross_call["out"]),
+                f"{name}_hidden": f32(hidden),
+            })
+        arrays["cross_k"] = f32(cross_call["k"])
+        arrays["cross_v"] = f32(cross_call["v"])
+    save(f"whisper_prefix_{tag}",
+         dict(config=config, dtype=str(dtype), tokens=tokens, batch=batch,
+              site="whisper.py:228-240 (eager branch), 847-849, 979-981"),
+         **arrays)
+
+
 def qwen3_step(qwen3, dtype: torch.dtype, tag: str) -> None:
     """One ``TextModel.step`` (bucket-mask path) of a 1-layer Qwen3 text model
     with 16 query / 8 key-value heads of 128."""
@@ -463,7 +505,7 @@ def main() -> None:
     from asrback.models import whisper  # noqa: E402
 
     torch.set_num_threads(8)
-    per_dtype = (whisper_step, qwen3_step, encoder_attention, qwen3_varlen)
+    per_dtype = (whisper_step, whisper_prefix, qwen3_step, encoder_attention, qwen3_varlen)
     for dtype, tag in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
         for make in per_dtype:
             if args.only in (None, make.__name__):

@@ -72,6 +72,39 @@ def test_whisper_cross_step_matches_reference(tag):
                                atol=TOL[dtype], rtol=0)
 
 
+def _heads_of(out, tokens, heads, dim):
+    """``(B, P, H*D)`` op output as the reference's ``(B, H, P, D)``."""
+    batch = out.shape[0]
+    return host(out).reshape(batch, tokens, heads, dim).transpose(0, 2, 1, 3)
+
+
+@pytest.mark.parametrize("name", ["detect", "prompt"])
+@pytest.mark.parametrize("tag", ["fp32", "bf16"])
+def test_whisper_prefix_matches_reference(tag, name):
+    """Prompt pass (P = 7) and language detection (P = 1): the caller writes
+    the keys at 0..P-1; the kernel reads keys 0..t for token t of the cache
+    cut to P positions, writes nothing; cross-attention of every token."""
+    dtype = DTYPES[tag]
+    g = load(f"whisper_prefix_{tag}")
+    q, k, v = g[f"{name}_self_q"], g[f"{name}_self_k"], g[f"{name}_self_v"]
+    batch, heads, tokens, dim = q.shape
+    gen = torch.Generator().manual_seed(tokens)
+    kc = _rand(gen, (batch, heads, 48, dim), dtype).to(DEV)
+    vc = _rand(gen, (batch, heads, 48, dim), dtype).to(DEV)
+    kc[:, :, :tokens] = dev(k, dtype)
+    vc[:, :, :tokens] = dev(v, dtype)
+    k_before, v_before = kc.clone(), vc.clone()
+    out = attention.whisper_self_attention_prefix(dev(q, dtype), kc[:, :, :tokens], vc[:, :, :tokens])
+    np.testing.assert_allclose(_heads_of(out, tokens, heads, dim), g[f"{name}_self_out"],
+                               atol=TOL[dtype], rtol=0)
+    assert torch.equal(kc, k_before) and torch.equal(vc, v_before)
+    cross = attention.whisper_cross_attention_prefix(dev(g[f"{name}_cross_q"], dtype),
+                                                     dev(g["cross_k"], dtype), dev(g["cross_v"], dtype))
+    np.testing.assert_allclose(_heads_of(cross, tokens, heads, dim), g[f"{name}_cross_out"],
+                               atol=TOL[dtype], rtol=0)
+    assert attention.read_status() == 0
+
+
 @pytest.mark.parametrize("tag", ["fp32", "bf16"])
 def test_qwen3_step_matches_reference(tag):
     dtype = DTYPES[tag]
@@ -142,6 +175,45 @@ def test_whisper_self_step_random(tag, batch, bucket):
     np.testing.assert_array_equal(got_k[:, :, bucket:], k_store[:, :, bucket:].float().numpy())
     np.testing.assert_array_equal(host(vc_dev)[:batch, :, :bucket], v_after)
     assert attention.read_status() == 0
+
+
+@pytest.mark.parametrize("tag", ["bf16", "fp32"])
+@pytest.mark.parametrize("batch,tokens,bucket", [(1, 1, 448), (5, 3, 448), (64, 5, 64),
+                                                 (2, 160, 448), (3, 448, 448)])
+def test_whisper_prefix_random(tag, batch, tokens, bucket):
+    """Prompt passes of 1..448 tokens in a bucket view of a larger cache: the
+    `_split_heads` query view (rows evenly spaced, heads interleaved), a cache
+    view longer than the pass (keys past token t never read), nothing
+    written; cross-attention over 1500 frames for the same rows."""
+    dtype = DTYPES[tag]
+    gen = torch.Generator().manual_seed(batch * 1000 + tokens)
+    heads, dim = 20, 64
+    kc = _rand(gen, (batch + 1, heads, 448, dim), dtype).to(DEV)
+    vc = _rand(gen, (batch + 1, heads, 448, dim), dtype).to(DEV)
+    x = _rand(gen, (batch, tokens, heads * dim), dtype).to(DEV)
+    query = x.view(batch, tokens, heads, dim).transpose(1, 2)
+    k_before = kc.clone()
+    out = attention.whisper_self_attention_prefix(query, kc[:batch, :, :bucket], vc[:batch, :, :bucket])
+    mask = np.arange(tokens)[None, :] <= np.arange(tokens)[:, None]
+    want = oracle.sdpa(host(query), host(kc[:batch, :, :tokens]), host(vc[:batch, :, :tokens]), mask)
+    np.testing.assert_allclose(_heads_of(out, tokens, heads, dim), want, atol=TOL[dtype], rtol=0)
+    assert torch.equal(kc, k_before)
+    if tokens <= 160:
+        ck = _rand(gen, (batch, heads, 1500, dim), dtype).to(DEV)
+        cv = _rand(gen, (batch, heads, 1500, dim), dtype).to(DEV)
+        cross = attention.whisper_cross_attention_prefix(query, ck, cv)
+        want = oracle.whisper_cross_attention_prefix(host(query), host(ck), host(cv))
+        np.testing.assert_allclose(_heads_of(cross, tokens, heads, dim), want, atol=TOL[dtype], rtol=0)
+    assert attention.read_status() == 0
+
+
+def test_whisper_prefix_rejects_bad_shapes():
+    q = torch.zeros(2, 20, 4, 64, device=DEV, dtype=torch.bfloat16)
+    kc = torch.zeros(2, 20, 448, 64, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(_native.NativeError, match="exceed the cache length"):
+        attention.whisper_self_attention_prefix(q, kc[:, :, :3], kc[:, :, :3])
+    with pytest.raises(ValueError, match="head_dim"):
+        attention.whisper_self_attention_prefix(q[:, :, :, 0], kc, kc)
 
 
 @pytest.mark.parametrize("tag", ["bf16", "fp32"])
@@ -327,6 +399,67 @@ def test_whisper_tiny_greedy_steps_match_reference():
             same.append(host(choice) == g["argmax"][:, t])
     assert max(hidden_err) < 1e-3, max(hidden_err)
     assert np.mean(same) >= 0.99, np.mean(same)
+
+
+@pytest.mark.parametrize("tag", ["fp32", "bf16"])
+def test_whisper_prefix_pass_matches_reference_decoder(tag):
+    """The mirror's eager pass (``decode(tokens, positions[:P], cache,
+    length=P)``): language detection then the prompt pass of a 1-layer
+    decoder with the reference's seeded weights; hidden states against the
+    reference's."""
+    from asrback_b200 import whisper
+    from asrback_b200.synthetic import seeded_normal, seeded_parameters
+
+    dtype = DTYPES[tag]
+    g = load(f"whisper_prefix_{tag}")
+    meta = g["meta"]
+    batch, tokens = meta["batch"], meta["tokens"]
+    model = whisper.WhisperForConditionalGeneration(meta["config"], encoder=False)
+    seeded_parameters(model.model.decoder, 1)
+    model = model.to(DEV, dtype).eval()
+    cache = model.allocate_cache(batch)
+    positions = torch.arange(48, device=DEV)
+    tol = 1e-3 if dtype == torch.float32 else 6e-2
+    with torch.no_grad():
+        model.set_encoder_output(cache, seeded_normal((batch, 40, 384), 12).to(DEV, dtype))
+        hidden = model.decode(torch.full((batch, 1), 5, device=DEV), positions[:1], cache, length=1)
+        np.testing.assert_allclose(host(hidden), g["detect_hidden"], atol=tol, rtol=0)
+        prompt = torch.arange(batch * tokens, device=DEV).view(batch, tokens) % 128
+        hidden = model.decode(prompt, positions[:tokens], cache, length=tokens)
+        np.testing.assert_allclose(host(hidden), g["prompt_hidden"], atol=tol, rtol=0)
+        np.testing.assert_allclose(host(cache.self_keys[0, :, :, :tokens]), g["prompt_self_k"],
+                                   atol=tol, rtol=0)
+    assert attention.read_status() == 0
+
+
+def test_whisper_prefix_pass_equals_token_steps():
+    """Size-independent property: the prompt pass over P tokens gives each
+    token the hidden state, and the cache the keys, that P one-token steps
+    give it (fp32, Whisper large-v3-turbo widths, 2 layers, P = 40)."""
+    from asrback_b200 import whisper
+    from asrback_b200.synthetic import seeded_normal, seeded_parameters
+
+    config = whisper.large_v3_turbo_config()
+    config["decoder_layers"] = 2
+    model = whisper.WhisperForConditionalGeneration(config, encoder=False)
+    seeded_parameters(model.model.decoder, 3)
+    model = model.to(DEV).eval()
+    batch, tokens = 4, 40
+    prompt = torch.randint(0, 51866, (batch, tokens), generator=torch.Generator().manual_seed(4)).to(DEV)
+    positions = torch.arange(448, device=DEV)
+    with torch.no_grad():
+        states = seeded_normal((batch, 1500, 1280), 5).to(DEV)
+        pass_cache, step_cache = model.allocate_cache(batch), model.allocate_cache(batch)
+        model.set_encoder_output(pass_cache, states)
+        model.set_encoder_output(step_cache, states)
+        together = model.decode(prompt, positions[:tokens], pass_cache, length=tokens)
+        steps = torch.stack([
+            model.decode(prompt[:, t:t + 1], positions[t].expand(batch), step_cache)[:, 0]
+            for t in range(tokens)], dim=1)
+    np.testing.assert_allclose(host(together), host(steps), atol=1e-3, rtol=0)
+    np.testing.assert_allclose(host(pass_cache.self_keys[:, :, :, :tokens]),
+                               host(step_cache.self_keys[:, :, :, :tokens]), atol=1e-4, rtol=0)
+    assert attention.read_status() == 0
 
 
 def test_qwen3_small_greedy_steps_match_reference():

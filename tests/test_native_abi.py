@@ -213,3 +213,35 @@ def test_cross_kv_invalid_arguments_are_rejected_on_the_host(lib, overrides, fra
     rc = _cross_kv_call(lib, **overrides)
     assert rc == _native.ERR_ARGUMENT
     assert fragment in lib.asrback_last_error().decode()
+
+
+def _prefix_call(lib, name, **overrides):
+    args = dict(dtype=_native.BF16, windows=4, tokens=6, heads=20, head_dim=64, length=448,
+                q=16, kc=16, vc=16, out=16, c_sh=448 * 64)
+    args.update(overrides)
+    return getattr(lib, name)(
+        args["dtype"], args["windows"], args["tokens"], args["heads"], args["head_dim"],
+        args["length"], args["q"], 1280, 64, args["kc"], args["vc"], 20 * args["c_sh"],
+        args["c_sh"], args["out"], 1280, 64, 0.125, None, 0, None, None)
+
+
+@pytest.mark.parametrize("name", ["asrback_whisper_self_attention_prefix",
+                                  "asrback_whisper_cross_attention_prefix"])
+@pytest.mark.parametrize("overrides,fragment", [
+    (dict(windows=0), "windows"),
+    (dict(windows=1000, tokens=100), "65535"),
+    (dict(head_dim=32), "head_dim must be 64"),
+    (dict(q=0), "null"),
+    (dict(kc=8), "aligned"),
+    (dict(c_sh=100 * 64), "cache strides"),
+])
+def test_prefix_invalid_arguments_are_rejected_on_the_host(lib, name, overrides, fragment):
+    rc = _prefix_call(lib, name, **overrides)
+    assert rc == _native.ERR_ARGUMENT
+    assert fragment in lib.asrback_last_error().decode()
+
+
+def test_self_prefix_tokens_fit_the_cache(lib):
+    rc = _prefix_call(lib, "asrback_whisper_self_attention_prefix", tokens=8, length=7)
+    assert rc == _native.ERR_ARGUMENT
+    assert "exceed the cache length" in lib.asrback_last_error().decode()

@@ -19,6 +19,30 @@ F32_TOL = 2e-5
 BF16_TOL = 2e-2
 
 
+@pytest.mark.parametrize("name", ["detect", "prompt"])
+@pytest.mark.parametrize("tag,tol", [("fp32", F32_TOL), ("bf16", BF16_TOL)])
+def test_whisper_prefix(tag, tol, name):
+    """The eager pass (prompt, P = 7) and language detection (P = 1):
+    index_copy_ at positions 0..P-1, then causal attention over the first P
+    positions; cross-attention of every prompt token."""
+    g = load(f"whisper_prefix_{tag}")
+    q, k, v = g[f"{name}_self_q"], g[f"{name}_self_k"], g[f"{name}_self_v"]
+    batch, heads, tokens, head_dim = q.shape
+    # A cache longer than the pass, holding other values past it: they are
+    # neither attended nor overwritten.
+    rng = np.random.default_rng(0)
+    cache_k = rng.standard_normal((batch, heads, 48, head_dim)).astype(np.float32)
+    cache_v = rng.standard_normal((batch, heads, 48, head_dim)).astype(np.float32)
+    out, k_after, v_after = oracle.whisper_self_attention_prefix(
+        q, k, v, cache_k, cache_v, np.arange(tokens), tokens)
+    np.testing.assert_allclose(out, g[f"{name}_self_out"], atol=tol, rtol=0)
+    np.testing.assert_array_equal(k_after[:, :, :tokens], k)
+    np.testing.assert_array_equal(k_after[:, :, tokens:], cache_k[:, :, tokens:])
+    np.testing.assert_array_equal(v_after[:, :, :tokens], v)
+    cross = oracle.whisper_cross_attention_prefix(g[f"{name}_cross_q"], g["cross_k"], g["cross_v"])
+    np.testing.assert_allclose(cross, g[f"{name}_cross_out"], atol=tol, rtol=0)
+
+
 @pytest.mark.parametrize("tag,tol", [("fp32", F32_TOL), ("bf16", BF16_TOL)])
 def test_whisper_self_step(tag, tol):
     g = load(f"whisper_step_{tag}")

@@ -56,6 +56,18 @@ def cpu_ops(monkeypatch):
         b, h, d = q.shape
         return torch.from_numpy(out).float().reshape(b, 1, h * d)
 
+    def self_prefix(query, key_cache, value_cache, scale=None):
+        b, h, p, d = query.shape
+        mask = np.arange(key_cache.shape[2])[None, :] <= np.arange(p)[:, None]
+        out = oracle.sdpa(query.numpy(), key_cache.numpy(), value_cache.numpy(), mask)
+        return torch.from_numpy(out).float().transpose(1, 2).reshape(b, p, h * d)
+
+    def cross_prefix(query, key_cache, value_cache, scale=None):
+        b, h, p, d = query.shape
+        out = oracle.whisper_cross_attention_prefix(query.numpy(), key_cache.numpy(),
+                                                    value_cache.numpy())
+        return torch.from_numpy(out).float().transpose(1, 2).reshape(b, p, h * d)
+
     def encoder(q, k, v, scale=None):
         out = oracle.encoder_attention(q.numpy(), k.numpy(), v.numpy())
         b, h, s, d = q.shape
@@ -87,6 +99,8 @@ def cpu_ops(monkeypatch):
     monkeypatch.setattr(attention, "varlen_attention", varlen)
     monkeypatch.setattr(attention, "whisper_self_attention_step", self_step)
     monkeypatch.setattr(attention, "whisper_cross_attention_step", cross_step)
+    monkeypatch.setattr(attention, "whisper_self_attention_prefix", self_prefix)
+    monkeypatch.setattr(attention, "whisper_cross_attention_prefix", cross_prefix)
     monkeypatch.setattr(attention, "whisper_encoder_attention", encoder)
     monkeypatch.setattr(attention, "qwen3_attention_step", qwen3_step)
     yield
@@ -129,17 +143,40 @@ def test_whisper_decoder_step(reference, cpu_ops):
 
 
 @torch.no_grad()
-def test_whisper_prefix_pass_keeps_reference_path(reference, cpu_ops):
-    """The eager multi-token prefix pass is not the plugin's: it runs the
-    reference's own code (and its results are unchanged)."""
+def test_whisper_prefix_pass(reference, cpu_ops):
+    """The eager pass with length == its token count (the prompt pass and
+    language detection) runs on the prefix ops: same hidden states and cache
+    as the reference's own code."""
+    whisper, _ = reference
+    model = _whisper(whisper)
+    want_cache, got_cache = model.allocate_cache(2), model.allocate_cache(2)
+    states = seeded_normal((2, 24, 128), 1)
+    model.set_encoder_output(want_cache, states)
+    tokens = torch.tensor([[1, 2, 3], [4, 5, 6]])
+    want = [model.decode(tokens[:, :1], torch.arange(1), want_cache, length=1),
+            model.decode(tokens, torch.arange(3), want_cache, length=3)]
+    plugin.install(whisper, None)
+    model.set_encoder_output(got_cache, states)
+    got = [model.decode(tokens[:, :1], torch.arange(1), got_cache, length=1),
+           model.decode(tokens, torch.arange(3), got_cache, length=3)]
+    for g, w in zip(got, want):
+        assert torch.allclose(g, w, atol=1e-4), (g - w).abs().max()
+    assert torch.allclose(got_cache.self_keys, want_cache.self_keys, atol=1e-5)
+    assert torch.allclose(got_cache.self_values, want_cache.self_values, atol=1e-5)
+
+
+@torch.no_grad()
+def test_whisper_eager_other_lengths_keep_reference_path(reference, cpu_ops):
+    """An eager call whose length differs from its token count is not the
+    plugin's: it runs the reference's own code, results unchanged."""
     whisper, _ = reference
     model = _whisper(whisper)
     cache = model.allocate_cache(2)
     model.set_encoder_output(cache, seeded_normal((2, 24, 128), 1))
     tokens = torch.tensor([[1, 2, 3], [4, 5, 6]])
-    want = model.decode(tokens, torch.arange(3), cache, length=3)
+    want = model.decode(tokens, torch.arange(3), cache, length=5)
     plugin.install(whisper, None)
-    got = model.decode(tokens, torch.arange(3), cache, length=3)
+    got = model.decode(tokens, torch.arange(3), cache, length=5)
     assert torch.equal(got, want)
 
 
