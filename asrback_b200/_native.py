@@ -60,6 +60,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
          _c_f, _c_p, _c_size, _c_p, _c_p],
         _c_int,
     ),
+    "asrback_whisper_prefix_workspace_bytes": ([_c_int, _c_int, _c_int, _c_int, _c_int], _c_size),
     "asrback_whisper_self_attention_prefix": (
         [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
          _c_p, _c_i64, _c_i64,

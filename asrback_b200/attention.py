@@ -252,7 +252,7 @@ def _prefix_query(t: Tensor, name: str) -> tuple[Tensor, int]:
 
 
 def _prefix_call(name: str, query: Tensor, key_cache: Tensor, value_cache: Tensor, length: int,
-                 max_keys: int, scale: float | None) -> Tensor:
+                 scale: float | None) -> Tensor:
     query, token_stride = _prefix_query(query, "query")
     key_cache, value_cache = _cache(key_cache, "key_cache"), _cache(value_cache, "value_cache")
     dtype = _dtype_code(query, key_cache, value_cache)
@@ -263,7 +263,10 @@ def _prefix_call(name: str, query: Tensor, key_cache: Tensor, value_cache: Tenso
         raise ValueError("asrback_b200: key and value caches differ in shape or strides")
     out = torch.empty((batch, tokens, heads * head_dim), dtype=query.dtype, device=query.device)
     state = _state(query.device)
-    ws, ws_bytes = _workspace(state, batch * tokens, heads, head_dim, max_keys)
+    lib = _native.load()
+    need = lib.asrback_whisper_prefix_workspace_bytes(batch, tokens, heads, head_dim, length)
+    workspace = state.workspace_for(need)
+    ws, ws_bytes = (workspace.data_ptr() if workspace.numel() else None), workspace.numel()
     _native.call(
         name,
         dtype, batch, tokens, heads, head_dim, length,
@@ -287,9 +290,8 @@ def whisper_self_attention_prefix(query: Tensor, key_cache: Tensor, value_cache:
     ``(B, H, L, D)`` with ``L >= P``. Returns ``(B, P, H*D)``, the layout
     ``attend`` hands to ``out_proj``.
     """
-    tokens = query.shape[2] if query.dim() == 4 else 0
     return _prefix_call("asrback_whisper_self_attention_prefix", query, key_cache, value_cache,
-                        key_cache.shape[2], tokens, scale)
+                        key_cache.shape[2], scale)
 
 
 def whisper_cross_attention_prefix(query: Tensor, key_cache: Tensor, value_cache: Tensor,
@@ -299,7 +301,7 @@ def whisper_cross_attention_prefix(query: Tensor, key_cache: Tensor, value_cache
     ``(B, P, H*D)``."""
     length = key_cache.shape[2] if key_cache.dim() == 4 else 0
     return _prefix_call("asrback_whisper_cross_attention_prefix", query, key_cache, value_cache,
-                        length, length, scale)
+                        length, scale)
 
 
 def qwen3_attention_step(qkv: Tensor, q_norm_weight: Tensor, k_norm_weight: Tensor, eps: float,

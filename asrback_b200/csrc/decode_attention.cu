@@ -211,9 +211,25 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
 
   const int split = blockIdx.x;
   const int grp = blockIdx.y;
-  const int b = blockIdx.z;  // query row
+  const int b = blockIdx.z;  // query row (grouped prefix: token group)
   const bool prefix = p.tokens_per_row > 0;
-  const int cb = prefix ? b / p.tokens_per_row : b;  // cache row
+  // Grouped prefix (cross-attention with QPK > 1): blockIdx.z is a group of
+  // QPK consecutive tokens of one window, so every staged key serves QPK
+  // queries. Query row qrow0 + qi is token tok0 + qi, present while below
+  // tokens_per_row; absent ones compute on zeros and write nothing.
+  constexpr bool kGrouped = MODE != kQwen3 && QPK > 1;
+  static_assert(!kGrouped || (MODE == kWhisperCross && G == 1),
+                "token groups serve the Whisper cross-attention prompt pass only");
+  int cb = b, tok0 = 0;  // cache row, first token
+  int64_t qrow0 = b;
+  if constexpr (kGrouped) {
+    const int groups = (p.tokens_per_row + QPK - 1) / QPK;
+    cb = b / groups;
+    tok0 = (b % groups) * QPK;
+    qrow0 = (int64_t)cb * p.tokens_per_row + tok0;
+  } else if (prefix) {
+    cb = b / p.tokens_per_row;
+  }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -348,6 +364,17 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
       S::load_global_nc(row + (p.q_heads + kv_head) * D, c, own_k);
       norm_rope<T, D>(own_k, static_cast<const T*>(p.k_norm_w), cos_row, sin_row, p.eps, c);
       S::load_global_nc(row + (p.q_heads + p.kv_heads + kv_head) * D, c, own_v);
+    }
+  } else if constexpr (kGrouped) {
+#pragma unroll
+    for (int qi = 0; qi < QPK; ++qi) {
+      if (tok0 + qi < p.tokens_per_row) {
+        S::load_global_nc(static_cast<const T*>(p.q) + (qrow0 + qi) * p.q_sb +
+                              (int64_t)kv_head * p.q_sh, c, q[qi]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[qi][j] = 0.f;
+      }
     }
   } else {
     const T* qrow = static_cast<const T*>(p.q) + b * p.q_sb + (int64_t)kv_head * p.q_sh;
@@ -510,7 +537,13 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
         float r[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) r[j] = o[qi][j] * inv;
-        S::store(out_row + (int64_t)(kv_head * QPK + qi) * p.o_sh, c, r);
+        if constexpr (kGrouped) {
+          if (tok0 + qi < p.tokens_per_row)
+            S::store(static_cast<T*>(p.out) + (qrow0 + qi) * p.o_sb + (int64_t)kv_head * p.o_sh, c,
+                     r);
+        } else {
+          S::store(out_row + (int64_t)(kv_head * QPK + qi) * p.o_sh, c, r);
+        }
       }
     }
     return;
@@ -562,7 +595,12 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
     float acc = 0.f;
     for (int s = 0; s < active; ++s)
       acc = fmaf(weights[h * kMaxSplits + s], __ldcg(part + ((size_t)s * QH + h) * (D + 2) + d), acc);
-    out_row[(int64_t)(grp * QH + h) * p.o_sh + d] = T(acc);
+    if constexpr (kGrouped) {
+      if (tok0 + h < p.tokens_per_row)
+        static_cast<T*>(p.out)[(qrow0 + h) * p.o_sb + (int64_t)grp * p.o_sh + d] = T(acc);
+    } else {
+      out_row[(int64_t)(grp * QH + h) * p.o_sh + d] = T(acc);
+    }
   }
   if (threadIdx.x == 0) p.counters[unit] = 0;
 }
@@ -647,6 +685,11 @@ void choose_split(int units, int max_keys, int tile, int granule_tiles, int ctas
 #ifndef ASRBACK_SHAPE_WHISPER_F32
 #define ASRBACK_SHAPE_WHISPER_F32 4, 32, 4
 #endif
+// Prompt-pass cross-attention with kPrefixTokens tokens per CTA.
+#ifndef ASRBACK_SHAPE_WHISPER_PREFIX_BF16
+#define ASRBACK_SHAPE_WHISPER_PREFIX_BF16 4, 64, 4
+#endif
+constexpr int kPrefixTokens = 4;
 // Qwen3: key/value heads per CTA (a divisor of 8), then the shape.
 #ifndef ASRBACK_QWEN3_GROUP
 #define ASRBACK_QWEN3_GROUP 8
@@ -663,6 +706,8 @@ using WhisperSelfBf16 = DecodeConfig<bf16, 64, 1, 1, ASRBACK_SHAPE_WHISPER_SELF_
 using WhisperSelfF32 = DecodeConfig<float, 64, 1, 1, ASRBACK_SHAPE_WHISPER_F32, kWhisperSelf>;
 using WhisperCrossBf16 = DecodeConfig<bf16, 64, 1, 1, ASRBACK_SHAPE_WHISPER_CROSS_BF16, kWhisperCross>;
 using WhisperCrossF32 = DecodeConfig<float, 64, 1, 1, ASRBACK_SHAPE_WHISPER_F32, kWhisperCross>;
+using WhisperCrossPrefixBf16 =
+    DecodeConfig<bf16, 64, 1, kPrefixTokens, ASRBACK_SHAPE_WHISPER_PREFIX_BF16, kWhisperCross>;
 template <int QPK>
 using Qwen3Bf16 = DecodeConfig<bf16, 128, ASRBACK_QWEN3_GROUP, QPK, ASRBACK_SHAPE_QWEN3_BF16, kQwen3>;
 template <int QPK>
@@ -675,6 +720,28 @@ using Qwen3F32 = DecodeConfig<float, 128, ASRBACK_QWEN3_GROUP, QPK, ASRBACK_SHAP
 template <class C>
 constexpr int split_granule_tiles() {
   return C::MODE == kQwen3 ? (64 + C::TP - 1) / C::TP : 1;
+}
+
+// Splits for units that all hold `keys` keys (the grouped prompt pass): the
+// launch takes ceil(units * s / resident) waves of CTAs that each stream 1/s
+// of a unit's keys, plus a merge once the unit is split (counted as 1/10 of a
+// unit's streaming). The s <= 8 with the least total is taken, the smallest on
+// ties; the keys are cut into whole tiles.
+void choose_split_waves(int units, int keys, int tile, int ctas_per_sm, int* chunk, int* splits) {
+  const int64_t resident = (int64_t)sm_count() * ctas_per_sm;
+  const int tiles = (keys + tile - 1) / tile;
+  int best = 1;
+  double best_cost = 0.0;
+  for (int s = 1; s <= 8 && s <= tiles; ++s) {
+    const int64_t waves = ((int64_t)units * s + resident - 1) / resident;
+    const double cost = (double)waves / s + (s > 1 ? 0.1 : 0.0);
+    if (s == 1 || cost < best_cost - 1e-9) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  *splits = best;
+  *chunk = (tiles + best - 1) / best * tile;
 }
 
 template <class C>
@@ -760,6 +827,27 @@ int whisper_common(int dtype, int batch, int heads, int head_dim, int length, co
 
 }  // namespace
 
+// Workspace bytes of the two prompt-pass calls for these sizes (the largest).
+size_t prefix_workspace_bytes(int windows, int tokens, int heads, int head_dim, int length) {
+  if (windows < 1 || tokens < 1 || heads < 1 || head_dim < 1 || length < 1) return 0;
+  const int units = windows * tokens * heads;
+  size_t need = 0;
+  for (size_t n : {workspace_for<WhisperSelfBf16>(units, 1, tokens),
+                   workspace_for<WhisperSelfF32>(units, 1, tokens),
+                   workspace_for<WhisperCrossBf16>(units, 1, length),
+                   workspace_for<WhisperCrossF32>(units, 1, length)})
+    need = n > need ? n : need;
+  if (tokens >= kPrefixTokens) {
+    const int grouped = windows * ((tokens + kPrefixTokens - 1) / kPrefixTokens) * heads;
+    int chunk, splits;
+    choose_split_waves(grouped, length, WhisperCrossPrefixBf16::TP,
+                       WhisperCrossPrefixBf16::MIN_BLOCKS, &chunk, &splits);
+    const size_t n = workspace_bytes_for(grouped, kPrefixTokens, 64, splits);
+    need = n > need ? n : need;
+  }
+  return need;
+}
+
 size_t decode_workspace_bytes(int batch, int heads, int head_dim, int max_keys) {
   if (batch < 1 || heads < 1 || head_dim < 1 || max_keys < 1) return 0;
   // Whisper: one unit per (row, head); Qwen3: one per row, all heads. The
@@ -784,6 +872,11 @@ extern "C" {
 
 size_t asrback_decode_workspace_bytes(int batch, int heads, int head_dim, int max_keys) {
   return decode_workspace_bytes(batch, heads, head_dim, max_keys);
+}
+
+size_t asrback_whisper_prefix_workspace_bytes(int windows, int tokens, int heads, int head_dim,
+                                              int length) {
+  return prefix_workspace_bytes(windows, tokens, heads, head_dim, length);
 }
 
 int asrback_whisper_self_attention_step(
@@ -902,11 +995,22 @@ int asrback_whisper_cross_attention_prefix(
   p.groups = heads;
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int rows = windows * tokens;
-  const int units = rows * heads;
-  int rc = dtype == ASRBACK_BF16
-               ? run<WhisperCrossBf16>(p, rows, units, 1, workspace, workspace_bytes, s)
-               : run<WhisperCrossF32>(p, rows, units, 1, workspace, workspace_bytes, s);
+  int rc;
+  if (dtype == ASRBACK_BF16 && tokens >= kPrefixTokens) {
+    // kPrefixTokens tokens of a window per CTA: each staged key serves them all.
+    using C = WhisperCrossPrefixBf16;
+    const int rows = windows * ((tokens + kPrefixTokens - 1) / kPrefixTokens);
+    const int units = rows * heads;
+    choose_split_waves(units, length, C::TP, C::MIN_BLOCKS, &p.chunk, &p.num_splits);
+    rc = bind_workspace(p, units, kPrefixTokens, C::D, workspace, workspace_bytes);
+    if (!rc) rc = launch<C>(p, rows, s);
+  } else {
+    const int rows = windows * tokens;
+    const int units = rows * heads;
+    rc = dtype == ASRBACK_BF16
+             ? run<WhisperCrossBf16>(p, rows, units, 1, workspace, workspace_bytes, s)
+             : run<WhisperCrossF32>(p, rows, units, 1, workspace, workspace_bytes, s);
+  }
   return rc ? rc : ok();
 }
 

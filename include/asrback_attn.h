@@ -153,10 +153,19 @@ ASRBACK_API int asrback_whisper_cross_attention_step(
  * key_cache,  (windows, heads, cache_length, head_dim) as for the step, with
  * value_cache   cache_length >= tokens
  * out         (windows*tokens, heads, head_dim), strides out_stride_*
- * workspace   asrback_decode_workspace_bytes(windows*tokens, heads, head_dim,
- *             tokens) bytes
+ * workspace   asrback_whisper_prefix_workspace_bytes(windows, tokens, heads,
+ *             head_dim, length) bytes (covers both prompt-pass calls)
  * windows*tokens <= 65535; other conditions as for the step.
  */
+/*
+ * Workspace bytes that asrback_whisper_self_attention_prefix (over `tokens`
+ * cache positions) and asrback_whisper_cross_attention_prefix (over `length`
+ * encoder keys) need for `windows` windows of `tokens` tokens: the larger of
+ * the two. Host-only; 0 for non-positive sizes.
+ */
+ASRBACK_API size_t asrback_whisper_prefix_workspace_bytes(int windows, int tokens, int heads,
+                                                          int head_dim, int length);
+
 ASRBACK_API int asrback_whisper_self_attention_prefix(
     int dtype, int windows, int tokens, int heads, int head_dim, int cache_length,
     const void* query, int64_t q_stride_token, int64_t q_stride_head,
@@ -171,7 +180,9 @@ ASRBACK_API int asrback_whisper_self_attention_prefix(
  * a mask, to all `length` encoder keys of that window. Query and output rows
  * as in asrback_whisper_self_attention_prefix, caches as in
  * asrback_whisper_cross_attention_step; workspace
- * asrback_decode_workspace_bytes(windows*tokens, heads, head_dim, length).
+ * asrback_whisper_prefix_workspace_bytes(windows, tokens, heads, head_dim,
+ * length). In bf16, from 4 tokens up, each CTA takes 4 tokens of a window, so
+ * that every key staged in shared memory serves all 4 queries.
  */
 ASRBACK_API int asrback_whisper_cross_attention_prefix(
     int dtype, int windows, int tokens, int heads, int head_dim, int length,

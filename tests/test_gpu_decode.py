@@ -178,13 +178,16 @@ def test_whisper_self_step_random(tag, batch, bucket):
 
 
 @pytest.mark.parametrize("tag", ["bf16", "fp32"])
-@pytest.mark.parametrize("batch,tokens,bucket", [(1, 1, 448), (5, 3, 448), (64, 5, 64),
-                                                 (2, 160, 448), (3, 448, 448)])
+@pytest.mark.parametrize("batch,tokens,bucket", [(1, 1, 448), (5, 3, 448), (2, 5, 448), (1, 4, 448),
+                                                 (64, 5, 64), (32, 4, 448), (2, 160, 448),
+                                                 (3, 448, 448)])
 def test_whisper_prefix_random(tag, batch, tokens, bucket):
     """Prompt passes of 1..448 tokens in a bucket view of a larger cache: the
     `_split_heads` query view (rows evenly spaced, heads interleaved), a cache
     view longer than the pass (keys past token t never read), nothing
-    written; cross-attention over 1500 frames for the same rows."""
+    written; cross-attention over 1500 frames for the same rows (in bf16 from 4
+    tokens up, 4 tokens per CTA: a last group with absent tokens, split and
+    unsplit launches)."""
     dtype = DTYPES[tag]
     gen = torch.Generator().manual_seed(batch * 1000 + tokens)
     heads, dim = 20, 64

@@ -245,3 +245,11 @@ def test_self_prefix_tokens_fit_the_cache(lib):
     rc = _prefix_call(lib, "asrback_whisper_self_attention_prefix", tokens=8, length=7)
     assert rc == _native.ERR_ARGUMENT
     assert "exceed the cache length" in lib.asrback_last_error().decode()
+
+
+def test_prefix_workspace_is_host_only(lib):
+    # 32 windows of 4 tokens: 4 tokens per CTA, 640 (window, head) units split
+    # in two over 1500 keys, so partials are needed.
+    assert lib.asrback_whisper_prefix_workspace_bytes(32, 4, 20, 64, 1500) > 0
+    assert lib.asrback_whisper_prefix_workspace_bytes(0, 4, 20, 64, 1500) == 0
+    assert lib.asrback_whisper_prefix_workspace_bytes(32, 4, 20, 64, 0) == 0
