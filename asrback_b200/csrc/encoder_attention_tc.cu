@@ -342,14 +342,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
                                fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
         const float m_tile = mx * p.scale_log2;
-        if (m_tile > m_used + kRescaleThreshold) {
+        // Rows whose tile max passes the used max by more than the threshold
+        // move it; the warp rescales O together (tcgen05.ld/st are
+        // warp-wide), the other rows with alpha = 1.
+        const bool move = m_tile > m_used + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, move)) {
+          const float m_new = move ? m_tile : m_used;
           if (j > 0) {
             // O_t must be idle: P_t(j-1) V done. (P_t(j-2) V is: S_t(j), just
             // completed, was issued after it.)
-            ok = mbar_wait_bounded(&o_full[t], (li * (n_k - 1) + j - 1) & 1);
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait_bounded(&o_full[t], (li * (n_k - 1) + j - 1) & 1));
             if (!ok) break;
             tc_fence_after();
-            const float alpha = fast_exp2(m_used - m_tile);
+            const float alpha = move ? fast_exp2(m_used - m_new) : 1.f;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               float o[16];
@@ -361,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_st();
             l *= alpha;
           }
-          m_used = m_tile;
+          m_used = m_new;
         }
         const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
         const uint64_t neg_m2 = pack2(-m_used, -m_used);

@@ -531,10 +531,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
                                fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
         const float m_tile = mx * p.scale_log2;
-        if (m_tile > m_used + kRescaleThreshold) {
+        // Rows whose tile max passes the used max by more than the threshold
+        // move it; the warp rescales O together (tcgen05.ld/st are
+        // warp-wide), the other rows with alpha = 1.
+        const bool move = m_tile > m_used + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, move)) {
+          const float m_new = move ? m_tile : m_used;
           if (j > 0) {
             // O_t is idle: P_t(j-1) V was issued before S_t(j), which is done.
-            const float alpha = fast_exp2(m_used - m_tile);
+            const float alpha = move ? fast_exp2(m_used - m_new) : 1.f;
 #pragma unroll
             for (int c = 0; c < D / 16; ++c) {
               float o[16];
@@ -545,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             l *= alpha;
           }
-          m_used = m_tile;
+          m_used = m_new;
         }
         const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
         const uint64_t neg_m2 = pack2(-m_used, -m_used);
