@@ -287,6 +287,25 @@ def test_encoder_attention_random(batch, length):
     np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
 
 
+def test_encoder_attention_rescales_when_a_later_key_dominates():
+    """Keys in later tiles that score far above a row's running max (8 x the
+    row's own query) move the max of some rows of a warp and not others: O is
+    rescaled for those rows only (the lazy rescale's j > 0 path)."""
+    gen = torch.Generator().manual_seed(11)
+    batch, length, heads, dim = 1, 1500, 4, 64
+    x = [_rand(gen, (batch, length, heads * dim), torch.bfloat16) for _ in range(3)]
+    q4, k4 = (t.view(batch, length, heads, dim) for t in x[:2])
+    for row, key in ((0, 700), (37, 1400), (130, 300), (255, 129), (900, 1000)):
+        k4[0, key] = (q4[0, row].float() * 8).bfloat16()
+    views = [t.to(DEV).view(batch, length, heads, dim).transpose(1, 2) for t in x]
+    out = attention.whisper_encoder_attention(*views)
+    q, k, v = (t.float().numpy().reshape(batch, length, heads, dim).transpose(0, 2, 1, 3) for t in x)
+    want = oracle.encoder_attention(q, k, v)
+    got = host(out).reshape(batch, length, heads, dim).transpose(0, 2, 1, 3)
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    assert attention.read_status() == 0
+
+
 # ------------------------------------------------------------ edge cases ----
 
 def test_position_outside_cache_sets_status_and_skips_row():

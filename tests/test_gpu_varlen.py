@@ -80,6 +80,29 @@ def test_varlen_random(tag, lengths, heads, kv_heads, head_dim, causal):
     assert attention.read_status() == 0
 
 
+@pytest.mark.parametrize("causal", [True, False])
+def test_varlen_rescales_when_a_later_key_dominates(causal):
+    """Keys in later tiles that score far above a row's running max (8 x the
+    row's own query) move the max of some rows of a warp only: O is rescaled
+    for those rows (the lazy rescale's j > 0 path), causal and not."""
+    gen = torch.Generator().manual_seed(12)
+    lengths, heads, kv_heads, head_dim = [410, 300], 16, 8, 128
+    tokens = sum(lengths)
+    q = _rand(gen, (tokens, heads, head_dim), torch.bfloat16)
+    k = _rand(gen, (tokens, kv_heads, head_dim), torch.bfloat16)
+    v = _rand(gen, (tokens, kv_heads, head_dim), torch.bfloat16)
+    # (query row, key row) within the first segment, key before the row.
+    for row, key in ((400, 300), (290, 200), (170, 130), (409, 390)):
+        k[key, 0] = (q[row, 0].float() * 8).bfloat16()
+    starts = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    out = attention.varlen_attention(q.to(DEV), k.to(DEV), v.to(DEV),
+                                     torch.from_numpy(starts).to(DEV), max(lengths), causal)
+    want = oracle.varlen_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                   starts, causal)
+    np.testing.assert_allclose(host(out), want, atol=2e-2, rtol=0)
+    assert attention.read_status() == 0
+
+
 @pytest.mark.parametrize("contiguous_k", [False, True])
 def test_varlen_strided_views_of_a_fused_projection(contiguous_k):
     """q, k, v as views into one (tokens, (16 + 8 + 8) * 128) projection, the
