@@ -167,7 +167,8 @@ __global__ void __launch_bounds__(256, 1)
     int lt = 0;
     for (int index = blockIdx.x; index < tiles; index += gridDim.x, ++lt) {
       const int a = lt & 1;
-      ok = ok && mbar_spin_bounded(&acc_full[a], (lt >> 1) & 1);
+      // Warp-uniform, since the TMEM reads below are warp-wide.
+      ok = __all_sync(0xffffffffu, ok && mbar_spin_bounded(&acc_full[a], (lt >> 1) & 1));
       if (!ok) break;
       tc_fence_after();
       int b, t0, n0;

@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (k / 3)-th completion of that buffer's barrier.
         const int buf = buf_of(t, J);
         const uint32_t tS = tmem + lane_bits + col_buf(buf);
-        ok = mbar_wait_bounded(&s_full[buf], ((2 * J + t) / 3) & 1);
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[buf], ((2 * J + t) / 3) & 1));
         if (!ok) break;
         tc_fence_after();
         const int valid = min(kKeys, p.length - j * kKeys);
@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // O_t is final after P_t(n_k - 1) V, whose commit has a barrier of its own.
-      ok = mbar_wait_bounded(&o_final[t], li & 1);
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&o_final[t], li & 1));
       if (!ok) break;
       tc_fence_after();
       const int index = item_index(li);

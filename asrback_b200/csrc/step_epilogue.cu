@@ -300,7 +300,8 @@ __global__ void __launch_bounds__(256, 1)
     int lt = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
       const int a = lt & 1;
-      ok = ok && mbar_spin_bounded(&acc_full[a], (lt >> 1) & 1);
+      // Warp-uniform, since the TMEM reads below are warp-wide.
+      ok = __all_sync(0xffffffffu, ok && mbar_spin_bounded(&acc_full[a], (lt >> 1) & 1));
       if (ok) {
         tc_fence_after();
         const int v = tile * kVocabTile + tid;

@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // fall in distinct banks); then each store instruction writes four rows'
     // 128 contiguous bytes.
     auto epilogue = [&](int start, int len, int h, int first_row, float l) {
-      ok = mbar_spin_bounded(&o_full[t], o_seen & 1);
+      ok = __all_sync(0xffffffffu, mbar_spin_bounded(&o_full[t], o_seen & 1));
       ++o_seen;
       if (!ok) return;
       tc_fence_after();
@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int limit = p.causal ? min(it.len, row + 1) : it.len;
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < it.n_k[tile] && ok; ++j) {
-        ok = mbar_spin_bounded(&s_full[t], s_seen & 1);
+        ok = __all_sync(0xffffffffu, mbar_spin_bounded(&s_full[t], s_seen & 1));
         ++s_seen;
         if (!ok) break;
         tc_fence_after();
