@@ -113,7 +113,8 @@ struct DecodeConfig {
   // The cross-warp merge slots and the split-merge weights are used only once
   // the ring has drained, so they share its shared memory when they fit.
   static constexpr int MERGE_FLOATS = CWARPS * QPK * (D + 2);
-  static constexpr int SCRATCH_BYTES = MERGE_FLOATS * 4 + QH * kMaxSplits * 4;
+  // Split merge: per (query head, split) the weight and the row sum.
+  static constexpr int SCRATCH_BYTES = MERGE_FLOATS * 4 + 2 * QH * kMaxSplits * 4;
   static constexpr bool SCRATCH_IN_RING = SCRATCH_BYTES <= RING_BYTES;
   static constexpr int OFF_MERGE = SCRATCH_IN_RING ? 0 : RING_BYTES;
   static constexpr int OFF_WEIGHTS = OFF_MERGE + MERGE_FLOATS * 4;
@@ -575,26 +576,51 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   if (!*last_flag) return;
   __threadfence();
 
-  float* weights = reinterpret_cast<float*>(smem + C::OFF_WEIGHTS);
-  for (int h = threadIdx.x; h < QH; h += C::CTHREADS) {
-    float mx = -INFINITY;
-    for (int s = 0; s < active; ++s) mx = fmaxf(mx, __ldcg(part + ((size_t)s * QH + h) * (D + 2) + D));
-    float den = 0.f;
-    for (int s = 0; s < active; ++s) {
-      const float* slot = part + ((size_t)s * QH + h) * (D + 2);
-      const float w = __ldcg(slot + D) == -INFINITY ? 0.f : fast_exp2(__ldcg(slot + D) - mx);
-      weights[h * kMaxSplits + s] = w;
-      den += w * __ldcg(slot + D + 1);
-    }
-    const float inv = 1.f / den;
-    for (int s = 0; s < active; ++s) weights[h * kMaxSplits + s] *= inv;
+  // The merge reads every split's (m, l) per head at once, one pair per
+  // thread, into shared memory; then one thread per head forms the weights;
+  // then each output element sums its splits with four loads in flight.
+  float* weights = reinterpret_cast<float*>(smem + C::OFF_WEIGHTS);  // [QH][kMaxSplits]
+  float* sums = weights + QH * kMaxSplits;                             // [QH][kMaxSplits]
+  for (int i = threadIdx.x; i < QH * active; i += C::CTHREADS) {
+    const int h = i / active, s = i - h * active;
+    const float* slot = part + ((size_t)s * QH + h) * (D + 2);
+    weights[h * kMaxSplits + s] = __ldcg(slot + D);
+    sums[h * kMaxSplits + s] = __ldcg(slot + D + 1);
   }
   named_sync(1, C::CTHREADS);
+  for (int h = threadIdx.x; h < QH; h += C::CTHREADS) {
+    float* w = weights + h * kMaxSplits;
+    const float* ls = sums + h * kMaxSplits;
+    float mx = -INFINITY;
+    for (int s = 0; s < active; ++s) mx = fmaxf(mx, w[s]);
+    float den = 0.f;
+    for (int s = 0; s < active; ++s) {
+      const float e = w[s] == -INFINITY ? 0.f : fast_exp2(w[s] - mx);
+      w[s] = e;
+      den += e * ls[s];
+    }
+    const float inv = 1.f / den;
+    for (int s = 0; s < active; ++s) w[s] *= inv;
+  }
+  named_sync(1, C::CTHREADS);
+  const size_t split_step = (size_t)QH * (D + 2);
   for (int i = threadIdx.x; i < QH * D; i += C::CTHREADS) {
     const int h = i / D, d = i % D;
+    const float* w = weights + h * kMaxSplits;
+    const float* col = part + (size_t)h * (D + 2) + d;
     float acc = 0.f;
-    for (int s = 0; s < active; ++s)
-      acc = fmaf(weights[h * kMaxSplits + s], __ldcg(part + ((size_t)s * QH + h) * (D + 2) + d), acc);
+    int s = 0;
+    for (; s + 4 <= active; s += 4) {
+      const float v0 = __ldcg(col + (s + 0) * split_step);
+      const float v1 = __ldcg(col + (s + 1) * split_step);
+      const float v2 = __ldcg(col + (s + 2) * split_step);
+      const float v3 = __ldcg(col + (s + 3) * split_step);
+      acc = fmaf(w[s], v0, acc);
+      acc = fmaf(w[s + 1], v1, acc);
+      acc = fmaf(w[s + 2], v2, acc);
+      acc = fmaf(w[s + 3], v3, acc);
+    }
+    for (; s < active; ++s) acc = fmaf(w[s], __ldcg(col + s * split_step), acc);
     if constexpr (kGrouped) {
       if (tok0 + h < p.tokens_per_row)
         static_cast<T*>(p.out)[(qrow0 + h) * p.o_sb + (int64_t)grp * p.o_sh + d] = T(acc);
