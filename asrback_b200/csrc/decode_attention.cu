@@ -144,9 +144,10 @@ __device__ __forceinline__ float group_sum(float x) {
 // (LPK = D/8 lanes per row). Rounds like the reference's elementwise ops in T:
 // F.rms_norm rounds x * rsqrt(mean(x^2) + eps) * w once; the rotation rounds
 // x*cos, rotated*sin and their sum (each torch op rounds its result).
+// The weight, cos and sin slices come in already loaded (w, cs, sn).
 template <typename T, int D>
-__device__ __forceinline__ void norm_rope(float* x, const T* weight, const T* cos_row,
-                                          const T* sin_row, float eps, int c) {
+__device__ __forceinline__ void norm_rope(float* x, const float* w, const float* cs,
+                                          const float* sn, float eps, int c) {
   using S = Slice<T, D>;
   constexpr int LPK = D / 8;
   float ss = 0.f;
@@ -154,10 +155,6 @@ __device__ __forceinline__ void norm_rope(float* x, const T* weight, const T* co
   for (int j = 0; j < 8; ++j) ss = fmaf(x[j], x[j], ss);
   ss = group_sum<LPK>(ss);
   const float r = rsqrtf(ss / (float)D + eps);
-  float w[8], cs[8], sn[8];
-  S::load_global_nc(weight, c, w);
-  S::load_global_nc(cos_row, c, cs);
-  S::load_global_nc(sin_row, c, sn);
   float y[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) y[j] = S::round(__fmul_rn(__fmul_rn(x[j], r), w[j]));
@@ -240,6 +237,48 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   // then the next launch may begin to be scheduled.
   griddep_wait();
   griddep_launch_dependents();
+
+  // The consumer warps' inputs that do not depend on the row's position
+  // (query, the step's own key/value, the norm weights) are loaded first,
+  // together, so that their latencies overlap the position read, the barrier
+  // set-up and each other.
+  const int g = warp / WPH;   // head within the group
+  const int wh = warp % WPH;  // warp within the head
+  const int ks = lane / LPK;  // key slot within a warp pass
+  const int c = lane % LPK;   // slice of the row
+  const int kv_head = grp * G + g;
+  float q[QPK][8];
+  float own_k[8], own_v[8], wq[8], wk[8];
+  if (warp < C::CWARPS) {
+    if constexpr (MODE == kQwen3) {
+      const T* row = static_cast<const T*>(p.qkv) + b * p.qkv_sb;
+#pragma unroll
+      for (int qi = 0; qi < QPK; ++qi) S::load_global_nc(row + (kv_head * QPK + qi) * D, c, q[qi]);
+      S::load_global_nc(row + (p.q_heads + kv_head) * D, c, own_k);
+      S::load_global_nc(row + (p.q_heads + p.kv_heads + kv_head) * D, c, own_v);
+      S::load_global_nc(static_cast<const T*>(p.q_norm_w), c, wq);
+      S::load_global_nc(static_cast<const T*>(p.k_norm_w), c, wk);
+    } else if constexpr (kGrouped) {
+#pragma unroll
+      for (int qi = 0; qi < QPK; ++qi) {
+        if (tok0 + qi < p.tokens_per_row) {
+          S::load_global_nc(static_cast<const T*>(p.q) + (qrow0 + qi) * p.q_sb +
+                                (int64_t)kv_head * p.q_sh, c, q[qi]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) q[qi][j] = 0.f;
+        }
+      }
+    } else {
+      S::load_global_nc(static_cast<const T*>(p.q) + b * p.q_sb + (int64_t)kv_head * p.q_sh, c,
+                        q[0]);
+      if (MODE == kWhisperSelf && !prefix) {
+        const int64_t off = b * p.kn_sb + (int64_t)kv_head * p.kn_sh;
+        S::load_global_nc(static_cast<const T*>(p.k_new) + off, c, own_k);
+        S::load_global_nc(static_cast<const T*>(p.v_new) + off, c, own_v);
+      }
+    }
+  }
 
   // Keys of this row: n_cached read from the cache, plus (self/Qwen3 steps)
   // the step's own key at index `pos`.
@@ -333,14 +372,8 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   }
 
   // ---------------- consumers ----------------
-  const int g = warp / WPH;   // head within the group
-  const int wh = warp % WPH;  // warp within the head
-  const int ks = lane / LPK;  // key slot within a warp pass
-  const int c = lane % LPK;   // slice of the row
-  const int kv_head = grp * G + g;
   const bool owner = wh == 0 && ks == 0;  // lanes that hold the row's own key state
 
-  float q[QPK][8];
   float m[QPK], l[QPK], o[QPK][8];
 #pragma unroll
   for (int qi = 0; qi < QPK; ++qi) {
@@ -350,43 +383,13 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
     for (int j = 0; j < 8; ++j) o[qi][j] = 0.f;
   }
 
-  float own_k[8], own_v[8];
   if constexpr (MODE == kQwen3) {
-    const T* row = static_cast<const T*>(p.qkv) + b * p.qkv_sb;
-    const T* cos_row = static_cast<const T*>(p.cos) + pos * p.table_s;
-    const T* sin_row = static_cast<const T*>(p.sin) + pos * p.table_s;
+    float cs[8], sn[8];
+    S::load_global_nc(static_cast<const T*>(p.cos) + pos * p.table_s, c, cs);
+    S::load_global_nc(static_cast<const T*>(p.sin) + pos * p.table_s, c, sn);
 #pragma unroll
-    for (int qi = 0; qi < QPK; ++qi) {
-      const int qh = kv_head * QPK + qi;
-      S::load_global_nc(row + qh * D, c, q[qi]);
-      norm_rope<T, D>(q[qi], static_cast<const T*>(p.q_norm_w), cos_row, sin_row, p.eps, c);
-    }
-    if (has_own_key) {
-      S::load_global_nc(row + (p.q_heads + kv_head) * D, c, own_k);
-      norm_rope<T, D>(own_k, static_cast<const T*>(p.k_norm_w), cos_row, sin_row, p.eps, c);
-      S::load_global_nc(row + (p.q_heads + p.kv_heads + kv_head) * D, c, own_v);
-    }
-  } else if constexpr (kGrouped) {
-#pragma unroll
-    for (int qi = 0; qi < QPK; ++qi) {
-      if (tok0 + qi < p.tokens_per_row) {
-        S::load_global_nc(static_cast<const T*>(p.q) + (qrow0 + qi) * p.q_sb +
-                              (int64_t)kv_head * p.q_sh, c, q[qi]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) q[qi][j] = 0.f;
-      }
-    }
-  } else {
-    const T* qrow = static_cast<const T*>(p.q) + b * p.q_sb + (int64_t)kv_head * p.q_sh;
-    S::load_global_nc(qrow, c, q[0]);
-    if constexpr (MODE == kWhisperSelf) {
-      if (has_own_key) {
-        const int64_t off = b * p.kn_sb + (int64_t)kv_head * p.kn_sh;
-        S::load_global_nc(static_cast<const T*>(p.k_new) + off, c, own_k);
-        S::load_global_nc(static_cast<const T*>(p.v_new) + off, c, own_v);
-      }
-    }
+    for (int qi = 0; qi < QPK; ++qi) norm_rope<T, D>(q[qi], wq, cs, sn, p.eps, c);
+    if (has_own_key) norm_rope<T, D>(own_k, wk, cs, sn, p.eps, c);
   }
 #pragma unroll
   for (int qi = 0; qi < QPK; ++qi)
