@@ -121,10 +121,12 @@ __device__ __forceinline__ bool take_ticket(const StepParams& p) {
 // The last CTA merges every CTA's partials row by row and updates the state.
 // All `nthreads` (a multiple of 32) threads of the CTA call it. R threads
 // (a power of two, at most 32, adjacent lanes) share a row: each merges every
-// R-th CTA's partial, loading 16 at a time so that the loads overlap, then the
-// R combine through shuffles.
+// R-th CTA's partial, loading 20 at a time so that the loads overlap (two
+// rounds for 148 CTAs at R = 4), then the R combine through shuffles. The
+// thread that updates a row loads the row's decode state first, so that those
+// loads overlap the partials' too.
 __device__ void finish_rows(const StepParams& p, int tid, int nthreads) {
-  constexpr int kUnroll = 16;
+  constexpr int kUnroll = 20;
   int R = 32;
   while (R > 1 && R * p.batch > nthreads) R >>= 1;
   const int rows_per_pass = nthreads / R;
@@ -132,6 +134,17 @@ __device__ void finish_rows(const StepParams& p, int tid, int nthreads) {
   const int parts = gridDim.x;
   for (int base = 0; base < p.batch; base += rows_per_pass) {
     const int b = base + tid / R;
+    const bool updates = b < p.batch && j == 0 && p.tokens;
+    bool done = false;
+    int64_t position = 0, end = 0, old_token = 0;
+    float sum = 0.f;
+    if (updates) {
+      done = p.finished[b] != 0;
+      position = p.position[b];
+      end = p.end[b];
+      old_token = p.tokens[b * p.tokens_stride];
+      sum = p.sum_logprobs[b];
+    }
     Running r;
     r.init();
     if (b < p.batch) {
@@ -159,11 +172,10 @@ __device__ void finish_rows(const StepParams& p, int tid, int nthreads) {
     const float logprob = r.m == -INFINITY ? __int_as_float(0x7fc00000) : -logf(r.s);
     if (p.out_token) p.out_token[b] = token;
     if (p.out_logprob) p.out_logprob[b] = logprob;
-    if (p.tokens) {
-      const bool done = p.finished[b] != 0;
-      const int64_t pos = p.position[b] + (done ? 0 : 1);
-      const int64_t tok = done ? p.tokens[b * p.tokens_stride] : token;
-      if (!done) p.sum_logprobs[b] += logprob;
+    if (updates) {
+      const int64_t pos = position + (done ? 0 : 1);
+      const int64_t tok = done ? old_token : token;
+      if (!done) p.sum_logprobs[b] = sum + logprob;
       bool eos = false;
       for (int e = 0; e < p.n_eos; ++e) eos |= tok == p.eos[e];
       if (pos >= 0 && pos < p.generated_cols) {
@@ -171,7 +183,7 @@ __device__ void finish_rows(const StepParams& p, int tid, int nthreads) {
       } else if (p.status) {
         atomicOr(p.status, ASRBACK_STATUS_POSITION);
       }
-      p.finished[b] = done || eos || pos >= p.end[b];
+      p.finished[b] = done || eos || pos >= end;
       p.position[b] = pos;
       p.tokens[b * p.tokens_stride] = tok;
     }
