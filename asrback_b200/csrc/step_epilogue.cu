@@ -45,7 +45,10 @@ constexpr int kMaxEos = 8;
 constexpr int kNoIndex = 0x7fffffff;
 constexpr int kSimtWarps = 8;
 constexpr int kSimtMaxBatch = 64;
-constexpr int kWorkspaceHeader = 256;  // ticket counter, then the partials
+// Workspace: a 256-byte header of tickets (the final one, then one per group
+// of CTAs in the tensor-core kernel), then the partials: one per (CTA, row),
+// then (tensor-core kernel) one per (group, row).
+constexpr int kWorkspaceHeader = 256;
 
 struct Partial {
   float m;  // largest logit seen
@@ -118,20 +121,80 @@ __device__ __forceinline__ bool take_ticket(const StepParams& p) {
   return last;
 }
 
-// The last CTA merges every CTA's partials row by row and updates the state.
-// All `nthreads` (a multiple of 32) threads of the CTA call it. R threads
-// (a power of two, at most 32, adjacent lanes) share a row: each merges every
-// R-th CTA's partial, loading 20 at a time so that the loads overlap (two
-// rounds for 148 CTAs at R = 4), then the R combine through shuffles. The
-// thread that updates a row loads the row's decode state first, so that those
-// loads overlap the partials' too.
-__device__ void finish_rows(const StepParams& p, int tid, int nthreads) {
-  constexpr int kUnroll = 20;
+// The tensor-core kernel merges in two levels. Its CTAs form groups of
+// kGroupCtas; each group counts on its own ticket (p.ticket[1 + group]),
+// which its last CTA resets. True for that last CTA.
+constexpr int kGroupCtas = 16;
+__device__ __forceinline__ bool take_group_ticket(const StepParams& p) {
+  const int group = blockIdx.x / kGroupCtas;
+  const int size = min(kGroupCtas, (int)gridDim.x - group * kGroupCtas);
+  unsigned* counter = p.ticket + 1 + group;
+  const bool last = atomicAdd(counter, 1u) == static_cast<unsigned>(size - 1);
+  if (last) *counter = 0u;
+  return last;
+}
+
+// Lanes per row in a merge over `nthreads` threads: R (a power of two, at
+// most 32, adjacent lanes) share a row.
+__device__ __forceinline__ int lanes_per_row(int batch, int nthreads) {
   int R = 32;
-  while (R > 1 && R * p.batch > nthreads) R >>= 1;
+  while (R > 1 && R * batch > nthreads) R >>= 1;
+  return R;
+}
+
+// Row b's summary over the partials src[c * batch + b], c < parts: each of the
+// row's R lanes (j = its index) merges every R-th one, loading 20 at a time so
+// that the loads overlap, then the R combine through shuffles. Every lane of
+// the warp takes part (rows past the batch merge nothing).
+__device__ __forceinline__ Running merge_row(const Partial* src, int parts, int batch, int b, int j,
+                                             int R) {
+  constexpr int kUnroll = 20;
+  Running r;
+  r.init();
+  if (b < batch) {
+    for (int c0 = j; c0 < parts; c0 += kUnroll * R) {
+      float4 q[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * R;
+        q[u] = c < parts ? __ldcg(reinterpret_cast<const float4*>(src + c * batch + b))
+                         : make_float4(-INFINITY, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) r.merge(q[u].x, q[u].y, __float_as_int(q[u].z));
+    }
+  }
+  for (int o = 1; o < R; o <<= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, r.m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, r.s, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, r.idx, o);
+    r.merge(m2, s2, i2);
+  }
+  return r;
+}
+
+// Merges `parts` partials per row from src into one per row in dst (a group
+// of CTAs' partials into the group's). All `nthreads` threads call it.
+__device__ void merge_rows(const Partial* src, int parts, Partial* dst, int batch, int tid,
+                           int nthreads) {
+  const int R = lanes_per_row(batch, nthreads);
+  const int j = tid % R;
+  for (int base = 0; base < batch; base += nthreads / R) {
+    const int b = base + tid / R;
+    const Running r = merge_row(src, parts, batch, b, j, R);
+    if (b < batch && j == 0) dst[b] = Partial{r.m, r.s, r.idx, 0};
+  }
+}
+
+// The last merge: `parts` partials per row from src, then each row's token,
+// log-probability and decode-state update. All `nthreads` (a multiple of 32)
+// threads of the CTA call it. The thread that updates a row loads the row's
+// decode state first, so that those loads overlap the partials'.
+__device__ void finish_rows(const StepParams& p, const Partial* src, int parts, int tid,
+                            int nthreads) {
+  const int R = lanes_per_row(p.batch, nthreads);
   const int rows_per_pass = nthreads / R;
   const int j = tid % R;
-  const int parts = gridDim.x;
   for (int base = 0; base < p.batch; base += rows_per_pass) {
     const int b = base + tid / R;
     const bool updates = b < p.batch && j == 0 && p.tokens;
@@ -145,27 +208,7 @@ __device__ void finish_rows(const StepParams& p, int tid, int nthreads) {
       old_token = p.tokens[b * p.tokens_stride];
       sum = p.sum_logprobs[b];
     }
-    Running r;
-    r.init();
-    if (b < p.batch) {
-      for (int c0 = j; c0 < parts; c0 += kUnroll * R) {
-        float4 q[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const int c = c0 + u * R;
-          q[u] = c < parts ? __ldcg(reinterpret_cast<const float4*>(p.partials + c * p.batch + b))
-                           : make_float4(-INFINITY, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) r.merge(q[u].x, q[u].y, __float_as_int(q[u].z));
-      }
-    }
-    for (int o = 1; o < R; o <<= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, r.m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, r.s, o);
-      const int i2 = __shfl_xor_sync(0xffffffffu, r.idx, o);
-      r.merge(m2, s2, i2);
-    }
+    const Running r = merge_row(src, parts, p.batch, b, j, R);
     if (b >= p.batch || j != 0) continue;
     // torch's argmax of a row that is all -inf is its first index.
     const int64_t token = r.idx == kNoIndex ? 0 : r.idx;
@@ -197,7 +240,7 @@ struct TcShape {
   static constexpr int kWBytes = kVocabTile * 128;  // 128 rows x 64 bf16
   static constexpr int kHBytes = kN * 128;          // kN rows x 64 bf16
   static constexpr int kStageBytes = kWBytes + kHBytes;
-  static constexpr int kStages = kN == 64 ? 6 : 4;
+  static constexpr int kStages = kN == 64 ? 7 : 4;
   static constexpr int kOffT = kStages * kStageBytes;  // logits tile, [128][kN + 1] f32
   static constexpr int kOffRed = kOffT + kVocabTile * (kN + 1) * 4;
   static constexpr int kOffBar = kOffRed + kVocabTile * static_cast<int>(sizeof(Partial));
@@ -356,7 +399,7 @@ __global__ void __launch_bounds__(256, 1)
       p.partials[blockIdx.x * p.batch + col] = Partial{run.m, run.s, run.idx, 0};
     __threadfence();
     named_sync(1, 128);
-    if (tid == 0) *last_flag = take_ticket(p);
+    if (tid == 0) *last_flag = take_group_ticket(p);
   }
   if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
   tc_fence_before();
@@ -365,9 +408,29 @@ __global__ void __launch_bounds__(256, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 2 * kN);
   }
+  // Two-level merge: the last CTA of each group of kGroupCtas merges the
+  // group's partials into one per row; the last group to finish merges those
+  // and updates the state.
   if (*last_flag) {
     __threadfence();
-    finish_rows(p, threadIdx.x, blockDim.x);
+    const int group = blockIdx.x / kGroupCtas;
+    const int first = group * kGroupCtas;
+    const int groups = (gridDim.x + kGroupCtas - 1) / kGroupCtas;
+    Partial* group_partials = p.partials + gridDim.x * p.batch;
+    merge_rows(p.partials + first * p.batch, min(kGroupCtas, (int)gridDim.x - first),
+               group_partials + group * p.batch, p.batch, threadIdx.x, blockDim.x);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const bool last = atomicAdd(p.ticket, 1u) == static_cast<unsigned>(groups - 1);
+      if (last) *p.ticket = 0u;
+      *last_flag = last;
+    }
+    __syncthreads();
+    if (*last_flag) {
+      __threadfence();
+      finish_rows(p, group_partials, groups, threadIdx.x, blockDim.x);
+    }
   }
 }
 
@@ -428,7 +491,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
   __syncthreads();
   if (last_flag) {
     __threadfence();
-    finish_rows(p, threadIdx.x, blockDim.x);
+    finish_rows(p, p.partials, gridDim.x, threadIdx.x, blockDim.x);
   }
 }
 
@@ -471,6 +534,10 @@ int launch_tc(const void* hidden, int64_t h_stride, const void* weight, int64_t 
   }
   const int tiles = (p.vocab + kVocabTile - 1) / kVocabTile;
   const int ctas = std::min(tiles, sm_count());
+  // One ticket per group of CTAs after the first in the workspace header.
+  if (1 + (ctas + kGroupCtas - 1) / kGroupCtas > kWorkspaceHeader / (int)sizeof(unsigned))
+    return fail(ASRBACK_ERR_ARGUMENT, "%d CTAs need more group tickets than the workspace holds",
+                ctas);
   kernel<<<ctas, 256, Sh::kSmemBytes, stream>>>(mw, mh, hidden_dim, p);
   return check_cuda(cudaGetLastError(), "greedy step (tensor core) launch");
 }

@@ -316,9 +316,10 @@ ASRBACK_API int asrback_whisper_cross_kv_projection(
     int32_t* status, void* stream);
 
 /*
- * Workspace of asrback_greedy_step for up to `batch` rows: a ticket counter
- * (zero before the first call; every call leaves it zero) and per-CTA
- * partials. 16-byte aligned; reusable by consecutive calls on one stream.
+ * Workspace of asrback_greedy_step for up to `batch` rows: a header of ticket
+ * counters (zero before the first call; every call leaves them zero) and the
+ * per-CTA and per-group partials. 16-byte aligned; reusable by consecutive
+ * calls on one stream.
  */
 ASRBACK_API size_t asrback_greedy_step_workspace_bytes(int batch);
 
