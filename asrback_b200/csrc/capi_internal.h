@@ -41,4 +41,25 @@ int launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cu
   return check_cuda(cudaLaunchKernelEx(&config, kernel, static_cast<Args&&>(args)...), what);
 }
 
+// As launch_pdl, with the grid's CTAs in clusters of `cluster_x` along x.
+template <typename... Params, typename... Args>
+int launch_pdl_cluster(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       unsigned cluster_x, cudaStream_t stream, const char* what, Args&&... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[2];
+  attribute[0].id = cudaLaunchAttributeClusterDimension;
+  attribute[0].val.clusterDim.x = cluster_x;
+  attribute[0].val.clusterDim.y = 1;
+  attribute[0].val.clusterDim.z = 1;
+  attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[1].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = ASRBACK_PDL ? 2 : 1;
+  return check_cuda(cudaLaunchKernelEx(&config, kernel, static_cast<Args&&>(args)...), what);
+}
+
 }  // namespace asrback

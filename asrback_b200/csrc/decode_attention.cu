@@ -77,6 +77,9 @@ struct DecodeParams {
   int groups;                // key/value head groups (grid.y)
   int chunk;                 // key positions per split
   int num_splits;            // grid.x
+  // Qwen3 with exactly two splits, launched as clusters of 2 CTAs along x:
+  // split 1 hands its partial to split 0 through split 0's shared memory.
+  int pair_splits;
   float* partial;            // workspace partials
   int* counters;             // workspace counters, one per (row, group)
   int32_t* status;           // device status word (may be null)
@@ -120,7 +123,11 @@ struct DecodeConfig {
   static constexpr int OFF_WEIGHTS = OFF_MERGE + MERGE_FLOATS * 4;
   static constexpr int OFF_BAR =
       ((SCRATCH_IN_RING ? RING_BYTES : RING_BYTES + SCRATCH_BYTES) + 15) / 16 * 16;
-  static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8 + 16;
+  // Split pair (Qwen3): a barrier and split 1's partial state, [QH][D + 2].
+  static constexpr int OFF_XBAR = OFF_BAR + 2 * STAGES * 8 + 16;
+  static constexpr int OFF_XFER = OFF_XBAR + 16;
+  static constexpr int XFER_BYTES = MODE == 2 ? 16 + QH * (D + 2) * 4 : 0;
+  static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8 + 16 + XFER_BYTES;
   // CTAs per SM that shared memory (228 KB, 1 KB reserved per CTA) and the
   // 2048-thread limit allow; registers are budgeted to match.
   static constexpr int BY_SMEM = (228 * 1024) / (SMEM + 1024);
@@ -235,6 +242,19 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   // before the previous kernel of the stream has finished, so it reads no
   // input (positions, caches, queries, workspace) before that kernel is done;
   // then the next launch may begin to be scheduled.
+  // A split pair's barrier is set up, and the pair meets, before anything
+  // can return: then split 1 may arrive on split 0's barrier at any time.
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + C::OFF_XBAR);
+  if constexpr (MODE == kQwen3) {
+    if (p.pair_splits) {
+      if (threadIdx.x == 0) {
+        mbar_init(xbar, 1);
+        fence_barrier_init();
+      }
+      cluster_sync();
+    }
+  }
+
   griddep_wait();
   griddep_launch_dependents();
 
@@ -553,6 +573,60 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
     return;
   }
 
+  // A split pair: split 1 writes its state into split 0's shared memory and
+  // arrives on split 0's barrier; split 0 folds it into its own and writes
+  // the output. No workspace, counter or global round trip.
+  if constexpr (MODE == kQwen3) {
+    if (p.pair_splits) {
+      float* xfer = reinterpret_cast<float*>(smem + C::OFF_XFER);
+      if (split == 1) {
+        if (owner) {
+#pragma unroll
+          for (int qi = 0; qi < QPK; ++qi) {
+            const uint32_t slot =
+                cluster_map(smem_addr(xfer + (g * QPK + qi) * (D + 2)), 0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) st_cluster_f32(slot + 4 * S::elem(c, j), o[qi][j]);
+            if (c == 0) {
+              st_cluster_f32(slot + 4 * D, m[qi]);
+              st_cluster_f32(slot + 4 * (D + 1), l[qi]);
+            }
+          }
+          fence_cluster();
+        }
+        named_sync(1, C::CTHREADS);
+        if (threadIdx.x == 0) mbar_arrive_cluster(cluster_map(smem_addr(xbar), 0));
+        return;
+      }
+      if (owner) {
+        // Two budgets: split 1 may itself have waited out one on its tiles.
+        bool got = false;
+        for (int attempt = 0; attempt < 2 && !got; ++attempt) {
+          const uint64_t until = global_timer_ns() + kWaitBudgetNs;
+          while (!(got = mbar_try_wait_cluster(xbar, 0)) && global_timer_ns() < until) {
+          }
+        }
+        if (!got && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+#pragma unroll
+        for (int qi = 0; qi < QPK; ++qi) {
+          if (got) {
+            const float* slot = xfer + (g * QPK + qi) * (D + 2);
+            float o2[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o2[j] = slot[S::elem(c, j)];
+            merge_state(m[qi], l[qi], o[qi], slot[D], slot[D + 1], o2);
+          }
+          const float inv = 1.f / l[qi];
+          float r[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) r[j] = o[qi][j] * inv;
+          S::store(out_row + (int64_t)(kv_head * QPK + qi) * p.o_sh, c, r);
+        }
+      }
+      return;
+    }
+  }
+
   // Several splits: publish this split's partial state, then the last CTA of
   // the (row, group) to arrive merges all of them.
   const int unit = b * p.groups + grp;
@@ -813,12 +887,45 @@ int run(DecodeParams& p, int batch, int units, int qh_per_unit, void* workspace,
   return launch<C>(p, batch, stream);
 }
 
-// Qwen3: one unit per (row, group of C::G key/value heads).
+// Split pairs are on unless ASRBACK_SPLIT_PAIR=0 (A/B timing); read at every
+// call so that one process can compare both.
+bool pair_enabled() {
+  const char* env = std::getenv("ASRBACK_SPLIT_PAIR");
+  return !(env && env[0] == '0');
+}
+
+// Launches config C with each row's two splits as one cluster of 2 CTAs.
+template <class C>
+int launch_pair(const DecodeParams& p, int batch, cudaStream_t stream) {
+  auto kernel = decode_attention_kernel<C>;
+  static thread_local int prepared_device = -1;
+  int device = 0;
+  if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
+  if (prepared_device != device) {
+    if (int rc = check_cuda(
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+            "cudaFuncSetAttribute(max dynamic shared memory)"))
+      return rc;
+    prepared_device = device;
+  }
+  return launch_pdl_cluster(kernel, dim3(2, p.groups, batch), dim3(C::THREADS), C::SMEM, 2,
+                            stream, "decode attention launch (split pairs)", p);
+}
+
+// Qwen3: one unit per (row, group of C::G key/value heads). Rows cut in two
+// splits run as split pairs (no workspace); others merge through it.
 template <class C>
 int run_qwen3(DecodeParams& p, int batch, void* workspace, size_t bytes, cudaStream_t stream) {
   static_assert(8 % C::G == 0, "key/value head groups must divide 8");
   p.groups = p.kv_heads / C::G;
-  return run<C>(p, batch, batch * p.groups, C::QH, workspace, bytes, stream);
+  const int units = batch * p.groups;
+  split_for<C>(p, units);
+  if (p.num_splits == 2 && pair_enabled()) {
+    p.pair_splits = 1;
+    return launch_pair<C>(p, batch, stream);
+  }
+  if (int rc = bind_workspace(p, units, C::QH, C::D, workspace, bytes)) return rc;
+  return launch<C>(p, batch, stream);
 }
 
 int check_dtype(int dtype) {
