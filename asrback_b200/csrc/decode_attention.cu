@@ -258,10 +258,11 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   griddep_wait();
   griddep_launch_dependents();
 
-  // The consumer warps' inputs that do not depend on the row's position
-  // (query, the step's own key/value, the norm weights) are loaded first,
-  // together, so that their latencies overlap the position read, the barrier
-  // set-up and each other.
+  // Qwen3: the consumer warps' inputs that do not depend on the row's
+  // position (query, the step's own key/value, the norm weights) are loaded
+  // first, together, so that their latencies overlap the position read, the
+  // barrier set-up and each other. (The Whisper modes load their query and
+  // key where they use them: hoisted, their launches took 1-3 % longer.)
   const int g = warp / WPH;   // head within the group
   const int wh = warp % WPH;  // warp within the head
   const int ks = lane / LPK;  // key slot within a warp pass
@@ -269,8 +270,8 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   const int kv_head = grp * G + g;
   float q[QPK][8];
   float own_k[8], own_v[8], wq[8], wk[8];
-  if (warp < C::CWARPS) {
-    if constexpr (MODE == kQwen3) {
+  if constexpr (MODE == kQwen3) {
+    if (warp < C::CWARPS) {
       const T* row = static_cast<const T*>(p.qkv) + b * p.qkv_sb;
 #pragma unroll
       for (int qi = 0; qi < QPK; ++qi) S::load_global_nc(row + (kv_head * QPK + qi) * D, c, q[qi]);
@@ -278,25 +279,6 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
       S::load_global_nc(row + (p.q_heads + p.kv_heads + kv_head) * D, c, own_v);
       S::load_global_nc(static_cast<const T*>(p.q_norm_w), c, wq);
       S::load_global_nc(static_cast<const T*>(p.k_norm_w), c, wk);
-    } else if constexpr (kGrouped) {
-#pragma unroll
-      for (int qi = 0; qi < QPK; ++qi) {
-        if (tok0 + qi < p.tokens_per_row) {
-          S::load_global_nc(static_cast<const T*>(p.q) + (qrow0 + qi) * p.q_sb +
-                                (int64_t)kv_head * p.q_sh, c, q[qi]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) q[qi][j] = 0.f;
-        }
-      }
-    } else {
-      S::load_global_nc(static_cast<const T*>(p.q) + b * p.q_sb + (int64_t)kv_head * p.q_sh, c,
-                        q[0]);
-      if (MODE == kWhisperSelf && !prefix) {
-        const int64_t off = b * p.kn_sb + (int64_t)kv_head * p.kn_sh;
-        S::load_global_nc(static_cast<const T*>(p.k_new) + off, c, own_k);
-        S::load_global_nc(static_cast<const T*>(p.v_new) + off, c, own_v);
-      }
     }
   }
 
@@ -410,6 +392,27 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
 #pragma unroll
     for (int qi = 0; qi < QPK; ++qi) norm_rope<T, D>(q[qi], wq, cs, sn, p.eps, c);
     if (has_own_key) norm_rope<T, D>(own_k, wk, cs, sn, p.eps, c);
+  } else if constexpr (kGrouped) {
+#pragma unroll
+    for (int qi = 0; qi < QPK; ++qi) {
+      if (tok0 + qi < p.tokens_per_row) {
+        S::load_global_nc(static_cast<const T*>(p.q) + (qrow0 + qi) * p.q_sb +
+                              (int64_t)kv_head * p.q_sh, c, q[qi]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[qi][j] = 0.f;
+      }
+    }
+  } else {
+    const T* qrow = static_cast<const T*>(p.q) + b * p.q_sb + (int64_t)kv_head * p.q_sh;
+    S::load_global_nc(qrow, c, q[0]);
+    if constexpr (MODE == kWhisperSelf) {
+      if (has_own_key) {
+        const int64_t off = b * p.kn_sb + (int64_t)kv_head * p.kn_sh;
+        S::load_global_nc(static_cast<const T*>(p.k_new) + off, c, own_k);
+        S::load_global_nc(static_cast<const T*>(p.v_new) + off, c, own_v);
+      }
+    }
   }
 #pragma unroll
   for (int qi = 0; qi < QPK; ++qi)
