@@ -74,6 +74,9 @@ def parse_args():
                         default="whisper-decode")
     parser.add_argument("--batch", type=int, default=None,
                         help="override the workload's batch (small profiling cases)")
+    parser.add_argument("--layers", type=int, default=None,
+                        help="override the workload's layer count (small profiling cases that "
+                             "keep the batch; not a bench line)")
     parser.add_argument("--cpu-seconds", type=float, default=10.0,
                         help="time budget of the CPU baseline sample")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -1510,6 +1513,8 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     work = WORKLOADS[args.workload](args.batch)
+    if args.layers:
+        work.layers = args.layers
     line = measure(args, work, torch, dist, device, rank, world, args.steps, args.warmup,
                    cpu=not args.no_cpu_baseline)
     if args.workload == "whisper-decode" and not args.no_extras and args.batch is None:
