@@ -783,7 +783,7 @@ void choose_split(int units, int max_keys, int tile, int granule_tiles, int ctas
 // (Qwen3) of keys, as much of values. The defaults come from sweeps on B200;
 // a build may override them with -D for new sweeps.
 #ifndef ASRBACK_SHAPE_WHISPER_SELF_BF16
-#define ASRBACK_SHAPE_WHISPER_SELF_BF16 4, 64, 3
+#define ASRBACK_SHAPE_WHISPER_SELF_BF16 4, 64, 2
 #endif
 #ifndef ASRBACK_SHAPE_WHISPER_CROSS_BF16
 #define ASRBACK_SHAPE_WHISPER_CROSS_BF16 8, 128, 2
