@@ -274,6 +274,32 @@ def test_qwen3_step_random(tag, batch, bucket, heads):
     assert attention.read_status() == 0
 
 
+@pytest.mark.parametrize("tag", ["bf16", "fp32"])
+def test_qwen3_split_pairs_match_the_workspace_merge(tag, monkeypatch):
+    """At 64 rows every row is cut in two splits, which run as a 2-CTA
+    cluster handing split 1's state to split 0 in shared memory; with
+    ASRBACK_SPLIT_PAIR=0 the same splits merge through the workspace. Both
+    give the same outputs (to merge rounding) and the same cache writes, for
+    rows that use one split or two."""
+    dtype = DTYPES[tag]
+    gen = torch.Generator().manual_seed(64)
+    batch, bucket, heads = 64, 1024, 16
+    qkv, qn, kn, cos, sin, k_store, v_store, positions = _qwen3_inputs(gen, batch, bucket, heads, dtype)
+    results = []
+    for pair in ("1", "0"):
+        monkeypatch.setenv("ASRBACK_SPLIT_PAIR", pair)
+        kd, vd = k_store.to(DEV), v_store.to(DEV)
+        out = attention.qwen3_attention_step(qkv.to(DEV), qn.to(DEV), kn.to(DEV), 1e-6, cos.to(DEV),
+                                             sin.to(DEV), positions.to(DEV), kd[:batch, :bucket],
+                                             vd[:batch, :bucket], heads, 8)
+        results.append((host(out), host(kd), host(vd)))
+    (o1, k1, v1), (o0, k0, v0) = results
+    np.testing.assert_allclose(o1, o0, atol=TOL[dtype], rtol=0)
+    np.testing.assert_array_equal(k1, k0)
+    np.testing.assert_array_equal(v1, v0)
+    assert attention.read_status() == 0
+
+
 @pytest.mark.parametrize("batch,length", [(1, 1500), (2, 300)])
 def test_encoder_attention_random(batch, length):
     gen = torch.Generator().manual_seed(length)
