@@ -104,6 +104,20 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
                : "memory");
 }
 
+// Stores `v` with release at cluster scope into another CTA's shared memory
+// (address from cluster_map): the writes before it are visible to a reader
+// that acquires the value.
+__device__ __forceinline__ void st_release_cluster_u32(uint32_t remote, uint32_t v) {
+  asm volatile("st.release.cluster.shared::cluster.u32 [%0], %1;" ::"r"(remote), "r"(v) : "memory");
+}
+
+// Loads this CTA's shared-memory word with acquire at cluster scope.
+__device__ __forceinline__ uint32_t ld_acquire_cluster_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cluster.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
+  return v;
+}
+
 // try_wait with acquire at cluster scope (the arrival came from another CTA).
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t done;

@@ -77,9 +77,10 @@ struct DecodeParams {
   int groups;                // key/value head groups (grid.y)
   int chunk;                 // key positions per split
   int num_splits;            // grid.x
-  // Qwen3 with exactly two splits, launched as clusters of 2 CTAs along x:
-  // split 1 hands its partial to split 0 through split 0's shared memory.
-  int pair_splits;
+  // Qwen3 split clusters: a row's num_splits CTAs (2..C::CLUSTER_MAX) are
+  // launched as one thread-block cluster along x, and splits 1.. hand their
+  // partial states to split 0 through split 0's shared memory. 0: off.
+  int cluster_splits;
   float* partial;            // workspace partials
   int* counters;             // workspace counters, one per (row, group)
   int32_t* status;           // device status word (may be null)
@@ -123,10 +124,15 @@ struct DecodeConfig {
   static constexpr int OFF_WEIGHTS = OFF_MERGE + MERGE_FLOATS * 4;
   static constexpr int OFF_BAR =
       ((SCRATCH_IN_RING ? RING_BYTES : RING_BYTES + SCRATCH_BYTES) + 15) / 16 * 16;
-  // Split pair (Qwen3): a barrier and split 1's partial state, [QH][D + 2].
-  static constexpr int OFF_XBAR = OFF_BAR + 2 * STAGES * 8 + 16;
-  static constexpr int OFF_XFER = OFF_XBAR + 16;
-  static constexpr int XFER_BYTES = MODE == 2 ? 16 + QH * (D + 2) * 4 : 0;
+  // Split cluster (Qwen3): a ready flag per split, then splits 1..'s partial
+  // states, [CLUSTER_MAX - 1][QH][D + 2], in split 0's shared memory. As
+  // many splits as fit in 227 KB, at most 4 (the cluster sizes used).
+  static constexpr int OFF_XFLAG = OFF_BAR + 2 * STAGES * 8 + 16;
+  static constexpr int OFF_XFER = OFF_XFLAG + 64;
+  static constexpr int XSLOT_BYTES = QH * (D + 2) * 4;
+  static constexpr int CLUSTER_FIT = 1 + (227 * 1024 - OFF_XFER - 1024) / XSLOT_BYTES;
+  static constexpr int CLUSTER_MAX = MODE != 2 ? 0 : CLUSTER_FIT > 4 ? 4 : CLUSTER_FIT;
+  static constexpr int XFER_BYTES = MODE == 2 ? 64 + (CLUSTER_MAX - 1) * XSLOT_BYTES : 0;
   static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8 + 16 + XFER_BYTES;
   // CTAs per SM that shared memory (228 KB, 1 KB reserved per CTA) and the
   // 2048-thread limit allow; registers are budgeted to match.
@@ -242,15 +248,12 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   // before the previous kernel of the stream has finished, so it reads no
   // input (positions, caches, queries, workspace) before that kernel is done;
   // then the next launch may begin to be scheduled.
-  // A split pair's barrier is set up, and the pair meets, before anything
-  // can return: then split 1 may arrive on split 0's barrier at any time.
-  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + C::OFF_XBAR);
+  // A split cluster's ready flags are cleared, and the cluster meets, before
+  // anything can return: then any split may set its flag in split 0.
+  uint32_t* xflag = reinterpret_cast<uint32_t*>(smem + C::OFF_XFLAG);
   if constexpr (MODE == kQwen3) {
-    if (p.pair_splits) {
-      if (threadIdx.x == 0) {
-        mbar_init(xbar, 1);
-        fence_barrier_init();
-      }
+    if (p.cluster_splits) {
+      if (threadIdx.x < 8) xflag[threadIdx.x] = 0u;
       cluster_sync();
     }
   }
@@ -576,18 +579,21 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
     return;
   }
 
-  // A split pair: split 1 writes its state into split 0's shared memory and
-  // arrives on split 0's barrier; split 0 folds it into its own and writes
-  // the output. No workspace, counter or global round trip.
+  // A split cluster: splits 1.. write their states into split 0's shared
+  // memory and set their ready flags there (release); split 0 waits for the
+  // flags of the row's active splits (acquire), folds the states into its own
+  // and writes the output. No workspace, counter or global round trip. A
+  // split past the row's active ones has already returned without touching
+  // split 0, and split 0 stays until every active split has set its flag.
   if constexpr (MODE == kQwen3) {
-    if (p.pair_splits) {
+    if (p.cluster_splits) {
       float* xfer = reinterpret_cast<float*>(smem + C::OFF_XFER);
-      if (split == 1) {
+      if (split > 0) {
         if (owner) {
 #pragma unroll
           for (int qi = 0; qi < QPK; ++qi) {
-            const uint32_t slot =
-                cluster_map(smem_addr(xfer + (g * QPK + qi) * (D + 2)), 0);
+            const uint32_t slot = cluster_map(
+                smem_addr(xfer + ((split - 1) * QH + g * QPK + qi) * (D + 2)), 0);
 #pragma unroll
             for (int j = 0; j < 8; ++j) st_cluster_f32(slot + 4 * S::elem(c, j), o[qi][j]);
             if (c == 0) {
@@ -598,22 +604,26 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
           fence_cluster();
         }
         named_sync(1, C::CTHREADS);
-        if (threadIdx.x == 0) mbar_arrive_cluster(cluster_map(smem_addr(xbar), 0));
+        if (threadIdx.x == 0) st_release_cluster_u32(cluster_map(smem_addr(xflag + split), 0), 1u);
         return;
       }
       if (owner) {
-        // Two budgets: split 1 may itself have waited out one on its tiles.
-        bool got = false;
-        for (int attempt = 0; attempt < 2 && !got; ++attempt) {
-          const uint64_t until = global_timer_ns() + kWaitBudgetNs;
-          while (!(got = mbar_try_wait_cluster(xbar, 0)) && global_timer_ns() < until) {
+        // Two budgets: a split may itself have waited out one on its tiles.
+        bool got = true;
+        for (int s2 = 1; s2 < active && got; ++s2) {
+          got = false;
+          for (int attempt = 0; attempt < 2 && !got; ++attempt) {
+            const uint64_t until = global_timer_ns() + kWaitBudgetNs;
+            while (!(got = ld_acquire_cluster_u32(xflag + s2) != 0u) &&
+                   global_timer_ns() < until) {
+            }
           }
         }
         if (!got && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
 #pragma unroll
         for (int qi = 0; qi < QPK; ++qi) {
-          if (got) {
-            const float* slot = xfer + (g * QPK + qi) * (D + 2);
+          for (int s2 = 1; s2 < active && got; ++s2) {
+            const float* slot = xfer + ((s2 - 1) * QH + g * QPK + qi) * (D + 2);
             float o2[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) o2[j] = slot[S::elem(c, j)];
@@ -890,16 +900,16 @@ int run(DecodeParams& p, int batch, int units, int qh_per_unit, void* workspace,
   return launch<C>(p, batch, stream);
 }
 
-// Split pairs are on unless ASRBACK_SPLIT_PAIR=0 (A/B timing); read at every
-// call so that one process can compare both.
+// Split clusters are on unless ASRBACK_SPLIT_PAIR=0 (A/B timing); read at
+// every call so that one process can compare both.
 bool pair_enabled() {
   const char* env = std::getenv("ASRBACK_SPLIT_PAIR");
   return !(env && env[0] == '0');
 }
 
-// Launches config C with each row's two splits as one cluster of 2 CTAs.
+// Sets config C's dynamic shared-memory limit once per device.
 template <class C>
-int launch_pair(const DecodeParams& p, int batch, cudaStream_t stream) {
+int prepare_smem(int* device_out) {
   auto kernel = decode_attention_kernel<C>;
   static thread_local int prepared_device = -1;
   int device = 0;
@@ -911,21 +921,72 @@ int launch_pair(const DecodeParams& p, int batch, cudaStream_t stream) {
       return rc;
     prepared_device = device;
   }
-  return launch_pdl_cluster(kernel, dim3(2, p.groups, batch), dim3(C::THREADS), C::SMEM, 2,
-                            stream, "decode attention launch (split pairs)", p);
+  *device_out = device;
+  return ASRBACK_OK;
 }
 
-// Qwen3: one unit per (row, group of C::G key/value heads). Rows cut in two
-// splits run as split pairs (no workspace); others merge through it.
+// How many clusters of `size` CTAs of config C the device runs at once
+// (cached per device and size; 0 if it cannot run one).
+template <class C>
+int active_clusters(int size) {
+  static thread_local int cached_device = -1;
+  static thread_local int cache[9];
+  int device = 0;
+  if (prepare_smem<C>(&device) != ASRBACK_OK) return 0;
+  if (cached_device != device) {
+    for (int& n : cache) n = -1;
+    cached_device = device;
+  }
+  if (cache[size] < 0) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(size, 1, 1);
+    config.blockDim = dim3(C::THREADS);
+    config.dynamicSmemBytes = C::SMEM;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeClusterDimension;
+    attribute[0].val.clusterDim.x = size;
+    attribute[0].val.clusterDim.y = 1;
+    attribute[0].val.clusterDim.z = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, decode_attention_kernel<C>, &config) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    cache[size] = n;
+  }
+  return cache[size];
+}
+
+// Launches config C with each row's splits as one cluster along x.
+template <class C>
+int launch_cluster(const DecodeParams& p, int batch, cudaStream_t stream) {
+  int device = 0;
+  if (int rc = prepare_smem<C>(&device)) return rc;
+  return launch_pdl_cluster(decode_attention_kernel<C>, dim3(p.num_splits, p.groups, batch),
+                            dim3(C::THREADS), C::SMEM, p.num_splits, stream,
+                            "decode attention launch (split clusters)", p);
+}
+
+// Qwen3: one unit per (row, group of C::G key/value heads). When the
+// heuristic cuts rows in 2 or 4 splits and all the clusters fit on the
+// device at once, a row's splits run as one cluster (no workspace);
+// otherwise, or with clusters off, the splits merge through the workspace.
+// (Measured on B200, 28-layer graphs: clusters of 2 and 4 splits were
+// faster than the workspace merge, 26.4 against 28.2 us at 64 rows and 18.9
+// against 19.8 at 32; clusters of 3 and 8 slower, 25.4 against 23.4 at 48
+// rows and 17.9 against 17.6 at 16.)
 template <class C>
 int run_qwen3(DecodeParams& p, int batch, void* workspace, size_t bytes, cudaStream_t stream) {
   static_assert(8 % C::G == 0, "key/value head groups must divide 8");
   p.groups = p.kv_heads / C::G;
   const int units = batch * p.groups;
   split_for<C>(p, units);
-  if (p.num_splits == 2 && pair_enabled()) {
-    p.pair_splits = 1;
-    return launch_pair<C>(p, batch, stream);
+  if ((p.num_splits == 2 || p.num_splits == 4) && p.num_splits <= C::CLUSTER_MAX &&
+      pair_enabled() && active_clusters<C>(p.num_splits) >= units) {
+    p.cluster_splits = p.num_splits;
+    return launch_cluster<C>(p, batch, stream);
   }
   if (int rc = bind_workspace(p, units, C::QH, C::D, workspace, bytes)) return rc;
   return launch<C>(p, batch, stream);

@@ -274,16 +274,17 @@ def test_qwen3_step_random(tag, batch, bucket, heads):
     assert attention.read_status() == 0
 
 
+@pytest.mark.parametrize("batch", [64, 32])
 @pytest.mark.parametrize("tag", ["bf16", "fp32"])
-def test_qwen3_split_pairs_match_the_workspace_merge(tag, monkeypatch):
-    """At 64 rows every row is cut in two splits, which run as a 2-CTA
-    cluster handing split 1's state to split 0 in shared memory; with
-    ASRBACK_SPLIT_PAIR=0 the same splits merge through the workspace. Both
-    give the same outputs (to merge rounding) and the same cache writes, for
-    rows that use one split or two."""
+def test_qwen3_split_clusters_match_the_workspace_merge(tag, batch, monkeypatch):
+    """At 64 (32) rows every row is cut in 2 (4) splits, which run as one
+    thread-block cluster handing the other splits' states to split 0 in its
+    shared memory; with ASRBACK_SPLIT_PAIR=0 the same splits merge through the
+    workspace. Both give the same outputs (to merge rounding) and the same
+    cache writes, for rows that use one split or several."""
     dtype = DTYPES[tag]
-    gen = torch.Generator().manual_seed(64)
-    batch, bucket, heads = 64, 1024, 16
+    gen = torch.Generator().manual_seed(batch)
+    bucket, heads = 1024, 16
     qkv, qn, kn, cos, sin, k_store, v_store, positions = _qwen3_inputs(gen, batch, bucket, heads, dtype)
     results = []
     for pair in ("1", "0"):
