@@ -1,6 +1,6 @@
 """Benchmarks of asrback's attention hot path on B200 (one replica per GPU).
 
-Default workload (the headline): Whisper large-v3-turbo
+Default workload (the headline configuration): Whisper large-v3-turbo
 decoder-step attention in bf16 -- 4 decoder layers, 20 heads x 64, batch 64
 slots whose self-attention lengths start uniform in [1, 448] and grow by one
 per step (rows that reach position 447, the last the cache holds, stay
@@ -11,10 +11,10 @@ key/value write, then the cross-attention; the 8 launches replay from one CUDA
 graph. Unit: decoded tokens (64 per step per GPU).
 
 Other workloads (``--workload``):
-  whisper-encoder  BASELINE config 3: encoder self-attention of 32 layers over
+  whisper-encoder  encoder self-attention of 32 layers over
                    32 windows of 1500 frames (20 x 64, bf16), non-causal; unit:
                    windows (32 per step);
-  qwen3-decode     BASELINE config 4: Qwen3-1.7B-style decode attention, 28
+  qwen3-decode     Qwen3-1.7B-style decode attention, 28
                    layers, 16 query / 8 key-value heads x 128, RoPE theta 1e6,
                    QK-RMSNorm, batch 64 rows whose caches hold the 410-position
                    prompt (390 audio + 20 text positions), then one position
@@ -228,7 +228,7 @@ def run_cpu(fn, rows, budget_s: float, threads: int):
 # -------------------------------------------------------------- workloads ----
 
 class WhisperDecode:
-    """Whisper large-v3-turbo decoder-step attention."""
+    """The headline: Whisper large-v3-turbo decoder-step attention."""
 
     name = "whisper-decode"
     metric = DECODE_METRIC
@@ -403,7 +403,7 @@ class WhisperDecode:
 
 
 class WhisperEncoder:
-    """the encoder's self-attention prefill."""
+    """Whisper large-v3-turbo encoder self-attention prefill."""
 
     name = "whisper-encoder"
     metric = "encoder windows/s/GPU (32 windows x 1500 frames, 32 layers, bf16); attention TFLOP/s"
@@ -518,7 +518,7 @@ class WhisperEncoder:
 
 
 class Qwen3Decode:
-    """BASELINE config 4: Qwen3-1.7B-style decode attention."""
+    """Qwen3-1.7B-style decode attention."""
 
     name = "qwen3-decode"
     metric = "decoder tokens/s/GPU (Qwen3 1.7B-style, batch 64, bf16); attention HBM GB/s"
@@ -663,7 +663,7 @@ class Qwen3Decode:
 
 
 class Qwen3Prefill:
-    """Admission prefill of BASELINE config 4's prompts: causal grouped-query
+    """Admission prefill of the Qwen3 decode workload's prompts: causal grouped-query
     attention within the packed prompts (TextAttention.prefill's `attend`)."""
 
     name = "qwen3-prefill"
@@ -809,7 +809,7 @@ class Qwen3AudioWindows(Qwen3Prefill):
 
     def config(self, world: int) -> dict:
         return {
-            "workload": "Qwen3-ASR-style audio encoder window attention (SURVEY 8(f) rank 3 row)",
+            "workload": "Qwen3-ASR-style audio encoder window attention (admission of audio windows)",
             "layers": self.layers, "heads": self.heads, "head_dim": self.head_dim,
             "causal": False, "requests_per_gpu": self.batch, "tokens_per_request": self.prompt,
             "window_tokens": self.window, "global_batch": self.batch * world,
@@ -883,8 +883,8 @@ class Qwen3AudioWindows(Qwen3Prefill):
 
 
 class WhisperCrossKV:
-    """Admission of BASELINE config 3's windows into the decoder (SURVEY 8(f)
-    rank 2): `set_encoder_output` (whisper.py:313-319), each of the 4 decoder
+    """Admission of 32 encoded windows into the decoder:
+    `set_encoder_output` (whisper.py:313-319), each of the 4 decoder
     layers' cross-attention keys/values projected from the encoder output and
     written into the cache."""
 
@@ -903,7 +903,7 @@ class WhisperCrossKV:
     def config(self, world: int) -> dict:
         return {
             "workload": "Whisper large-v3-turbo set_encoder_output: k_proj/v_proj of the encoder "
-                        "output into the cross-attention cache (SURVEY 8(f) rank 2 row)",
+                        "output into the cross-attention cache (window admission)",
             "layers": self.layers, "width": self.width, "heads": self.heads,
             "frames": self.tokens, "windows_per_gpu": self.batch,
             "global_batch": self.batch * world,
@@ -1000,8 +1000,8 @@ class WhisperCrossKV:
 
 
 class WhisperPrefix:
-    """The prompt pass of BASELINE config 3's windows at admission (SURVEY
-    8(f) rank 2): `decode(tokens, positions[:P], cache, length=P)`
+    """The prompt pass of 32 windows at admission:
+    `decode(tokens, positions[:P], cache, length=P)`
     (whisper.py:847-849) for 32 windows sharing the 4-token start sequence
     (windows queued together share a prefix length), the attention of its 4
     decoder layers: causal self-attention over the P written keys
@@ -1025,7 +1025,7 @@ class WhisperPrefix:
     def config(self, world: int) -> dict:
         return {
             "workload": "Whisper large-v3-turbo prompt pass attention (decode with length=P, "
-                        "SURVEY 8(f) rank 2 row)",
+                        "window admission)",
             "layers": self.layers, "heads": self.heads, "head_dim": self.dim,
             "prompt_tokens": self.tokens, "frames": self.frames,
             "windows_per_gpu": self.batch, "global_batch": self.batch * world,
@@ -1147,9 +1147,9 @@ class WhisperPrefix:
 
 
 class WhisperGreedyStep:
-    """The step epilogue after the decoder (SURVEY 8(f) rank 4): logits against
+    """The step epilogue after the decoder: logits against
     the tied embedding, greedy `_choose` with the suppress mask and the state
-    update (whisper.py:949-975), BASELINE config 2 widths, 64 rows."""
+    update (whisper.py:949-975), Whisper large-v3-turbo widths, 64 rows."""
 
     name = "whisper-step"
     family = "whisper"
@@ -1169,7 +1169,7 @@ class WhisperGreedyStep:
     def config(self, world: int) -> dict:
         return {
             "workload": f"{self.family} greedy step epilogue (logits GEMM + _choose + state "
-                        "update; SURVEY 8(f) rank 4 row)",
+                        "update after the decoder)",
             "vocab": self.vocab, "hidden": self.width, "rows_per_gpu": self.batch,
             "global_batch": self.batch * world, "suppress": self.family == "whisper",
             "eos_ids": list(self.eos), "steps_per_replay": self.copies,

@@ -98,7 +98,7 @@ def test_step_matches_reference(family, tag):
 
 
 @pytest.mark.parametrize("vocab,width,batch", [
-    (51866, 1280, 64),    # Whisper large-v3-turbo
+    (51866, 1280, 64),    # Whisper large-v3-turbo, the headline widths
     (151936, 2048, 64),   # Qwen3-ASR-1.7B lm_head, config 4
     (151936, 1024, 64),   # Qwen3-0.6B, config 5
     (51866, 1280, 1),
