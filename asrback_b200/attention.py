@@ -55,11 +55,20 @@ class DeviceStatusError(RuntimeError):
 
 class _DeviceState:
     """Per-device status word and split-KV workspace (zero-filled, grown on
-    demand outside graph capture; the kernels leave its counters at zero)."""
+    demand outside graph capture; the kernels leave its counters at zero).
+
+    A workspace that a call has used is never freed. The reference captures one
+    graph per (batch, length) bucket in turn (``whisper.py:710-725``,
+    ``qwen3_asr.py:930-948``), and the workspace a bucket needs is not monotonic
+    in the bucket, so a later capture's warm-up may grow it; graphs captured
+    before keep the old buffer's address baked in and must find it intact (its
+    counters at zero) on every replay. Superseded buffers therefore stay alive
+    in ``retired`` for the life of the process."""
 
     def __init__(self, device: torch.device) -> None:
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.workspace = torch.zeros(0, dtype=torch.uint8, device=device)
+        self.retired: list[Tensor] = []
 
     def workspace_for(self, nbytes: int) -> Tensor:
         if nbytes > self.workspace.numel():
@@ -69,6 +78,8 @@ class _DeviceState:
                     "capture; run the step once before capturing it (CapturedGraph's "
                     "warm-up does) or call reserve_workspace() first"
                 )
+            if self.workspace.numel():
+                self.retired.append(self.workspace)
             self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.status.device)
         return self.workspace
 

@@ -82,6 +82,20 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
+// The cluster's exit barrier: a thread that will not touch another CTA's
+// shared memory again arrives (release: its remote stores come first) and may
+// then return without waiting.
+__device__ __forceinline__ void cluster_exit_arrive() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+
+// The exit barrier for a CTA whose shared memory others write: arrive, then
+// wait until every thread of the cluster has arrived, so that no remote store
+// can land after this CTA has returned.
+__device__ __forceinline__ void cluster_exit_wait() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
 // This CTA's shared-memory address `addr` as seen in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
   uint32_t out;

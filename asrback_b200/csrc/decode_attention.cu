@@ -251,6 +251,11 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   // A split cluster's ready flags are cleared, and the cluster meets, before
   // anything can return: then any split may set its flag in split 0.
   uint32_t* xflag = reinterpret_cast<uint32_t*>(smem + C::OFF_XFLAG);
+  // In a split cluster every thread also meets the cluster's exit barrier
+  // exactly once before it returns: split 0's threads wait there, the others
+  // only arrive. So split 0 stays resident until no other split can store
+  // into its shared memory, even when its bounded wait for a flag gave up.
+  const bool in_cluster = MODE == kQwen3 && p.cluster_splits != 0;
   if constexpr (MODE == kQwen3) {
     if (p.cluster_splits) {
       if (threadIdx.x < 8) xflag[threadIdx.x] = 0u;
@@ -303,6 +308,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
         }
         if (threadIdx.x == 0 && p.status) atomicOr(p.status, ASRBACK_STATUS_POSITION);
       }
+      if (in_cluster) cluster_exit_arrive();
       return;
     }
     pos = static_cast<int>(given);
@@ -314,7 +320,10 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   int active = min(p.num_splits, (n_total + p.chunk - 1) / p.chunk);
   const int per = ((n_total + active - 1) / active + TP - 1) / TP * TP;
   active = (n_total + per - 1) / per;
-  if (split >= active) return;
+  if (split >= active) {
+    if (in_cluster) cluster_exit_arrive();
+    return;
+  }
   const int k0 = split * per;
   const int k1 = min(k0 + per, n_cached);
   const int n_tiles = k1 > k0 ? (k1 - k0 + TP - 1) / TP : 0;
@@ -373,6 +382,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
         }
       }
     }
+    if (in_cluster) cluster_exit_arrive();
     return;
   }
 
@@ -576,6 +586,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
         }
       }
     }
+    if (in_cluster) cluster_exit_arrive();
     return;
   }
 
@@ -605,6 +616,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
         }
         named_sync(1, C::CTHREADS);
         if (threadIdx.x == 0) st_release_cluster_u32(cluster_map(smem_addr(xflag + split), 0), 1u);
+        cluster_exit_arrive();
         return;
       }
       if (owner) {
@@ -636,6 +648,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
           S::store(out_row + (int64_t)(kv_head * QPK + qi) * p.o_sh, c, r);
         }
       }
+      cluster_exit_wait();
       return;
     }
   }

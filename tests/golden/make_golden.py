@@ -3,6 +3,9 @@ PyTorch modules (asrback, imported read-only) on CPU.
 
     python tests/golden/make_golden.py [--reference /path/to/asrback]
 
+Without ``--reference`` the reference is looked up as ``oracle/reference.py``
+describes (``$ASRBACK_REFERENCE``, then ``baseline/_ref``).
+
 The reference imports ``asrfront`` (its audio front end), which is not
 installed; none of the code run here calls into it, so a stub module with the
 constants read at import time stands in for it. Each fixture records the
@@ -20,8 +23,8 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
-import types
 from pathlib import Path
 
 import numpy as np
@@ -33,21 +36,8 @@ REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
 
 from asrback_b200.synthetic import seeded_normal, seeded_parameters  # noqa: E402
-
-
-def install_asrfront_stub() -> None:
-    """An ``asrfront`` with the module constants the reference reads at import."""
-    constants = dict(SAMPLE_RATE=16000, N_SAMPLES=480000, HOP_LENGTH=160, MAX_SAMPLES=480000,
-                     N_MELS=128)
-    stub = types.ModuleType("asrfront")
-    for name in ("whisper", "qwen3_asr", "sensevoice", "gemma4"):
-        setattr(stub, name, types.SimpleNamespace(**constants))
-
-    def unavailable(*args, **kwargs):
-        raise RuntimeError("asrfront is not installed (stub)")
-
-    stub.load = unavailable
-    sys.modules["asrfront"] = stub
+from oracle import reference as reference_env  # noqa: E402
+from oracle.reference import install_asrfront_stub  # noqa: E402,F401
 
 
 class SdpaRecorder:
@@ -492,17 +482,83 @@ def step_epilogue(whisper, qwen3, dtype: torch.dtype, tag: str) -> None:
          **arrays)
 
 
+def whisper_config1(ref) -> None:
+    """BASELINE config 1 on the reference's own classes, unpatched, CPU fp32:
+    the model-level run (encoder over the mel batch, ``set_encoder_output``,
+    the prompt pass, 64 greedy ``Transcriber._step`` calls) and the engine run
+    (the eight windows queued to a ``Transcriber`` loaded from a checkpoint
+    directory of the same weights; its worker admits, prefills, steps and
+    finishes them)."""
+    import tempfile
+
+    from tests import reference_models as rm
+
+    model, mel = rm.whisper_config1(ref)
+    out = rm.run_whisper_steps(ref, model, mel, rm.CONFIG1_STEPS, graph=False)
+    save("whisper_config1_model",
+         dict(config=rm.WHISPER_TINY, seed=0, steps=rm.CONFIG1_STEPS, prefix=rm.WHISPER_PREFIX,
+              site="whisper.py:140-153 (encoder), :313-319, :828-878 (prompt pass), "
+                   ":942-975 (_step)", encoder_sample="encoded[:, ::50]", hidden_every=4),
+         **out)
+    with tempfile.TemporaryDirectory() as tmp:
+        directory = rm.write_whisper_model_dir(Path(tmp) / "whisper-config1", model)
+        transcriber = ref.whisper.Transcriber(directory, device="cpu", dtype="float32",
+                                              max_batch_size=8, batch_wait_ms=500.0,
+                                              cuda_graphs=False)
+        results = rm.submit_whisper_jobs(ref, transcriber, mel.numpy(), rm.CONFIG1_STEPS)
+    width = max(len(r["tokens"]) for r in results)
+    tokens = np.full((len(results), width), -1, np.int64)
+    for i, r in enumerate(results):
+        tokens[i, :len(r["tokens"])] = r["tokens"]
+    save("whisper_config1_engine",
+         dict(config=rm.WHISPER_TINY, seed=0, max_new_tokens=rm.CONFIG1_STEPS,
+              jobs=rm.config1_jobs(), languages=[r["language"] for r in results],
+              site="whisper.py:728-940 (Transcriber._serve/_admit/_prefill/_advance/_finish)"),
+         tokens=tokens, lengths=np.array([len(r["tokens"]) for r in results]),
+         avg_logprob=np.array([r["avg_logprob"] for r in results]),
+         no_speech_prob=np.array([r["no_speech_prob"] for r in results]))
+
+
+def qwen3_graph_decode(ref) -> None:
+    """The reference's ``TextModel`` (Qwen3-1.7B widths, 4 layers) in bf16 on
+    the CPU: packed prefill of four ragged prompts, then 16 greedy steps."""
+    from tests import reference_models as rm
+
+    model, lm_head = rm.qwen3_text_model(ref, torch.bfloat16, "cpu")
+    out = rm.run_qwen3_steps(ref, model, lm_head, None, graph=False)
+    save("qwen3_graph_decode_bf16",
+         dict(config=rm.QWEN3_1_7B_4L, seed=3, lm_head_seed=4, prompts=rm.QWEN3_PROMPTS,
+              steps=rm.QWEN3_STEPS, bucket=rm.QWEN3_BUCKET, rope_theta=1e6,
+              site="qwen3_asr.py:463-524 (TextModel.prefill / step) + lm_head argmax"),
+         **out)
+
+
+def whisper_turbo_decode(ref) -> None:
+    """The reference's Whisper decoder at large-v3-turbo widths (4 layers) in
+    bf16 on the CPU: ``set_encoder_output``, the prompt pass, ragged rows, then
+    24 greedy fixed-shape steps over the 64-position bucket view."""
+    from tests import reference_models as rm
+
+    model = rm.whisper_turbo_decoder(ref, torch.bfloat16, "cpu")
+    out = rm.run_turbo_steps(ref, model, None, graph=False)
+    save("whisper_turbo_decode_bf16",
+         dict(config=rm.WHISPER_TURBO_4L, seed=1, encoder_seed=41, steps=rm.TURBO_STEPS,
+              site="whisper.py:255-342 (decoder step, logits argmax), :313-319"),
+         **out)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", default="/root/reference",
-                        help="checkout of sjjeong94/asrback (read-only)")
+    parser.add_argument("--reference", default=None,
+                        help="checkout of sjjeong94/asrback (read-only); default: "
+                             "$ASRBACK_REFERENCE, then baseline/_ref")
     parser.add_argument("--only", default=None, help="generate only the fixtures whose "
                         "generator function has this name")
     args = parser.parse_args()
-    install_asrfront_stub()
-    sys.path.insert(0, str(Path(args.reference) / "src"))
-    from asrback.models import qwen3_asr as qwen3  # noqa: E402
-    from asrback.models import whisper  # noqa: E402
+    if args.reference:
+        os.environ["ASRBACK_REFERENCE"] = args.reference
+    ref = reference_env.load()
+    whisper, qwen3 = ref.whisper, ref.qwen3_asr
 
     torch.set_num_threads(8)
     per_dtype = (whisper_step, whisper_prefix, qwen3_step, encoder_attention, qwen3_varlen)
@@ -518,6 +574,12 @@ def main() -> None:
         whisper_tiny_decode(whisper)
     if args.only in (None, "qwen3_small_decode"):
         qwen3_small_decode(qwen3)
+    if args.only in (None, "whisper_config1"):
+        whisper_config1(ref)
+    if args.only in (None, "qwen3_graph_decode"):
+        qwen3_graph_decode(ref)
+    if args.only in (None, "whisper_turbo_decode"):
+        whisper_turbo_decode(ref)
 
 
 if __name__ == "__main__":

@@ -35,3 +35,22 @@ def initial_state(g: dict, family: str) -> dict:
     state = {name: g[f"{family}_{name}0"] for name in STATE_FIELDS}
     state["generated"] = g[f"{family}_generated0"]
     return state
+
+
+def cross_kv_weights(config: dict, seed: int, bf16: bool) -> list[tuple]:
+    """Each decoder layer's cross-attention ``(k_proj.weight, v_proj.weight,
+    v_proj.bias)`` as float32 arrays, as ``seeded_parameters(model.model.decoder,
+    seed)`` fills the reference's decoder (rounded through bf16 when ``bf16``)."""
+    from asrback_b200.synthetic import seeded_parameter
+
+    width = config["d_model"]
+    layers = []
+    for index in range(config["decoder_layers"]):
+        prefix = f"layers.{index}.encoder_attn."
+        tensors = (seeded_parameter(prefix + "k_proj.weight", (width, width), seed),
+                   seeded_parameter(prefix + "v_proj.weight", (width, width), seed),
+                   seeded_parameter(prefix + "v_proj.bias", (width,), seed))
+        if bf16:
+            tensors = tuple(t.to(torch.bfloat16).float() for t in tensors)
+        layers.append(tuple(t.numpy() for t in tensors))
+    return layers

@@ -15,9 +15,8 @@ import torch
 import torch.nn.functional as F
 
 from asrback_b200 import attention
-from asrback_b200.synthetic import seeded_parameters
-from asrback_b200.whisper import WhisperForConditionalGeneration
 from tests.golden import load
+from tests.step_fixtures import cross_kv_weights
 
 pytestmark = pytest.mark.gpu
 
@@ -32,19 +31,28 @@ def clean_status():
 
 @pytest.mark.parametrize("tag", ["fp32", "bf16"])
 def test_set_encoder_output_matches_reference(tag):
+    """The op, one call per decoder layer into the ``(layers, rows, heads,
+    frames, 64)`` cross cache, as ``set_encoder_output`` runs it, against the
+    reference's recorded cache (two windows into a three-row cache: the third
+    row stays zero)."""
     g = load(f"cross_kv_{tag}")
     dtype = torch.float32 if tag == "fp32" else torch.bfloat16
-    model = WhisperForConditionalGeneration(g["meta"]["config"], encoder=False)
-    seeded_parameters(model.model.decoder, g["meta"]["seed"])
-    model = model.to(DEV, dtype)
-    cache = model.allocate_cache(3)
+    config = g["meta"]["config"]
+    heads, width = config["decoder_attention_heads"], config["d_model"]
+    shape = (config["decoder_layers"], 3, heads, config["max_source_positions"], width // heads)
+    cross_keys = torch.zeros(shape, dtype=dtype, device=DEV)
+    cross_values = torch.zeros(shape, dtype=dtype, device=DEV)
     states = torch.from_numpy(g["states"]).to(DEV, dtype)
-    with torch.no_grad():
-        model.set_encoder_output(cache, states)
+    batch = states.shape[0]
+    for index, (k_weight, v_weight, v_bias) in enumerate(
+            cross_kv_weights(config, g["meta"]["seed"], bf16=tag == "bf16")):
+        attention.whisper_cross_kv_projection(
+            states, *(torch.from_numpy(t).to(DEV, dtype) for t in (k_weight, v_weight, v_bias)),
+            cross_keys[index, :batch], cross_values[index, :batch])
     tol = 1e-4 if tag == "fp32" else 2e-2
-    np.testing.assert_allclose(cache.cross_keys.float().cpu().numpy(), g["cross_keys"], atol=tol,
+    np.testing.assert_allclose(cross_keys.float().cpu().numpy(), g["cross_keys"], atol=tol,
                                rtol=0)
-    np.testing.assert_allclose(cache.cross_values.float().cpu().numpy(), g["cross_values"],
+    np.testing.assert_allclose(cross_values.float().cpu().numpy(), g["cross_values"],
                                atol=tol, rtol=0)
     assert attention.read_status() == 0
 

@@ -416,167 +416,37 @@ def test_graph_capture_replays_with_new_positions():
     assert torch.equal(got_cross, result["cross"])
 
 
-# ------------------------------------------------------------ model level ----
+def test_graphs_of_earlier_buckets_survive_a_workspace_growth():
+    """The reference captures one graph per batch bucket in ascending order;
+    when a later bucket's warm-up needs a larger split workspace, the graphs
+    captured before keep the buffer they baked in (it is never freed), so
+    replaying them still matches an eager call."""
+    from asrback_b200.transcription import CapturedGraph
 
-def test_whisper_tiny_greedy_steps_match_reference():
-    """Whisper-tiny decoder (fp32, seeded weights) over the fixture's ragged
-    rows: hidden states within 1e-3 and argmax tokens identical on >= 99% of
-    the steps (teacher-forced on the reference's tokens)."""
-    from asrback_b200 import whisper
-    from asrback_b200.synthetic import seeded_normal, seeded_parameters
+    lib = _native.load()
+    heads, dim, length = 20, 64, 1500
+    need = {b: lib.asrback_decode_workspace_bytes(b, heads, dim, length) for b in range(1, 65)}
+    small = 1
+    large = next((b for b in range(2, 65) if need[b] > need[small]), None)
+    assert large is not None, need
+    gen = torch.Generator().manual_seed(21)
+    xk = _rand(gen, (large, heads, length, dim), torch.bfloat16).to(DEV)
+    xv = _rand(gen, (large, heads, length, dim), torch.bfloat16).to(DEV)
+    q = _rand(gen, (large, heads, dim), torch.bfloat16).to(DEV)
+    result = {}
 
-    g = load("whisper_tiny_decode")
-    meta = g["meta"]
-    model = whisper.WhisperForConditionalGeneration(meta["config"], encoder=False)
-    seeded_parameters(model.model.decoder, meta["seed"])
-    model = model.to(DEV).eval()
-    batch = len(meta["prompts"])
-    cache = model.allocate_cache(batch)
-    with torch.no_grad():
-        model.set_encoder_output(cache, seeded_normal((batch, 1500, 384), meta["encoder_seed"]).to(DEV))
-        for b, prompt in enumerate(meta["prompts"]):
-            row = cache.rows(b, b + 1)
-            for p, token in enumerate(prompt[:-1]):
-                model.decode(torch.tensor([[token]], device=DEV), torch.tensor([p], device=DEV), row)
-        hidden_err, same = [], []
-        for t in range(meta["steps"]):
-            tokens = dev(g["tokens"][:, t:t + 1], torch.int64)
-            positions = dev(g["positions"][:, t], torch.int64)
-            hidden = model.decode(tokens, positions, cache)[:, -1]
-            choice = model.logits(hidden).float().argmax(dim=-1)
-            hidden_err.append(np.abs(host(hidden) - g["hidden"][:, t]).max())
-            same.append(host(choice) == g["argmax"][:, t])
-    assert max(hidden_err) < 1e-3, max(hidden_err)
-    assert np.mean(same) >= 0.99, np.mean(same)
+    def step(batch):
+        result[batch] = attention.whisper_cross_attention_step(q[:batch], xk[:batch], xv[:batch])
 
-
-@pytest.mark.parametrize("tag", ["fp32", "bf16"])
-def test_whisper_prefix_pass_matches_reference_decoder(tag):
-    """The mirror's eager pass (``decode(tokens, positions[:P], cache,
-    length=P)``): language detection then the prompt pass of a 1-layer
-    decoder with the reference's seeded weights; hidden states against the
-    reference's."""
-    from asrback_b200 import whisper
-    from asrback_b200.synthetic import seeded_normal, seeded_parameters
-
-    dtype = DTYPES[tag]
-    g = load(f"whisper_prefix_{tag}")
-    meta = g["meta"]
-    batch, tokens = meta["batch"], meta["tokens"]
-    model = whisper.WhisperForConditionalGeneration(meta["config"], encoder=False)
-    seeded_parameters(model.model.decoder, 1)
-    model = model.to(DEV, dtype).eval()
-    cache = model.allocate_cache(batch)
-    positions = torch.arange(48, device=DEV)
-    tol = 1e-3 if dtype == torch.float32 else 6e-2
-    with torch.no_grad():
-        model.set_encoder_output(cache, seeded_normal((batch, 40, 384), 12).to(DEV, dtype))
-        hidden = model.decode(torch.full((batch, 1), 5, device=DEV), positions[:1], cache, length=1)
-        np.testing.assert_allclose(host(hidden), g["detect_hidden"], atol=tol, rtol=0)
-        prompt = torch.arange(batch * tokens, device=DEV).view(batch, tokens) % 128
-        hidden = model.decode(prompt, positions[:tokens], cache, length=tokens)
-        np.testing.assert_allclose(host(hidden), g["prompt_hidden"], atol=tol, rtol=0)
-        np.testing.assert_allclose(host(cache.self_keys[0, :, :, :tokens]), g["prompt_self_k"],
-                                   atol=tol, rtol=0)
+    graphs = {batch: CapturedGraph(lambda batch=batch: step(batch)) for batch in (small, large)}
+    for _ in range(3):
+        graphs[small].replay()
+        graphs[large].replay()
+    torch.cuda.synchronize()
+    got = {batch: result[batch].clone() for batch in (small, large)}
+    for batch in (small, large):
+        step(batch)
+    torch.cuda.synchronize()
+    for batch in (small, large):
+        assert torch.equal(got[batch], result[batch]), batch
     assert attention.read_status() == 0
-
-
-def test_whisper_prefix_pass_equals_token_steps():
-    """Size-independent property: the prompt pass over P tokens gives each
-    token the hidden state, and the cache the keys, that P one-token steps
-    give it (fp32, Whisper large-v3-turbo widths, 2 layers, P = 40)."""
-    from asrback_b200 import whisper
-    from asrback_b200.synthetic import seeded_normal, seeded_parameters
-
-    config = whisper.large_v3_turbo_config()
-    config["decoder_layers"] = 2
-    model = whisper.WhisperForConditionalGeneration(config, encoder=False)
-    seeded_parameters(model.model.decoder, 3)
-    model = model.to(DEV).eval()
-    batch, tokens = 4, 40
-    prompt = torch.randint(0, 51866, (batch, tokens), generator=torch.Generator().manual_seed(4)).to(DEV)
-    positions = torch.arange(448, device=DEV)
-    with torch.no_grad():
-        states = seeded_normal((batch, 1500, 1280), 5).to(DEV)
-        pass_cache, step_cache = model.allocate_cache(batch), model.allocate_cache(batch)
-        model.set_encoder_output(pass_cache, states)
-        model.set_encoder_output(step_cache, states)
-        together = model.decode(prompt, positions[:tokens], pass_cache, length=tokens)
-        steps = torch.stack([
-            model.decode(prompt[:, t:t + 1], positions[t].expand(batch), step_cache)[:, 0]
-            for t in range(tokens)], dim=1)
-    np.testing.assert_allclose(host(together), host(steps), atol=1e-3, rtol=0)
-    np.testing.assert_allclose(host(pass_cache.self_keys[:, :, :, :tokens]),
-                               host(step_cache.self_keys[:, :, :, :tokens]), atol=1e-4, rtol=0)
-    assert attention.read_status() == 0
-
-
-def test_qwen3_small_greedy_steps_match_reference():
-    from asrback_b200 import qwen3_asr
-    from asrback_b200.synthetic import seeded_parameters
-
-    g = load("qwen3_small_decode")
-    meta = g["meta"]
-    config = dict(meta["config"], rope_theta=meta["rope_theta"])
-    model = qwen3_asr.TextModel(config)
-    lm_head = torch.nn.Linear(config["hidden_size"], config["vocab_size"], bias=False)
-    seeded_parameters(model, meta["seed"])
-    seeded_parameters(lm_head, meta["lm_head_seed"])
-    model, lm_head = model.to(DEV).eval(), lm_head.to(DEV)
-    cos, sin = qwen3_asr.rope_tables(meta["rope_theta"], 128, 1024, device=DEV)
-    batch = len(meta["prompts"])
-    cache = qwen3_asr.KVCache.allocate(config, batch, 1024, device=DEV, dtype=torch.float32)
-    with torch.no_grad():
-        for b, prompt in enumerate(meta["prompts"]):
-            row = qwen3_asr.KVCache(cache.keys[:, b:b + 1], cache.values[:, b:b + 1])
-            for p, token in enumerate(prompt[:-1]):
-                model.step(torch.tensor([token], device=DEV), torch.tensor([p], device=DEV), row,
-                           cos, sin)
-        hidden_err, same = [], []
-        for t in range(meta["steps"]):
-            hidden = model.step(dev(g["tokens"][:, t], torch.int64),
-                                dev(g["positions"][:, t], torch.int64), cache, cos, sin)
-            choice = lm_head(hidden).argmax(dim=-1)
-            hidden_err.append(np.abs(host(hidden) - g["hidden"][:, t]).max())
-            same.append(host(choice) == g["argmax"][:, t])
-    assert max(hidden_err) < 1e-3, max(hidden_err)
-    assert np.mean(same) >= 0.99, np.mean(same)
-
-
-def test_qwen3_small_packed_prefill_then_steps_match_reference():
-    """The prompts filled by one packed causal prefill (TextModel.prefill on
-    the varlen kernel) instead of one position per step, then the same greedy
-    steps: the same hidden states and tokens as the reference."""
-    from asrback_b200 import qwen3_asr
-    from asrback_b200.synthetic import seeded_parameters
-
-    g = load("qwen3_small_decode")
-    meta = g["meta"]
-    config = dict(meta["config"], rope_theta=meta["rope_theta"])
-    model = qwen3_asr.TextModel(config)
-    lm_head = torch.nn.Linear(config["hidden_size"], config["vocab_size"], bias=False)
-    seeded_parameters(model, meta["seed"])
-    seeded_parameters(lm_head, meta["lm_head_seed"])
-    model, lm_head = model.to(DEV).eval(), lm_head.to(DEV)
-    cos, sin = qwen3_asr.rope_tables(meta["rope_theta"], 128, 1024, device=DEV)
-    batch = len(meta["prompts"])
-    cache = qwen3_asr.KVCache.allocate(config, batch, 1024, device=DEV, dtype=torch.float32)
-    prompts = [prompt[:-1] for prompt in meta["prompts"]]
-    lengths = [len(prompt) for prompt in prompts]
-    tokens = torch.tensor([t for prompt in prompts for t in prompt], device=DEV)
-    rows = torch.tensor([b for b, n in enumerate(lengths) for _ in range(n)], device=DEV)
-    positions = torch.cat([torch.arange(n) for n in lengths]).to(DEV)
-    segments = qwen3_asr.Segments.from_lengths(lengths, torch.device(DEV))
-    with torch.no_grad():
-        model.prefill(model.embed_tokens(tokens), cache, rows, positions, segments,
-                      cos[positions], sin[positions])
-        hidden_err, same = [], []
-        for t in range(meta["steps"]):
-            hidden = model.step(dev(g["tokens"][:, t], torch.int64),
-                                dev(g["positions"][:, t], torch.int64), cache, cos, sin)
-            choice = lm_head(hidden).argmax(dim=-1)
-            hidden_err.append(np.abs(host(hidden) - g["hidden"][:, t]).max())
-            same.append(host(choice) == g["argmax"][:, t])
-    assert attention.read_status() == 0
-    assert max(hidden_err) < 1e-3, max(hidden_err)
-    assert np.mean(same) >= 0.99, np.mean(same)

@@ -205,23 +205,14 @@ def test_cross_kv_projection(tag, tol):
     """``set_encoder_output`` of the reference: each layer's k/v projections,
     split into heads, in the cache rows of the windows given; other rows as
     allocated."""
-    import torch
-
-    from asrback_b200.synthetic import seeded_parameters
-    from asrback_b200.whisper import WhisperForConditionalGeneration
+    from tests.step_fixtures import cross_kv_weights
 
     g = load(f"cross_kv_{tag}")
-    model = WhisperForConditionalGeneration(g["meta"]["config"], encoder=False)
-    seeded_parameters(model.model.decoder, g["meta"]["seed"])
-    if tag == "bf16":
-        model = model.to(torch.bfloat16)
     batch = g["states"].shape[0]
-    for index, layer in enumerate(model.model.decoder.layers):
-        attn = layer.encoder_attn
-        keys, values = oracle.cross_kv_projection(
-            g["states"], attn.k_proj.weight.float().detach().numpy(),
-            attn.v_proj.weight.float().detach().numpy(), attn.v_proj.bias.float().detach().numpy(),
-            bf16=tag == "bf16")
+    for index, (k_weight, v_weight, v_bias) in enumerate(
+            cross_kv_weights(g["meta"]["config"], g["meta"]["seed"], bf16=tag == "bf16")):
+        keys, values = oracle.cross_kv_projection(g["states"], k_weight, v_weight, v_bias,
+                                                  bf16=tag == "bf16")
         length = keys.shape[2]
         np.testing.assert_allclose(keys, g["cross_keys"][index, :batch, :, :length], atol=tol, rtol=0)
         np.testing.assert_allclose(values, g["cross_values"][index, :batch, :, :length], atol=tol,

@@ -10,8 +10,6 @@ writes. This pins the argument layouts the plugin hands to the kernels.
 
 from __future__ import annotations
 
-import sys
-from pathlib import Path
 
 import numpy as np
 import pytest
@@ -20,20 +18,17 @@ import torch
 from asrback_b200 import attention, plugin
 from asrback_b200.synthetic import seeded_normal, seeded_parameters
 from oracle import attention as oracle
+from oracle import reference as reference_env
 
-REFERENCE = Path("/root/reference/src")
-pytestmark = pytest.mark.skipif(not REFERENCE.is_dir(), reason="reference checkout not mounted")
+pytestmark = pytest.mark.skipif(reference_env.find() is None,
+                                reason="asrback reference not found ($ASRBACK_REFERENCE or "
+                                       "baseline/_ref)")
 
 
 @pytest.fixture(scope="module")
 def reference():
-    from tests.golden.make_golden import install_asrfront_stub
-
-    install_asrfront_stub()
-    sys.path.insert(0, str(REFERENCE))
-    from asrback.models import qwen3_asr, whisper
-
-    return whisper, qwen3_asr
+    ref = reference_env.load()
+    return ref.whisper, ref.qwen3_asr
 
 
 @pytest.fixture
