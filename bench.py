@@ -5,10 +5,9 @@ decoder-step attention in bf16 -- 4 decoder layers, 20 heads x 64, batch 64
 slots whose self-attention lengths start uniform in [1, 448] and grow by one
 per step (rows that reach position 447, the last the cache holds, stay
 computed, as in the reference), cross-attention over 1500 encoder frames whose
-keys/values come from N(0, 1) encoder states through the decoder's own k/v
-projections (seeded weights). One step = per layer, the self-attention with its
-key/value write, then the cross-attention; the 8 launches replay from one CUDA
-graph. Unit: decoded tokens (64 per step per GPU).
+keys/values come from N(0, 1) encoder states through seeded k/v projections.
+One step = per layer, the self-attention with its key/value write, then the
+cross-attention. Unit: decoded tokens (64 per step per GPU).
 
 Other workloads (``--workload``):
   whisper-encoder  encoder self-attention of 32 layers over
@@ -31,15 +30,31 @@ Other workloads (``--workload``):
                    windows;
   whisper-prefix   the prompt pass's attention for 32 windows of 4 prompt
                    tokens (decode with length=P): causal self-attention and
-                   cross-attention over 1500 frames, 4 layers; unit: windows.
+                   cross-attention over 1500 frames, 4 layers; unit: windows;
+  qwen3-serve      continuous-batching serving: a
+                   Qwen3-0.6B-style text model (28 layers, hidden 1024) per
+                   GPU fed by seeded Poisson arrivals, rows joining with a
+                   packed prefill and leaving after their tokens; unit:
+                   generated tokens (see ``serve.py``-free notes in the class).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
                     [--workload NAME] [--batch B]
 
-``--impl reference`` times the reference's CPU path for the same workload (the
-CPU oracle port of its attention in float32, all host threads) on a bounded
-sample. Under torchrun every rank runs its own replica (weak scaling, no
-collective on the data path); rank 0 prints one JSON line.
+Timing: W untimed warm-up steps run eagerly; the K timed steps are captured
+as ONE CUDA graph (inputs already in HBM, the step's own inputs per step) and
+the timed region is one replay of it, bracketed by a barrier and a
+synchronize, timed with CUDA events on the launching stream; the value is the
+slowest rank's. The same graph replayed for about ``--sustain-seconds`` gives
+the ``sustained`` figure. ``e2e`` runs the same K steps through the public ops
+with each step's inputs copied from pinned host memory and its outputs copied
+back, double-buffered on two copy streams so the copies overlap the steps.
+
+``--impl reference`` times the reference's CPU path for the same workload:
+the reference's attention call written with torch's CPU operators (its
+``F.scaled_dot_product_attention`` calls with the same masks and grouped
+views), float32 on all host threads, over a bounded sample. Under torchrun
+every rank runs its own replica (weak scaling, no collective on the data
+path); rank 0 prints one JSON line.
 """
 
 from __future__ import annotations
@@ -51,7 +66,6 @@ import os
 import statistics
 import sys
 import time
-from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 import numpy as np
@@ -67,18 +81,16 @@ def parse_args():
     parser.add_argument("--steps", type=int, default=128)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
-    parser.add_argument("--workload", choices=("whisper-decode", "whisper-encoder", "qwen3-decode",
-                                               "qwen3-prefill", "qwen3-audio", "whisper-step",
-                                               "qwen3-step", "whisper-cross-kv",
-                                               "whisper-prefix"),
-                        default="whisper-decode")
+    parser.add_argument("--workload", choices=tuple(WORKLOADS), default="whisper-decode")
     parser.add_argument("--batch", type=int, default=None,
                         help="override the workload's batch (small profiling cases)")
     parser.add_argument("--layers", type=int, default=None,
                         help="override the workload's layer count (small profiling cases that "
                              "keep the batch; not a bench line)")
-    parser.add_argument("--cpu-seconds", type=float, default=10.0,
+    parser.add_argument("--cpu-seconds", type=float, default=8.0,
                         help="time budget of the CPU baseline sample")
+    parser.add_argument("--sustain-seconds", type=float, default=1.0,
+                        help="device time of the sustained (repeated graph replay) figure")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-extras", action="store_true",
                         help="skip the short runs of the other workloads in the default line")
@@ -201,9 +213,48 @@ def profiled_traffic(name: str) -> float | None:
     return None
 
 
-def run_cpu(fn, rows, budget_s: float, threads: int):
-    """Runs fn(step, row) over rows (a list) per step on `threads` threads until
-    `budget_s` seconds have passed (at least one step); returns (steps, seconds)."""
+def rope_tables(torch, theta: float, dim: int, length: int, device=None, dtype=None):
+    """RoPE ``cos``/``sin`` tables ``(length, dim)`` over ``cat(angles,
+    angles)``, computed in float32 then cast (as the reference's engine builds
+    them, qwen3_asr.py:795-803)."""
+    inverse = 1.0 / (theta ** (torch.arange(0, dim, 2).float() / dim))
+    angles = torch.arange(length).float()[:, None] * inverse[None, :]
+    angles = torch.cat((angles, angles), dim=-1)
+    return angles.cos().to(device, dtype), angles.sin().to(device, dtype)
+
+
+def kv_bucket(length: int, buckets=(128, 256, 512, 768, 1024)) -> int:
+    """The reference's Qwen3 key/value view for a step whose longest row holds
+    ``length`` keys (qwen3_asr.py:62, :805-816, :1108-1109)."""
+    return next(size for size in buckets if size >= length)
+
+
+def time_cpu(fn, budget_s: float, limit: int = 4096) -> tuple[int, float]:
+    """Calls fn(i) for i = 0, 1, ... until ``budget_s`` seconds have passed (at
+    least once); returns (calls, seconds)."""
+    start = time.perf_counter()
+    done = 0
+    while True:
+        fn(done)
+        done += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= budget_s or done >= limit:
+            return done, elapsed
+
+
+def cpu_torch(threads: int):
+    """torch on the host cores for a CPU baseline (float32, all threads)."""
+    import torch
+
+    torch.set_num_threads(threads)
+    return torch
+
+
+def run_numpy_pool(fn, rows, budget_s: float, threads: int):
+    """Runs fn(step, row) over rows per step on `threads` threads (numpy, one
+    BLAS thread each) until `budget_s` seconds have passed; returns (steps, s)."""
+    from concurrent.futures import ThreadPoolExecutor
+
     try:
         from threadpoolctl import threadpool_limits
     except ImportError:  # pragma: no cover
@@ -211,14 +262,7 @@ def run_cpu(fn, rows, budget_s: float, threads: int):
     limit = threadpool_limits(1) if threadpool_limits else None
     try:
         with ThreadPoolExecutor(max_workers=threads) as pool:
-            start = time.perf_counter()
-            done = 0
-            while True:
-                list(pool.map(lambda r: fn(done, r), rows))
-                done += 1
-                if time.perf_counter() - start >= budget_s or done >= 1024:
-                    break
-            elapsed = time.perf_counter() - start
+            done, elapsed = time_cpu(lambda i: list(pool.map(lambda r: fn(i, r), rows)), budget_s)
     finally:
         if limit is not None and hasattr(limit, "unregister"):
             limit.unregister()
@@ -227,7 +271,31 @@ def run_cpu(fn, rows, budget_s: float, threads: int):
 
 # -------------------------------------------------------------- workloads ----
 
-class WhisperDecode:
+class Workload:
+    """One pass of a hot-path call site over a batch of synthetic inputs.
+
+    ``inputs_at(t)`` are step t's own device inputs (the tensors a caller
+    hands the ops each step); ``launch(inputs)`` runs the step's kernels on
+    them and returns its outputs. Everything else the step reads (caches,
+    weights, later layers' activations) is set up once in HBM."""
+
+    reference_in_graph = False
+    episode = 1  # distinct per-step inputs kept in HBM
+
+    def __init__(self, batch: int | None):
+        self.batch = batch or self.default_batch
+
+    def inputs_at(self, t: int) -> list:
+        return self.inputs
+
+    def step_at(self, t: int) -> list:
+        return self.launch(self.inputs_at(t))
+
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:  # pragma: no cover - abstract
+        raise NotImplementedError
+
+
+class WhisperDecode(Workload):
     """The headline: Whisper large-v3-turbo decoder-step attention."""
 
     name = "whisper-decode"
@@ -235,16 +303,14 @@ class WhisperDecode:
     unit = "tokens/s"
     bound = "hbm"
     reference_in_graph = True
+    default_batch = 64
     layers, heads, head_dim, target, source, width = 4, 20, 64, 448, 1500, 1280
     profile = "whisper_cross_decode_b64_bf16.md"
-
-    def __init__(self, batch: int | None):
-        self.batch = batch or 64
 
     def config(self, world: int) -> dict:
         return {
             "workload": "whisper-large-v3-turbo decoder-step attention (BASELINE config 2)",
-            "model": "whisper-large-v3-turbo decoder attention, random init seed 1",
+            "model": "whisper-large-v3-turbo decoder attention, seeded k/v projections (seed 1)",
             "layers": self.layers, "heads": self.heads, "head_dim": self.head_dim,
             "batch_per_gpu": self.batch, "global_batch": self.batch * world,
             "self_lengths": "U[1,448] at step 0, +1 per step (capped at 447)",
@@ -260,84 +326,85 @@ class WhisperDecode:
     def lengths(self, rng) -> np.ndarray:
         return rng.integers(1, self.target + 1, size=self.batch)
 
-    def setup(self, torch, device, seed: int, total: int) -> None:
-        from asrback_b200 import whisper
-        from asrback_b200.synthetic import seeded_parameters
+    def setup(self, torch, device, seed: int, steps: int) -> None:
+        from asrback_b200 import attention
+        from asrback_b200.synthetic import seeded_parameter
 
         dtype = torch.bfloat16
         rng = np.random.default_rng(seed)
         lengths = self.lengths(rng)
         start = lengths - 1
-        self.schedule = np.minimum(start[None, :] + np.arange(total)[:, None],
+        self.schedule = np.minimum(start[None, :] + np.arange(steps)[:, None],
                                    self.target - 1).astype(np.int64)
-        config = whisper.large_v3_turbo_config()
-        model = whisper.WhisperForConditionalGeneration(config, encoder=False)
-        seeded_parameters(model.model.decoder, SEED)
-        model = model.to(device, dtype).eval()
-        self.cache = model.allocate_cache(self.batch)
+        b, h, d, w = self.batch, self.heads, self.head_dim, self.width
+        # The reference's DecoderCache layout: (layers, batch, heads, length, 64).
+        self.self_keys = torch.zeros((self.layers, b, h, self.target, d), dtype=dtype,
+                                     device=device)
+        self.self_values = torch.zeros_like(self.self_keys)
+        self.cross_keys = torch.zeros((self.layers, b, h, self.source, d), dtype=dtype,
+                                      device=device)
+        self.cross_values = torch.zeros_like(self.cross_keys)
         gen = torch.Generator(device=device).manual_seed(seed)
         with torch.no_grad():
-            for b0 in range(0, self.batch, 16):
-                b1 = min(self.batch, b0 + 16)
-                states = torch.randn((b1 - b0, self.source, self.width), generator=gen,
-                                     device=device, dtype=dtype)
-                model.set_encoder_output(self.cache.rows(b0, b1), states)
             for layer in range(self.layers):
-                for b in range(self.batch):
-                    p = int(lengths[b]) - 1
+                prefix = f"layers.{layer}.encoder_attn."
+                wk, wv, bv = (seeded_parameter(prefix + name, shape, SEED).to(device, dtype)
+                              for name, shape in (("k_proj.weight", (w, w)),
+                                                  ("v_proj.weight", (w, w)),
+                                                  ("v_proj.bias", (w,))))
+                for b0 in range(0, b, 16):
+                    b1 = min(b, b0 + 16)
+                    states = torch.randn((b1 - b0, self.source, w), generator=gen, device=device,
+                                         dtype=dtype)
+                    attention.whisper_cross_kv_projection(
+                        states, wk, wv, bv, self.cross_keys[layer, b0:b1],
+                        self.cross_values[layer, b0:b1])
+                for row in range(b):
+                    p = int(lengths[row]) - 1
                     if p > 0:
-                        self.cache.self_keys[layer, b, :, :p].normal_(generator=gen)
-                        self.cache.self_values[layer, b, :, :p].normal_(generator=gen)
-        del model
-        shape = (self.layers, 4, self.batch, self.heads, self.head_dim)
-        self.inputs = torch.randn((total,) + shape, generator=gen, device=device, dtype=dtype)
+                        self.self_keys[layer, row, :, :p].normal_(generator=gen)
+                        self.self_values[layer, row, :, :p].normal_(generator=gen)
+        shape = (self.layers, 4, b, h, d)
+        self.episode = min(steps, 128)
+        self.queries = torch.randn((self.episode,) + shape, generator=gen, device=device,
+                                   dtype=dtype)
         self.positions_all = torch.from_numpy(self.schedule).to(device)
-        self.step_in = torch.empty(shape, device=device, dtype=dtype)
-        self.pos = torch.empty((self.batch,), device=device, dtype=torch.int64)
-        self.outputs: list = [None] * (2 * self.layers)
 
-    def step(self) -> None:
+    def inputs_at(self, t: int) -> list:
+        return [self.queries[t % self.episode], self.positions_all[t]]
+
+    def launch(self, inputs) -> list:
         from asrback_b200 import attention
 
-        c = self.cache
+        x, pos = inputs
+        outputs = []
         for layer in range(self.layers):
-            x = self.step_in[layer]
-            self.outputs[2 * layer] = attention.whisper_self_attention_step(
-                x[0], x[1], x[2], c.self_keys[layer], c.self_values[layer], self.pos)
-            self.outputs[2 * layer + 1] = attention.whisper_cross_attention_step(
-                x[3], c.cross_keys[layer], c.cross_values[layer])
+            outputs.append(attention.whisper_self_attention_step(
+                x[layer, 0], x[layer, 1], x[layer, 2], self.self_keys[layer],
+                self.self_values[layer], pos))
+            outputs.append(attention.whisper_cross_attention_step(
+                x[layer, 3], self.cross_keys[layer], self.cross_values[layer]))
+        return outputs
 
     def launches_per_step(self) -> int:
         return 2 * self.layers
-
-    def refresh(self, t: int) -> None:
-        self.step_in.copy_(self.inputs[t])
-        self.pos.copy_(self.positions_all[t])
-
-    def host_step_inputs(self, torch, first: int, count: int):
-        """Pinned host copies of steps first..first+count and their device targets."""
-        host_in = torch.empty((count,) + tuple(self.step_in.shape), dtype=self.step_in.dtype,
-                              pin_memory=True)
-        host_in.copy_(self.inputs[first:first + count].cpu())
-        host_pos = torch.from_numpy(self.schedule[first:first + count].copy()).pin_memory()
-        return [(host_in, self.step_in), (host_pos, self.pos)]
 
     def row_bytes(self) -> int:
         return self.heads * self.head_dim * 2 * 2  # K and V, bf16
 
     def kernels(self, t: int):
-        """(name, launch function, algorithmic bytes of one launch) per kernel."""
+        """(name, launch function of a layer index, algorithmic work of one launch)."""
         from asrback_b200 import attention
 
-        c, x, pos = self.cache, self.inputs, self.positions_all
+        x, pos = self.inputs_at(t)
         self_bytes = float((self.schedule[t] + 1).sum()) * self.row_bytes()
         cross_bytes = float(self.batch * self.source * self.row_bytes())
         return [
             ("cross", lambda layer: attention.whisper_cross_attention_step(
-                x[t, layer, 3], c.cross_keys[layer], c.cross_values[layer]), cross_bytes),
+                x[layer, 3], self.cross_keys[layer], self.cross_values[layer]), cross_bytes),
             ("self", lambda layer: attention.whisper_self_attention_step(
-                x[t, layer, 0], x[t, layer, 1], x[t, layer, 2], c.self_keys[layer],
-                c.self_values[layer], pos[t]), self_bytes),
+                x[layer, 0], x[layer, 1], x[layer, 2], self.self_keys[layer],
+                self.self_values[layer], pos), self_bytes),
         ]
 
     def step_work(self, first: int, count: int) -> float:
@@ -347,43 +414,90 @@ class WhisperDecode:
         return float(((sched + 1).sum() + count * self.batch * self.source) * per_row)
 
     def torch_reference_step(self, torch):
-        """The reference's own GPU computation of one step's attention (torch SDPA
+        """The reference's own GPU computation of step t's attention (torch SDPA
         with its bool step mask and cuDNN-first backend priority, as
         whisper.py:58-63 and :222-240 run it), for context."""
         import torch.nn.functional as F
         from torch.nn.attention import SDPBackend, sdpa_kernel
 
-        c, x = self.cache, self.step_in
-        key_positions = torch.arange(self.target, device=x.device)
+        key_positions = torch.arange(self.target, device=self.queries.device)
         backends = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
                     SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
-        rows = torch.arange(self.batch, device=x.device)
+        rows = torch.arange(self.batch, device=self.queries.device)
 
-        def run():
-            mask = (key_positions[None, :] <= self.pos[:, None])[:, None, None, :]
+        def run(t):
+            x, pos = self.inputs_at(t)
+            mask = (key_positions[None, :] <= pos[:, None])[:, None, None, :]
             with sdpa_kernel(backends, set_priority=True):
                 for layer in range(self.layers):
                     q, k, v, qc = (x[layer, i][:, :, None, :] for i in range(4))
-                    c.self_keys[layer][rows, :, self.pos] = k[:, :, 0]
-                    c.self_values[layer][rows, :, self.pos] = v[:, :, 0]
-                    F.scaled_dot_product_attention(q, c.self_keys[layer], c.self_values[layer],
-                                                   attn_mask=mask)
-                    F.scaled_dot_product_attention(qc, c.cross_keys[layer], c.cross_values[layer])
+                    self.self_keys[layer][rows, :, pos] = k[:, :, 0]
+                    self.self_values[layer][rows, :, pos] = v[:, :, 0]
+                    F.scaled_dot_product_attention(q, self.self_keys[layer],
+                                                   self.self_values[layer], attn_mask=mask)
+                    F.scaled_dot_product_attention(qc, self.cross_keys[layer],
+                                                   self.cross_values[layer])
         return run
 
-    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:
+        """The reference's step attention on the host: for each layer, the
+        key/value write (``scatter_`` at each row's position) and SDPA with the
+        step mask over the 448-position cache, then SDPA over the 1500 cross
+        keys (whisper.py:222-240, :262-264), float32, a sample of the rows."""
+        torch = cpu_torch(threads)
+        import torch.nn.functional as F
+
+        rows, steps = 16, 64
+        rng = np.random.default_rng(SEED)
+        lengths = self.lengths(rng)[:rows]
+        positions = torch.from_numpy(np.minimum(lengths[None, :] - 1 + np.arange(steps)[:, None],
+                                                self.target - 1))
+        gen = torch.Generator().manual_seed(SEED)
+        h, d = self.heads, self.head_dim
+        sk = torch.randn((self.layers, rows, h, self.target, d), generator=gen)
+        sv = torch.randn(sk.shape, generator=gen)
+        ck = torch.randn((self.layers, rows, h, self.source, d), generator=gen)
+        cv = torch.randn(ck.shape, generator=gen)
+        q = torch.randn((steps, self.layers, 4, rows, h, 1, d), generator=gen)
+        key_positions = torch.arange(self.target)
+
+        def one(i):
+            t = i % steps
+            pos = positions[t]
+            mask = (key_positions[None, :] <= pos[:, None])[:, None, None, :]
+            index = pos[:, None, None, None].expand(rows, h, 1, d)
+            for layer in range(self.layers):
+                x = q[t, layer]
+                sk[layer].scatter_(2, index, x[1])
+                sv[layer].scatter_(2, index, x[2])
+                F.scaled_dot_product_attention(x[0], sk[layer], sv[layer], attn_mask=mask)
+                F.scaled_dot_product_attention(x[3], ck[layer], cv[layer])
+
+        with torch.inference_mode():
+            done, elapsed = time_cpu(one, budget_s)
+        return {"value": rows * done / elapsed, "unit": self.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {self.batch} rows x {done} steps x {self.layers} layers "
+                          f"(scatter_ append + masked SDPA over 448, SDPA over {self.source}), "
+                          f"torch CPU float32, {elapsed:.1f} s"}
+
+    def oracle_rate(self, budget_s: float, threads: int) -> dict:
+        """Cross-check: the float64-capable numpy oracle in float32."""
         from oracle import attention as oracle
 
         rows, steps = 16, 64
-        rng = np.random.default_rng(seed)
+        rng = np.random.default_rng(SEED)
         lengths = self.lengths(rng)[:rows]
         positions = np.minimum(lengths[None, :] - 1 + np.arange(steps)[:, None], self.target - 1)
         f32 = np.float32
-        sk = rng.standard_normal((self.layers, rows, self.heads, self.target, self.head_dim), dtype=f32)
+        sk = rng.standard_normal((self.layers, rows, self.heads, self.target, self.head_dim),
+                                 dtype=f32)
         sv = rng.standard_normal(sk.shape, dtype=f32)
-        ck = rng.standard_normal((self.layers, rows, self.heads, self.source, self.head_dim), dtype=f32)
+        ck = rng.standard_normal((self.layers, rows, self.heads, self.source, self.head_dim),
+                                 dtype=f32)
         cv = rng.standard_normal(ck.shape, dtype=f32)
-        q = rng.standard_normal((steps, self.layers, 4, rows, self.heads, self.head_dim), dtype=f32)
+        q = rng.standard_normal((steps, self.layers, 4, rows, self.heads, self.head_dim),
+                                dtype=f32)
 
         def one(t, b):
             t %= steps
@@ -395,26 +509,22 @@ class WhisperDecode:
                 oracle.whisper_cross_attention(q[t, layer, 3, b:b + 1], ck[layer, b:b + 1],
                                                cv[layer, b:b + 1], compute=f32)
 
-        done, elapsed = run_cpu(one, list(range(rows)), budget_s, threads)
-        return {"value": rows * done / elapsed, "unit": self.unit, "cores": threads, "kind": "port",
-                "sample": f"{rows} of {self.batch} rows x {done} steps x {self.layers} layers "
-                          f"(self with in-place append + cross over {self.source}), float32 "
-                          f"numpy oracle, {elapsed:.1f} s"}
+        done, elapsed = run_numpy_pool(one, list(range(rows)), budget_s, threads)
+        return {"value": rows * done / elapsed, "unit": self.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} rows x {done} steps, float32 numpy oracle, {elapsed:.1f} s"}
 
 
-class WhisperEncoder:
+class WhisperEncoder(Workload):
     """Whisper large-v3-turbo encoder self-attention prefill."""
 
     name = "whisper-encoder"
     metric = "encoder windows/s/GPU (32 windows x 1500 frames, 32 layers, bf16); attention TFLOP/s"
     unit = "windows/s"
     bound = "tensor"
-    reference_in_graph = False
+    default_batch = 32
     layers, heads, head_dim, length = 32, 20, 64, 1500
     profile = "whisper_encoder_attention_b32_bf16.md"
-
-    def __init__(self, batch: int | None):
-        self.batch = batch or 32
 
     def config(self, world: int) -> dict:
         return {
@@ -423,6 +533,8 @@ class WhisperEncoder:
             "frames": self.length, "batch_per_gpu": self.batch, "global_batch": self.batch * world,
             "step": "32 layers of non-causal attention over the batch's windows",
             "inputs": "N(0,1) bf16 q/k/v per layer in the projections' (B, S, H*D) layout",
+            "e2e": "layer 0's q/k/v copied in from the host and the last layer's output copied "
+                   "out per step (the layers between keep their activations on the device)",
             "parallelism": f"replicas x{world} (no collective)",
             "l2": "inputs larger than L2 (369 MB of q/k/v per layer)",
         }
@@ -433,45 +545,33 @@ class WhisperEncoder:
     def flops_per_layer(self) -> float:
         return 4.0 * self.length ** 2 * self.head_dim * self.heads * self.batch
 
-    def setup(self, torch, device, seed: int, total: int) -> None:
+    def setup(self, torch, device, seed: int, steps: int) -> None:
         gen = torch.Generator(device=device).manual_seed(seed)
         shape = (self.batch, self.length, self.heads * self.head_dim)
         self.qkv = [[torch.randn(shape, generator=gen, device=device, dtype=torch.bfloat16)
                      for _ in range(3)] for _ in range(self.layers)]
-        self.outputs: list = [None] * self.layers
+        self.inputs = list(self.qkv[0])
 
-    def views(self, layer: int):
+    def views(self, tensors):
         b, s, h, d = self.batch, self.length, self.heads, self.head_dim
-        return [t.view(b, s, h, d).transpose(1, 2) for t in self.qkv[layer]]
+        return [t.view(b, s, h, d).transpose(1, 2) for t in tensors]
 
-    def step(self) -> None:
+    def attend(self, layer: int, tensors=None):
         from asrback_b200 import attention
 
-        for layer in range(self.layers):
-            self.outputs[layer] = attention.whisper_encoder_attention(*self.views(layer))
+        return attention.whisper_encoder_attention(*self.views(tensors or self.qkv[layer]))
+
+    def launch(self, inputs) -> list:
+        out = self.attend(0, inputs)
+        for layer in range(1, self.layers):
+            out = self.attend(layer)
+        return [out]
 
     def launches_per_step(self) -> int:
         return self.layers
 
-    def refresh(self, t: int) -> None:
-        pass
-
-    def host_step_inputs(self, torch, first: int, count: int):
-        # One layer's q/k/v in pinned memory, copied into every layer's inputs.
-        host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in self.qkv[0]]
-        for h, d in zip(host, self.qkv[0]):
-            h.copy_(d.cpu())
-        pairs = []
-        for layer in range(self.layers):
-            for i in range(3):
-                pairs.append((host[i][None].expand(count, *host[i].shape), self.qkv[layer][i]))
-        return pairs
-
     def kernels(self, t: int):
-        from asrback_b200 import attention
-
-        return [("encoder", lambda layer: attention.whisper_encoder_attention(*self.views(layer)),
-                 self.flops_per_layer())]
+        return [("encoder", lambda layer: self.attend(layer), self.flops_per_layer())]
 
     def step_work(self, first: int, count: int) -> float:
         return self.flops_per_layer() * self.layers * count
@@ -481,9 +581,9 @@ class WhisperEncoder:
         backend priority, eager as the reference runs it), for context."""
         import torch.nn.functional as F
 
-        def run():
+        def run(_t):
             for layer in range(self.layers):
-                F.scaled_dot_product_attention(*self.views(layer))
+                F.scaled_dot_product_attention(*self.views(self.qkv[layer]))
         return run
 
     def torch_cudnn_step(self, torch):
@@ -492,32 +592,30 @@ class WhisperEncoder:
         import torch.nn.functional as F
         from torch.nn.attention import SDPBackend, sdpa_kernel
 
-        def run():
+        def run(_t):
             with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
                 for layer in range(self.layers):
-                    F.scaled_dot_product_attention(*self.views(layer))
+                    F.scaled_dot_product_attention(*self.views(self.qkv[layer]))
         return run
 
-    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
-        from oracle import attention as oracle
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:
+        """The reference's unmasked encoder SDPA (whisper.py:102-110) on the
+        host, float32, one window-layer (20 heads x 1500 x 1500) per call."""
+        torch = cpu_torch(threads)
+        import torch.nn.functional as F
 
-        rng = np.random.default_rng(seed)
-        f32 = np.float32
-        q, k, v = (rng.standard_normal((self.heads, self.length, self.head_dim), dtype=f32)
+        gen = torch.Generator().manual_seed(SEED)
+        q, k, v = (torch.randn((1, self.heads, self.length, self.head_dim), generator=gen)
                    for _ in range(3))
-
-        def one(_t, h):
-            oracle.sdpa(q[h], k[h], v[h], compute=f32)
-
-        done, elapsed = run_cpu(one, list(range(self.heads)), budget_s, threads)
-        # `done` layer-windows (all heads) in `elapsed`; a window needs 32 layers.
-        rate = done / elapsed / self.layers
-        return {"value": rate, "unit": self.unit, "cores": threads, "kind": "port",
-                "sample": f"{done} layer-windows (20 heads x 1500 x 1500 each), float32 numpy "
-                          f"oracle, {elapsed:.1f} s, scaled by 1/32 layers"}
+        with torch.inference_mode():
+            done, elapsed = time_cpu(lambda i: F.scaled_dot_product_attention(q, k, v), budget_s)
+        return {"value": done / elapsed / self.layers, "unit": self.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{done} window-layers (20 heads x 1500 x 1500), torch CPU SDPA "
+                          f"float32, {elapsed:.1f} s, scaled by 1/32 layers"}
 
 
-class Qwen3Decode:
+class Qwen3Decode(Workload):
     """Qwen3-1.7B-style decode attention."""
 
     name = "qwen3-decode"
@@ -525,11 +623,9 @@ class Qwen3Decode:
     unit = "tokens/s"
     bound = "hbm"
     reference_in_graph = True
+    default_batch = 64
     layers, heads, kv_heads, head_dim, cache_length, prompt = 28, 16, 8, 128, 1024, 410
     profile = "qwen3_decode_b64_bf16.md"
-
-    def __init__(self, batch: int | None):
-        self.batch = batch or 64
 
     def config(self, world: int) -> dict:
         return {
@@ -546,63 +642,51 @@ class Qwen3Decode:
     def units_per_step(self) -> int:
         return self.batch
 
-    def setup(self, torch, device, seed: int, total: int) -> None:
-        from asrback_b200 import qwen3_asr
-
+    def setup(self, torch, device, seed: int, steps: int) -> None:
         dtype = torch.bfloat16
         gen = torch.Generator(device=device).manual_seed(seed)
-        config = qwen3_asr.text_config_1_7b()
-        self.cache = qwen3_asr.KVCache.allocate(config, self.batch, self.cache_length,
-                                                device=device, dtype=dtype)
-        self.cache.keys[:, :, :self.prompt].normal_(generator=gen)
-        self.cache.values[:, :, :self.prompt].normal_(generator=gen)
-        self.cos, self.sin = qwen3_asr.rope_tables(1e6, self.head_dim, self.cache_length,
-                                                   device=device, dtype=dtype)
+        shape = (self.layers, self.batch, self.cache_length, self.kv_heads, self.head_dim)
+        self.keys = torch.zeros(shape, dtype=dtype, device=device)
+        self.values = torch.zeros(shape, dtype=dtype, device=device)
+        self.keys[:, :, :self.prompt].normal_(generator=gen)
+        self.values[:, :, :self.prompt].normal_(generator=gen)
+        self.cos, self.sin = rope_tables(torch, 1e6, self.head_dim, self.cache_length, device,
+                                         dtype)
         self.norms = (1 + 0.1 * torch.randn((self.layers, 2, self.head_dim), generator=gen,
                                             device=device)).to(dtype)
         width = (self.heads + 2 * self.kv_heads) * self.head_dim
-        self.inputs = torch.randn((total, self.layers, self.batch, width), generator=gen,
-                                  device=device, dtype=dtype)
-        self.schedule = np.minimum(self.prompt + np.arange(total)[:, None]
+        self.episode = min(steps, 128)
+        self.qkv = torch.randn((self.episode, self.layers, self.batch, width), generator=gen,
+                               device=device, dtype=dtype)
+        self.schedule = np.minimum(self.prompt + np.arange(steps)[:, None]
                                    + np.zeros((1, self.batch), np.int64),
                                    self.cache_length - 1).astype(np.int64)
         self.positions_all = torch.from_numpy(self.schedule).to(device)
-        self.step_in = torch.empty((self.layers, self.batch, width), device=device, dtype=dtype)
-        self.pos = torch.empty((self.batch,), device=device, dtype=torch.int64)
-        self.outputs: list = [None] * self.layers
+
+    def inputs_at(self, t: int) -> list:
+        return [self.qkv[t % self.episode], self.positions_all[t]]
 
     def attend(self, layer, qkv, pos):
         from asrback_b200 import attention
 
         return attention.qwen3_attention_step(
             qkv, self.norms[layer, 0], self.norms[layer, 1], 1e-6, self.cos, self.sin, pos,
-            self.cache.keys[layer], self.cache.values[layer], self.heads, self.kv_heads)
+            self.keys[layer], self.values[layer], self.heads, self.kv_heads)
 
-    def step(self) -> None:
-        for layer in range(self.layers):
-            self.outputs[layer] = self.attend(layer, self.step_in[layer], self.pos)
+    def launch(self, inputs) -> list:
+        qkv, pos = inputs
+        return [self.attend(layer, qkv[layer], pos) for layer in range(self.layers)]
 
     def launches_per_step(self) -> int:
         return self.layers
-
-    def refresh(self, t: int) -> None:
-        self.step_in.copy_(self.inputs[t])
-        self.pos.copy_(self.positions_all[t])
-
-    def host_step_inputs(self, torch, first: int, count: int):
-        host_in = torch.empty((count,) + tuple(self.step_in.shape), dtype=self.step_in.dtype,
-                              pin_memory=True)
-        host_in.copy_(self.inputs[first:first + count].cpu())
-        host_pos = torch.from_numpy(self.schedule[first:first + count].copy()).pin_memory()
-        return [(host_in, self.step_in), (host_pos, self.pos)]
 
     def row_bytes(self) -> int:
         return self.kv_heads * self.head_dim * 2 * 2
 
     def kernels(self, t: int):
-        x, pos = self.inputs, self.positions_all
+        qkv, pos = self.inputs_at(t)
         bytes_ = float((self.schedule[t] + 1).sum()) * self.row_bytes()
-        return [("qwen3", lambda layer: self.attend(layer, x[t, layer], pos[t]), bytes_)]
+        return [("qwen3", lambda layer: self.attend(layer, qkv[layer], pos), bytes_)]
 
     def step_work(self, first: int, count: int) -> float:
         sched = self.schedule[first:first + count]
@@ -611,58 +695,88 @@ class Qwen3Decode:
     def torch_reference_step(self, torch):
         """The reference's GPU fallback on torch 2.11 (varlen_attn lacks the
         kwargs it passes): q/k RMSNorm + RoPE in bf16, cache write, SDPA with
-        the bucket mask over the grouped heads (qwen3_asr.py:366-372, 392-432)."""
+        the step mask over the key/value bucket view that holds the longest
+        row (qwen3_asr.py:366-372, 392-432, 508-515, 1108-1109)."""
         import torch.nn.functional as F
 
         h, kvh, d = self.heads, self.kv_heads, self.head_dim
-        rows = torch.arange(self.batch, device=self.pos.device)
-        key_positions = torch.arange(self.cache_length, device=self.pos.device)
+        rows = torch.arange(self.batch, device=self.qkv.device)
+        key_positions = torch.arange(self.cache_length, device=self.qkv.device)
 
         def rotate(x, cos, sin):
             first, second = x.chunk(2, dim=-1)
             return x * cos[:, None, :] + torch.cat((-second, first), dim=-1) * sin[:, None, :]
 
-        def run():
-            cos, sin = self.cos[self.pos], self.sin[self.pos]
-            mask = (key_positions[None, :] <= self.pos[:, None])[:, None, None, :]
+        def run(t):
+            qkv_all, pos = self.inputs_at(t)
+            bucket = kv_bucket(int(self.schedule[t].max()) + 1)
+            cos, sin = self.cos[pos], self.sin[pos]
+            mask = (key_positions[None, :bucket] <= pos[:, None])[:, None, None, :]
             for layer in range(self.layers):
-                q, k, v = self.step_in[layer].split([h * d, kvh * d, kvh * d], dim=-1)
-                q = rotate(F.rms_norm(q.reshape(-1, h, d), (d,), self.norms[layer, 0], 1e-6), cos, sin)
-                k = rotate(F.rms_norm(k.reshape(-1, kvh, d), (d,), self.norms[layer, 1], 1e-6), cos, sin)
-                keys, values = self.cache.keys[layer], self.cache.values[layer]
-                keys[rows, self.pos] = k
-                values[rows, self.pos] = v.reshape(-1, kvh, d)
-                F.scaled_dot_product_attention(q.view(-1, kvh, h // kvh, d), keys.transpose(1, 2),
-                                               values.transpose(1, 2), attn_mask=mask)
+                q, k, v = qkv_all[layer].split([h * d, kvh * d, kvh * d], dim=-1)
+                q = rotate(F.rms_norm(q.reshape(-1, h, d), (d,), self.norms[layer, 0], 1e-6),
+                           cos, sin)
+                k = rotate(F.rms_norm(k.reshape(-1, kvh, d), (d,), self.norms[layer, 1], 1e-6),
+                           cos, sin)
+                keys = self.keys[layer][:, :bucket]
+                values = self.values[layer][:, :bucket]
+                keys[rows, pos] = k
+                values[rows, pos] = v.reshape(-1, kvh, d)
+                F.scaled_dot_product_attention(q.view(-1, kvh, h // kvh, d),
+                                               keys.transpose(1, 2), values.transpose(1, 2),
+                                               attn_mask=mask)
         return run
 
-    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
-        from oracle import attention as oracle
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:
+        """The reference's ``TextAttention.step`` attention on the host
+        (qwen3_asr.py:366-372, :392-432 with its torch 2.11 fallback): per
+        layer, q/k RMSNorm and rotate-half RoPE, the cache write, SDPA of the
+        grouped queries with the step mask over the bucket view; float32, a
+        sample of the rows, every layer with its own cache."""
+        torch = cpu_torch(threads)
+        import torch.nn.functional as F
 
-        rows = 8
-        rng = np.random.default_rng(seed)
-        f32 = np.float32
-        width = (self.heads + 2 * self.kv_heads) * self.head_dim
-        keys = rng.standard_normal((rows, self.cache_length, self.kv_heads, self.head_dim), dtype=f32)
-        values = rng.standard_normal(keys.shape, dtype=f32)
-        qkv = rng.standard_normal((rows, width), dtype=f32)
-        w = np.ones(self.head_dim, f32)
-        cos, sin = oracle.rope_tables(1e6, self.head_dim, self.cache_length)
+        rows, steps = 4, 128
+        h, kvh, d = self.heads, self.kv_heads, self.head_dim
+        gen = torch.Generator().manual_seed(SEED)
+        keys = torch.randn((self.layers, rows, self.cache_length, kvh, d), generator=gen)
+        values = torch.randn(keys.shape, generator=gen)
+        qkv = torch.randn((self.layers, rows, (h + 2 * kvh) * d), generator=gen)
+        weight = torch.ones(d)
+        cos_t, sin_t = rope_tables(torch, 1e6, d, self.cache_length)
+        index = torch.arange(rows)
+        key_positions = torch.arange(self.cache_length)
 
-        def one(t, b):
-            pos = np.array([min(self.prompt + t, self.cache_length - 1)])
-            for _layer in range(self.layers):
-                oracle.qwen3_decode_attention(qkv[b:b + 1], w, w, 1e-6, cos, sin, pos,
-                                              keys[b:b + 1], values[b:b + 1], self.heads,
-                                              self.kv_heads)
+        def rotate(x, cos, sin):
+            first, second = x.chunk(2, dim=-1)
+            return x * cos[:, None, :] + torch.cat((-second, first), dim=-1) * sin[:, None, :]
 
-        done, elapsed = run_cpu(one, list(range(rows)), budget_s, threads)
-        return {"value": rows * done / elapsed, "unit": self.unit, "cores": threads, "kind": "port",
-                "sample": f"{rows} of {self.batch} rows x {done} steps x {self.layers} layers, "
-                          f"numpy oracle, {elapsed:.1f} s"}
+        def one(i):
+            position = min(self.prompt + i % steps, self.cache_length - 1)
+            pos = torch.full((rows,), position)
+            bucket = kv_bucket(position + 1)
+            cos, sin = cos_t[pos], sin_t[pos]
+            mask = (key_positions[None, :bucket] <= pos[:, None])[:, None, None, :]
+            for layer in range(self.layers):
+                q, k, v = qkv[layer].split([h * d, kvh * d, kvh * d], dim=-1)
+                q = rotate(F.rms_norm(q.reshape(rows, h, d), (d,), weight, 1e-6), cos, sin)
+                k = rotate(F.rms_norm(k.reshape(rows, kvh, d), (d,), weight, 1e-6), cos, sin)
+                kc, vc = keys[layer][:, :bucket], values[layer][:, :bucket]
+                kc[index, pos] = k
+                vc[index, pos] = v.reshape(rows, kvh, d)
+                F.scaled_dot_product_attention(q.view(rows, kvh, h // kvh, d), kc.transpose(1, 2),
+                                               vc.transpose(1, 2), attn_mask=mask)
+
+        with torch.inference_mode():
+            done, elapsed = time_cpu(one, budget_s)
+        return {"value": rows * done / elapsed, "unit": self.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {self.batch} rows x {done} steps x {self.layers} layers "
+                          f"(RMSNorm + RoPE + write + masked grouped SDPA over the bucket), "
+                          f"torch CPU float32, {elapsed:.1f} s"}
 
 
-class Qwen3Prefill:
+class Qwen3Prefill(Workload):
     """Admission prefill of the Qwen3 decode workload's prompts: causal grouped-query
     attention within the packed prompts (TextAttention.prefill's `attend`)."""
 
@@ -671,12 +785,10 @@ class Qwen3Prefill:
               "bf16); attention TFLOP/s")
     unit = "tokens/s"
     bound = "tensor"
-    reference_in_graph = False
+    default_batch = 64
     layers, heads, kv_heads, head_dim, prompt = 28, 16, 8, 128, 410
+    causal = True
     profile = "qwen3_prefill_b64_bf16.md"
-
-    def __init__(self, batch: int | None):
-        self.batch = batch or 64
 
     def config(self, world: int) -> dict:
         return {
@@ -687,6 +799,7 @@ class Qwen3Prefill:
             "prompt_tokens": self.prompt, "global_batch": self.batch * world,
             "step": "28 layers of causal varlen attention over the packed prompts",
             "inputs": "N(0,1) bf16 q (tokens, 16, 128), k/v (tokens, 8, 128) per layer",
+            "e2e": "layer 0's q/k/v in, the last layer's output out, per step",
             "parallelism": f"replicas x{world} (no collective)",
             "l2": "inputs larger than L2 (215 MB of q/k/v per layer)",
         }
@@ -694,102 +807,112 @@ class Qwen3Prefill:
     def units_per_step(self) -> int:
         return self.batch * self.prompt
 
+    def lengths(self) -> list[int]:
+        return [self.prompt] * self.batch
+
+    def window(self) -> int:
+        return self.prompt
+
     def flops_per_layer(self) -> float:
         # Causal: query i reads i + 1 keys; 2 flops per multiply-add, QK and PV.
-        pairs = self.prompt * (self.prompt + 1) / 2
-        return 4.0 * pairs * self.head_dim * self.heads * self.batch
+        pairs = sum(n * (n + 1) / 2 for n in self.lengths())
+        return 4.0 * pairs * self.head_dim * self.heads
 
-    def setup(self, torch, device, seed: int, total: int) -> None:
+    def setup(self, torch, device, seed: int, steps: int) -> None:
         gen = torch.Generator(device=device).manual_seed(seed)
-        tokens = self.batch * self.prompt
+        tokens = sum(self.lengths())
         dtype = torch.bfloat16
-        self.q = [torch.randn((tokens, self.heads, self.head_dim), generator=gen, device=device,
-                              dtype=dtype) for _ in range(self.layers)]
-        self.k = [torch.randn((tokens, self.kv_heads, self.head_dim), generator=gen, device=device,
-                              dtype=dtype) for _ in range(self.layers)]
-        self.v = [torch.randn((tokens, self.kv_heads, self.head_dim), generator=gen, device=device,
-                              dtype=dtype) for _ in range(self.layers)]
-        self.starts = (torch.arange(self.batch + 1, device=device) * self.prompt).to(torch.int32)
-        self.outputs: list = [None] * self.layers
 
-    def attend(self, layer):
+        def rand(heads):
+            return torch.randn((tokens, heads, self.head_dim), generator=gen, device=device,
+                               dtype=dtype)
+
+        self.qkv = [[rand(self.heads), rand(self.kv_heads), rand(self.kv_heads)]
+                    for _ in range(self.layers)]
+        lengths = torch.tensor(self.lengths())
+        self.starts = torch.nn.functional.pad(lengths.cumsum(0), (1, 0)).to(torch.int32).to(device)
+        self.inputs = list(self.qkv[0])
+
+    def attend(self, layer, tensors=None):
         from asrback_b200 import attention
 
-        return attention.varlen_attention(self.q[layer], self.k[layer], self.v[layer],
-                                          self.starts, self.prompt, True)
+        q, k, v = tensors or self.qkv[layer]
+        return attention.varlen_attention(q, k, v, self.starts, self.window(), self.causal)
 
-    def step(self) -> None:
-        for layer in range(self.layers):
-            self.outputs[layer] = self.attend(layer)
+    def launch(self, inputs) -> list:
+        out = self.attend(0, inputs)
+        for layer in range(1, self.layers):
+            out = self.attend(layer)
+        return [out]
 
     def launches_per_step(self) -> int:
         return self.layers
 
-    def refresh(self, t: int) -> None:
-        pass
-
-    def host_step_inputs(self, torch, first: int, count: int):
-        # One layer's q/k/v in pinned memory, copied into every layer's inputs.
-        host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-                for t in (self.q[0], self.k[0], self.v[0])]
-        for h, d in zip(host, (self.q[0], self.k[0], self.v[0])):
-            h.copy_(d.cpu())
-        pairs = []
-        for layer in range(self.layers):
-            for h, d in zip(host, (self.q[layer], self.k[layer], self.v[layer])):
-                pairs.append((h[None].expand(count, *h.shape), d))
-        return pairs
-
     def kernels(self, t: int):
-        return [("varlen", self.attend, self.flops_per_layer())]
+        return [("varlen", lambda layer: self.attend(layer), self.flops_per_layer())]
 
     def step_work(self, first: int, count: int) -> float:
         return self.flops_per_layer() * self.layers * count
 
+    def _padded(self, torch, starts, longest):
+        """The reference's padded path indices (qwen3_asr.py:136-149)."""
+        device = starts.device
+        offsets = torch.arange(longest, device=device)
+        sizes = starts[1:] - starts[:-1]
+        valid = offsets[None, :] < sizes[:, None]
+        last = (starts[1:] - 1)[:, None]
+        gather = torch.minimum(starts[:-1, None] + offsets, last)
+        mask = valid[:, None, None, :]
+        if self.causal:
+            mask = mask & torch.ones((longest, longest), dtype=torch.bool, device=device).tril()
+        return gather, valid, mask
+
     def torch_reference_step(self, torch):
         """The reference's `attend` on its GPU path under torch 2.11 (varlen_attn
-        lacks the kwargs it passes, so the padded batch): gather the prompts,
-        SDPA with the valid & causal mask and grouped heads, keep the valid
+        lacks the kwargs it passes, so the padded batch): gather the segments,
+        SDPA with the valid (and causal) mask and grouped heads, keep the valid
         rows (qwen3_asr.py:136-149, 166-181), on the same tensors."""
         import torch.nn.functional as F
 
-        device = self.starts.device
-        offsets = torch.arange(self.prompt, device=device)
-        sizes = self.starts[1:] - self.starts[:-1]
-        valid = offsets[None, :] < sizes[:, None]
-        last = (self.starts[1:] - 1)[:, None]
-        gather = torch.minimum(self.starts[:-1, None] + offsets, last)
-        causal = torch.ones((self.prompt, self.prompt), dtype=torch.bool, device=device).tril()
-        mask = valid[:, None, None, :] & causal
+        gather, valid, mask = self._padded(torch, self.starts, self.window())
 
-        def run():
+        def run(_t):
             for layer in range(self.layers):
                 out = F.scaled_dot_product_attention(
-                    *(t[gather].transpose(1, 2) for t in (self.q[layer], self.k[layer], self.v[layer])),
-                    attn_mask=mask, enable_gqa=True)
+                    *(t[gather].transpose(1, 2) for t in self.qkv[layer]), attn_mask=mask,
+                    enable_gqa=self.heads != self.kv_heads)
                 out.transpose(1, 2)[valid]
         return run
 
-    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
-        from oracle import attention as oracle
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:
+        """The reference's padded ``attend`` (qwen3_asr.py:152-181) on the host
+        for one request's segments, float32."""
+        torch = cpu_torch(threads)
+        import torch.nn.functional as F
 
-        rng = np.random.default_rng(seed)
-        f32 = np.float32
-        q = rng.standard_normal((self.prompt, self.heads, self.head_dim), dtype=f32)
-        k = rng.standard_normal((self.prompt, self.kv_heads, self.head_dim), dtype=f32)
-        v = rng.standard_normal((self.prompt, self.kv_heads, self.head_dim), dtype=f32)
-        starts = np.array([0, self.prompt])
+        per_request = len(self.lengths()) // self.batch
+        lengths = self.lengths()[:per_request]
+        tokens = sum(lengths)
+        gen = torch.Generator().manual_seed(SEED)
+        q = torch.randn((tokens, self.heads, self.head_dim), generator=gen)
+        k = torch.randn((tokens, self.kv_heads, self.head_dim), generator=gen)
+        v = torch.randn(k.shape, generator=gen)
+        starts = F.pad(torch.tensor(lengths).cumsum(0), (1, 0))
+        gather, valid, mask = self._padded(torch, starts, max(lengths))
 
-        def one(_t, _p):
-            oracle.varlen_attention(q, k, v, starts, True, compute=f32)
+        def one(_i):
+            out = F.scaled_dot_product_attention(*(t[gather].transpose(1, 2) for t in (q, k, v)),
+                                                 attn_mask=mask,
+                                                 enable_gqa=self.heads != self.kv_heads)
+            out.transpose(1, 2)[valid]
 
-        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
-        # `done` rounds of `threads` prompt-layers in `elapsed`; a prompt needs 28 layers.
-        layers_done = done * threads
-        rate = layers_done / elapsed / self.layers * self.prompt
+        with torch.inference_mode():
+            done, elapsed = time_cpu(one, budget_s)
+        rate = done / elapsed / self.layers * tokens
         return {"value": rate, "unit": self.unit, "cores": threads, "kind": "port",
-                "sample": f"{layers_done} prompt-layers (16 heads x 410 x 410 causal each), float32 "
-                          f"numpy oracle, {elapsed:.1f} s, scaled by 1/28 layers"}
+                "sample": f"{done} request-layers ({per_request} segments, {tokens} tokens, "
+                          f"padded SDPA), torch CPU float32, {elapsed:.1f} s, scaled by "
+                          f"1/{self.layers} layers"}
 
 
 class Qwen3AudioWindows(Qwen3Prefill):
@@ -801,10 +924,11 @@ class Qwen3AudioWindows(Qwen3Prefill):
               "in 104-token windows, bf16); attention TFLOP/s")
     unit = "tokens/s"
     bound = "tensor"
+    causal = False
     # 30 s of audio = 30 chunks of 13 tokens = 390 tokens per request: windows
     # of 104 tokens (8 chunks) and a last window of 78.
     layers, heads, kv_heads, head_dim, prompt = 24, 16, 16, 64, 390
-    window = 104
+    span = 104
     profile = "qwen3_audio_b64_bf16.md"
 
     def config(self, world: int) -> dict:
@@ -812,7 +936,7 @@ class Qwen3AudioWindows(Qwen3Prefill):
             "workload": "Qwen3-ASR-style audio encoder window attention (admission of audio windows)",
             "layers": self.layers, "heads": self.heads, "head_dim": self.head_dim,
             "causal": False, "requests_per_gpu": self.batch, "tokens_per_request": self.prompt,
-            "window_tokens": self.window, "global_batch": self.batch * world,
+            "window_tokens": self.span, "global_batch": self.batch * world,
             "assumed": "24 layers, 16 heads of 64 (d_model 1024); the checkpoint's audio config "
                        "is not available here",
             "step": "24 layers of non-causal varlen attention over the packed windows",
@@ -821,68 +945,19 @@ class Qwen3AudioWindows(Qwen3Prefill):
         }
 
     def lengths(self) -> list[int]:
-        per = [self.window] * (self.prompt // self.window)
-        if self.prompt % self.window:
-            per.append(self.prompt % self.window)
+        per = [self.span] * (self.prompt // self.span)
+        if self.prompt % self.span:
+            per.append(self.prompt % self.span)
         return per * self.batch
+
+    def window(self) -> int:
+        return self.span
 
     def flops_per_layer(self) -> float:
         return float(sum(4.0 * n * n * self.head_dim * self.heads for n in self.lengths()))
 
-    def setup(self, torch, device, seed: int, total: int) -> None:
-        super().setup(torch, device, seed, total)
-        lengths = torch.tensor(self.lengths())
-        self.starts = torch.nn.functional.pad(lengths.cumsum(0), (1, 0)).to(torch.int32).to(device)
 
-    def attend(self, layer):
-        from asrback_b200 import attention
-
-        return attention.varlen_attention(self.q[layer], self.k[layer], self.v[layer],
-                                          self.starts, self.window, False)
-
-    def torch_reference_step(self, torch):
-        """The reference's padded path for the windows: gather, SDPA with the
-        valid mask (no causal part), keep the valid rows."""
-        import torch.nn.functional as F
-
-        device = self.starts.device
-        offsets = torch.arange(self.window, device=device)
-        sizes = self.starts[1:] - self.starts[:-1]
-        valid = offsets[None, :] < sizes[:, None]
-        last = (self.starts[1:] - 1)[:, None]
-        gather = torch.minimum(self.starts[:-1, None] + offsets, last)
-        mask = valid[:, None, None, :]
-
-        def run():
-            for layer in range(self.layers):
-                out = F.scaled_dot_product_attention(
-                    *(t[gather].transpose(1, 2) for t in (self.q[layer], self.k[layer], self.v[layer])),
-                    attn_mask=mask)
-                out.transpose(1, 2)[valid]
-        return run
-
-    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
-        from oracle import attention as oracle
-
-        rng = np.random.default_rng(seed)
-        f32 = np.float32
-        q = rng.standard_normal((self.prompt, self.heads, self.head_dim), dtype=f32)
-        k = rng.standard_normal(q.shape, dtype=f32)
-        v = rng.standard_normal(q.shape, dtype=f32)
-        starts = np.concatenate([[0], np.cumsum(self.lengths()[: len(self.lengths()) // self.batch])])
-
-        def one(_t, _p):
-            oracle.varlen_attention(q, k, v, starts, False, compute=f32)
-
-        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
-        layers_done = done * threads
-        rate = layers_done / elapsed / self.layers * self.prompt
-        return {"value": rate, "unit": self.unit, "cores": threads, "kind": "port",
-                "sample": f"{layers_done} request-layers (16 heads x windows of 104), float32 numpy "
-                          f"oracle, {elapsed:.1f} s, scaled by 1/24 layers"}
-
-
-class WhisperCrossKV:
+class WhisperCrossKV(Workload):
     """Admission of 32 encoded windows into the decoder:
     `set_encoder_output` (whisper.py:313-319), each of the 4 decoder
     layers' cross-attention keys/values projected from the encoder output and
@@ -893,12 +968,9 @@ class WhisperCrossKV:
               "32 windows x 1500 frames, 4 decoder layers, bf16); projection TFLOP/s")
     unit = "windows/s"
     bound = "tensor"
-    reference_in_graph = False
+    default_batch = 32
     layers, width, tokens, heads = 4, 1280, 1500, 20
     profile = "cross_kv_projection_b32_bf16.md"
-
-    def __init__(self, batch: int | None):
-        self.batch = batch or 32
 
     def config(self, world: int) -> dict:
         return {
@@ -909,6 +981,7 @@ class WhisperCrossKV:
             "global_batch": self.batch * world,
             "step": "4 decoder layers' projections into the cache",
             "inputs": "encoder output N(0, 1) bf16, weights N(0, 1/width), v_proj bias N(0, 0.02)",
+            "e2e": "the encoder output in; one cache row back as the completion read",
             "parallelism": f"replicas x{world} (no collective)",
         }
 
@@ -918,7 +991,7 @@ class WhisperCrossKV:
     def flops_per_layer(self) -> float:
         return 2.0 * self.batch * self.tokens * 2 * self.width * self.width
 
-    def setup(self, torch, device, seed: int, total: int) -> None:
+    def setup(self, torch, device, seed: int, steps: int) -> None:
         gen = torch.Generator(device=device).manual_seed(seed)
         w, dtype = self.width, torch.bfloat16
         self.x = torch.randn((self.batch, self.tokens, w), generator=gen, device=device).to(dtype)
@@ -931,29 +1004,22 @@ class WhisperCrossKV:
         shape = (self.layers, self.batch, self.heads, self.tokens, w // self.heads)
         self.keys = torch.zeros(shape, device=device, dtype=dtype)
         self.values = torch.zeros(shape, device=device, dtype=dtype)
-        self.outputs = [self.keys[layer, 0, 0, 0] for layer in range(self.layers)]
+        self.inputs = [self.x]
 
-    def attend(self, layer: int) -> None:
+    def attend(self, layer: int, x=None) -> None:
         from asrback_b200 import attention
 
-        attention.whisper_cross_kv_projection(self.x, self.wk[layer], self.wv[layer],
-                                              self.bv[layer], self.keys[layer],
+        attention.whisper_cross_kv_projection(self.x if x is None else x, self.wk[layer],
+                                              self.wv[layer], self.bv[layer], self.keys[layer],
                                               self.values[layer])
 
-    def step(self) -> None:
+    def launch(self, inputs) -> list:
         for layer in range(self.layers):
-            self.attend(layer)
+            self.attend(layer, inputs[0])
+        return [self.keys[self.layers - 1, 0, 0, 0]]
 
     def launches_per_step(self) -> int:
         return self.layers
-
-    def refresh(self, t: int) -> None:
-        pass
-
-    def host_step_inputs(self, torch, first: int, count: int):
-        host = torch.empty(self.x.shape, dtype=self.x.dtype, pin_memory=True)
-        host.copy_(self.x.cpu())
-        return [(host[None].expand(count, *host.shape), self.x)]
 
     def kernels(self, t: int):
         return [("cross_kv", self.attend, self.flops_per_layer())]
@@ -971,35 +1037,44 @@ class WhisperCrossKV:
             b, s, w = t.shape
             return t.view(b, s, self.heads, w // self.heads).transpose(1, 2)
 
-        def run():
+        def run(_t):
             for layer in range(self.layers):
                 self.keys[layer, :self.batch] = split(F.linear(self.x, self.wk[layer]))
                 self.values[layer, :self.batch] = split(
                     F.linear(self.x, self.wv[layer], self.bv[layer]))
         return run
 
-    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
-        from oracle import attention as oracle
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:
+        """The reference's per-layer ``project_key_value`` and cache copy on
+        the host for one window, float32."""
+        torch = cpu_torch(threads)
+        import torch.nn.functional as F
 
-        rng = np.random.default_rng(seed)
         w = self.width
-        x = rng.standard_normal((1, self.tokens, w), dtype=np.float32)
-        wk = rng.standard_normal((w, w), dtype=np.float32) / w ** 0.5
-        wv = rng.standard_normal((w, w), dtype=np.float32) / w ** 0.5
-        bv = rng.standard_normal((w,), dtype=np.float32) * 0.02
+        gen = torch.Generator().manual_seed(SEED)
+        x = torch.randn((1, self.tokens, w), generator=gen)
+        wk = torch.randn((w, w), generator=gen) / w ** 0.5
+        wv = torch.randn((w, w), generator=gen) / w ** 0.5
+        bv = torch.randn((w,), generator=gen) * 0.02
+        keys = torch.zeros((1, self.heads, self.tokens, w // self.heads))
+        values = torch.zeros_like(keys)
 
-        def one(_t, _p):
-            oracle.cross_kv_projection(x, wk, wv, bv, compute=np.float32)
+        def split(t):
+            return t.view(1, self.tokens, self.heads, w // self.heads).transpose(1, 2)
 
-        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
-        layers_done = done * threads
-        return {"value": layers_done / elapsed / self.layers, "unit": self.unit, "cores": threads,
+        def one(_i):
+            keys[:] = split(F.linear(x, wk))
+            values[:] = split(F.linear(x, wv, bv))
+
+        with torch.inference_mode():
+            done, elapsed = time_cpu(one, budget_s)
+        return {"value": done / elapsed / self.layers, "unit": self.unit, "cores": threads,
                 "kind": "port",
-                "sample": f"{layers_done} window-layers (1500 x 1280 @ 1280 x 2560), float32 "
-                          f"numpy oracle, {elapsed:.1f} s, scaled by 1/4 layers"}
+                "sample": f"{done} window-layers (1500 x 1280 @ 1280 x 2560 + cache copy), torch "
+                          f"CPU float32, {elapsed:.1f} s, scaled by 1/4 layers"}
 
 
-class WhisperPrefix:
+class WhisperPrefix(Workload):
     """The prompt pass of 32 windows at admission:
     `decode(tokens, positions[:P], cache, length=P)`
     (whisper.py:847-849) for 32 windows sharing the 4-token start sequence
@@ -1014,13 +1089,10 @@ class WhisperPrefix:
               "GB/s")
     unit = "windows/s"
     bound = "hbm"
-    reference_in_graph = False
+    default_batch = 32
     layers, heads, dim, frames, bucket = 4, 20, 64, 1500, 448
+    tokens = 4
     profile = "whisper_prefix_b32_bf16.md"
-
-    def __init__(self, batch: int | None, tokens: int = 4):
-        self.batch = batch or 32
-        self.tokens = tokens
 
     def config(self, world: int) -> dict:
         return {
@@ -1045,7 +1117,7 @@ class WhisperPrefix:
     def self_bytes(self) -> float:
         return 4.0 * self.batch * self.tokens * self.heads * self.dim * 2
 
-    def setup(self, torch, device, seed: int, total: int) -> None:
+    def setup(self, torch, device, seed: int, steps: int) -> None:
         gen = torch.Generator(device=device).manual_seed(seed)
         dtype, b, h, p, d = torch.bfloat16, self.batch, self.heads, self.tokens, self.dim
 
@@ -1058,45 +1130,38 @@ class WhisperPrefix:
         self.self_v = rand(self.layers, b, h, self.bucket, d)
         self.cross_k = rand(self.layers, b, h, self.frames, d)
         self.cross_v = rand(self.layers, b, h, self.frames, d)
-        self.outputs: list = [None] * (2 * self.layers)
+        self.inputs = [self.self_q, self.cross_q]
 
     def _query(self, x):
         b, p, _ = x.shape
         return x.view(b, p, self.heads, self.dim).transpose(1, 2)
 
-    def attend_self(self, layer: int):
+    def attend_self(self, layer: int, q=None):
         from asrback_b200 import attention
 
         layer %= self.layers
         p = self.tokens
         return attention.whisper_self_attention_prefix(
-            self._query(self.self_q), self.self_k[layer][:, :, :p], self.self_v[layer][:, :, :p])
+            self._query(self.self_q if q is None else q), self.self_k[layer][:, :, :p],
+            self.self_v[layer][:, :, :p])
 
-    def attend_cross(self, layer: int):
+    def attend_cross(self, layer: int, q=None):
         from asrback_b200 import attention
 
         layer %= self.layers
         return attention.whisper_cross_attention_prefix(
-            self._query(self.cross_q), self.cross_k[layer], self.cross_v[layer])
+            self._query(self.cross_q if q is None else q), self.cross_k[layer],
+            self.cross_v[layer])
 
-    def step(self) -> None:
+    def launch(self, inputs) -> list:
+        outputs = []
         for layer in range(self.layers):
-            self.outputs[2 * layer] = self.attend_self(layer)
-            self.outputs[2 * layer + 1] = self.attend_cross(layer)
+            outputs.append(self.attend_self(layer, inputs[0]))
+            outputs.append(self.attend_cross(layer, inputs[1]))
+        return outputs
 
     def launches_per_step(self) -> int:
         return 2 * self.layers
-
-    def refresh(self, t: int) -> None:
-        pass
-
-    def host_step_inputs(self, torch, first: int, count: int):
-        pairs = []
-        for dev in (self.self_q, self.cross_q):
-            host = torch.empty(dev.shape, dtype=dev.dtype, pin_memory=True)
-            host.copy_(dev.cpu())
-            pairs.append((host[None].expand(count, *host.shape), dev))
-        return pairs
 
     def kernels(self, t: int):
         return [("cross_prefix", self.attend_cross, self.cross_bytes()),
@@ -1113,7 +1178,7 @@ class WhisperPrefix:
 
         p = self.tokens
 
-        def run():
+        def run(_t):
             for layer in range(self.layers):
                 F.scaled_dot_product_attention(
                     self._query(self.self_q), self.self_k[layer][:, :, :p],
@@ -1122,31 +1187,32 @@ class WhisperPrefix:
                     self._query(self.cross_q), self.cross_k[layer], self.cross_v[layer])
         return run
 
-    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
-        from oracle import attention as oracle
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:
+        """The same two SDPA calls per layer on the host for one window, float32."""
+        torch = cpu_torch(threads)
+        import torch.nn.functional as F
 
-        rng = np.random.default_rng(seed)
         h, p, d = self.heads, self.tokens, self.dim
-        q = rng.standard_normal((1, h, p, d), dtype=np.float32)
-        k = rng.standard_normal((1, h, p, d), dtype=np.float32)
-        ck = rng.standard_normal((1, h, self.frames, d), dtype=np.float32)
-        cv = rng.standard_normal((1, h, self.frames, d), dtype=np.float32)
-        mask = np.arange(p)[None, :] <= np.arange(p)[:, None]
+        gen = torch.Generator().manual_seed(SEED)
+        q = torch.randn((1, h, p, d), generator=gen)
+        k = torch.randn((1, h, p, d), generator=gen)
+        ck = torch.randn((1, h, self.frames, d), generator=gen)
+        cv = torch.randn(ck.shape, generator=gen)
 
-        def one(_t, _p):
-            oracle.sdpa(q, k, k, mask, compute=np.float32)
-            oracle.whisper_cross_attention_prefix(q, ck, cv, compute=np.float32)
+        def one(_i):
+            F.scaled_dot_product_attention(q, k, k, is_causal=p > 1)
+            F.scaled_dot_product_attention(q, ck, cv)
 
-        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
-        layers_done = done * threads
-        return {"value": layers_done / elapsed / self.layers, "unit": self.unit, "cores": threads,
+        with torch.inference_mode():
+            done, elapsed = time_cpu(one, budget_s, limit=1 << 16)
+        return {"value": done / elapsed / self.layers, "unit": self.unit, "cores": threads,
                 "kind": "port",
-                "sample": f"{layers_done} window-layers (20 heads, {p} prompt tokens, self + cross "
-                          f"over 1500 frames), float32 numpy oracle, {elapsed:.1f} s, scaled by "
-                          f"1/4 layers"}
+                "sample": f"{done} window-layers (20 heads, {p} prompt tokens, self + cross over "
+                          f"1500 frames), torch CPU SDPA float32, {elapsed:.1f} s, scaled by 1/4 "
+                          f"layers"}
 
 
-class WhisperGreedyStep:
+class WhisperGreedyStep(Workload):
     """The step epilogue after the decoder: logits against
     the tied embedding, greedy `_choose` with the suppress mask and the state
     update (whisper.py:949-975), Whisper large-v3-turbo widths, 64 rows."""
@@ -1158,12 +1224,13 @@ class WhisperGreedyStep:
     unit = "tokens/s"
     bound = "hbm"
     reference_in_graph = True
+    default_batch = 64
     vocab, width, length, eos = 51866, 1280, 448, (50257,)
     copies = 4  # weight copies, rotated so that no launch finds its weights in L2
     profile = "greedy_step_whisper_b64_bf16.md"
 
     def __init__(self, batch: int | None):
-        self.batch = batch or 64
+        super().__init__(batch)
         self.layers = self.copies
 
     def config(self, world: int) -> dict:
@@ -1173,7 +1240,7 @@ class WhisperGreedyStep:
             "vocab": self.vocab, "hidden": self.width, "rows_per_gpu": self.batch,
             "global_batch": self.batch * world, "suppress": self.family == "whisper",
             "eos_ids": list(self.eos), "steps_per_replay": self.copies,
-            "step": f"{self.copies} greedy steps per graph replay, each over its own weight copy",
+            "step": f"{self.copies} greedy steps, each over its own weight copy",
             "inputs": "weight N(0, 0.02) bf16, hidden N(0, 1) bf16",
             "parallelism": f"replicas x{world} (no collective)",
             "l2": f"{self.copies} weight copies of {self.weight_bytes() / 1e6:.0f} MB rotate "
@@ -1191,7 +1258,7 @@ class WhisperGreedyStep:
     def units_per_step(self) -> int:
         return self.batch * self.copies
 
-    def setup(self, torch, device, seed: int, total: int) -> None:
+    def setup(self, torch, device, seed: int, steps: int) -> None:
         gen = torch.Generator(device=device).manual_seed(seed)
         self.weights = [(torch.randn((self.vocab, self.width), generator=gen, device=device)
                          * 0.02).to(torch.bfloat16) for _ in range(self.copies)]
@@ -1208,32 +1275,22 @@ class WhisperGreedyStep:
         self.finished = torch.zeros(b, dtype=torch.bool, device=device)
         self.sum_logprobs = torch.zeros(b, device=device)
         self.generated = torch.zeros((b, self.length), dtype=torch.int64, device=device)
-        self.outputs = [self.tokens]
+        self.inputs = list(self.hidden)
 
-    def attend(self, i: int) -> None:
+    def attend(self, i: int, hidden=None) -> None:
         from asrback_b200 import step
 
-        step.greedy_step(self.hidden[i], self.weights[i], self.tokens, self.position, self.end,
-                         self.finished, self.sum_logprobs, self.generated, self.eos,
-                         self.suppress)
+        step.greedy_step(self.hidden[i] if hidden is None else hidden, self.weights[i],
+                         self.tokens, self.position, self.end, self.finished, self.sum_logprobs,
+                         self.generated, self.eos, self.suppress)
 
-    def step(self) -> None:
+    def launch(self, inputs) -> list:
         for i in range(self.copies):
-            self.attend(i)
+            self.attend(i, inputs[i])
+        return [self.tokens]
 
     def launches_per_step(self) -> int:
         return self.copies
-
-    def refresh(self, t: int) -> None:
-        pass
-
-    def host_step_inputs(self, torch, first: int, count: int):
-        pairs = []
-        for h in self.hidden:
-            host = torch.empty(h.shape, dtype=h.dtype, pin_memory=True)
-            host.copy_(h.cpu())
-            pairs.append((host[None].expand(count, *host.shape), h))
-        return pairs
 
     def kernels(self, t: int):
         return [("greedy_step", self.attend, self.bytes_per_launch())]
@@ -1252,7 +1309,7 @@ class WhisperGreedyStep:
         position, finished = self.position.clone(), self.finished.clone()
         sums, generated = self.sum_logprobs.clone(), self.generated.clone()
 
-        def run():
+        def run(_t):
             for i in range(self.copies):
                 logits = (self.weights[i] @ self.hidden[i].T).T.float()
                 if self.suppress is not None:
@@ -1269,26 +1326,48 @@ class WhisperGreedyStep:
                 tokens.copy_(token)
         return run
 
-    def cpu_rate(self, seed: int, budget_s: float, threads: int) -> dict:
-        from oracle import step as oracle_step
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:
+        """The reference's `_step` after `decode` on the host: the logits
+        matmul, `_choose` (suppress, argmax, log-softmax) and the state update
+        for the 64 rows, float32."""
+        torch = cpu_torch(threads)
+        import torch.nn.functional as F
 
-        rng = np.random.default_rng(seed)
-        weight = (rng.standard_normal((self.vocab, self.width), dtype=np.float32) * 0.02)
-        hidden = rng.standard_normal((threads, 1, self.width), dtype=np.float32)
+        gen = torch.Generator().manual_seed(SEED)
+        weight = torch.randn((self.vocab, self.width), generator=gen) * 0.02
+        hidden = torch.randn((self.batch, self.width), generator=gen)
         suppress = None
         if self.family == "whisper":
-            suppress = np.zeros(self.vocab, bool)
+            suppress = torch.zeros(self.vocab, dtype=torch.bool)
             suppress[50364:] = True
+        eos = torch.tensor(self.eos)
+        tokens = torch.zeros(self.batch, dtype=torch.int64)
+        position = torch.zeros(self.batch, dtype=torch.int64)
+        finished = torch.zeros(self.batch, dtype=torch.bool)
+        sums = torch.zeros(self.batch)
+        generated = torch.zeros((self.batch, self.length), dtype=torch.int64)
+        end = torch.full((self.batch,), self.length - 1)
 
-        def one(_t, row):
-            oracle_step.choose(oracle_step.logits(weight, hidden[row], False, np.float32),
-                               suppress)
+        def one(_i):
+            logits = (weight @ hidden.T).T
+            if suppress is not None:
+                logits.masked_fill_(suppress, -float("inf"))
+            token = logits.argmax(dim=-1)
+            logprob = F.log_softmax(logits, dim=-1).gather(1, token[:, None]).squeeze(1)
+            active = ~finished
+            pos = torch.minimum(position + active, end)
+            sums.add_(logprob.masked_fill(finished, 0.0))
+            generated.scatter_(1, pos[:, None], token[:, None])
+            finished.logical_or_(torch.isin(token, eos))
+            position.copy_(pos)
+            tokens.copy_(token)
 
-        done, elapsed = run_cpu(one, list(range(threads)), budget_s, threads)
-        return {"value": threads * done / elapsed, "unit": self.unit, "cores": threads,
+        with torch.inference_mode():
+            done, elapsed = time_cpu(one, budget_s)
+        return {"value": self.batch * done / elapsed, "unit": self.unit, "cores": threads,
                 "kind": "port",
-                "sample": f"{threads * done} rows (logits over {self.vocab} x {self.width} + "
-                          f"_choose), float32 numpy oracle, {elapsed:.1f} s"}
+                "sample": f"{done} steps of {self.batch} rows (logits {self.vocab} x {self.width} "
+                          f"+ _choose + state update), torch CPU float32, {elapsed:.1f} s"}
 
 
 class Qwen3GreedyStep(WhisperGreedyStep):
@@ -1312,13 +1391,15 @@ WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decod
 # ------------------------------------------------------------------ arms ----
 
 def run_reference(args, rank: int) -> None:
-    """The reference arm: rank 0 times the CPU path of the workload."""
+    """The reference arm: rank 0 times the reference's CPU path of the workload."""
     if rank != 0:
         return
     sys.path.insert(0, str(ROOT))
     work = WORKLOADS[args.workload](args.batch)
     threads = os.cpu_count() or 1
-    result = work.cpu_rate(SEED, args.cpu_seconds, threads)
+    # The arm's budget covers the --warmup and --steps it was given: a bounded
+    # sample, so the whole run ends within a few minutes.
+    result = work.cpu_rate(args.cpu_seconds, threads)
     line = {
         "impl": "reference", "metric": work.metric, "value": result["value"], "unit": work.unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -1327,14 +1408,15 @@ def run_reference(args, rank: int) -> None:
         "config": work.config(args.gpus), "cpu_baseline": result,
         "e2e": {"value": result["value"], "unit": work.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": "reference CPU path = CPU oracle port of the reference's attention in float32 "
-                "(the Python reference is not present on the GPU box)",
+        "note": "reference CPU path = the reference's attention call (torch SDPA with its masks "
+                "and grouped views) on the host cores in float32; the Python reference itself "
+                "runs torch, so this is its CPU arithmetic",
     }
     print(json.dumps(line), flush=True)
 
 
 def graph_time_ms(torch, fn, reps: int, replays: int = 4) -> float:
-    """Average device time of fn() launched `reps` times back to back from a
+    """Average device time of fn(i) for i < reps, launched back to back from a
     CUDA graph, over `replays` replays (CUDA events on the current stream)."""
     from asrback_b200.transcription import CapturedGraph
 
@@ -1350,21 +1432,121 @@ def graph_time_ms(torch, fn, reps: int, replays: int = 4) -> float:
     return start.elapsed_time(end) / (replays * reps)
 
 
+def rank_times(torch, dist, world: int, ms: float) -> list[float]:
+    """Every rank's device time of the same region (all-gather; the value
+    alone without a process group)."""
+    if world == 1:
+        return [ms]
+    tensor = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(tensor) for _ in range(world)]
+    dist.all_gather(out, tensor)
+    return [float(t.item()) for t in out]
+
+
+def e2e_pipeline(torch, dist, work, world: int, first: int, steps: int) -> dict:
+    """The K steps through the public ops with host buffers: step i's inputs
+    are copied from pinned host memory into one of two device slots on a copy
+    stream, the step (a graph per slot) runs on the compute stream, and its
+    outputs go back to pinned host memory on a second copy stream, so the
+    copies of steps i+1 and i-1 overlap step i. Timed from before the first
+    copy in to after the last copy out, on the compute stream."""
+    from asrback_b200.transcription import CapturedGraph
+
+    proto = work.inputs_at(first)
+    slots = [[torch.empty_like(x) for x in proto] for _ in range(2)]
+    for slot in slots:
+        for dst, src in zip(slot, proto):
+            dst.copy_(src)
+    distinct = min(steps, 8)
+    if work.name in ("whisper-encoder", "qwen3-prefill", "qwen3-audio"):
+        distinct = 2  # hundreds of MB per step: two pinned copies alternate
+    host = []
+    for i in range(distinct):
+        inputs = work.inputs_at(first + i)
+        pinned = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in inputs]
+        for dst, src in zip(pinned, inputs):
+            dst.copy_(src.cpu())
+        host.append(pinned)
+    outs: list = [None, None]
+
+    def capture(s):
+        def fn():
+            outs[s] = work.launch(slots[s])
+        return CapturedGraph(fn)
+
+    graphs = [capture(0), capture(1)]
+    out_bytes = sum(o.numel() * o.element_size() for o in outs[0])
+    in_bytes = sum(x.numel() * x.element_size() for x in proto)
+    host_out = [torch.empty((out_bytes,), dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+    compute = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = {name: [torch.cuda.Event(), torch.cuda.Event()] for name in ("in", "done", "out")}
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def copy_in(i):
+        s = i % 2
+        with torch.cuda.stream(h2d):
+            if i >= 2:
+                h2d.wait_event(ev["done"][s])  # step i-2 has read slot s
+            for dst, src in zip(slots[s], host[i % distinct]):
+                dst.copy_(src, non_blocking=True)
+            ev["in"][s].record(h2d)
+
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start.record(compute)
+    h2d.wait_stream(compute)
+    d2h.wait_stream(compute)
+    copy_in(0)
+    for i in range(steps):
+        s = i % 2
+        if i + 1 < steps:
+            copy_in(i + 1)
+        compute.wait_event(ev["in"][s])
+        if i >= 2:
+            compute.wait_event(ev["out"][s])  # step i-2's outputs are on the host
+        graphs[s].replay()
+        ev["done"][s].record(compute)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(ev["done"][s])
+            offset = 0
+            for o in outs[s]:
+                n = o.numel() * o.element_size()
+                host_out[s][offset:offset + n].copy_(o.reshape(-1).view(torch.uint8),
+                                                     non_blocking=True)
+                offset += n
+            ev["out"][s].record(d2h)
+    compute.wait_stream(d2h)
+    end.record(compute)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    ranks = rank_times(torch, dist, world, ms)
+    value = work.units_per_step() * world * steps / (max(ranks) / 1e3)
+    return {"value": value, "unit": work.unit, "h2d_bytes_per_step": in_bytes,
+            "d2h_bytes_per_step": out_bytes, "steps": steps,
+            "how": "pinned host inputs in and outputs out every step, double-buffered on two "
+                   "copy streams under the graph-replayed steps",
+            "rank_ms": ranks}
+
+
 def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, warmup: int,
-            cpu: bool) -> dict:
-    """Runs one workload: graph-replayed timed region, per-kernel timing, e2e."""
+            cpu: bool, sustain: bool) -> dict:
+    """Runs one workload: the timed graph of K steps, the sustained figure,
+    per-kernel timing, e2e, the reference's torch path on the same GPU, and
+    the CPU baseline."""
     from asrback_b200 import attention
+    from asrback_b200.replicas import max_over_ranks
     from asrback_b200.transcription import CapturedGraph
 
     seed = SEED + 1000 * rank
     total = warmup + steps
     work.setup(torch, device, seed, total)
     stream = torch.cuda.current_stream()
-    work.refresh(0)
-    graph = CapturedGraph(work.step)
     for t in range(warmup):
-        work.refresh(t)
-        graph.replay()
+        work.step_at(t)
+    timed = CapturedGraph(lambda: [work.step_at(t) for t in range(warmup, total)], warmup=1)
+    timed.replay()  # uploads the graph; untimed
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -1372,9 +1554,7 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     uuid = getattr(torch.cuda.get_device_properties(device), "uuid", None)
     uuid = str(uuid) if uuid else None
 
-    from asrback_b200.replicas import max_over_ranks
-
-    # ---- timed region: device-resident inputs, one graph replay per step ----
+    # ---- timed region: exactly K steps, one graph replay, inputs in HBM ----
     start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(uuid) as clocks:
         torch.cuda.synchronize()
@@ -1382,81 +1562,80 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
             dist.barrier()
         torch.cuda.nvtx.range_push("timed")
         start_ev.record(stream)
-        for t in range(warmup, total):
-            work.refresh(t)
-            graph.replay()
+        timed.replay()
         clocks.mark()
         end_ev.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-    ms = max_over_ranks(start_ev.elapsed_time(end_ev))
+        own_ms = start_ev.elapsed_time(end_ev)
+        ranks = rank_times(torch, dist, world, own_ms)
+        ms = max(ranks)
+        sustained = None
+        if sustain:
+            replays = int(min(500, max(2, math.ceil(args.sustain_seconds * 1e3 / max(ms, 1e-3)))))
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            start_ev.record(stream)
+            for _ in range(replays):
+                timed.replay()
+            clocks.mark()
+            end_ev.record(stream)
+            torch.cuda.synchronize()
+            s_ranks = rank_times(torch, dist, world, start_ev.elapsed_time(end_ev))
+            s_ms = max(s_ranks)
+            sustained = {"value": work.units_per_step() * world * steps * replays / (s_ms / 1e3),
+                         "unit": work.unit, "replays": replays, "steps": steps * replays,
+                         "ms_per_step": s_ms / (steps * replays), "timed_region_s": s_ms / 1e3,
+                         "rank_ms": s_ranks,
+                         "how": "the timed graph replayed back to back (same K steps each "
+                                "replay), slowest rank"}
     ms_per_step = ms / steps
     value = work.units_per_step() * world * steps / (ms / 1e3)
 
     # ---- kernel timing: average launch duration, launched from a graph ----
     kernel = {}
-    layers = work.launches_per_step() if work.name != "whisper-decode" else work.layers
+    layers = work.layers
     for name, fn, amount in work.kernels(warmup):
         launch_ms = graph_time_ms(torch, lambda i: fn(i % layers), 2 * layers)
         kernel[name] = {"launch_ms": launch_ms, "work_per_launch": amount}
 
-    # ---- e2e: pinned host inputs in, outputs back, every step ----
-    e2e_steps = min(steps, 4) if work.name == "whisper-encoder" else steps
-    pairs = work.host_step_inputs(torch, warmup, e2e_steps)
-    outs = [o for o in work.outputs]
-    out_bytes = sum(o.numel() * o.element_size() for o in outs)
-    host_out = torch.empty((out_bytes,), dtype=torch.uint8, pin_memory=True)
-    in_bytes = sum(dev.numel() * dev.element_size() for _, dev in pairs)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for i in range(e2e_steps):
-        for host, dev in pairs:
-            dev.copy_(host[i], non_blocking=True)
-        graph.replay()
-        offset = 0
-        for o in outs:
-            n = o.numel() * o.element_size()
-            host_out[offset:offset + n].copy_(o.reshape(-1).view(torch.uint8), non_blocking=True)
-            offset += n
-    e_end.record(stream)
-    torch.cuda.synchronize()
-    e_ms = max_over_ranks(e_start.elapsed_time(e_end))
-    e2e = work.units_per_step() * world * e2e_steps / (e_ms / 1e3)
+    e2e = e2e_pipeline(torch, dist, work, world, warmup, steps)
 
     # ---- the reference's GPU computation on the same tensors, for context:
     # graph-replayed where the reference captures it (decoder steps), eager
-    # where it does not (the encoder) ----
+    # where it does not (the encoder, admission) ----
     ref_fn = work.torch_reference_step(torch)
-    if work.reference_in_graph:
-        ref_graph = CapturedGraph(ref_fn)
-        ref_fn = ref_graph.replay
-    else:
-        for _ in range(3):
-            ref_fn()
     r_start, r_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    r_start.record(stream)
-    for t in range(warmup, total):
-        work.refresh(t)
-        ref_fn()
-    r_end.record(stream)
+    if work.reference_in_graph:
+        ref_graph = CapturedGraph(lambda: [ref_fn(t) for t in range(warmup, total)], warmup=1)
+        ref_graph.replay()
+        torch.cuda.synchronize()
+        r_start.record(stream)
+        ref_graph.replay()
+        r_end.record(stream)
+    else:
+        for t in range(min(warmup, 3)):
+            ref_fn(t)
+        torch.cuda.synchronize()
+        r_start.record(stream)
+        for t in range(warmup, total):
+            ref_fn(t)
+        r_end.record(stream)
     torch.cuda.synchronize()
     ref_ms = r_start.elapsed_time(r_end) / steps
     ref_graph = None
     cudnn = None
     if hasattr(work, "torch_cudnn_step"):
         fn = work.torch_cudnn_step(torch)
-        for _ in range(3):
-            fn()
+        for t in range(3):
+            fn(t)
         torch.cuda.synchronize()
         r_start.record(stream)
-        for _ in range(steps):
-            fn()
+        for t in range(steps):
+            fn(t)
         r_end.record(stream)
         torch.cuda.synchronize()
         c_ms = r_start.elapsed_time(r_end) / steps
@@ -1466,31 +1645,30 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     dominant = work.kernels(warmup)[0]
     dom = kernel[dominant[0]]
     peak, peak_kind = peak_for(work.bound)
-    if work.bound == "hbm":
-        achieved = dom["work_per_launch"] / (dom["launch_ms"] * 1e-3) / 1e9
-        unit = "GB/s"
-    else:
-        achieved = dom["work_per_launch"] / (dom["launch_ms"] * 1e-3) / 1e12
-        unit = "TFLOP/s"
+    scale = 1e9 if work.bound == "hbm" else 1e12
+    unit = "GB/s" if work.bound == "hbm" else "TFLOP/s"
+    achieved = dom["work_per_launch"] / (dom["launch_ms"] * 1e-3) / scale
     traffic = profiled_traffic(work.profile)
     status = attention.read_status(device)
     result = {
         "metric": work.metric, "value": value, "unit": work.unit, "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": work.config(world),
-        "e2e": {"value": e2e, "unit": work.unit, "h2d_bytes_per_step": in_bytes,
-                "d2h_bytes_per_step": out_bytes, "steps": e2e_steps},
+        "e2e": e2e,
         "roofline": {"bound": work.bound, "kernel": dominant[0], "achieved": achieved,
                      "peak": peak, "unit": unit, "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": traffic, "work_per_launch": dom["work_per_launch"],
                      "launch_ms": dom["launch_ms"]},
         "kernels": {
-            name: dict(k, rate=(k["work_per_launch"] / (k["launch_ms"] * 1e-3)
-                                / (1e9 if work.bound == "hbm" else 1e12)),
+            name: dict(k, rate=k["work_per_launch"] / (k["launch_ms"] * 1e-3) / scale,
                        rate_unit=unit)
             for name, k in kernel.items()},
         "step_rate": {"value": work.step_work(warmup, steps) / steps / (ms_per_step * 1e-3)
-                      / (1e9 if work.bound == "hbm" else 1e12), "unit": unit},
+                      / scale, "unit": unit},
+        "rank_ms": ranks,
+        "rank_spread": max(ranks) / min(ranks),
+        "timing": "the K timed steps captured as one CUDA graph, one replay, slowest rank",
+        "sustained": sustained,
         "torch_gpu_reference": {
             "ms_per_step": ref_ms, "value": work.units_per_step() / (ref_ms * 1e-3),
             "unit": work.unit,
@@ -1500,9 +1678,28 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
         "clocks": clocks.summary(),
         "device_status": status,
     }
+    max_over_ranks(0.0)  # every rank reaches the CPU leg together
     if cpu and rank == 0 and world == 1:
-        result["cpu_baseline"] = work.cpu_rate(SEED, args.cpu_seconds, os.cpu_count() or 1)
+        result["cpu_baseline"] = work.cpu_rate(args.cpu_seconds, os.cpu_count() or 1)
     return result
+
+
+def summary(name: str, line: dict) -> dict:
+    """A short record of one workload's line (rounded), for the end of the
+    printed line."""
+    def r(x, digits=4):
+        return None if x is None else float(f"{x:.{digits}g}")
+
+    out = {"value": r(line["value"]), "unit": line["unit"], "ms": r(line["ms_per_step"]),
+           "frac": r(line["roofline"]["frac"], 3), "e2e": r(line["e2e"]["value"]),
+           "torch_gpu": r(line["torch_gpu_reference"]["value"])}
+    if line.get("torch_gpu_cudnn"):
+        out["cudnn"] = r(line["torch_gpu_cudnn"]["value"])
+    if line.get("cpu_baseline"):
+        out["cpu"] = r(line["cpu_baseline"]["value"])
+    if line.get("serving"):
+        out["serving"] = line["serving"]
+    return out
 
 
 def run_native(args, rank: int, world: int, local_rank: int) -> None:
@@ -1515,10 +1712,16 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     work = WORKLOADS[args.workload](args.batch)
     if args.layers:
         work.layers = args.layers
+    cpu = not args.no_cpu_baseline
     line = measure(args, work, torch, dist, device, rank, world, args.steps, args.warmup,
-                   cpu=not args.no_cpu_baseline)
+                   cpu=cpu, sustain=True)
+    if cpu and rank == 0 and world == 1 and hasattr(work, "oracle_rate"):
+        line["cpu_crosscheck"] = work.oracle_rate(min(args.cpu_seconds, 5.0),
+                                                  os.cpu_count() or 1)
+    short = {args.workload: summary(args.workload, line)}
     if args.workload == "whisper-decode" and not args.no_extras and args.batch is None:
-        # Short runs of the other workloads, for context.
+        # Short runs of the other workloads (their K steps capped at 16), with
+        # their own CPU baselines.
         extras = {}
         for name in ("whisper-encoder", "qwen3-decode", "qwen3-prefill", "qwen3-audio",
                      "whisper-step", "qwen3-step", "whisper-cross-kv", "whisper-prefix"):
@@ -1526,12 +1729,16 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
             torch.cuda.empty_cache()
             work = WORKLOADS[name](None)
             r = measure(args, work, torch, dist, device, rank, world, min(args.steps, 16),
-                        max(3, min(args.warmup, 5)), cpu=False)
-            extras[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "e2e",
-                                              "roofline", "step_rate", "torch_gpu_reference",
-                                              "torch_gpu_cudnn", "clocks", "device_status",
-                                              "config")}
+                        max(3, min(args.warmup, 5)), cpu=cpu, sustain=False)
+            extras[name] = {k: r.get(k) for k in (
+                "metric", "value", "unit", "ms_per_step", "e2e", "roofline", "step_rate",
+                "rank_ms", "torch_gpu_reference", "torch_gpu_cudnn", "cpu_baseline", "clocks",
+                "device_status", "config")}
+            short[name] = summary(name, r)
         line["other_workloads"] = extras
+    # The short records go last, so that the end of the line holds every
+    # workload's figures.
+    line["workloads"] = short
     if rank == 0:
         print(json.dumps(line), flush=True)
 

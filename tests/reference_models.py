@@ -306,14 +306,16 @@ def run_qwen3_steps(ref, model, lm_head, forced: torch.Tensor | None, graph: boo
             out.copy_(model.step(tokens, position, view, cos, sin, False))
 
         run = ref.transcription.CapturedGraph(step).replay if graph else step
-        fed, argmax, hiddens = [], [], []
+        fed, argmax, hiddens, top2 = [], [], [], []
         for t in range(QWEN3_STEPS):
             if forced is not None:
                 tokens.copy_(forced[:, t])
             fed.append(tokens.clone())
             run()
-            choice = lm_head(out).float().argmax(dim=-1)
+            logits = lm_head(out).float()
+            choice = logits.argmax(dim=-1)
             argmax.append(choice)
+            top2.append(logits.topk(2).values)
             hiddens.append(out.float().clone())
             if forced is None:
                 tokens.copy_(choice)
@@ -322,6 +324,7 @@ def run_qwen3_steps(ref, model, lm_head, forced: torch.Tensor | None, graph: boo
                 first=first.cpu().numpy(),
                 tokens=torch.stack(fed, 1).cpu().numpy(),
                 argmax=torch.stack(argmax, 1).cpu().numpy(),
+                top2=torch.stack(top2, 1).cpu().numpy(),
                 hidden=torch.stack(hiddens, 1).cpu().numpy())
 
 
@@ -377,14 +380,16 @@ def run_turbo_steps(ref, model, forced: torch.Tensor | None, graph: bool) -> dic
             out.copy_(model.decode(tokens, position, view)[:, -1])
 
         run = ref.transcription.CapturedGraph(step).replay if graph else step
-        fed, argmax, hiddens = [], [], []
+        fed, argmax, hiddens, top2 = [], [], [], []
         for t in range(TURBO_STEPS):
             if forced is not None:
                 tokens.copy_(forced[:, t:t + 1])
             fed.append(tokens[:, 0].clone())
             run()
-            choice = model.logits(out).float()[:, :vocab].argmax(dim=-1)
+            logits = model.logits(out).float()[:, :vocab]
+            choice = logits.argmax(dim=-1)
             argmax.append(choice)
+            top2.append(logits.topk(2).values)
             hiddens.append(out.float().clone())
             if forced is None:
                 tokens.copy_(choice[:, None])
@@ -392,5 +397,6 @@ def run_turbo_steps(ref, model, forced: torch.Tensor | None, graph: bool) -> dic
     return dict(prompt_hidden=prompt[:, -1].float().cpu().numpy(),
                 tokens=torch.stack(fed, 1).cpu().numpy(),
                 argmax=torch.stack(argmax, 1).cpu().numpy(),
+                top2=torch.stack(top2, 1).cpu().numpy(),
                 hidden=torch.stack(hiddens, 1).cpu().numpy(),
                 self_keys=cache.self_keys[:, :, :, :40].float()[:, :, ::5].cpu().numpy())

@@ -12,7 +12,9 @@ Tolerances: float32 encoder output 1e-4 and decoder hidden states 1e-3
 (max-abs relative to the largest element: the CPU and GPU round their bf16
 GEMMs differently at every layer); greedy tokens identical on >= 99 % of the
 steps (teacher-forced on the reference's tokens where a step's choice would
-otherwise feed the next).
+otherwise feed the next); in bf16, a step may differ only where the
+reference's own two largest logits lie within 4 bf16 steps of each other
+(exact ties are common at bf16 resolution).
 """
 
 from __future__ import annotations
@@ -56,6 +58,27 @@ def clean_status():
 
 def _relative(got: np.ndarray, want: np.ndarray) -> float:
     return float(np.abs(got - want).max() / np.abs(want).max())
+
+
+def _bf16_ulp(x: np.ndarray) -> np.ndarray:
+    """The spacing of bf16 numbers at ``|x|`` (8 significant bits)."""
+    return np.exp2(np.floor(np.log2(np.maximum(np.abs(x), 1e-30))) - 7)
+
+
+def _assert_greedy_tokens(got: np.ndarray, want: np.ndarray, top2: np.ndarray,
+                          ulps: int = 4) -> None:
+    """Greedy tokens identical on >= 99 % of the steps, or else every step that
+    differs is a near-tie of the reference's own bf16 logits: its two largest
+    logits within ``ulps`` bf16 steps of each other (bf16 logits tie exactly
+    on some steps, and argmax then takes the lower id). At least 90 % of the
+    steps must be identical either way."""
+    same = got == want
+    assert same.mean() >= 0.9, same.mean()
+    if same.mean() >= 0.99:
+        return
+    margin = top2[..., 0] - top2[..., 1]
+    tie = margin <= ulps * _bf16_ulp(top2[..., 0])
+    assert (same | tie).all(), (np.argwhere(~same).tolist(), margin[~same].tolist())
 
 
 # ------------------------------------------------------------- config 1 ----
@@ -114,14 +137,23 @@ def test_whisper_turbo_decoder_graph_bf16(ref):
     ``CapturedGraph``, teacher-forced on the CPU run's tokens."""
     g = load("whisper_turbo_decode_bf16")
     model = rm.whisper_turbo_decoder(ref, torch.bfloat16, DEV)
-    out = rm.run_turbo_steps(ref, model, torch.from_numpy(g["tokens"]).to(DEV), graph=True)
+    forced = torch.from_numpy(g["tokens"]).to(DEV)
+    out = rm.run_turbo_steps(ref, model, forced, graph=True)
     assert attention.read_status() == 0
     assert _relative(out["prompt_hidden"], g["prompt_hidden"]) <= BF16_HIDDEN
     assert _relative(out["hidden"], g["hidden"]) <= BF16_HIDDEN, _relative(out["hidden"],
                                                                          g["hidden"])
     assert _relative(out["self_keys"], g["self_keys"]) <= BF16_HIDDEN
-    same = out["argmax"] == g["argmax"]
-    assert same.mean() >= 0.99, same.mean()
+    _assert_greedy_tokens(out["argmax"], g["argmax"], g["top2"])
+    # The unpatched reference on the same GPU (torch SDPA, cuDNN first): only
+    # the attention differs between the two runs.
+    plugin.uninstall()
+    try:
+        torch_run = rm.run_turbo_steps(ref, model, forced, graph=True)
+    finally:
+        plugin.install(ref.whisper, ref.qwen3_asr)
+    assert _relative(out["hidden"], torch_run["hidden"]) <= BF16_HIDDEN
+    _assert_greedy_tokens(out["argmax"], torch_run["argmax"], torch_run["top2"])
 
 
 def test_qwen3_text_model_graph_bf16(ref):
@@ -132,14 +164,22 @@ def test_qwen3_text_model_graph_bf16(ref):
     ``CapturedGraph``, teacher-forced on the CPU run's tokens."""
     g = load("qwen3_graph_decode_bf16")
     model, lm_head = rm.qwen3_text_model(ref, torch.bfloat16, DEV)
-    out = rm.run_qwen3_steps(ref, model, lm_head, torch.from_numpy(g["tokens"]).to(DEV),
-                             graph=True)
+    forced = torch.from_numpy(g["tokens"]).to(DEV)
+    out = rm.run_qwen3_steps(ref, model, lm_head, forced, graph=True)
     assert attention.read_status() == 0
     assert _relative(out["prefill_last"], g["prefill_last"]) <= BF16_HIDDEN
     assert _relative(out["hidden"], g["hidden"]) <= BF16_HIDDEN, _relative(out["hidden"],
                                                                          g["hidden"])
-    same = out["argmax"] == g["argmax"]
-    assert same.mean() >= 0.99, same.mean()
+    _assert_greedy_tokens(out["argmax"], g["argmax"], g["top2"])
+    # The unpatched reference on the same GPU (padded-SDPA prefill, masked
+    # SDPA steps: its torch 2.11 path).
+    plugin.uninstall()
+    try:
+        torch_run = rm.run_qwen3_steps(ref, model, lm_head, forced, graph=True)
+    finally:
+        plugin.install(ref.whisper, ref.qwen3_asr)
+    assert _relative(out["hidden"], torch_run["hidden"]) <= BF16_HIDDEN
+    _assert_greedy_tokens(out["argmax"], torch_run["argmax"], torch_run["top2"])
 
 
 # ------------------------------------------------ seeded small decoders ----
