@@ -35,7 +35,7 @@ Other workloads (``--workload``):
                    Qwen3-0.6B-style text model (28 layers, hidden 1024) per
                    GPU fed by seeded Poisson arrivals, rows joining with a
                    packed prefill and leaving after their tokens; unit:
-                   generated tokens (see ``serve.py``-free notes in the class).
+                   generated tokens; also timed at the offered load.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
                     [--workload NAME] [--batch B]
@@ -1383,9 +1383,494 @@ class Qwen3GreedyStep(WhisperGreedyStep):
     profile = "greedy_step_qwen3_b64_bf16.md"
 
 
+class _Request:
+    """One synthetic request of the serving trace."""
+
+    __slots__ = ("index", "arrival", "seconds", "audio", "length", "replica", "done_at")
+
+    def __init__(self, index: int, arrival: float, seconds: float, audio: int, text: int):
+        self.index, self.arrival, self.seconds = index, arrival, seconds
+        self.audio = audio
+        self.length = audio + text
+        self.replica = 0
+        self.done_at = None
+
+
+class Qwen3Serve:
+    """continuous-batching serving, one replica per GPU.
+
+    Each GPU holds a Qwen3-ASR-0.6B-style text model (28 layers, hidden 1024,
+    16 query / 8 key-value heads of 128, MLP 3072, vocabulary 151936 tied to
+    the embedding; seeded weights, seed 4) and the reference engine's
+    scheduling (qwen3_asr.py:950-982, :1018-1151): a pool of 64 rows over a
+    ``(28, 64, 1024, 8, 128)`` cache; requests that find a free row join with
+    one packed causal prefill of their prompts (audio positions injected as
+    N(0, 0.02) embeddings -- the audio front end and tower are not on this
+    path -- plus 20 text positions); the rows decode together, one CUDA graph
+    per batch bucket (1, 2, ..., 64: the highest occupied row decides), four
+    steps between host checks for finished rows, which then leave; each request
+    generates 128 tokens.
+
+    Requests come from one seeded trace: Poisson arrivals at 25 requests/s per
+    GPU (200/s over 8 GPUs), 16 kHz audio of U[1, 30] s, 13 audio positions per
+    second (``architecture.md:471``), so a prompt holds 33 to 410 positions.
+    ``ReplicaDispatcher`` assigns each request to the least-loaded replica
+    (cost: its prompt plus its 128 tokens); every rank builds the same trace
+    and serves its own share.
+
+    Two runs: ``capacity`` queues every request of the replica's share at
+    once (the engine's throughput under join/leave churn, the line's value),
+    and ``paced`` releases them at their arrival times (tokens/s at the offered
+    load, and per-request latency)."""
+
+    name = "qwen3-serve"
+    metric = ("whole-box generated tokens/s (Qwen3-ASR-0.6B-style LM, continuous batching, "
+              "max batch 64, Poisson arrivals 200 req/s over 8 GPUs, 128 new tokens)")
+    unit = "tokens/s"
+    bound = "hbm"
+    hidden, layers, heads, kv_heads, head_dim, inter, vocab = 1024, 28, 16, 8, 128, 3072, 151936
+    cache_length, max_new, interval, eps = 1024, 128, 4, 1e-6
+    rate_per_gpu, audio_rate, text_tokens = 25.0, 13, 20
+    eos = (151643, 151645)
+
+    def __init__(self, batch: int | None):
+        self.max_batch = batch or 64
+        self.buckets = sorted({min(2 ** i, self.max_batch)
+                               for i in range(self.max_batch.bit_length())} | {self.max_batch})
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": "Qwen3-ASR-0.6B-style continuous-batching serving (BASELINE config 5)",
+            "layers": self.layers, "hidden": self.hidden, "heads": self.heads,
+            "kv_heads": self.kv_heads, "head_dim": self.head_dim, "intermediate": self.inter,
+            "vocab": self.vocab, "seed": 4, "max_batch": self.max_batch,
+            "max_new_tokens": self.max_new,
+            "arrivals": f"Poisson, {self.rate_per_gpu * world:g} req/s over {world} GPUs "
+                        f"({self.rate_per_gpu:g} per GPU; 200/s at 8)",
+            "audio": "U[1,30] s per request, 13 audio positions per second, injected as "
+                     "N(0, 0.02) embeddings, plus 20 text positions",
+            "engine": "pool of rows over a (28, 64, 1024, 8, 128) cache; packed causal prefill on "
+                      "join; one CUDA graph per batch bucket; finished rows checked every 4 steps",
+            "parallelism": f"replicas x{world} (no collective), least-loaded dispatch",
+        }
+
+    def units_per_step(self) -> int:
+        """Tokens of one decode step of a full pool."""
+        return self.max_batch
+
+    # ---- the trace ----
+    def trace(self, world: int, count: int) -> list:
+        from asrback_b200.replicas import ReplicaDispatcher
+
+        rng = np.random.default_rng(4)
+        rate = self.rate_per_gpu * world
+        arrivals = np.cumsum(rng.exponential(1.0 / rate, size=count))
+        seconds = rng.uniform(1.0, 30.0, size=count)
+        requests = []
+        for i in range(count):
+            audio = int(math.ceil(seconds[i] * self.audio_rate))
+            requests.append(_Request(i, float(arrivals[i]), float(seconds[i]), audio,
+                                     self.text_tokens))
+        dispatcher = ReplicaDispatcher(world)
+        for request in requests:
+            request.replica = dispatcher.assign(request.length + self.max_new)
+        return requests
+
+    # ---- the engine ----
+    def setup(self, torch, device, seed: int, native: bool = True) -> None:
+        dtype = torch.bfloat16
+        self.torch, self.device, self.native = torch, device, native
+        gen = torch.Generator(device=device).manual_seed(4)
+        h, L = self.hidden, self.layers
+        q, kv, d = self.heads, self.kv_heads, self.head_dim
+
+        def weight(rows, cols):
+            return (torch.randn((rows, cols), generator=gen, device=device)
+                    / math.sqrt(cols)).to(dtype)
+
+        def norm(*shape):
+            return (1 + 0.1 * torch.randn(shape, generator=gen, device=device)).to(dtype)
+
+        self.embed = (torch.randn((self.vocab, h), generator=gen, device=device) * 0.02).to(dtype)
+        self.w_qkv = [weight((q + 2 * kv) * d, h) for _ in range(L)]
+        self.w_o = [weight(h, q * d) for _ in range(L)]
+        self.w_gate_up = [weight(2 * self.inter, h) for _ in range(L)]
+        self.w_down = [weight(h, self.inter) for _ in range(L)]
+        self.n_in, self.n_post, self.n_q, self.n_k = (norm(L, h), norm(L, h), norm(L, d),
+                                                      norm(L, d))
+        self.n_final = norm(h)
+        shape = (L, self.max_batch, self.cache_length, kv, d)
+        self.keys = torch.zeros(shape, dtype=dtype, device=device)
+        self.values = torch.zeros(shape, dtype=dtype, device=device)
+        self.cos, self.sin = rope_tables(torch, 1e6, d, self.cache_length, device, dtype)
+        b = self.max_batch
+        self.tokens = torch.zeros(b, dtype=torch.int64, device=device)
+        self.position = torch.zeros(b, dtype=torch.int64, device=device)
+        self.end = torch.zeros(b, dtype=torch.int64, device=device)
+        self.finished = torch.ones(b, dtype=torch.bool, device=device)
+        self.sum_logprobs = torch.zeros(b, device=device)
+        self.generated = torch.zeros((b, self.cache_length), dtype=torch.int64, device=device)
+        self.eos_t = torch.tensor(self.eos, device=device)
+        self.audio_gen = torch.Generator(device=device).manual_seed(seed)
+        self.graphs = {}
+
+    def _rotate(self, x, cos, sin):
+        first, second = x.chunk(2, dim=-1)
+        return x * cos[:, None, :] + self.torch.cat((-second, first), dim=-1) * sin[:, None, :]
+
+    def _mlp(self, layer, x):
+        F = self.torch.nn.functional
+        h = F.rms_norm(x, (self.hidden,), self.n_post[layer], self.eps)
+        gate, up = (h @ self.w_gate_up[layer].T).chunk(2, dim=-1)
+        return x + (F.silu(gate) * up) @ self.w_down[layer].T
+
+    def _decode(self, b: int, kv_len: int | None) -> None:
+        """One decode step of rows 0..b-1 (the graph body)."""
+        torch = self.torch
+        F = torch.nn.functional
+        from asrback_b200 import attention, step
+
+        q, kvh, d = self.heads, self.kv_heads, self.head_dim
+        tokens, position = self.tokens[:b], self.position[:b]
+        x = self.embed[tokens]
+        if not self.native:
+            rows = torch.arange(b, device=self.device)
+            cos, sin = self.cos[position], self.sin[position]
+            key_positions = torch.arange(kv_len, device=self.device)
+            mask = (key_positions[None, :] <= position[:, None])[:, None, None, :]
+        for layer in range(self.layers):
+            h = F.rms_norm(x, (self.hidden,), self.n_in[layer], self.eps)
+            qkv = h @ self.w_qkv[layer].T
+            keys, values = self.keys[layer][:b], self.values[layer][:b]
+            if self.native:
+                out = attention.qwen3_attention_step(
+                    qkv, self.n_q[layer], self.n_k[layer], self.eps, self.cos, self.sin,
+                    position, keys, values, q, kvh)
+            else:
+                # The reference's TextAttention.step on its torch 2.11 path.
+                qq, kk, vv = qkv.split([q * d, kvh * d, kvh * d], dim=-1)
+                qq = self._rotate(F.rms_norm(qq.reshape(b, q, d), (d,), self.n_q[layer], self.eps),
+                                  cos, sin)
+                kk = self._rotate(F.rms_norm(kk.reshape(b, kvh, d), (d,), self.n_k[layer],
+                                             self.eps), cos, sin)
+                keys, values = keys[:, :kv_len], values[:, :kv_len]
+                keys[rows, position] = kk
+                values[rows, position] = vv.reshape(b, kvh, d)
+                out = F.scaled_dot_product_attention(
+                    qq.view(b, kvh, q // kvh, d), keys.transpose(1, 2), values.transpose(1, 2),
+                    attn_mask=mask).reshape(b, q * d)
+            x = self._mlp(layer, x + out @ self.w_o[layer].T)
+        x = F.rms_norm(x, (self.hidden,), self.n_final, self.eps)
+        if self.native:
+            step.greedy_step(x, self.embed, tokens, position, self.end[:b], self.finished[:b],
+                             self.sum_logprobs[:b], self.generated[:b], self.eos)
+        else:
+            logits = (x @ self.embed.T).float()
+            token = logits.argmax(dim=-1)
+            logprob = F.log_softmax(logits, dim=-1).gather(1, token[:, None]).squeeze(1)
+            finished = self.finished[:b]
+            active = ~finished
+            pos = position + active
+            token = torch.where(active, token, tokens)
+            self.sum_logprobs[:b].add_(logprob.masked_fill(finished, 0.0))
+            self.generated[:b].scatter_(1, pos[:, None], token[:, None])
+            finished.logical_or_(torch.isin(token, self.eos_t) | (pos >= self.end[:b]))
+            position.copy_(pos)
+            tokens.copy_(token)
+
+    def capture(self) -> None:
+        """One graph per batch bucket (per key/value bucket too on the torch
+        path, which reads the whole bucket view), captured before serving."""
+        from asrback_b200.transcription import CapturedGraph
+
+        pool = self.torch.cuda.graph_pool_handle()
+        kv_buckets = (None,) if self.native else (128, 256, 512, 768, 1024)
+        for b in self.buckets:
+            for kv_len in kv_buckets:
+                self.finished.zero_()
+                self.position.zero_()
+                self.end.fill_(self.cache_length - 1)
+                self.graphs[b, kv_len] = CapturedGraph(
+                    lambda b=b, kv_len=kv_len: self._decode(b, kv_len), pool)
+        self.finished.fill_(True)
+        self.position.zero_()
+        self.tokens.zero_()
+
+    def _prefill(self, requests: list, slots: list[int]) -> None:
+        """Packed causal prefill of the joining requests into their rows, and
+        their first tokens (qwen3_asr.py:1018-1091)."""
+        torch = self.torch
+        F = torch.nn.functional
+        from asrback_b200 import attention, step
+
+        q, kvh, d = self.heads, self.kv_heads, self.head_dim
+        lengths = [r.length for r in requests]
+        total = sum(lengths)
+        ids = np.empty(total, np.int64)
+        audio_rows = []
+        offset = 0
+        for r in requests:
+            # <system + user> text, the audio positions, <assistant> text.
+            head = self.text_tokens // 2
+            ids[offset:offset + r.length] = (np.arange(r.length) * 7919 + r.index * 104729) \
+                % 150000
+            audio_rows.append(np.arange(offset + head, offset + head + r.audio))
+            offset += r.length
+        positions = np.concatenate([np.arange(n) for n in lengths])
+        rows = np.repeat(np.asarray(slots), lengths)
+        starts = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+        first = np.asarray(lengths, np.int64)
+        ends = first - 1 + np.minimum(self.max_new, self.cache_length - first)
+        host = [torch.from_numpy(a).pin_memory() for a in
+                (ids, positions, rows, starts, np.concatenate(audio_rows), np.asarray(slots),
+                 first, ends)]
+        ids, positions, rows, starts, audio, slot_rows, first, ends = (
+            t.to(self.device, non_blocking=True) for t in host)
+        x = self.embed[ids]
+        x[audio] = (torch.randn((audio.shape[0], self.hidden), generator=self.audio_gen,
+                                device=self.device) * 0.02).to(x.dtype)
+        cos, sin = self.cos[positions], self.sin[positions]
+        longest = max(lengths)
+        if not self.native:
+            sizes = starts[1:] - starts[:-1]
+            offsets = torch.arange(longest, device=self.device)
+            valid = offsets[None, :] < sizes[:, None]
+            gather = torch.minimum(starts[:-1, None] + offsets, (starts[1:] - 1)[:, None])
+            mask = valid[:, None, None, :] & torch.ones((longest, longest), dtype=torch.bool,
+                                                        device=self.device).tril()
+        for layer in range(self.layers):
+            h = F.rms_norm(x, (self.hidden,), self.n_in[layer], self.eps)
+            qq, kk, vv = (h @ self.w_qkv[layer].T).split([q * d, kvh * d, kvh * d], dim=-1)
+            qq = self._rotate(F.rms_norm(qq.reshape(total, q, d), (d,), self.n_q[layer],
+                                         self.eps), cos, sin)
+            kk = self._rotate(F.rms_norm(kk.reshape(total, kvh, d), (d,), self.n_k[layer],
+                                         self.eps), cos, sin)
+            vv = vv.reshape(total, kvh, d)
+            self.keys[layer][rows, positions] = kk
+            self.values[layer][rows, positions] = vv
+            if self.native:
+                out = attention.varlen_attention(qq, kk, vv, starts, longest, True)
+            else:
+                out = F.scaled_dot_product_attention(
+                    *(t[gather].transpose(1, 2) for t in (qq, kk, vv)), attn_mask=mask,
+                    enable_gqa=True).transpose(1, 2)[valid]
+            x = self._mlp(layer, x + out.reshape(total, q * d) @ self.w_o[layer].T)
+        last = F.rms_norm(x[starts[1:].long() - 1], (self.hidden,), self.n_final, self.eps)
+        if self.native:
+            token, logprob = step.greedy_choose(last, self.embed)
+        else:
+            logits = (last @ self.embed.T).float()
+            token = logits.argmax(dim=-1)
+            logprob = F.log_softmax(logits, dim=-1).gather(1, token[:, None]).squeeze(1)
+        self.tokens[slot_rows] = token
+        self.position[slot_rows] = first
+        self.end[slot_rows] = ends
+        self.finished[slot_rows] = torch.isin(token, self.eos_t) | (first >= ends)
+        self.sum_logprobs[slot_rows] = logprob
+        self.generated[slot_rows, first] = token
+
+    def serve(self, requests: list, paced: bool) -> dict:
+        """Serves ``requests`` (sorted by arrival) to the end; returns counts
+        and device/host times."""
+        torch = self.torch
+        import collections
+
+        pending = collections.deque()
+        queue = collections.deque(requests)
+        rows: dict[int, _Request] = {}
+        bounds: dict[int, int] = {}
+        generated = steps = prefills = 0
+        stream = torch.cuda.current_stream()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        start.record(stream)
+        while queue or pending or rows:
+            now = time.perf_counter() - t0
+            while queue and (not paced or queue[0].arrival <= now):
+                pending.append(queue.popleft())
+            free = [slot for slot in range(self.max_batch) if slot not in rows]
+            if pending and free:
+                joining = [pending.popleft() for _ in range(min(len(free), len(pending)))]
+                slots = free[:len(joining)]
+                self._prefill(joining, slots)
+                prefills += 1
+                for slot, r in zip(slots, joining):
+                    rows[slot] = r
+                    bounds[slot] = r.length
+            if not rows:
+                if queue:
+                    time.sleep(max(0.0, min(queue[0].arrival - now, 0.002)))
+                continue
+            bucket = next(size for size in self.buckets if size > max(rows))
+            count = min(self.interval,
+                        max(r.length - 1 + self.max_new - bounds[s] for s, r in rows.items()))
+            count = max(count, 1)
+            kv_len = None
+            if not self.native:
+                length = max(min(bounds[s] + count, rows[s].length - 1 + self.max_new)
+                             for s in rows) + 1
+                kv_len = kv_bucket(length)
+            graph = self.graphs[bucket, kv_len]
+            for _ in range(count):
+                graph.replay()
+            steps += count
+            for slot in rows:
+                bounds[slot] = min(bounds[slot] + count, rows[slot].length - 1 + self.max_new)
+            finished = self.finished[:max(rows) + 1].tolist()
+            done = [slot for slot in rows if finished[slot]]
+            if done:
+                index = torch.tensor(done, device=self.device)
+                last = self.position[index].tolist()
+                now = time.perf_counter() - t0
+                for slot, position in zip(done, last):
+                    r = rows.pop(slot)
+                    generated += position - r.length + 1
+                    r.done_at = now
+                self.finished[index] = True
+                self.position[index] = 0
+                self.tokens[index] = 0
+        end.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        return {"tokens": generated, "requests": len(requests), "device_ms": start.elapsed_time(end),
+                "wall_s": wall, "decode_steps": steps, "prefills": prefills}
+
+    def cpu_rate(self, budget_s: float, threads: int) -> dict:
+        """The reference's decode step of this model on the host (float32):
+        embedding, 28 layers of RMSNorm, qkv, q/k RMSNorm + RoPE, cache write,
+        masked grouped SDPA over the 512-position bucket, o_proj and the MLP,
+        then the logits and ``_choose`` for 64 rows at positions 400..."""
+        torch = cpu_torch(threads)
+        F = torch.nn.functional
+        gen = torch.Generator().manual_seed(4)
+        h, L, q, kvh, d, b = self.hidden, self.layers, self.heads, self.kv_heads, self.head_dim, 64
+        w_qkv = [torch.randn(((q + 2 * kvh) * d, h), generator=gen) / 32 for _ in range(L)]
+        w_o = [torch.randn((h, q * d), generator=gen) / 45 for _ in range(L)]
+        w_gu = [torch.randn((2 * self.inter, h), generator=gen) / 32 for _ in range(L)]
+        w_d = [torch.randn((h, self.inter), generator=gen) / 55 for _ in range(L)]
+        embed = torch.randn((self.vocab, h), generator=gen) * 0.02
+        keys = torch.randn((L, b, 512, kvh, d), generator=gen)
+        values = torch.randn(keys.shape, generator=gen)
+        ones_h, ones_d = torch.ones(h), torch.ones(d)
+        cos_t, sin_t = rope_tables(torch, 1e6, d, self.cache_length)
+        rows = torch.arange(b)
+        key_positions = torch.arange(512)
+
+        def one(i):
+            pos = torch.full((b,), 400 + i % 100)
+            cos, sin = cos_t[pos], sin_t[pos]
+            mask = (key_positions[None, :] <= pos[:, None])[:, None, None, :]
+            x = embed[torch.arange(b)]
+            for layer in range(L):
+                hh = F.rms_norm(x, (h,), ones_h, 1e-6)
+                qq, kk, vv = (hh @ w_qkv[layer].T).split([q * d, kvh * d, kvh * d], dim=-1)
+                qq = self._rotate(F.rms_norm(qq.reshape(b, q, d), (d,), ones_d, 1e-6), cos, sin)
+                kk = self._rotate(F.rms_norm(kk.reshape(b, kvh, d), (d,), ones_d, 1e-6), cos, sin)
+                keys[layer][rows, pos] = kk
+                values[layer][rows, pos] = vv.reshape(b, kvh, d)
+                out = F.scaled_dot_product_attention(
+                    qq.view(b, kvh, q // kvh, d), keys[layer].transpose(1, 2),
+                    values[layer].transpose(1, 2), attn_mask=mask).reshape(b, q * d)
+                x = x + out @ w_o[layer].T
+                hh = F.rms_norm(x, (h,), ones_h, 1e-6)
+                gate, up = (hh @ w_gu[layer].T).chunk(2, dim=-1)
+                x = x + (F.silu(gate) * up) @ w_d[layer].T
+            logits = F.rms_norm(x, (h,), ones_h, 1e-6) @ embed.T
+            token = logits.argmax(dim=-1)
+            F.log_softmax(logits, dim=-1).gather(1, token[:, None])
+
+        self.torch = torch
+        with torch.inference_mode():
+            done, elapsed = time_cpu(one, budget_s)
+        return {"value": b * done / elapsed, "unit": self.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{done} decode steps of 64 rows through the 28-layer model (no churn), "
+                          f"torch CPU float32, {elapsed:.1f} s"}
+
+
+def measure_serve(args, work, torch, dist, device, rank: int, world: int, requests_per_gpu: int,
+                  cpu: bool, paced: bool) -> dict:
+    """The serving workload: capacity (every request of this replica's share
+    queued at once), then the same engine on the reference's torch attention
+    path, then (optionally) the arrival-paced run; the slowest rank's time."""
+    trace = work.trace(world, requests_per_gpu * world)
+    mine = [r for r in trace if r.replica == rank]
+    total_tokens = len(trace) * work.max_new
+    results = {}
+    with torch.inference_mode():
+        for native in (True, False):
+            work.setup(torch, device, SEED + 1000 * rank, native=native)
+            work.capture()
+            warm = work.trace(1, 8)  # a short warm-up through every code path
+            work.serve(warm, paced=False)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            uuid = getattr(torch.cuda.get_device_properties(device), "uuid", None)
+            with ClockSampler(str(uuid) if uuid else None) as clocks:
+                run = work.serve(mine, paced=False)
+            ranks = rank_times(torch, dist, world, run["device_ms"])
+            tokens = rank_times(torch, dist, world, float(run["tokens"]))
+            results["native" if native else "torch"] = dict(
+                run, rank_ms=ranks, value=sum(tokens) / (max(ranks) / 1e3),
+                clocks=clocks.summary())
+            if native and paced:
+                for r in mine:
+                    r.done_at = None
+                work.serve(work.trace(1, 4), paced=False)
+                if world > 1:
+                    dist.barrier()
+                paced_run = work.serve(mine, paced=True)
+                latency = sorted(r.done_at - r.arrival for r in mine if r.done_at is not None)
+                walls = rank_times(torch, dist, world, paced_run["wall_s"])
+                tokens_paced = rank_times(torch, dist, world, float(paced_run["tokens"]))
+                results["paced"] = {
+                    "value": sum(tokens_paced) / max(walls), "unit": work.unit,
+                    "offered_tokens_per_s": work.rate_per_gpu * world * work.max_new,
+                    "wall_s": max(walls), "requests": paced_run["requests"],
+                    "latency_s_p50": latency[len(latency) // 2] if latency else None,
+                    "latency_s_p99": latency[min(len(latency) - 1, int(0.99 * len(latency)))]
+                    if latency else None,
+                    "how": "requests released at their Poisson arrival times (host clock); "
+                           "tokens/s over the wall time from the first arrival to the last "
+                           "finish"}
+            del work.graphs
+            work.graphs = {}
+            torch.cuda.empty_cache()
+    native, ref = results["native"], results["torch"]
+    steps = native["decode_steps"]
+    ms = max(native["rank_ms"])
+    line = {
+        "metric": work.metric, "value": native["value"], "unit": work.unit, "n_gpus": world,
+        "steps": steps, "warmup": 8, "ms_per_step": ms / max(steps, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": dict(work.config(world), requests_per_gpu=len(mine),
+                                            requests_total=len(trace),
+                                            tokens_total=total_tokens),
+        "rank_ms": native["rank_ms"], "rank_spread": max(native["rank_ms"]) / min(
+            native["rank_ms"]),
+        "serving": {"decode_steps": steps, "prefills": native["prefills"],
+                    "tokens": native["tokens"], "requests": native["requests"]},
+        "timing": "capacity run: this replica's whole share queued at once, device time from the "
+                  "first prefill to the last finish (host checks every 4 steps included), "
+                  "slowest rank",
+        "torch_gpu_reference": {
+            "value": ref["value"], "unit": work.unit, "ms_per_step": max(ref["rank_ms"]) / max(
+                ref["decode_steps"], 1),
+            "what": "the same engine with the reference's torch 2.11 attention path (padded SDPA "
+                    "prefill, masked SDPA over key/value buckets, torch logits and _choose)"},
+        "paced": results.get("paced"),
+        "clocks": native["clocks"],
+    }
+    if cpu and rank == 0 and world == 1:
+        line["cpu_baseline"] = work.cpu_rate(args.cpu_seconds, os.cpu_count() or 1)
+    return line
+
+
 WORKLOADS = {cls.name: cls for cls in (WhisperDecode, WhisperEncoder, Qwen3Decode, Qwen3Prefill,
                                        Qwen3AudioWindows, WhisperGreedyStep, Qwen3GreedyStep,
-                                       WhisperCrossKV, WhisperPrefix)}
+                                       WhisperCrossKV, WhisperPrefix, Qwen3Serve)}
 
 
 # ------------------------------------------------------------------ arms ----
@@ -1690,15 +2175,19 @@ def summary(name: str, line: dict) -> dict:
     def r(x, digits=4):
         return None if x is None else float(f"{x:.{digits}g}")
 
-    out = {"value": r(line["value"]), "unit": line["unit"], "ms": r(line["ms_per_step"]),
-           "frac": r(line["roofline"]["frac"], 3), "e2e": r(line["e2e"]["value"]),
-           "torch_gpu": r(line["torch_gpu_reference"]["value"])}
+    out = {"value": r(line["value"]), "unit": line["unit"], "ms": r(line["ms_per_step"])}
+    if line.get("roofline"):
+        out["frac"] = r(line["roofline"]["frac"], 3)
+    if line.get("e2e"):
+        out["e2e"] = r(line["e2e"]["value"])
+    out["torch_gpu"] = r(line["torch_gpu_reference"]["value"])
     if line.get("torch_gpu_cudnn"):
         out["cudnn"] = r(line["torch_gpu_cudnn"]["value"])
     if line.get("cpu_baseline"):
         out["cpu"] = r(line["cpu_baseline"]["value"])
-    if line.get("serving"):
-        out["serving"] = line["serving"]
+    if line.get("paced"):
+        out["paced"] = r(line["paced"]["value"])
+        out["p99_s"] = r(line["paced"]["latency_s_p99"], 3)
     return out
 
 
@@ -1713,6 +2202,13 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     if args.layers:
         work.layers = args.layers
     cpu = not args.no_cpu_baseline
+    if args.workload == "qwen3-serve":
+        line = measure_serve(args, work, torch, dist, device, rank, world, 3 * work.max_batch,
+                             cpu=cpu, paced=True)
+        line["workloads"] = {work.name: summary(work.name, line)}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
     line = measure(args, work, torch, dist, device, rank, world, args.steps, args.warmup,
                    cpu=cpu, sustain=True)
     if cpu and rank == 0 and world == 1 and hasattr(work, "oracle_rate"):
@@ -1735,6 +2231,15 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
                 "rank_ms", "torch_gpu_reference", "torch_gpu_cudnn", "cpu_baseline", "clocks",
                 "device_status", "config")}
             short[name] = summary(name, r)
+        del work
+        torch.cuda.empty_cache()
+        work = WORKLOADS["qwen3-serve"](None)
+        r = measure_serve(args, work, torch, dist, device, rank, world, 3 * work.max_batch,
+                          cpu=cpu, paced=False)
+        extras["qwen3-serve"] = {k: r.get(k) for k in (
+            "metric", "value", "unit", "ms_per_step", "rank_ms", "serving", "torch_gpu_reference",
+            "cpu_baseline", "clocks", "config")}
+        short["qwen3-serve"] = summary("qwen3-serve", r)
         line["other_workloads"] = extras
     # The short records go last, so that the end of the line holds every
     # workload's figures.
