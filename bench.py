@@ -1414,9 +1414,9 @@ class Qwen3Serve:
     Requests come from one seeded trace: Poisson arrivals at 25 requests/s per
     GPU (200/s over 8 GPUs), 16 kHz audio of U[1, 30] s, 13 audio positions per
     second (``architecture.md:471``), so a prompt holds 33 to 410 positions.
-    ``ReplicaDispatcher`` assigns each request to the least-loaded replica
-    (cost: its prompt plus its 128 tokens); every rank builds the same trace
-    and serves its own share.
+    ``ReplicaDispatcher`` assigns each request to the replica with the fewest
+    outstanding requests (each holds one row for its 128 steps); every rank
+    builds the same trace and serves its own share.
 
     Two runs: ``capacity`` queues every request of the replica's share at
     once (the engine's throughput under join/leave churn, the line's value),
@@ -1471,9 +1471,12 @@ class Qwen3Serve:
             audio = int(math.ceil(seconds[i] * self.audio_rate))
             requests.append(_Request(i, float(arrivals[i]), float(seconds[i]), audio,
                                      self.text_tokens))
+        # Every request costs one row of the pool for its 128 steps whatever
+        # its prompt, so the dispatcher balances rows (least outstanding
+        # requests; in arrival order this deals them out in turn).
         dispatcher = ReplicaDispatcher(world)
         for request in requests:
-            request.replica = dispatcher.assign(request.length + self.max_new)
+            request.replica = dispatcher.assign(1.0)
         return requests
 
     # ---- the engine ----
@@ -1931,12 +1934,13 @@ def rank_times(torch, dist, world: int, ms: float) -> list[float]:
 def e2e_pipeline(torch, dist, work, world: int, first: int, steps: int) -> dict:
     """The K steps through the public ops with host buffers: step i's inputs
     are copied from pinned host memory into one of two device slots on a copy
-    stream, the step (a graph per slot) runs on the compute stream, and its
-    outputs go back to pinned host memory on a second copy stream, so the
-    copies of steps i+1 and i-1 overlap step i. Timed from before the first
-    copy in to after the last copy out, on the compute stream."""
-    from asrback_b200.transcription import CapturedGraph
-
+    stream, the step runs on the compute stream once its copy has landed, and
+    its outputs go back to pinned host memory on a second copy stream, so the
+    copies of steps i+1 and i-1 overlap step i. The K steps, with their copies
+    and the cross-stream dependencies (a slot is refilled only after the step
+    two before has read it), are captured as one multi-stream CUDA graph and
+    timed, like the device-resident steps, as one replay: from before the
+    first copy in to after the last copy out, on the compute stream."""
     proto = work.inputs_at(first)
     slots = [[torch.empty_like(x) for x in proto] for _ in range(2)]
     for slot in slots:
@@ -1952,58 +1956,53 @@ def e2e_pipeline(torch, dist, work, world: int, first: int, steps: int) -> dict:
         for dst, src in zip(pinned, inputs):
             dst.copy_(src.cpu())
         host.append(pinned)
-    outs: list = [None, None]
-
-    def capture(s):
-        def fn():
-            outs[s] = work.launch(slots[s])
-        return CapturedGraph(fn)
-
-    graphs = [capture(0), capture(1)]
-    out_bytes = sum(o.numel() * o.element_size() for o in outs[0])
     in_bytes = sum(x.numel() * x.element_size() for x in proto)
-    host_out = [torch.empty((out_bytes,), dtype=torch.uint8, pin_memory=True) for _ in range(2)]
-    compute = torch.cuda.current_stream()
-    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    ev = {name: [torch.cuda.Event(), torch.cuda.Event()] for name in ("in", "done", "out")}
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
-    def copy_in(i):
-        s = i % 2
-        with torch.cuda.stream(h2d):
-            if i >= 2:
-                h2d.wait_event(ev["done"][s])  # step i-2 has read slot s
-            for dst, src in zip(slots[s], host[i % distinct]):
-                dst.copy_(src, non_blocking=True)
-            ev["in"][s].record(h2d)
-
+    probe = work.launch(slots[0])
+    out_bytes = sum(o.numel() * o.element_size() for o in probe)
+    del probe
+    host_out = [torch.empty((max(out_bytes, 1),), dtype=torch.uint8, pin_memory=True)
+                for _ in range(2)]
     torch.cuda.synchronize()
+    compute = torch.cuda.Stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    landed = [torch.cuda.Event() for _ in range(steps)]
+    done = [torch.cuda.Event() for _ in range(steps)]
+    outs = []
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(compute), torch.cuda.graph(graph, stream=compute):
+        h2d.wait_stream(compute)
+        d2h.wait_stream(compute)
+        for i in range(steps):
+            s = i % 2
+            with torch.cuda.stream(h2d):
+                if i >= 2:
+                    h2d.wait_event(done[i - 2])  # step i-2 has read slot s
+                for dst, src in zip(slots[s], host[i % distinct]):
+                    dst.copy_(src, non_blocking=True)
+                landed[i].record(h2d)
+            compute.wait_event(landed[i])
+            out = work.launch(slots[s])
+            outs.append(out)
+            done[i].record(compute)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done[i])
+                offset = 0
+                for o in out:
+                    n = o.numel() * o.element_size()
+                    host_out[s][offset:offset + n].copy_(o.reshape(-1).view(torch.uint8),
+                                                         non_blocking=True)
+                    offset += n
+        compute.wait_stream(h2d)
+        compute.wait_stream(d2h)
+    graph.replay()  # uploads the graph; untimed
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
-    start.record(compute)
-    h2d.wait_stream(compute)
-    d2h.wait_stream(compute)
-    copy_in(0)
-    for i in range(steps):
-        s = i % 2
-        if i + 1 < steps:
-            copy_in(i + 1)
-        compute.wait_event(ev["in"][s])
-        if i >= 2:
-            compute.wait_event(ev["out"][s])  # step i-2's outputs are on the host
-        graphs[s].replay()
-        ev["done"][s].record(compute)
-        with torch.cuda.stream(d2h):
-            d2h.wait_event(ev["done"][s])
-            offset = 0
-            for o in outs[s]:
-                n = o.numel() * o.element_size()
-                host_out[s][offset:offset + n].copy_(o.reshape(-1).view(torch.uint8),
-                                                     non_blocking=True)
-                offset += n
-            ev["out"][s].record(d2h)
-    compute.wait_stream(d2h)
-    end.record(compute)
+    stream = torch.cuda.current_stream()
+    start.record(stream)
+    graph.replay()
+    end.record(stream)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
     ranks = rank_times(torch, dist, world, ms)
@@ -2011,7 +2010,8 @@ def e2e_pipeline(torch, dist, work, world: int, first: int, steps: int) -> dict:
     return {"value": value, "unit": work.unit, "h2d_bytes_per_step": in_bytes,
             "d2h_bytes_per_step": out_bytes, "steps": steps,
             "how": "pinned host inputs in and outputs out every step, double-buffered on two "
-                   "copy streams under the graph-replayed steps",
+                   "copy streams; the K steps with their copies captured as one multi-stream "
+                   "graph, one replay, slowest rank",
             "rank_ms": ranks}
 
 

@@ -314,6 +314,39 @@ def test_encoder_attention_random(batch, length):
     np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
 
 
+@pytest.mark.parametrize("length", [1, 95, 96, 97, 136, 257, 385])
+def test_encoder_attention_ragged_tiles(length):
+    """Lengths that end inside or exactly at a 96-key tile and leave a work
+    item's three 128-row query tiles partly or wholly past the window."""
+    gen = torch.Generator().manual_seed(1000 + length)
+    batch, heads, dim = 2, 20, 64
+    x = [_rand(gen, (batch, length, heads * dim), torch.bfloat16) for _ in range(3)]
+    views = [t.to(DEV).view(batch, length, heads, dim).transpose(1, 2) for t in x]
+    out = attention.whisper_encoder_attention(*views)
+    q, k, v = (t.float().numpy().reshape(batch, length, heads, dim).transpose(0, 2, 1, 3) for t in x)
+    want = oracle.encoder_attention(q, k, v)
+    got = host(out).reshape(batch, length, heads, dim).transpose(0, 2, 1, 3)
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    assert attention.read_status() == 0
+
+
+def test_encoder_attention_many_items_per_cta():
+    """More work items than SMs (10 windows x 8 heads x 4 query-tile groups),
+    so every persistent CTA runs several items through its Q buffers and K/V
+    ring; against torch's float32 SDPA of the same bf16 inputs."""
+    import torch.nn.functional as F
+
+    gen = torch.Generator().manual_seed(77)
+    batch, length, heads, dim = 10, 1500, 8, 64
+    x = [_rand(gen, (batch, length, heads * dim), torch.bfloat16).to(DEV) for _ in range(3)]
+    views = [t.view(batch, length, heads, dim).transpose(1, 2) for t in x]
+    out = attention.whisper_encoder_attention(*views)
+    want = F.scaled_dot_product_attention(*(t.float() for t in views))
+    got = out.float().view(batch, length, heads, dim).transpose(1, 2)
+    assert (got - want).abs().max().item() <= 2e-2
+    assert attention.read_status() == 0
+
+
 def test_encoder_attention_rescales_when_a_later_key_dominates():
     """Keys in later tiles that score far above a row's running max (8 x the
     row's own query) move the max of some rows of a warp and not others: O is
