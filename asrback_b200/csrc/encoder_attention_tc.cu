@@ -120,8 +120,9 @@ __device__ __forceinline__ void exp2_pair_fma(float x0, float x1, float& e0, flo
 #endif
 constexpr int kPolyEvery = ASRBACK_ENCODER_POLY_EVERY;
 
-// 448 threads: up to 144 registers each (the softmax rows hold 96 scores).
-__global__ void __maxnreg__(144)
+// 448 threads in 14 warps: an SM sub-partition holds 4 of them in its 16K
+// registers, so a thread has at most 128.
+__global__ void __launch_bounds__(kThreads, 1)
     encoder_attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                 const __grid_constant__ CUtensorMap map_k,
                                 const __grid_constant__ CUtensorMap map_v,
@@ -305,25 +306,37 @@ __global__ void __maxnreg__(144)
         if (!ok) break;
         tc_fence_after();
         const int valid = min(kKeys, p.length - j * kKeys);
-        float v[kKeys];
-        tmem_ld64(tS, v);
-        tmem_ld32(tS + 64, v + 64);
-        if (valid < kKeys) {
-          // Keys past the window (the ragged last tile) take no weight.
+        // Row max over the 96 scores (eight short independent chains); keys
+        // past the window (the ragged last tile) take no weight. The scores
+        // are read again, 32 columns at a time, for the exponentials, so no
+        // more than 96 of them are live at once.
+        float mx;
+        {
+          float v[64], w[32];
+          tmem_ld64(tS, v);
+          tmem_ld32(tS + 64, w);
+          if (valid < kKeys) {
 #pragma unroll
-          for (int i = 0; i < kKeys; ++i)
-            if (i >= valid) v[i] = -INFINITY;
+            for (int i = 0; i < 64; ++i)
+              if (i >= valid) v[i] = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (64 + i >= valid) w[i] = -INFINITY;
+          }
+          float acc[8];
+#pragma unroll
+          for (int a = 0; a < 8; ++a) acc[a] = fmax3(v[a], v[8 + a], w[a]);
+#pragma unroll
+          for (int i = 16; i < 64; i += 16)
+#pragma unroll
+            for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
+#pragma unroll
+          for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], w[8 + a], w[16 + a]);
+#pragma unroll
+          for (int a = 0; a < 8; ++a) acc[a] = fmaxf(acc[a], w[24 + a]);
+          mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
+                     fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
         }
-        // Row max as eight short independent chains.
-        float acc[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
-#pragma unroll
-        for (int i = 16; i < kKeys; i += 16)
-#pragma unroll
-          for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
-        const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
-                               fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
         const float m_tile = mx * p.scale_log2;
         // Rows whose tile max passes the used max by more than the threshold
         // move it; the warp rescales O together (tcgen05.ld/st are
@@ -350,14 +363,22 @@ __global__ void __maxnreg__(144)
         uint64_t sum2[4];
 #pragma unroll
         for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
+        // Chunk c reads score columns [32c, 32c + 32) and writes its P over
+        // [16c, 16c + 16): below every column a later chunk still reads.
 #pragma unroll
         for (int chunk = 0; chunk < kKeys / 32; ++chunk) {
+          float v[32];
+          tmem_ld32(tS + 32 * chunk, v);
+          if (valid < kKeys) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * chunk + i >= valid) v[i] = -INFINITY;
+          }
           uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int col = 32 * chunk + 2 * i;
             float x0, x1, p0, p1;
-            unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
+            unpack2(ffma2(pack2(v[2 * i], v[2 * i + 1]), scale2, neg_m2), x0, x1);
             if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
               exp2_pair_fma(x0, x1, p0, p1);
             } else {
