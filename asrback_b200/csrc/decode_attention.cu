@@ -823,8 +823,10 @@ constexpr int kPrefixTokens = 4;
 #ifndef ASRBACK_QWEN3_GROUP
 #define ASRBACK_QWEN3_GROUP 8
 #endif
+// Three stages (192 KB of ring, one CTA per SM, as the grid holds at most one
+// wave): batch 64 26.6 -> 25.2 us per launch; 32 and 16 rows unchanged.
 #ifndef ASRBACK_SHAPE_QWEN3_BF16
-#define ASRBACK_SHAPE_QWEN3_BF16 2, 16, 2
+#define ASRBACK_SHAPE_QWEN3_BF16 2, 16, 3
 #endif
 #ifndef ASRBACK_SHAPE_QWEN3_F32
 #define ASRBACK_SHAPE_QWEN3_F32 1, 8, 3

@@ -4,42 +4,39 @@
 // Replaces F.scaled_dot_product_attention in MultiHeadAttention.forward
 // (whisper.py:108-110, via attend :102-104) for the encoder layers.
 //
-// At head_dim 64 a score costs 256 flops of MMA and one exponential, so the
-// SFU (16 exponentials per SM and clock) bounds the kernel before the tensor
-// core does. The design keeps the SFU fed: three query tiles per CTA, each
-// with its own softmax warpgroup, so that an SM sub-partition always holds
-// three softmax warps of which at most one waits on the tensor core.
-//
-// A work item is one (window b, head h) and three 128-row query tiles; the
+// A work item is one (window b, head h) and two 128-row query tiles; the
 // kernel is persistent (one CTA per SM takes items blockIdx.x, + gridDim.x,
-// ..., the triple index fastest so that CTAs running together share each
-// (window, head)'s keys and values in L2). Warp roles (14 warps):
-//   warp 0      TMA producer: each item's three Q tiles into one of two Q
+// ..., the pair index fastest so that CTAs running together share each
+// (window, head)'s keys and values in L2). Warp roles:
+//   warp 0      TMA producer: each item's two Q tiles into one of two Q
 //               buffers (once the item two before has issued its last S), and
-//               its K/V tiles of 96 keys into a STAGES-deep ring that runs on
+//               its K/V tiles of 128 keys into a STAGES-deep ring that runs on
 //               across items (4-D tensor maps over the projections' (batch,
 //               length, heads, 64) layout, 128-byte swizzle; rows past the
 //               window read as zeros);
 //   warp 1      allocates the 512 TMEM columns; one lane issues every MMA:
-//               S_t = Q_t K^T (SS: both operands from shared memory) and
-//               O_t += P_t V (TS: P from TMEM, V from shared memory);
-//   warps 2-13  three softmax warpgroups: query tile t is warps 2+4t .. 5+4t
-//               (thread = TMEM lane = query row; a warp reads the lane
-//               quarter warp % 4).
-// TMEM columns: S_t at [96t, 96t + 96), P_t (packed bf16 pairs) written over
-// its first 48 columns, O_t at [288 + 64t, 352 + 64t).
-// Key tiles are numbered X over all of a CTA's items. The MMA lane issues,
-// for each X, PV_0(X), S_0(X+1), PV_1(X), S_1(X+1), PV_2(X), S_2(X+1): the
-// next S of a tile goes into its buffer right after the P V that reads the
-// old P (one thread's MMAs execute in order), and each tile's S completes
-// while the other two tiles' softmaxes run. The completion of S_t(X) also
-// means PV_t(X-1) is done, so a softmax may rescale O_t then without a
-// barrier of its own; an item's first PV_t overwrites O_t, and is issued
-// only after the softmax has arrived for that tile, i.e. after its epilogue
-// has read O_t.
+//               S = Q_t K^T (SS: both operands from shared memory) and
+//               O_t += P V (TS: P from TMEM, V from shared memory);
+//   warps 4-7   softmax of query tile 0 (thread = TMEM lane = query row);
+//   warps 8-11  softmax of query tile 1.
+// TMEM columns: three S buffers [0,128) [128,256) [256,384), O0 [384,448),
+// O1 [448,512). Key tiles are numbered J over all of a CTA's items (item i,
+// tile j: J = i * n_k + j). The k-th S (tile t, k = 2J + t) goes to buffer
+// k % 3; its softmax writes P (packed bf16 pairs) over the buffer's first 64
+// columns, and the next S into that buffer is issued right after that P V
+// (the tensor core runs one thread's MMAs in order). So S_1(J+1) follows
+// P_0(J) V and S_0(J+2) follows P_1(J) V: each tile's next S is computed
+// while the other tile's softmax runs, and a softmax goes from one key tile
+// to the next without waiting for the tensor core, across item boundaries
+// too; an item's first P V into O_t waits only until the previous item's
+// epilogue has read O_t.
+// Barriers that can run ahead of their waiters come in copies so that no
+// waiter ever sees one complete twice: one S barrier per buffer, two P
+// barriers per tile (alternating), and O's last P V commits to a barrier of
+// its own.
 // The running max is rescaled lazily: P uses a stale max m until a tile's max
-// exceeds it by more than 8 (log2 units), and only then are O (in TMEM) and
-// the row sum rescaled, so P stays <= 2^8.
+// exceeds it by more than 8 (log2 units), and only then are O (in TMEM, once
+// its previous P V is done) and the row sum rescaled, so P stays <= 2^8.
 #include "tcgen05.cuh"
 
 namespace asrback {
@@ -49,39 +46,41 @@ namespace {
 using namespace tc;
 
 constexpr int kRows = 128;  // query rows per tile (= TMEM lanes)
-constexpr int kTiles = 3;   // query tiles per work item
-constexpr int kKeys = 96;   // keys per tile
+constexpr int kKeys = 128;  // keys per tile
 constexpr int kDim = 64;
 constexpr int kStages = 4;
-constexpr int kQTileBytes = kRows * kDim * 2;   // 16 KB
-constexpr int kKVTileBytes = kKeys * kDim * 2;  // 12 KB
-constexpr int kSoftmaxWarp0 = 2;
-constexpr int kThreads = (kSoftmaxWarp0 + 4 * kTiles) * 32;  // 448
+constexpr int kTileBytes = kRows * kDim * 2;  // 16 KB, one Q, K or V tile
+// warp 0 TMA, warp 1 MMA (and TMEM owner), warps 2-3 idle, warps 4-11 softmax.
+constexpr int kThreads = 12 * 32;
 constexpr int kTmemCols = 512;
-__host__ __device__ constexpr int col_s(int t) { return kKeys * t; }
-__host__ __device__ constexpr int col_o(int t) { return kKeys * kTiles + kDim * t; }
-static_assert(col_o(kTiles - 1) + kDim <= kTmemCols, "TMEM columns");
+// TMEM column of S, O and P for query tile t.
+// Three S buffers of 128 columns rotate over the two query tiles: the k-th
+// S (k = 2j + t) goes to buffer k % 3, and P overwrites the first 64 columns
+// of its own S buffer.
+__host__ __device__ constexpr int col_buf(int b) { return 128 * b; }
+__host__ __device__ constexpr int buf_of(int t, int j) { return (2 * j + t) % 3; }
+__host__ __device__ constexpr int col_o(int t) { return 384 + 64 * t; }
 // Lazy rescale threshold (log2 units): P <= 2^8 between rescales.
 constexpr float kRescaleThreshold = 8.0f;
 
-constexpr int kOffQ = 0;  // two Q buffers of three tiles
-constexpr int kOffK = 2 * kTiles * kQTileBytes;
-constexpr int kOffV = kOffK + kStages * kKVTileBytes;
-constexpr int kOffBar = kOffV + kStages * kKVTileBytes;
+constexpr int kOffQ = 0;  // two Q buffers of two tiles
+constexpr int kOffK = 4 * kTileBytes;
+constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kOffBar = kOffV + kStages * kTileBytes;
 // barriers: q_full[2], q_empty[2] (per Q buffer), k_full[S], v_full[S],
-// kv_empty[S], s_full[3], p_full[3], o_final[3] (per query tile)
-constexpr int kNumBars = 2 + 2 + 3 * kStages + 3 * kTiles;
+// kv_empty[S], s_full[3] (one per S buffer), p_full[2][2] (per tile,
+// alternating), o_full[2], o_final[2], o_free[2]
+constexpr int kNumBars = 2 + 2 + 3 * kStages + 3 + 4 + 2 + 2 + 2;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
-static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 
 struct TcParams {
   void* out;
   int64_t sb, sh, ss;  // output strides (elements)
   int length;
-  int q_groups;  // work items per (window, head): ceil(query tiles / 3)
+  int q_pairs;
   int heads;
-  int items;  // q_groups * heads * batch
+  int items;  // q_pairs * heads * batch
   float scale_log2;
   int32_t* status;
 };
@@ -114,14 +113,13 @@ __device__ __forceinline__ void exp2_pair_fma(float x0, float x1, float& e0, flo
   e1 = __int_as_float(__float_as_int(q1) + (__float_as_int(y1) << 23));
 }
 
-// One pair in kPolyEvery takes the FMA-pipe exp2 (0: none).
+// One pair in kPolyEvery takes the FMA-pipe exp2 (0: none). Sweeps on B200
+// found the SFU is not the binding limit of this kernel, so it is off.
 #ifndef ASRBACK_ENCODER_POLY_EVERY
 #define ASRBACK_ENCODER_POLY_EVERY 0
 #endif
 constexpr int kPolyEvery = ASRBACK_ENCODER_POLY_EVERY;
 
-// 448 threads in 14 warps: an SM sub-partition holds 4 of them in its 16K
-// registers, so a thread has at most 128.
 __global__ void __launch_bounds__(kThreads, 1)
     encoder_attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                                 const __grid_constant__ CUtensorMap map_k,
@@ -136,9 +134,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_full = q_empty + 2;
   uint64_t* v_full = k_full + kStages;
   uint64_t* kv_empty = v_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;  // [query tile]
-  uint64_t* p_full = s_full + kTiles;
-  uint64_t* o_final = p_full + kTiles;
+  uint64_t* s_full = kv_empty + kStages;  // [buffer]
+  uint64_t* p_full = s_full + 3;          // [2 * t + (J & 1)]
+  uint64_t* o_full = p_full + 4;
+  uint64_t* o_final = o_full + 2;
+  uint64_t* o_free = o_final + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -161,10 +161,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int t = 0; t < kTiles; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
+    for (int b = 0; b < 3; ++b) mbar_init(&s_full[b], 1);
+    for (int t = 0; t < 4; ++t) mbar_init(&p_full[t], 4);  // one arrival per softmax warp
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&o_full[t], 1);
       mbar_init(&o_final[t], 1);
+      mbar_init(&o_free[t], 4);
     }
     fence_barrier_init();
   }
@@ -183,31 +185,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      int g = 0;  // key tiles loaded (= X)
+      int g = 0;  // key tiles loaded (= J)
       for (int li = 0; li < n_items && !timed_out; ++li) {
         const int index = item_index(li);
-        const int group = index % p.q_groups, h = (index / p.q_groups) % p.heads;
-        const int b = index / (p.q_groups * p.heads);
+        const int pair = index % p.q_pairs, h = (index / p.q_pairs) % p.heads;
+        const int b = index / (p.q_pairs * p.heads);
         const int qb = li & 1;
         if (li >= 2 && !mbar_wait_bounded(&q_empty[qb], ((li >> 1) - 1) & 1)) {
           timed_out = true;
           break;
         }
-        uint8_t* qdst = smem + kOffQ + qb * kTiles * kQTileBytes;
-        mbar_arrive_expect_tx(&q_full[qb], kTiles * kQTileBytes);
-        for (int t = 0; t < kTiles; ++t)
-          tma_load_4d(qdst + t * kQTileBytes, &map_q, 0, h, (kTiles * group + t) * kRows, b,
-                      &q_full[qb]);
+        uint8_t* qdst = smem + kOffQ + qb * 2 * kTileBytes;
+        mbar_arrive_expect_tx(&q_full[qb], 2 * kTileBytes);
+        tma_load_4d(qdst, &map_q, 0, h, (2 * pair) * kRows, b, &q_full[qb]);
+        tma_load_4d(qdst + kTileBytes, &map_q, 0, h, (2 * pair + 1) * kRows, b, &q_full[qb]);
         for (int j = 0; j < n_k; ++j, ++g) {
           const int s = g % kStages;
           if (g >= kStages && !mbar_wait_bounded(&kv_empty[s], ((g / kStages) - 1) & 1)) {
             timed_out = true;
             break;
           }
-          mbar_arrive_expect_tx(&k_full[s], kKVTileBytes);
-          tma_load_4d(smem + kOffK + s * kKVTileBytes, &map_k, 0, h, j * kKeys, b, &k_full[s]);
-          mbar_arrive_expect_tx(&v_full[s], kKVTileBytes);
-          tma_load_4d(smem + kOffV + s * kKVTileBytes, &map_v, 0, h, j * kKeys, b, &v_full[s]);
+          mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+          tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, b, &k_full[s]);
+          mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+          tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, b, &v_full[s]);
         }
       }
     }
@@ -218,18 +219,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t kIdescPV = idesc_bf16(kRows, kDim, true);
       // Descriptors are built once; a step moves the start-address field
       // (address >> 4): 32 bytes along K inside a swizzled row (Q, K), two
-      // 8-row swizzle atoms of V (2048 bytes), one tile.
+      // 8-row swizzle atoms of V (2048 bytes), one tile (kTileBytes). This lane
+      // shares its sub-partition's issue slots with softmax warps, so its
+      // per-MMA work is an add and the MMA.
       const uint64_t q_desc = sw128_desc(smem_addr(smem + kOffQ), 16, 1024);
       const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
-      const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kKVTileBytes, 1024);
-      constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4;
-      constexpr uint64_t kQTile = kQTileBytes >> 4, kKVTile = kKVTileBytes >> 4;
+      const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
+      constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4, kTile = kTileBytes >> 4;
       bool ok = true;
-      // Position of key tile X in the sequence: item li (Q buffer li & 1),
-      // tile j within it, ring slot s and lap. Running counters, so the lane
-      // divides nothing.
+      // Position of key tile X in the sequence: item li (Q buffer li & 1), tile
+      // j within it, ring slot s, ring lap, S buffer of tile 0. Kept as running
+      // counters (one per tile stream below) so the lane divides nothing.
       struct Cursor {
-        int X, li, j, s, lap;
+        int X, li, j, s, lap, buf0;
         __device__ void next(int n_k) {
           ++X;
           if (++j == n_k) {
@@ -240,112 +242,119 @@ __global__ void __launch_bounds__(kThreads, 1)
             s = 0;
             ++lap;
           }
+          buf0 = buf0 == 0 ? 2 : buf0 - 1;  // (2X) % 3 steps by 2 mod 3
         }
       };
-      // S_t(X); the first S of an item waits for its Q, the last frees it.
+      // S_t(X): query tile t of item li against key tile X. The item's first S
+      // (t = 0, j == 0) waits for its Q; after its last S (t = 1, j == n_k - 1)
+      // the Q buffer is free.
       auto issue_qk = [&](int t, const Cursor& c) {
         const int qb = c.li & 1;
-        if (t == 0) {
-          if (c.j == 0) ok = ok && mbar_wait_bounded(&q_full[qb], (c.li >> 1) & 1);
-          ok = ok && mbar_wait_bounded(&k_full[c.s], c.lap & 1);
-        }
+        if (t == 0 && c.j == 0) ok = ok && mbar_wait_bounded(&q_full[qb], (c.li >> 1) & 1);
+        ok = ok && mbar_wait_bounded(&k_full[c.s], c.lap & 1);
         if (!ok) return;
         tc_fence_after();
+        const int s = c.s;
+        const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
         // K = 64 in four steps of 16 elements.
 #pragma unroll
         for (int k = 0; k < kDim / 16; ++k)
-          mma_ss(tmem + col_s(t), q_desc + (kTiles * qb + t) * kQTile + k * kStepK,
-                 k_desc + c.s * kKVTile + k * kStepK, kIdescQK, k > 0);
-        mma_commit(&s_full[t]);
-        if (t == kTiles - 1 && c.j == n_k - 1) mma_commit(&q_empty[qb]);
+          mma_ss(tmem + col_buf(buf), q_desc + (2 * qb + t) * kTile + k * kStepK,
+                 k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
+        mma_commit(&s_full[buf]);
+        if (t == 1 && c.j == n_k - 1) mma_commit(&q_empty[qb]);
       };
-      // O_t (+)= P_t(X) V(X); the item's last one commits o_final.
+      // O_t (+)= P_t(J) V(J); an item's first one waits until the previous
+      // item's epilogue has read O_t; the item's last one commits o_final.
       auto issue_pv = [&](int t, const Cursor& c) {
-        if (t == 0) ok = ok && mbar_wait_bounded(&v_full[c.s], c.lap & 1);
-        ok = ok && mbar_wait_bounded(&p_full[t], c.X & 1);
+        const int J = c.X, li = c.li, j = c.j, s = c.s;
+        if (t == 0) ok = ok && mbar_wait_bounded(&v_full[s], c.lap & 1);
+        ok = ok && mbar_wait_bounded(&p_full[2 * t + (J & 1)], (J >> 1) & 1);
+        if (j == 0 && li > 0) ok = ok && mbar_wait_bounded(&o_free[t], (li - 1) & 1);
         if (!ok) return;
         tc_fence_after();
-        // K = 96 keys in six steps of 16: P advances 8 TMEM columns (bf16
+        const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
+        // K = 128 keys in eight steps of 16: P advances 8 TMEM columns (bf16
         // pairs), V two 8-row swizzle atoms.
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k)
-          mma_ts(tmem + col_o(t), tmem + col_s(t) + k * 8, v_desc + c.s * kKVTile + k * kStepV,
-                 kIdescPV, (c.j > 0 || k > 0));
-        if (c.j == n_k - 1) mma_commit(&o_final[t]);
+          mma_ts(tmem + col_o(t), tmem + col_buf(buf) + k * 8, v_desc + s * kTile + k * kStepV,
+                 kIdescPV, (j > 0 || k > 0));
+        mma_commit(j + 1 < n_k ? &o_full[t] : &o_final[t]);
       };
-      Cursor cur{0, 0, 0, 0, 0};
-      Cursor ahead = cur;
-      for (int t = 0; t < kTiles; ++t) issue_qk(t, cur);
-      ahead.next(n_k);
-      for (int X = 0; X < total && ok; ++X) {
-        for (int t = 0; t < kTiles && ok; ++t) {
-          issue_pv(t, cur);
-          if (ok && X + 1 < total) issue_qk(t, ahead);
-        }
-        if (ok && X + kStages < total) mma_commit(&kv_empty[cur.s]);
-        cur.next(n_k);
-        ahead.next(n_k);
+      // Three cursors: the P V tile J, and the S tiles J + 1 and J + 2.
+      Cursor c0{0, 0, 0, 0, 0, 0};
+      Cursor c1 = c0, c2 = c0;
+      issue_qk(0, c0);
+      issue_qk(1, c0);
+      c1.next(n_k);
+      c2.next(n_k);
+      c2.next(n_k);
+      if (total > 1) issue_qk(0, c1);
+      for (int J = 0; J < total && ok; ++J) {
+        issue_pv(0, c0);
+        if (ok && J + 1 < total) issue_qk(1, c1);
+        if (ok) issue_pv(1, c0);
+        if (ok && J + 2 < total) issue_qk(0, c2);
+        if (ok && J + kStages < total) mma_commit(&kv_empty[c0.s]);
+        c0.next(n_k);
+        c1.next(n_k);
+        c2.next(n_k);
       }
       timed_out = !ok;
     }
-  } else {
+  } else if (warp >= 4) {
     // ---------------- softmax and epilogue (one query row per thread) ----------------
-    const int t = (warp - kSoftmaxWarp0) >> 2;
+    const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_bits + col_s(t);
     const uint32_t tO = tmem + lane_bits + col_o(t);
-    const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
     bool ok = true;
     for (int li = 0; li < n_items && ok; ++li) {
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < n_k && ok; ++j) {
-        const int X = li * n_k + j;
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[t], X & 1));
+        const int J = li * n_k + j;
+        // This tile's S is the k-th (k = 2J + t): buffer k % 3, the
+        // (k / 3)-th completion of that buffer's barrier.
+        const int buf = buf_of(t, J);
+        const uint32_t tS = tmem + lane_bits + col_buf(buf);
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[buf], ((2 * J + t) / 3) & 1));
         if (!ok) break;
         tc_fence_after();
         const int valid = min(kKeys, p.length - j * kKeys);
-        // Row max over the 96 scores (eight short independent chains); keys
-        // past the window (the ragged last tile) take no weight. The scores
-        // are read again, 32 columns at a time, for the exponentials, so no
-        // more than 96 of them are live at once.
-        float mx;
-        {
-          float v[64], w[32];
-          tmem_ld64(tS, v);
-          tmem_ld32(tS + 64, w);
-          if (valid < kKeys) {
+        float v[kKeys];
+        tmem_ld128(tS, v);
+        if (valid < kKeys) {
+          // Keys past the window (the ragged last tile) take no weight.
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (i >= valid) v[i] = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (64 + i >= valid) w[i] = -INFINITY;
-          }
-          float acc[8];
-#pragma unroll
-          for (int a = 0; a < 8; ++a) acc[a] = fmax3(v[a], v[8 + a], w[a]);
-#pragma unroll
-          for (int i = 16; i < 64; i += 16)
-#pragma unroll
-            for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
-#pragma unroll
-          for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], w[8 + a], w[16 + a]);
-#pragma unroll
-          for (int a = 0; a < 8; ++a) acc[a] = fmaxf(acc[a], w[24 + a]);
-          mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
-                     fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
+          for (int i = 0; i < kKeys; ++i)
+            if (i >= valid) v[i] = -INFINITY;
         }
+        // Row max as eight short independent chains.
+        float acc[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
+#pragma unroll
+        for (int i = 16; i < kKeys; i += 16)
+#pragma unroll
+          for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
+        const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
+                               fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
         const float m_tile = mx * p.scale_log2;
         // Rows whose tile max passes the used max by more than the threshold
         // move it; the warp rescales O together (tcgen05.ld/st are
-        // warp-wide), the other rows with alpha = 1. PV_t(X-1), issued before
-        // S_t(X), is complete: O_t is idle.
+        // warp-wide), the other rows with alpha = 1.
         const bool move = m_tile > m_used + kRescaleThreshold;
         if (__any_sync(0xffffffffu, move)) {
           const float m_new = move ? m_tile : m_used;
           if (j > 0) {
+            // O_t must be idle: P_t(j-1) V done. (P_t(j-2) V is: S_t(j), just
+            // completed, was issued after it.)
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait_bounded(&o_full[t], (li * (n_k - 1) + j - 1) & 1));
+            if (!ok) break;
+            tc_fence_after();
             const float alpha = move ? fast_exp2(m_used - m_new) : 1.f;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -355,30 +364,24 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 16; ++i) o[i] *= alpha;
               tmem_st16f(tO + 16 * c, o);
             }
+            tmem_wait_st();
             l *= alpha;
           }
           m_used = m_new;
         }
+        const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
         const uint64_t neg_m2 = pack2(-m_used, -m_used);
         uint64_t sum2[4];
 #pragma unroll
         for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
-        // Chunk c reads score columns [32c, 32c + 32) and writes its P over
-        // [16c, 16c + 16): below every column a later chunk still reads.
 #pragma unroll
-        for (int chunk = 0; chunk < kKeys / 32; ++chunk) {
-          float v[32];
-          tmem_ld32(tS + 32 * chunk, v);
-          if (valid < kKeys) {
+        for (int half = 0; half < 2; ++half) {
+          uint32_t packed[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (32 * chunk + i >= valid) v[i] = -INFINITY;
-          }
-          uint32_t packed[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < 32; ++i) {
+            const int col = 64 * half + 2 * i;
             float x0, x1, p0, p1;
-            unpack2(ffma2(pack2(v[2 * i], v[2 * i + 1]), scale2, neg_m2), x0, x1);
+            unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
             if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
               exp2_pair_fma(x0, x1, p0, p1);
             } else {
@@ -388,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
             packed[i] = bf16x2(p0, p1);
           }
-          tmem_st16(tS + 16 * chunk, packed);
+          tmem_st32u(tS + 32 * half, packed);
         }
         float lo0, hi0;
         unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
@@ -396,17 +399,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t]);
+        if (lane == 0) mbar_arrive(&p_full[2 * t + (J & 1)]);
       }
       if (!ok) break;
-      // O_t is final after PV_t of the item's last key tile.
+      // O_t is final after P_t(n_k - 1) V, whose commit has a barrier of its own.
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(&o_final[t], li & 1));
       if (!ok) break;
       tc_fence_after();
       const int index = item_index(li);
-      const int group = index % p.q_groups, h = (index / p.q_groups) % p.heads;
-      const int b = index / (p.q_groups * p.heads);
-      const int row = (kTiles * group + t) * kRows + row_in_tile;
+      const int pair = index % p.q_pairs, h = (index / p.q_pairs) % p.heads;
+      const int b = index / (p.q_pairs * p.heads);
+      const int row = (2 * pair + t) * kRows + row_in_tile;
       const float inv = 1.f / l;
       __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + b * p.sb + h * p.sh +
                            static_cast<int64_t>(row) * p.ss;
@@ -426,9 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // The next item's first PV_t overwrites O_t; it is issued only after
-      // this warp's next p_full arrival, which follows these loads.
+      // O_t has been read: the next item's first P V may overwrite it.
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[t]);
     }
     timed_out = !ok;
   }
@@ -444,16 +448,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---- host side ----
 
 // (batch, length, heads, 64) bf16 view with the given element strides as a
-// 4-D tensor map {d, head, position, batch}; 64 x 1 x `rows` x 1 boxes,
-// 128-byte swizzle, zero fill past the window.
+// 4-D tensor map {d, head, position, batch}; 64 x 1 x 128 x 1 boxes, 128-byte
+// swizzle, zero fill past the window.
 int make_map(CUtensorMap* map, const void* base, int batch, int heads, int length, int64_t sb,
-             int64_t sh, int64_t ss, int rows) {
+             int64_t sh, int64_t ss) {
   int rc = ASRBACK_OK;
   auto encode = tensor_map_encoder(&rc);
   if (!encode) return rc;
   cuuint64_t dims[4] = {(cuuint64_t)kDim, (cuuint64_t)heads, (cuuint64_t)length, (cuuint64_t)batch};
   cuuint64_t strides[3] = {(cuuint64_t)sh * 2, (cuuint64_t)ss * 2, (cuuint64_t)sb * 2};
-  cuuint32_t box[4] = {kDim, 1, (cuuint32_t)rows, 1};
+  cuuint32_t box[4] = {kDim, 1, kRows, 1};
   cuuint32_t elem_strides[4] = {1, 1, 1, 1};
   CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
                         strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -474,9 +478,9 @@ int encoder_attention_tc(int batch, int heads, int length, const void* q, const 
                          const void* v, void* out, int64_t sb, int64_t sh, int64_t ss, float scale,
                          int32_t* status, cudaStream_t stream) {
   CUtensorMap mq, mk, mv;
-  if (int rc = make_map(&mq, q, batch, heads, length, sb, sh, ss, kRows)) return rc;
-  if (int rc = make_map(&mk, k, batch, heads, length, sb, sh, ss, kKeys)) return rc;
-  if (int rc = make_map(&mv, v, batch, heads, length, sb, sh, ss, kKeys)) return rc;
+  if (int rc = make_map(&mq, q, batch, heads, length, sb, sh, ss)) return rc;
+  if (int rc = make_map(&mk, k, batch, heads, length, sb, sh, ss)) return rc;
+  if (int rc = make_map(&mv, v, batch, heads, length, sb, sh, ss)) return rc;
   static thread_local int prepared_device = -1;
   int device = 0;
   if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
@@ -488,9 +492,8 @@ int encoder_attention_tc(int batch, int heads, int length, const void* q, const 
       return rc;
     prepared_device = device;
   }
-  const int q_tiles = (length + kRows - 1) / kRows;
-  const int q_groups = (q_tiles + kTiles - 1) / kTiles;
-  TcParams p{out, sb, sh, ss, length, q_groups, heads, q_groups * heads * batch,
+  const int q_pairs = (length + 2 * kRows - 1) / (2 * kRows);
+  TcParams p{out, sb, sh, ss, length, q_pairs, heads, q_pairs * heads * batch,
              scale * 1.4426950408889634f, status};
   // Persistent: one CTA per SM (512 TMEM columns each), at most one per item.
   const int ctas = p.items < sm_count() ? p.items : sm_count();
