@@ -68,3 +68,24 @@ def test_every_workload_is_on_the_command_line(monkeypatch):
     monkeypatch.setattr(sys, "argv", ["bench.py"])
     args = bench.parse_args()
     assert args.workload == "whisper-decode" and args.gpus == 1 and args.warmup >= 3
+
+
+def test_serving_trace_is_seeded_and_deals_rows_evenly():
+    """The config-5 trace: Poisson arrivals at 25 requests/s per GPU, prompts of
+    13 audio positions per second of U[1, 30] s audio plus 20 text positions,
+    the same on every rank, and an equal share of requests per replica."""
+    import numpy as np
+
+    work = bench.WORKLOADS["qwen3-serve"](None)
+    for world in (1, 2, 8):
+        trace = work.trace(world, 192 * world)
+        again = work.trace(world, 192 * world)
+        assert [(r.arrival, r.length) for r in trace] == [(r.arrival, r.length) for r in again]
+        counts = np.bincount([r.replica for r in trace], minlength=world)
+        assert counts.tolist() == [192] * world
+        arrivals = np.array([r.arrival for r in trace])
+        assert (np.diff(arrivals) > 0).all()
+        rate = len(trace) / arrivals[-1]
+        assert 0.8 * 25 * world < rate < 1.2 * 25 * world
+        lengths = np.array([r.length for r in trace])
+        assert lengths.min() >= 13 + 20 and lengths.max() <= 390 + 20
