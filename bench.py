@@ -2034,7 +2034,14 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     timed.replay()  # uploads the graph; untimed
     torch.cuda.synchronize()
     if world > 1:
+        # Ranks finish their captures at different times, and a GPU left idle
+        # while its rank waits drops its clocks: after this barrier every rank
+        # keeps its GPU busy with untimed replays through the barrier that
+        # opens the timed region (the collective waits for them), so the timed
+        # replay starts on a GPU that is already running.
         dist.barrier()
+        for _ in range(3):
+            timed.replay()
 
     uuid = getattr(torch.cuda.get_device_properties(device), "uuid", None)
     uuid = str(uuid) if uuid else None
@@ -2042,9 +2049,9 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     # ---- timed region: exactly K steps, one graph replay, inputs in HBM ----
     start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(uuid) as clocks:
-        torch.cuda.synchronize()
         if world > 1:
-            dist.barrier()
+            dist.barrier()  # its collective runs after this rank's queued replays
+        torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed")
         start_ev.record(stream)
         timed.replay()
