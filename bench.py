@@ -577,23 +577,29 @@ class WhisperEncoder(Workload):
         return self.flops_per_layer() * self.layers * count
 
     def torch_reference_step(self, torch):
-        """torch SDPA on the same tensors (the reference's encoder call, default
-        backend priority, eager as the reference runs it), for context."""
-        import torch.nn.functional as F
-
-        def run(_t):
-            for layer in range(self.layers):
-                F.scaled_dot_product_attention(*self.views(self.qkv[layer]))
-        return run
-
-    def torch_cudnn_step(self, torch):
-        """The same with torch's cuDNN attention backend forced (the fastest
-        torch kernel for this shape on B200)."""
+        """The reference's encoder call on the same tensors, eager as the
+        reference runs it: torch SDPA, which on B200 with torch 2.11 dispatches
+        this shape to cuDNN's sm100 kernel (in a fresh process and after the
+        decoder step's cuDNN-first priority context alike; probed with the
+        torch profiler). cuDNN is named here so that the figure does not depend
+        on what ran before in the bench's process."""
         import torch.nn.functional as F
         from torch.nn.attention import SDPBackend, sdpa_kernel
 
         def run(_t):
             with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                for layer in range(self.layers):
+                    F.scaled_dot_product_attention(*self.views(self.qkv[layer]))
+        return run
+
+    def torch_flash_step(self, torch):
+        """The same with torch's flash-attention backend forced (SDPA's first
+        choice by its priority list; slower than cuDNN for this shape)."""
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        def run(_t):
+            with sdpa_kernel([SDPBackend.FLASH_ATTENTION]):
                 for layer in range(self.layers):
                     F.scaled_dot_product_attention(*self.views(self.qkv[layer]))
         return run
@@ -2015,6 +2021,117 @@ def e2e_pipeline(torch, dist, work, world: int, first: int, steps: int) -> dict:
             "rank_ms": ranks}
 
 
+def reference_whisper_module():
+    """The reference's ``asrback.models.whisper`` from ``$ASRBACK_REFERENCE`` (a
+    checkout) or ``baseline/_ref`` (where a copy of its package is laid down),
+    or None. Its audio front end ``asrfront`` is not installed and nothing
+    timed here calls it, so a module with the constants read at import stands
+    in for it."""
+    import types
+
+    roots = [Path(os.environ["ASRBACK_REFERENCE"]) if os.environ.get("ASRBACK_REFERENCE")
+             else None, ROOT / "baseline" / "_ref"]
+    found = None
+    for root in roots:
+        if root is None:
+            continue
+        for candidate in (root / "src", root):
+            if (candidate / "asrback" / "__init__.py").is_file():
+                found = candidate
+                break
+        if found:
+            break
+    if found is None:
+        return None
+    if "asrfront" not in sys.modules:
+        stub = types.ModuleType("asrfront")
+        constants = dict(SAMPLE_RATE=16000, N_SAMPLES=480000, HOP_LENGTH=160, MAX_SAMPLES=480000,
+                         N_MELS=128)
+        for name in ("whisper", "qwen3_asr", "sensevoice", "gemma4"):
+            setattr(stub, name, types.SimpleNamespace(**constants))
+        sys.modules["asrfront"] = stub
+    if str(found) not in sys.path:
+        sys.path.insert(0, str(found))
+    from asrback.models import whisper
+
+    return whisper
+
+
+def measure_admission(torch, dist, device, world: int, batches: int = 4) -> dict:
+    """Window admission at the caller's boundary, through the reference's own
+    modules: log-mel windows copied in from pinned host memory, the encoder
+    (``WhisperEncoder.forward``, ``whisper.py:140-153``: convolution stem, 32
+    layers, final norm) and ``set_encoder_output`` (``:313-319``) into the
+    cross-attention cache of a 4-layer decoder, one cache row read back. Timed
+    with ``asrback_b200.plugin`` installed (the encoder attention and the
+    cross K/V projection on this package's kernels, the linears on cuBLAS),
+    installed with ``encoder=False`` (the encoder attention left to the
+    reference's SDPA, the cross K/V projection on this package's kernel) and
+    without it (the reference's torch path: default SDPA, ``F.linear`` and the
+    cache copy), eager as the reference runs ``_encode``; large-v3-turbo
+    widths, 32 windows of N(0, 1) log-mel, seeded random weights."""
+    whisper = reference_whisper_module()
+    if whisper is None:
+        return {"unavailable": "the reference's package is not present ($ASRBACK_REFERENCE or "
+                               "baseline/_ref)"}
+    from asrback_b200 import plugin
+
+    config = dict(d_model=1280, encoder_attention_heads=20, decoder_attention_heads=20,
+                  encoder_layers=32, decoder_layers=4, encoder_ffn_dim=5120, decoder_ffn_dim=5120,
+                  num_mel_bins=128, max_source_positions=1500, max_target_positions=448,
+                  vocab_size=51866)
+    torch.manual_seed(2)
+    with torch.device(device):  # nn's default initialisation, drawn on the GPU
+        model = whisper.WhisperForConditionalGeneration(config)
+    model = model.eval().to(torch.bfloat16)
+    windows = 32
+    gen = torch.Generator().manual_seed(2)
+    host_mel = torch.randn((windows, 128, 3000), generator=gen).to(torch.bfloat16).pin_memory()
+    cache = model.allocate_cache(windows)
+    host_row = torch.empty(cache.cross_keys[3, 0, 0].shape, dtype=torch.bfloat16, pin_memory=True)
+    stream = torch.cuda.current_stream()
+
+    def admit():
+        mel = host_mel.to(device, non_blocking=True)
+        model.set_encoder_output(cache, model.model.encoder(mel))
+        host_row.copy_(cache.cross_keys[3, windows - 1, 19], non_blocking=True)
+
+    out = {}
+    with torch.inference_mode():
+        for label, patched in (("value", "all"), ("cross_only", "cross"), ("torch", None)):
+            if patched:
+                plugin.install(whisper, None, encoder=patched == "all")
+            try:
+                for _ in range(2):
+                    admit()
+                torch.cuda.synchronize()
+                if world > 1:
+                    dist.barrier()
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                for _ in range(batches):
+                    admit()
+                end.record(stream)
+                torch.cuda.synchronize()
+            finally:
+                if patched:
+                    plugin.uninstall()
+            ranks = rank_times(torch, dist, world, start.elapsed_time(end))
+            out[label] = windows * batches * world / (max(ranks) / 1e3)
+            out[f"{label}_ms_per_batch"] = max(ranks) / batches
+    del model, cache
+    torch.cuda.empty_cache()
+    return {"value": out["value"], "unit": "windows/s", "ms_per_batch": out["value_ms_per_batch"],
+            "cross_only": out["cross_only"],
+            "cross_only_ms_per_batch": out["cross_only_ms_per_batch"],
+            "torch": out["torch"], "torch_ms_per_batch": out["torch_ms_per_batch"],
+            "what": "32 windows of host log-mel through the reference's encoder and "
+                    "set_encoder_output (large-v3-turbo widths) into the cross cache, eager; "
+                    "value with the plugin installed, cross_only with install(encoder=False), "
+                    "torch without"}
+
+
 def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, warmup: int,
             cpu: bool, sustain: bool) -> dict:
     """Runs one workload: the timed graph of K steps, the sustained figure,
@@ -2119,9 +2236,9 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     torch.cuda.synchronize()
     ref_ms = r_start.elapsed_time(r_end) / steps
     ref_graph = None
-    cudnn = None
-    if hasattr(work, "torch_cudnn_step"):
-        fn = work.torch_cudnn_step(torch)
+    flash = None
+    if hasattr(work, "torch_flash_step"):
+        fn = work.torch_flash_step(torch)
         for t in range(3):
             fn(t)
         torch.cuda.synchronize()
@@ -2131,8 +2248,8 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
         r_end.record(stream)
         torch.cuda.synchronize()
         c_ms = r_start.elapsed_time(r_end) / steps
-        cudnn = {"ms_per_step": c_ms, "value": work.units_per_step() / (c_ms * 1e-3),
-                 "unit": work.unit, "what": "torch SDPA with the cuDNN backend forced, eager"}
+        flash = {"ms_per_step": c_ms, "value": work.units_per_step() / (c_ms * 1e-3),
+                 "unit": work.unit, "what": "torch SDPA with the flash backend forced, eager"}
 
     dominant = work.kernels(warmup)[0]
     dom = kernel[dominant[0]]
@@ -2165,11 +2282,13 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
             "ms_per_step": ref_ms, "value": work.units_per_step() / (ref_ms * 1e-3),
             "unit": work.unit,
             "what": "the reference's attention computation in torch on this GPU (same tensors)"},
-        "torch_gpu_cudnn": cudnn,
+        "torch_gpu_flash": flash,
         "gpu_launches": work.launches_per_step() * steps,
         "clocks": clocks.summary(),
         "device_status": status,
     }
+    if work.name == "whisper-encoder":
+        result["admission"] = measure_admission(torch, dist, device, world)
     max_over_ranks(0.0)  # every rank reaches the CPU leg together
     if cpu and rank == 0 and world == 1:
         result["cpu_baseline"] = work.cpu_rate(args.cpu_seconds, os.cpu_count() or 1)
@@ -2188,10 +2307,14 @@ def summary(name: str, line: dict) -> dict:
     if line.get("e2e"):
         out["e2e"] = r(line["e2e"]["value"])
     out["torch_gpu"] = r(line["torch_gpu_reference"]["value"])
-    if line.get("torch_gpu_cudnn"):
-        out["cudnn"] = r(line["torch_gpu_cudnn"]["value"])
+    if line.get("torch_gpu_flash"):
+        out["flash"] = r(line["torch_gpu_flash"]["value"])
     if line.get("cpu_baseline"):
         out["cpu"] = r(line["cpu_baseline"]["value"])
+    if line.get("admission") and "value" in line["admission"]:
+        out["admission"] = r(line["admission"]["value"])
+        out["admission_torch"] = r(line["admission"]["torch"])
+        out["admission_cross_only"] = r(line["admission"]["cross_only"])
     if line.get("paced"):
         out["paced"] = r(line["paced"]["value"])
         out["p99_s"] = r(line["paced"]["latency_s_p99"], 3)
@@ -2235,8 +2358,8 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
                         max(3, min(args.warmup, 5)), cpu=cpu, sustain=False)
             extras[name] = {k: r.get(k) for k in (
                 "metric", "value", "unit", "ms_per_step", "e2e", "roofline", "step_rate",
-                "rank_ms", "torch_gpu_reference", "torch_gpu_cudnn", "cpu_baseline", "clocks",
-                "device_status", "config")}
+                "rank_ms", "torch_gpu_reference", "torch_gpu_flash", "cpu_baseline", "clocks",
+                "device_status", "config", "admission")}
             short[name] = summary(name, r)
         del work
         torch.cuda.empty_cache()

@@ -386,3 +386,19 @@ def test_uninstall_restores_reference(reference):
              whisper.Transcriber._step, qwen3.Qwen3ASRTranscriber._step,
              whisper.WhisperForConditionalGeneration.set_encoder_output)
     assert after == before
+
+
+def test_install_without_encoder_keeps_reference_encoder_attention(reference):
+    whisper, qwen3 = reference
+    encoder_forward = whisper.MultiHeadAttention.forward
+    decoder_forward = whisper.DecoderLayer.forward
+    set_output = whisper.WhisperForConditionalGeneration.set_encoder_output
+    plugin.install(whisper, qwen3, encoder=False)
+    try:
+        assert whisper.MultiHeadAttention.forward is encoder_forward
+        assert whisper.DecoderLayer.forward is not decoder_forward
+        assert whisper.WhisperForConditionalGeneration.set_encoder_output is not set_output
+    finally:
+        plugin.uninstall()
+    assert whisper.DecoderLayer.forward is decoder_forward
+    assert whisper.WhisperForConditionalGeneration.set_encoder_output is set_output
