@@ -52,6 +52,15 @@ constexpr int kStages = 4;
 constexpr int kTileBytes = kRows * kDim * 2;  // 16 KB, one Q, K or V tile
 // warp 0 TMA, warp 1 MMA (and TMEM owner), warps 2-3 idle, warps 4-11 softmax.
 constexpr int kThreads = 12 * 32;
+// Registers per thread: the launch gives every thread 168 (384 x 168 = 64512);
+// the TMA/MMA warpgroup keeps 56 and the two softmax warpgroups take 224
+// (128 x 56 + 256 x 224 = 64512), enough for a key tile's 128 scores, its 64
+// packed P words and the row state without spilling.
+constexpr int kLaunchRegs = 168;
+constexpr int kControlRegs = 56;
+constexpr int kSoftmaxRegs = 224;
+static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch's register pool");
 constexpr int kTmemCols = 512;
 // TMEM column of S, O and P for query tile t.
 // Three S buffers of 128 columns rotate over the two query tiles: the k-th
@@ -179,131 +188,145 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_launch_dependents();
   bool timed_out = false;
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      prefetch_tensormap(&map_q);
-      prefetch_tensormap(&map_k);
-      prefetch_tensormap(&map_v);
-      int g = 0;  // key tiles loaded (= J)
-      for (int li = 0; li < n_items && !timed_out; ++li) {
-        const int index = item_index(li);
-        const int pair = index % p.q_pairs, h = (index / p.q_pairs) % p.heads;
-        const int b = index / (p.q_pairs * p.heads);
-        const int qb = li & 1;
-        if (li >= 2 && !mbar_wait_bounded(&q_empty[qb], ((li >> 1) - 1) & 1)) {
-          timed_out = true;
-          break;
-        }
-        uint8_t* qdst = smem + kOffQ + qb * 2 * kTileBytes;
-        mbar_arrive_expect_tx(&q_full[qb], 2 * kTileBytes);
-        tma_load_4d(qdst, &map_q, 0, h, (2 * pair) * kRows, b, &q_full[qb]);
-        tma_load_4d(qdst + kTileBytes, &map_q, 0, h, (2 * pair + 1) * kRows, b, &q_full[qb]);
-        for (int j = 0; j < n_k; ++j, ++g) {
-          const int s = g % kStages;
-          if (g >= kStages && !mbar_wait_bounded(&kv_empty[s], ((g / kStages) - 1) & 1)) {
+  // Each warpgroup leaves through its own branch (status, fences, one
+  // CTA-wide named barrier, the TMEM release): a register budget is fixed per
+  // branch, so the branches never rejoin.
+  if (warp < 4) {
+    reg_release<kControlRegs>();
+    if (warp == 0) {
+      // ---------------- TMA producer ----------------
+      if (lane == 0) {
+        prefetch_tensormap(&map_q);
+        prefetch_tensormap(&map_k);
+        prefetch_tensormap(&map_v);
+        int g = 0;  // key tiles loaded (= J)
+        for (int li = 0; li < n_items && !timed_out; ++li) {
+          const int index = item_index(li);
+          const int pair = index % p.q_pairs, h = (index / p.q_pairs) % p.heads;
+          const int b = index / (p.q_pairs * p.heads);
+          const int qb = li & 1;
+          if (li >= 2 && !mbar_wait_bounded(&q_empty[qb], ((li >> 1) - 1) & 1)) {
             timed_out = true;
             break;
           }
-          mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-          tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, b, &k_full[s]);
-          mbar_arrive_expect_tx(&v_full[s], kTileBytes);
-          tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, b, &v_full[s]);
+          uint8_t* qdst = smem + kOffQ + qb * 2 * kTileBytes;
+          mbar_arrive_expect_tx(&q_full[qb], 2 * kTileBytes);
+          tma_load_4d(qdst, &map_q, 0, h, (2 * pair) * kRows, b, &q_full[qb]);
+          tma_load_4d(qdst + kTileBytes, &map_q, 0, h, (2 * pair + 1) * kRows, b, &q_full[qb]);
+          for (int j = 0; j < n_k; ++j, ++g) {
+            const int s = g % kStages;
+            if (g >= kStages && !mbar_wait_bounded(&kv_empty[s], ((g / kStages) - 1) & 1)) {
+              timed_out = true;
+              break;
+            }
+            mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+            tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, b, &k_full[s]);
+            mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+            tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, b, &v_full[s]);
+          }
         }
       }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0 && total > 0) {
-      constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
-      constexpr uint32_t kIdescPV = idesc_bf16(kRows, kDim, true);
-      // Descriptors are built once; a step moves the start-address field
-      // (address >> 4): 32 bytes along K inside a swizzled row (Q, K), two
-      // 8-row swizzle atoms of V (2048 bytes), one tile (kTileBytes). This lane
-      // shares its sub-partition's issue slots with softmax warps, so its
-      // per-MMA work is an add and the MMA.
-      const uint64_t q_desc = sw128_desc(smem_addr(smem + kOffQ), 16, 1024);
-      const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
-      const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
-      constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4, kTile = kTileBytes >> 4;
-      bool ok = true;
-      // Position of key tile X in the sequence: item li (Q buffer li & 1), tile
-      // j within it, ring slot s, ring lap, S buffer of tile 0. Kept as running
-      // counters (one per tile stream below) so the lane divides nothing.
-      struct Cursor {
-        int X, li, j, s, lap, buf0;
-        __device__ void next(int n_k) {
-          ++X;
-          if (++j == n_k) {
-            j = 0;
-            ++li;
+    } else if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      if (lane == 0 && total > 0) {
+        constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
+        constexpr uint32_t kIdescPV = idesc_bf16(kRows, kDim, true);
+        // Descriptors are built once; a step moves the start-address field
+        // (address >> 4): 32 bytes along K inside a swizzled row (Q, K), two
+        // 8-row swizzle atoms of V (2048 bytes), one tile (kTileBytes). This lane
+        // shares its sub-partition's issue slots with softmax warps, so its
+        // per-MMA work is an add and the MMA.
+        const uint64_t q_desc = sw128_desc(smem_addr(smem + kOffQ), 16, 1024);
+        const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
+        const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
+        constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4, kTile = kTileBytes >> 4;
+        bool ok = true;
+        // Position of key tile X in the sequence: item li (Q buffer li & 1), tile
+        // j within it, ring slot s, ring lap, S buffer of tile 0. Kept as running
+        // counters (one per tile stream below) so the lane divides nothing.
+        struct Cursor {
+          int X, li, j, s, lap, buf0;
+          __device__ void next(int n_k) {
+            ++X;
+            if (++j == n_k) {
+              j = 0;
+              ++li;
+            }
+            if (++s == kStages) {
+              s = 0;
+              ++lap;
+            }
+            buf0 = buf0 == 0 ? 2 : buf0 - 1;  // (2X) % 3 steps by 2 mod 3
           }
-          if (++s == kStages) {
-            s = 0;
-            ++lap;
-          }
-          buf0 = buf0 == 0 ? 2 : buf0 - 1;  // (2X) % 3 steps by 2 mod 3
-        }
-      };
-      // S_t(X): query tile t of item li against key tile X. The item's first S
-      // (t = 0, j == 0) waits for its Q; after its last S (t = 1, j == n_k - 1)
-      // the Q buffer is free.
-      auto issue_qk = [&](int t, const Cursor& c) {
-        const int qb = c.li & 1;
-        if (t == 0 && c.j == 0) ok = ok && mbar_wait_bounded(&q_full[qb], (c.li >> 1) & 1);
-        ok = ok && mbar_wait_bounded(&k_full[c.s], c.lap & 1);
-        if (!ok) return;
-        tc_fence_after();
-        const int s = c.s;
-        const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
-        // K = 64 in four steps of 16 elements.
-#pragma unroll
-        for (int k = 0; k < kDim / 16; ++k)
-          mma_ss(tmem + col_buf(buf), q_desc + (2 * qb + t) * kTile + k * kStepK,
-                 k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
-        mma_commit(&s_full[buf]);
-        if (t == 1 && c.j == n_k - 1) mma_commit(&q_empty[qb]);
-      };
-      // O_t (+)= P_t(J) V(J); an item's first one waits until the previous
-      // item's epilogue has read O_t; the item's last one commits o_final.
-      auto issue_pv = [&](int t, const Cursor& c) {
-        const int J = c.X, li = c.li, j = c.j, s = c.s;
-        if (t == 0) ok = ok && mbar_wait_bounded(&v_full[s], c.lap & 1);
-        ok = ok && mbar_wait_bounded(&p_full[2 * t + (J & 1)], (J >> 1) & 1);
-        if (j == 0 && li > 0) ok = ok && mbar_wait_bounded(&o_free[t], (li - 1) & 1);
-        if (!ok) return;
-        tc_fence_after();
-        const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
-        // K = 128 keys in eight steps of 16: P advances 8 TMEM columns (bf16
-        // pairs), V two 8-row swizzle atoms.
-#pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k)
-          mma_ts(tmem + col_o(t), tmem + col_buf(buf) + k * 8, v_desc + s * kTile + k * kStepV,
-                 kIdescPV, (j > 0 || k > 0));
-        mma_commit(j + 1 < n_k ? &o_full[t] : &o_final[t]);
-      };
-      // Three cursors: the P V tile J, and the S tiles J + 1 and J + 2.
-      Cursor c0{0, 0, 0, 0, 0, 0};
-      Cursor c1 = c0, c2 = c0;
-      issue_qk(0, c0);
-      issue_qk(1, c0);
-      c1.next(n_k);
-      c2.next(n_k);
-      c2.next(n_k);
-      if (total > 1) issue_qk(0, c1);
-      for (int J = 0; J < total && ok; ++J) {
-        issue_pv(0, c0);
-        if (ok && J + 1 < total) issue_qk(1, c1);
-        if (ok) issue_pv(1, c0);
-        if (ok && J + 2 < total) issue_qk(0, c2);
-        if (ok && J + kStages < total) mma_commit(&kv_empty[c0.s]);
-        c0.next(n_k);
+        };
+        // S_t(X): query tile t of item li against key tile X. The item's first S
+        // (t = 0, j == 0) waits for its Q; after its last S (t = 1, j == n_k - 1)
+        // the Q buffer is free.
+        auto issue_qk = [&](int t, const Cursor& c) {
+          const int qb = c.li & 1;
+          if (t == 0 && c.j == 0) ok = ok && mbar_wait_bounded(&q_full[qb], (c.li >> 1) & 1);
+          ok = ok && mbar_wait_bounded(&k_full[c.s], c.lap & 1);
+          if (!ok) return;
+          tc_fence_after();
+          const int s = c.s;
+          const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
+          // K = 64 in four steps of 16 elements.
+  #pragma unroll
+          for (int k = 0; k < kDim / 16; ++k)
+            mma_ss(tmem + col_buf(buf), q_desc + (2 * qb + t) * kTile + k * kStepK,
+                   k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
+          mma_commit(&s_full[buf]);
+          if (t == 1 && c.j == n_k - 1) mma_commit(&q_empty[qb]);
+        };
+        // O_t (+)= P_t(J) V(J); an item's first one waits until the previous
+        // item's epilogue has read O_t; the item's last one commits o_final.
+        auto issue_pv = [&](int t, const Cursor& c) {
+          const int J = c.X, li = c.li, j = c.j, s = c.s;
+          if (t == 0) ok = ok && mbar_wait_bounded(&v_full[s], c.lap & 1);
+          ok = ok && mbar_wait_bounded(&p_full[2 * t + (J & 1)], (J >> 1) & 1);
+          if (j == 0 && li > 0) ok = ok && mbar_wait_bounded(&o_free[t], (li - 1) & 1);
+          if (!ok) return;
+          tc_fence_after();
+          const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
+          // K = 128 keys in eight steps of 16: P advances 8 TMEM columns (bf16
+          // pairs), V two 8-row swizzle atoms.
+  #pragma unroll
+          for (int k = 0; k < kKeys / 16; ++k)
+            mma_ts(tmem + col_o(t), tmem + col_buf(buf) + k * 8, v_desc + s * kTile + k * kStepV,
+                   kIdescPV, (j > 0 || k > 0));
+          mma_commit(j + 1 < n_k ? &o_full[t] : &o_final[t]);
+        };
+        // Three cursors: the P V tile J, and the S tiles J + 1 and J + 2.
+        Cursor c0{0, 0, 0, 0, 0, 0};
+        Cursor c1 = c0, c2 = c0;
+        issue_qk(0, c0);
+        issue_qk(1, c0);
         c1.next(n_k);
         c2.next(n_k);
+        c2.next(n_k);
+        if (total > 1) issue_qk(0, c1);
+        for (int J = 0; J < total && ok; ++J) {
+          issue_pv(0, c0);
+          if (ok && J + 1 < total) issue_qk(1, c1);
+          if (ok) issue_pv(1, c0);
+          if (ok && J + 2 < total) issue_qk(0, c2);
+          if (ok && J + kStages < total) mma_commit(&kv_empty[c0.s]);
+          c0.next(n_k);
+          c1.next(n_k);
+          c2.next(n_k);
+        }
+        timed_out = !ok;
       }
-      timed_out = !ok;
     }
-  } else if (warp >= 4) {
+    if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+    tc_fence_before();
+    named_sync(1, kThreads);
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, kTmemCols);
+    }
+  } else {
+    reg_acquire<kSoftmaxRegs>();
     // ---------------- softmax and epilogue (one query row per thread) ----------------
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
@@ -435,13 +458,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&o_free[t]);
     }
     timed_out = !ok;
-  }
-  if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+    tc_fence_before();
+    named_sync(1, kThreads);
   }
 }
 

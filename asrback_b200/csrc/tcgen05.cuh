@@ -71,6 +71,22 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Per-thread register budget of the calling warpgroup (every warp of the
+// warpgroup executes the same one). `reg_release` returns registers to the
+// CTA's pool; `reg_acquire` waits until the pool holds enough, so the
+// acquiring warpgroups' total must fit in what the CTA was launched with
+// (threads x registers per thread at launch) less what the others keep.
+template <int kRegs>
+__device__ __forceinline__ void reg_release() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "setmaxnreg range");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void reg_acquire() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "setmaxnreg range");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T (both K-major or as the descriptors say).
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accumulate) {
