@@ -14,7 +14,8 @@
 //               across items (4-D tensor maps over the projections' (batch,
 //               length, heads, 64) layout, 128-byte swizzle; rows past the
 //               window read as zeros);
-//   warp 1      allocates the 512 TMEM columns; one lane issues every MMA:
+//   warp 1      allocates the 512 TMEM columns and issues every MMA (the
+//               loop runs warp-wide, an elected lane issues):
 //               S = Q_t K^T (SS: both operands from shared memory) and
 //               O_t += P V (TS: P from TMEM, V from shared memory);
 //   warps 4-7   softmax of query tile 0 (thread = TMEM lane = query row);
@@ -76,10 +77,10 @@ constexpr int kOffQ = 0;  // two Q buffers of two tiles
 constexpr int kOffK = 4 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffBar = kOffV + kStages * kTileBytes;
-// barriers: q_full[2], q_empty[2] (per Q buffer), k_full[S], v_full[S],
-// kv_empty[S], s_full[3] (one per S buffer), p_full[2][2] (per tile,
-// alternating), o_full[2], o_final[2], o_free[2]
-constexpr int kNumBars = 2 + 2 + 3 * kStages + 3 + 4 + 2 + 2 + 2;
+// barriers: q_full[2], q_empty[2] (per Q buffer), kv_full[S], kv_empty[S],
+// s_full[3] (one per S buffer), p_full[2][2] (per tile, alternating),
+// o_full[2], o_final[2], o_free[2]
+constexpr int kNumBars = 2 + 2 + 2 * kStages + 3 + 4 + 2 + 2 + 2;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
 
@@ -140,9 +141,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars;  // [Q buffer]
   uint64_t* q_empty = q_full + 2;
-  uint64_t* k_full = q_empty + 2;
-  uint64_t* v_full = k_full + kStages;
-  uint64_t* kv_empty = v_full + kStages;
+  uint64_t* kv_full = q_empty + 2;
+  uint64_t* kv_empty = kv_full + kStages;
   uint64_t* s_full = kv_empty + kStages;  // [buffer]
   uint64_t* p_full = s_full + 3;          // [2 * t + (J & 1)]
   uint64_t* o_full = p_full + 4;
@@ -166,8 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&q_empty[q], 1);
     }
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
     for (int b = 0; b < 3; ++b) mbar_init(&s_full[b], 1);
@@ -193,49 +192,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   // branch, so the branches never rejoin.
   if (warp < 4) {
     reg_release<kControlRegs>();
+    // Both control warps run their loops warp-wide (waits by every lane, so
+    // the loop state stays warp-uniform) and issue from one elected lane.
+    auto wait_warp = [](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
+    };
     if (warp == 0) {
       // ---------------- TMA producer ----------------
-      if (lane == 0) {
+      if (elect_one()) {
         prefetch_tensormap(&map_q);
         prefetch_tensormap(&map_k);
         prefetch_tensormap(&map_v);
-        int g = 0;  // key tiles loaded (= J)
-        for (int li = 0; li < n_items && !timed_out; ++li) {
-          const int index = item_index(li);
-          const int pair = index % p.q_pairs, h = (index / p.q_pairs) % p.heads;
-          const int b = index / (p.q_pairs * p.heads);
-          const int qb = li & 1;
-          if (li >= 2 && !mbar_wait_bounded(&q_empty[qb], ((li >> 1) - 1) & 1)) {
-            timed_out = true;
-            break;
-          }
+      }
+      __syncwarp();
+      bool ok = true;
+      int g = 0;  // key tiles loaded (= J)
+      for (int li = 0; li < n_items && ok; ++li) {
+        const int index = item_index(li);
+        const int pair = index % p.q_pairs, h = (index / p.q_pairs) % p.heads;
+        const int b = index / (p.q_pairs * p.heads);
+        const int qb = li & 1;
+        if (li >= 2) ok = wait_warp(&q_empty[qb], ((li >> 1) - 1) & 1);
+        if (!ok) break;
+        if (elect_one()) {
           uint8_t* qdst = smem + kOffQ + qb * 2 * kTileBytes;
           mbar_arrive_expect_tx(&q_full[qb], 2 * kTileBytes);
           tma_load_4d(qdst, &map_q, 0, h, (2 * pair) * kRows, b, &q_full[qb]);
           tma_load_4d(qdst + kTileBytes, &map_q, 0, h, (2 * pair + 1) * kRows, b, &q_full[qb]);
-          for (int j = 0; j < n_k; ++j, ++g) {
-            const int s = g % kStages;
-            if (g >= kStages && !mbar_wait_bounded(&kv_empty[s], ((g / kStages) - 1) & 1)) {
-              timed_out = true;
-              break;
-            }
-            mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-            tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, b, &k_full[s]);
-            mbar_arrive_expect_tx(&v_full[s], kTileBytes);
-            tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, b, &v_full[s]);
+        }
+        __syncwarp();
+        for (int j = 0; j < n_k; ++j, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages) ok = wait_warp(&kv_empty[s], ((g / kStages) - 1) & 1);
+          if (!ok) break;
+          if (elect_one()) {
+            // K and V of a key tile complete one barrier: the first MMA that
+            // reads the tile (its S of query tile 0) waits once for both.
+            mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+            tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, b, &kv_full[s]);
+            tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, b, &kv_full[s]);
           }
+          __syncwarp();
         }
       }
+      timed_out = !ok;
     } else if (warp == 1) {
       // ---------------- MMA issuer ----------------
-      if (lane == 0 && total > 0) {
+      if (total > 0) {
         constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
         constexpr uint32_t kIdescPV = idesc_bf16(kRows, kDim, true);
         // Descriptors are built once; a step moves the start-address field
         // (address >> 4): 32 bytes along K inside a swizzled row (Q, K), two
-        // 8-row swizzle atoms of V (2048 bytes), one tile (kTileBytes). This lane
-        // shares its sub-partition's issue slots with softmax warps, so its
-        // per-MMA work is an add and the MMA.
+        // 8-row swizzle atoms of V (2048 bytes), one tile (kTileBytes). The
+        // tensor core takes few MMAs ahead, so the instructions between two
+        // MMAs are kept to adds and the waits that are needed.
         const uint64_t q_desc = sw128_desc(smem_addr(smem + kOffQ), 16, 1024);
         const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
         const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
@@ -243,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         // Position of key tile X in the sequence: item li (Q buffer li & 1), tile
         // j within it, ring slot s, ring lap, S buffer of tile 0. Kept as running
-        // counters (one per tile stream below) so the lane divides nothing.
+        // counters (one per tile stream below) so the loop divides nothing.
         struct Cursor {
           int X, li, j, s, lap, buf0;
           __device__ void next(int n_k) {
@@ -259,42 +269,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             buf0 = buf0 == 0 ? 2 : buf0 - 1;  // (2X) % 3 steps by 2 mod 3
           }
         };
-        // S_t(X): query tile t of item li against key tile X. The item's first S
-        // (t = 0, j == 0) waits for its Q; after its last S (t = 1, j == n_k - 1)
-        // the Q buffer is free.
+        // S_t(X): query tile t of item li against key tile X. In issue order
+        // S_0(X) comes first of the MMAs that read key tile X (then S_1(X),
+        // P_0 V, P_1 V), so it alone waits for the tile; an item's first S also
+        // waits for its Q. After the item's last S (t = 1, j == n_k - 1) the Q
+        // buffer is free.
         auto issue_qk = [&](int t, const Cursor& c) {
           const int qb = c.li & 1;
-          if (t == 0 && c.j == 0) ok = ok && mbar_wait_bounded(&q_full[qb], (c.li >> 1) & 1);
-          ok = ok && mbar_wait_bounded(&k_full[c.s], c.lap & 1);
+          if (t == 0) {
+            if (c.j == 0) ok = ok && wait_warp(&q_full[qb], (c.li >> 1) & 1);
+            ok = ok && wait_warp(&kv_full[c.s], c.lap & 1);
+          }
           if (!ok) return;
           tc_fence_after();
           const int s = c.s;
           const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
-          // K = 64 in four steps of 16 elements.
-  #pragma unroll
-          for (int k = 0; k < kDim / 16; ++k)
-            mma_ss(tmem + col_buf(buf), q_desc + (2 * qb + t) * kTile + k * kStepK,
-                   k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
-          mma_commit(&s_full[buf]);
-          if (t == 1 && c.j == n_k - 1) mma_commit(&q_empty[qb]);
+          if (elect_one()) {
+            // K = 64 in four steps of 16 elements.
+#pragma unroll
+            for (int k = 0; k < kDim / 16; ++k)
+              mma_ss(tmem + col_buf(buf), q_desc + (2 * qb + t) * kTile + k * kStepK,
+                     k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
+            mma_commit(&s_full[buf]);
+            if (t == 1 && c.j == n_k - 1) mma_commit(&q_empty[qb]);
+          }
+          __syncwarp();
         };
         // O_t (+)= P_t(J) V(J); an item's first one waits until the previous
         // item's epilogue has read O_t; the item's last one commits o_final.
         auto issue_pv = [&](int t, const Cursor& c) {
           const int J = c.X, li = c.li, j = c.j, s = c.s;
-          if (t == 0) ok = ok && mbar_wait_bounded(&v_full[s], c.lap & 1);
-          ok = ok && mbar_wait_bounded(&p_full[2 * t + (J & 1)], (J >> 1) & 1);
-          if (j == 0 && li > 0) ok = ok && mbar_wait_bounded(&o_free[t], (li - 1) & 1);
+          ok = ok && wait_warp(&p_full[2 * t + (J & 1)], (J >> 1) & 1);
+          if (j == 0 && li > 0) ok = ok && wait_warp(&o_free[t], (li - 1) & 1);
           if (!ok) return;
           tc_fence_after();
           const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
-          // K = 128 keys in eight steps of 16: P advances 8 TMEM columns (bf16
-          // pairs), V two 8-row swizzle atoms.
-  #pragma unroll
-          for (int k = 0; k < kKeys / 16; ++k)
-            mma_ts(tmem + col_o(t), tmem + col_buf(buf) + k * 8, v_desc + s * kTile + k * kStepV,
-                   kIdescPV, (j > 0 || k > 0));
-          mma_commit(j + 1 < n_k ? &o_full[t] : &o_final[t]);
+          if (elect_one()) {
+            // K = 128 keys in eight steps of 16: P advances 8 TMEM columns
+            // (bf16 pairs), V two 8-row swizzle atoms.
+#pragma unroll
+            for (int k = 0; k < kKeys / 16; ++k)
+              mma_ts(tmem + col_o(t), tmem + col_buf(buf) + k * 8, v_desc + s * kTile + k * kStepV,
+                     kIdescPV, (j > 0 || k > 0));
+            mma_commit(j + 1 < n_k ? &o_full[t] : &o_final[t]);
+          }
+          __syncwarp();
         };
         // Three cursors: the P V tile J, and the S tiles J + 1 and J + 2.
         Cursor c0{0, 0, 0, 0, 0, 0};
@@ -310,7 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ok && J + 1 < total) issue_qk(1, c1);
           if (ok) issue_pv(1, c0);
           if (ok && J + 2 < total) issue_qk(0, c2);
-          if (ok && J + kStages < total) mma_commit(&kv_empty[c0.s]);
+          if (ok && J + kStages < total) {
+            if (elect_one()) mma_commit(&kv_empty[c0.s]);
+            __syncwarp();
+          }
           c0.next(n_k);
           c1.next(n_k);
           c2.next(n_k);
@@ -318,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         timed_out = !ok;
       }
     }
-    if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+    if (timed_out && p.status && lane == 0) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
     tc_fence_before();
     named_sync(1, kThreads);
     if (warp == 1) {

@@ -71,6 +71,24 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// True in one lane of the (converged, full) warp. A role that issues
+// tcgen05.mma runs warp-wide and issues from the elected lane: the tensor
+// core's issue queue is shallow, and an issue loop run by the whole warp keeps
+// its descriptors and control in uniform registers (about twice the MMA issue
+// rate of the same loop run by one divergent lane).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n"
+      ".reg .b32 r;\n"
+      ".reg .pred p;\n"
+      "elect.sync r|p, 0xffffffff;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Per-thread register budget of the calling warpgroup (every warp of the
 // warpgroup executes the same one). `reg_release` returns registers to the
 // CTA's pool; `reg_acquire` waits until the pool holds enough, so the
