@@ -123,10 +123,13 @@ __device__ __forceinline__ void exp2_pair_fma(float x0, float x1, float& e0, flo
   e1 = __int_as_float(__float_as_int(q1) + (__float_as_int(y1) << 23));
 }
 
-// One pair in kPolyEvery takes the FMA-pipe exp2 (0: none). Sweeps on B200
-// found the SFU is not the binding limit of this kernel, so it is off.
+// One pair in kPolyEvery takes the FMA-pipe exp2 (0: none). With the MMA
+// issue loop warp-wide the SFU is the busiest unit of the softmax; moving a
+// quarter of the pairs to the FMA pipe took a layer over 32 windows from 465
+// to 442 us on B200 (one in 3: 446, one in 6: 442, one in 8: 443, one in 16:
+// 449).
 #ifndef ASRBACK_ENCODER_POLY_EVERY
-#define ASRBACK_ENCODER_POLY_EVERY 0
+#define ASRBACK_ENCODER_POLY_EVERY 4
 #endif
 constexpr int kPolyEvery = ASRBACK_ENCODER_POLY_EVERY;
 

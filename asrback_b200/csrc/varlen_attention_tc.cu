@@ -18,8 +18,9 @@
 //               rows past the segment belong to the next one and are masked,
 //               rows past the tensor read as zeros. The next item's Q loads
 //               once the current item's last S is done;
-//   warp 1      allocates the 512 TMEM columns; one lane issues every MMA:
-//               S = Q K^T (SS) and O += P V (TS: P from TMEM);
+//   warp 1      allocates the 512 TMEM columns and issues every MMA (the
+//               loop runs warp-wide, an elected lane issues): S = Q K^T (SS)
+//               and O += P V (TS: P from TMEM);
 //   warp 2      the item list: 32 lanes look up 32 of the CTA's items at a
 //               time (the segment bounds are global loads) and publish the
 //               valid ones, in order, into an 8-entry shared-memory ring
@@ -56,6 +57,15 @@ using namespace tc;
 constexpr int kRows = 128;  // query rows per tile (= TMEM lanes)
 constexpr int kKeys = 128;  // keys per tile
 constexpr int kThreads = 12 * 32;
+// Registers per thread: 168 at launch (384 x 168 = 64512); the warpgroup of
+// the TMA, MMA and item-list warps keeps 72, the two softmax warpgroups take
+// 208 (128 x 72 + 256 x 208 = 62464), so neither spills: a key tile's 128
+// scores and the row state stay in registers.
+constexpr int kLaunchRegs = 168;
+constexpr int kControlRegs = 72;
+constexpr int kSoftmaxRegs = 208;
+static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch's register pool");
 constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;
 constexpr int kItemSlots = 8;        // entries of the shared-memory item ring
@@ -83,9 +93,9 @@ struct VarlenShape {
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
   static constexpr int kOffStage = kOffV + kStages * kTileBytes;  // 8 warps x 32 rows
   static constexpr int kOffBar = kOffStage + 8 * kStageWarpBytes;
-  // barriers: q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S],
-  // s_full[2], p_full[2], o_full[2], o_free[2], item_full[R], item_empty[R]
-  static constexpr int kNumBars = 2 + 2 + 3 * kStages + 2 + 2 + 2 + 2 + 2 * kItemSlots;
+  // barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], s_full[2],
+  // p_full[2], o_full[2], o_free[2], item_full[R], item_empty[R]
+  static constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 + 2 + 2 + 2 + 2 * kItemSlots;
   static constexpr int kOffItems = kOffBar + kNumBars * 8;
   static constexpr int kOffTmemSlot = kOffItems + kItemSlots * static_cast<int>(sizeof(Item));
   static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
@@ -157,9 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBar);
   uint64_t* q_full = bars;  // [2]: per Q buffer (pair mode: [0] only)
   uint64_t* q_empty = q_full + 2;
-  uint64_t* k_full = q_empty + 2;
-  uint64_t* v_full = k_full + S;
-  uint64_t* kv_empty = v_full + S;
+  uint64_t* kv_full = q_empty + 2;  // K and V of a ring slot, one barrier
+  uint64_t* kv_empty = kv_full + S;
   uint64_t* s_full = kv_empty + S;  // [2]: per query tile (single-tile mode: per item parity)
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
@@ -184,8 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_free[t], 4);
     }
     for (int s = 0; s < S; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
     for (int e = 0; e < kItemSlots; ++e) {
@@ -206,198 +214,232 @@ __global__ void __launch_bounds__(kThreads, 1)
   // every entry, the end-of-list entry (n_max 0) included.
   auto read_item = [&](int n, Item& it, bool warp_wide) {
     const int e = n % kItemSlots;
-    if (!mbar_wait_bounded(&item_full[e], (n / kItemSlots) & 1)) return false;
+    bool ok = mbar_wait_bounded(&item_full[e], (n / kItemSlots) & 1);
+    if (warp_wide) ok = __all_sync(0xffffffffu, ok);
+    if (!ok) return false;
     it = ring[e];
     if (warp_wide) __syncwarp();
     if (!warp_wide || lane == 0) mbar_arrive(&item_empty[e]);
     return true;
   };
 
+  // Waits of a role run warp-wide: every lane polls, the warp agrees.
+  auto wait_warp = [](uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
+  };
+
+  // Each warpgroup leaves through its own branch (status, fences, one
+  // CTA-wide named barrier, the TMEM release): a register budget is fixed per
+  // branch, so the branches never rejoin.
+  if (warp < 4) {
+  reg_release<kControlRegs>();
+  // The TMA and MMA warps run their loops warp-wide (the loop state stays
+  // warp-uniform) and issue from one elected lane.
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
+    if (elect_one()) {
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      int g = 0;  // K/V tiles loaded, over all items
-      auto load_kv = [&](const Item& it, int j) {
-        const int s = g % S;
-        if (g >= S && !mbar_wait_bounded(&kv_empty[s], ((g / S) - 1) & 1)) return false;
-        mbar_arrive_expect_tx(&k_full[s], Sh::kTileBytes);
+    }
+    __syncwarp();
+    int g = 0;  // K/V tiles loaded, over all items
+    auto load_kv = [&](const Item& it, int j) {
+      const int s = g % S;
+      if (g >= S && !wait_warp(&kv_empty[s], ((g / S) - 1) & 1)) return false;
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&kv_full[s], 2 * Sh::kTileBytes);
 #pragma unroll
         for (int a = 0; a < Sh::kAtoms; ++a)
           tma_load_3d(smem + Sh::kOffK + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_k,
-                      64 * a, it.kvh, it.start + j * kKeys, &k_full[s]);
-        mbar_arrive_expect_tx(&v_full[s], Sh::kTileBytes);
+                      64 * a, it.kvh, it.start + j * kKeys, &kv_full[s]);
 #pragma unroll
         for (int a = 0; a < Sh::kAtoms; ++a)
           tma_load_3d(smem + Sh::kOffV + s * Sh::kTileBytes + a * Sh::kAtomBytes, &map_v,
-                      64 * a, it.kvh, it.start + j * kKeys, &v_full[s]);
-        ++g;
-        return true;
-      };
-      for (int n = 0;; ++n) {
-        Item it;
-        if (!read_item(n, it, false)) {
+                      64 * a, it.kvh, it.start + j * kKeys, &kv_full[s]);
+      }
+      __syncwarp();
+      ++g;
+      return true;
+    };
+    for (int n = 0;; ++n) {
+      Item it;
+      if (!read_item(n, it, true)) {
+        timed_out = true;
+        break;
+      }
+      if (it.n_max == 0) break;
+      if constexpr (kSingle) {
+        // Item n: Q into buffer n & 1 once item n-2's S is done, then its
+        // one key/value tile.
+        const int b = n & 1;
+        if (n >= 2 && !wait_warp(&q_empty[b], ((n >> 1) - 1) & 1)) {
           timed_out = true;
           break;
         }
-        if (it.n_max == 0) break;
-        if constexpr (kSingle) {
-          // Item n: Q into buffer n & 1 once item n-2's S is done, then its
-          // one key/value tile.
-          const int b = n & 1;
-          if (n >= 2 && !mbar_wait_bounded(&q_empty[b], ((n >> 1) - 1) & 1)) {
-            timed_out = true;
-            break;
-          }
+        if (elect_one()) {
           mbar_arrive_expect_tx(&q_full[b], Sh::kTileBytes);
 #pragma unroll
           for (int a = 0; a < Sh::kAtoms; ++a)
             tma_load_3d(smem + Sh::kOffQ + b * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q,
                         64 * a, it.h, it.start, &q_full[b]);
-          if (!load_kv(it, 0)) {
-            timed_out = true;
-            break;
-          }
-        } else {
-          // Q of the previous item is in use until its last S is done.
-          if (n > 0 && !mbar_wait_bounded(q_empty, (n - 1) & 1)) {
-            timed_out = true;
-            break;
-          }
-          const int q_tiles = it.n_k[1] > 0 ? 2 : 1;
+        }
+        __syncwarp();
+        if (!load_kv(it, 0)) {
+          timed_out = true;
+          break;
+        }
+      } else {
+        // Q of the previous item is in use until its last S is done.
+        if (n > 0 && !wait_warp(q_empty, (n - 1) & 1)) {
+          timed_out = true;
+          break;
+        }
+        const int q_tiles = it.n_k[1] > 0 ? 2 : 1;
+        if (elect_one()) {
           mbar_arrive_expect_tx(q_full, q_tiles * Sh::kTileBytes);
           for (int t = 0; t < q_tiles; ++t)
 #pragma unroll
             for (int a = 0; a < Sh::kAtoms; ++a)
               tma_load_3d(smem + Sh::kOffQ + t * Sh::kTileBytes + a * Sh::kAtomBytes, &map_q,
                           64 * a, it.h, it.start + it.first_row[t], q_full);
-          for (int j = 0; j < it.n_max && !timed_out; ++j) timed_out = !load_kv(it, j);
-          if (timed_out) break;
         }
+        __syncwarp();
+        for (int j = 0; j < it.n_max && !timed_out; ++j) timed_out = !load_kv(it, j);
+        if (timed_out) break;
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
-      constexpr uint32_t kIdescPV = idesc_bf16(kRows, 64, true);
-      // Descriptors are built once and stepped by adds of address >> 4:
-      // 32 bytes per 16 elements along K inside a 128-byte block, one block
-      // (kAtomBytes) per 64 elements, 2048 bytes per 16 rows of V.
-      const uint64_t q_desc = sw128_desc(smem_addr(smem + Sh::kOffQ), 16, 1024);
-      const uint64_t k_desc = sw128_desc(smem_addr(smem + Sh::kOffK), 16, 1024);
-      const uint64_t v_desc = sw128_desc(smem_addr(smem + Sh::kOffV), Sh::kAtomBytes, 1024);
-      constexpr uint64_t kTile = Sh::kTileBytes >> 4, kAtom = Sh::kAtomBytes >> 4;
-      // S_t = Q buffer t . K tile of ring slot s.
-      auto issue_qk = [&](int t, int s) {
-        // K = head_dim in steps of 16: four per 128-byte block.
+    constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
+    constexpr uint32_t kIdescPV = idesc_bf16(kRows, 64, true);
+    // Descriptors are built once and stepped by adds of address >> 4:
+    // 32 bytes per 16 elements along K inside a 128-byte block, one block
+    // (kAtomBytes) per 64 elements, 2048 bytes per 16 rows of V.
+    const uint64_t q_desc = sw128_desc(smem_addr(smem + Sh::kOffQ), 16, 1024);
+    const uint64_t k_desc = sw128_desc(smem_addr(smem + Sh::kOffK), 16, 1024);
+    const uint64_t v_desc = sw128_desc(smem_addr(smem + Sh::kOffV), Sh::kAtomBytes, 1024);
+    constexpr uint64_t kTile = Sh::kTileBytes >> 4, kAtom = Sh::kAtomBytes >> 4;
+    // S_t = Q buffer t . K tile of ring slot s (called by the elected lane).
+    auto issue_qk = [&](int t, int s) {
+      // K = head_dim in steps of 16: four per 128-byte block.
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint64_t off = (k / 4) * kAtom + (k % 4) * (32 >> 4);
-          mma_ss(tmem + s_col(t), q_desc + t * kTile + off, k_desc + s * kTile + off, kIdescQK,
-                 k > 0);
-        }
-      };
-      // O_t (+)= P_t . V tile of ring slot s.
-      auto issue_pv = [&](int t, int s, bool accumulate) {
-        // N = head_dim as 64-column blocks of V; K = 128 keys in steps of 16:
-        // P advances 8 TMEM columns (bf16 pairs), V 16 rows (2048 bytes).
+      for (int k = 0; k < D / 16; ++k) {
+        const uint64_t off = (k / 4) * kAtom + (k % 4) * (32 >> 4);
+        mma_ss(tmem + s_col(t), q_desc + t * kTile + off, k_desc + s * kTile + off, kIdescQK,
+               k > 0);
+      }
+    };
+    // O_t (+)= P_t . V tile of ring slot s (called by the elected lane).
+    auto issue_pv = [&](int t, int s, bool accumulate) {
+      // N = head_dim as 64-column blocks of V; K = 128 keys in steps of 16:
+      // P advances 8 TMEM columns (bf16 pairs), V 16 rows (2048 bytes).
 #pragma unroll
-        for (int a = 0; a < Sh::kAtoms; ++a)
+      for (int a = 0; a < Sh::kAtoms; ++a)
 #pragma unroll
-          for (int k = 0; k < kKeys / 16; ++k)
-            mma_ts(tmem + o_col(t) + 64 * a, tmem + s_col(t) + k * 8,
-                   v_desc + s * kTile + a * kAtom + k * (2048 >> 4), kIdescPV,
-                   accumulate || k > 0);
-      };
-      bool ok = true;
-      if constexpr (kSingle) {
-        // Before P(k) V(k), S is issued for items up to k + 1: S(m)
-        // overwrites P(m - 2), whose P V is already issued. P V(k) overwrites
-        // O_{k & 1} once item k-2's epilogue has read it.
-        int k_s = 0;  // items whose S is issued
-        bool more = true;
-        for (int k = 0; ok; ++k) {
-          while (more && k_s < k + 2) {
-            Item it;
-            ok = read_item(k_s, it, false);
-            if (!ok) break;
-            if (it.n_max == 0) {
-              more = false;
-              break;
-            }
-            const int t = k_s & 1;
-            ok = mbar_wait_bounded(&q_full[t], (k_s >> 1) & 1) &&
-                 mbar_wait_bounded(&k_full[k_s % S], (k_s / S) & 1);
-            if (!ok) break;
-            tc_fence_after();
+        for (int k = 0; k < kKeys / 16; ++k)
+          mma_ts(tmem + o_col(t) + 64 * a, tmem + s_col(t) + k * 8,
+                 v_desc + s * kTile + a * kAtom + k * (2048 >> 4), kIdescPV,
+                 accumulate || k > 0);
+    };
+    bool ok = true;
+    if constexpr (kSingle) {
+      // Before P(k) V(k), S is issued for items up to k + 1: S(m)
+      // overwrites P(m - 2), whose P V is already issued. P V(k) overwrites
+      // O_{k & 1} once item k-2's epilogue has read it. S(k) waited for its
+      // K/V slot (one barrier for both), so P V(k) reads V without a wait.
+      int k_s = 0;  // items whose S is issued
+      bool more = true;
+      for (int k = 0; ok; ++k) {
+        while (more && k_s < k + 2) {
+          Item it;
+          ok = read_item(k_s, it, true);
+          if (!ok) break;
+          if (it.n_max == 0) {
+            more = false;
+            break;
+          }
+          const int t = k_s & 1;
+          ok = wait_warp(&q_full[t], (k_s >> 1) & 1) &&
+               wait_warp(&kv_full[k_s % S], (k_s / S) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
             issue_qk(t, k_s % S);
             mma_commit(&s_full[t]);
             mma_commit(&q_empty[t]);
-            ++k_s;
           }
-          if (!ok || k >= k_s) break;
-          const int t = k & 1;
-          ok = mbar_wait_bounded(&p_full[t], (k >> 1) & 1);
-          if (ok && k >= 2) ok = mbar_wait_bounded(&o_free[t], ((k >> 1) - 1) & 1);
-          if (ok) ok = mbar_wait_bounded(&v_full[k % S], (k / S) & 1);
-          if (!ok) break;
-          tc_fence_after();
+          __syncwarp();
+          ++k_s;
+        }
+        if (!ok || k >= k_s) break;
+        const int t = k & 1;
+        ok = wait_warp(&p_full[t], (k >> 1) & 1);
+        if (ok && k >= 2) ok = wait_warp(&o_free[t], ((k >> 1) - 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        if (elect_one()) {
           issue_pv(t, k % S, false);
           mma_commit(&o_full[t]);
           mma_commit(&kv_empty[k % S]);
         }
-      } else {
-        int base = 0;            // global index of the item's first K/V tile
-        int p_seen[2] = {0, 0};  // p_full completions consumed, per query tile
-        int o_done[2] = {0, 0};  // items whose O_t is final (o_full commits)
-        for (int n = 0; ok; ++n) {
-          Item it;
-          ok = read_item(n, it, false);
-          if (!ok || it.n_max == 0) break;
-          ok = mbar_wait_bounded(q_full, n & 1);
-          // Step j: for each query tile still reading keys, P_t(j-1) V(j-1)
-          // once its softmax has written P_t(j-1) (the first of an item also
-          // once the previous item's epilogue has read O_t), then S_t(j) over
-          // the same columns (or, after its last key tile, the commit that
-          // O_t is final). After the item's last S its Q buffer is released.
-          for (int j = 0; j <= it.n_max && ok; ++j) {
-            const int g = base + j;
-            if (j < it.n_max) ok = mbar_wait_bounded(&k_full[g % S], (g / S) & 1);
-            if (ok && j > 0) ok = mbar_wait_bounded(&v_full[(g - 1) % S], ((g - 1) / S) & 1);
-            if (!ok) break;
-            tc_fence_after();
+        __syncwarp();
+      }
+    } else {
+      int base = 0;            // global index of the item's first K/V tile
+      int p_seen[2] = {0, 0};  // p_full completions consumed, per query tile
+      int o_done[2] = {0, 0};  // items whose O_t is final (o_full commits)
+      for (int n = 0; ok; ++n) {
+        Item it;
+        ok = read_item(n, it, true);
+        if (!ok || it.n_max == 0) break;
+        ok = wait_warp(q_full, n & 1);
+        // Step j: for each query tile still reading keys, P_t(j-1) V(j-1)
+        // once its softmax has written P_t(j-1) (the first of an item also
+        // once the previous item's epilogue has read O_t), then S_t(j) over
+        // the same columns (or, after its last key tile, the commit that
+        // O_t is final). After the item's last S its Q buffer is released.
+        // The wait for K/V tile j (one barrier for both) comes before S(j),
+        // so P V(j) at step j + 1 reads V without another wait.
+        for (int j = 0; j <= it.n_max && ok; ++j) {
+          const int g = base + j;
+          if (j < it.n_max) ok = wait_warp(&kv_full[g % S], (g / S) & 1);
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              if (it.n_k[t] == 0 || j > it.n_k[t]) continue;
-              if (j > 0) {
-                ok = mbar_wait_bounded(&p_full[t], p_seen[t] & 1);
-                ++p_seen[t];
-                if (ok && j == 1 && o_done[t] > 0)
-                  ok = mbar_wait_bounded(&o_free[t], (o_done[t] - 1) & 1);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(t, (g - 1) % S, j > 1);
-              }
+          for (int t = 0; t < 2; ++t) {
+            if (it.n_k[t] == 0 || j > it.n_k[t]) continue;
+            if (j > 0) {
+              ok = wait_warp(&p_full[t], p_seen[t] & 1);
+              ++p_seen[t];
+              if (ok && j == 1 && o_done[t] > 0) ok = wait_warp(&o_free[t], (o_done[t] - 1) & 1);
+              if (!ok) break;
+              tc_fence_after();
+              if (elect_one()) issue_pv(t, (g - 1) % S, j > 1);
+              __syncwarp();
+            }
+            if (elect_one()) {
               if (j < it.n_k[t]) {
                 issue_qk(t, g % S);
                 mma_commit(&s_full[t]);
               } else {
                 mma_commit(&o_full[t]);
-                ++o_done[t];
               }
             }
-            if (!ok) break;
+            __syncwarp();
+            if (j >= it.n_k[t]) ++o_done[t];
+          }
+          if (!ok) break;
+          if (elect_one()) {
             if (j == it.n_max - 1) mma_commit(q_empty);
             if (j > 0) mma_commit(&kv_empty[(g - 1) % S]);
           }
-          base += it.n_max;
+          __syncwarp();
         }
+        base += it.n_max;
       }
-      timed_out = !ok;
     }
+    timed_out = !ok;
   } else if (warp == 2) {
     // ---------------- item list ----------------
     // Lane i looks up item base + i * gridDim.x; the valid ones are published
@@ -443,7 +485,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&item_full[e]);
       }
     }
-  } else if (warp >= 4) {
+  }
+  if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+  tc_fence_before();
+  named_sync(1, kThreads);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  } else {
+    reg_acquire<kSoftmaxRegs>();
     // ---------------- softmax and epilogue (one query row per thread) ----------------
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
@@ -583,13 +634,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       epilogue(it.start, it.len, it.h, it.first_row[tile], l);
     }
     timed_out = !ok;
-  }
-  if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if (timed_out && p.status) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+    tc_fence_before();
+    named_sync(1, kThreads);
   }
 }
 
