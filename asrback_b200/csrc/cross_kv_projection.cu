@@ -15,7 +15,8 @@
 // window's rows and every CTA shares the weights in L2. Warp 0 streams the
 // chunks (TMA: a 3-D map over the windows' rows, tokens past the window read
 // as zeros; 2-D maps over the weights) through a 4-stage ring; warp 1 issues
-// tcgen05.mma into two TMEM accumulators; warps 4-7 (thread = token) add the
+// tcgen05.mma into two TMEM accumulators (both warps run their loops
+// warp-wide and issue from an elected lane); warps 4-7 (thread = token) add the
 // bias, round to bf16 and store each head's 32 rows per warp as 4 KB of
 // contiguous cache, staged through shared memory. float32 runs a SIMT tiled
 // GEMM with the same output layout.
@@ -105,59 +106,72 @@ __global__ void __launch_bounds__(256, 1)
     b = index / (p.tiles_n * p.tiles_m);
   };
 
+  // The TMA and MMA warps run their loops warp-wide (waits by every lane, the
+  // loop state warp-uniform) and issue from one elected lane.
+  auto wait_warp = [](uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
+  };
   if (warp == 0) {
-    if (lane == 0) {
+    if (elect_one()) {
       prefetch_tensormap(&map_x);
       prefetch_tensormap(&map_wk);
       prefetch_tensormap(&map_wv);
-      const uint64_t keep = l2_evict_last_policy();
-      int g = 0;
-      for (int index = blockIdx.x; index < tiles && !timed_out; index += gridDim.x) {
-        int b, t0, n0;
-        tile_coords(index, b, t0, n0);
-        const bool is_v = n0 >= p.width;
-        const CUtensorMap* map_w = is_v ? &map_wv : &map_wk;
-        const int row0 = is_v ? n0 - p.width : n0;
-        for (int kc = 0; kc < chunks; ++kc, ++g) {
-          const int s = g % S;
-          if (g >= S && !mbar_wait_bounded(&empty[s], ((g / S) - 1) & 1)) {
-            timed_out = true;
-            break;
-          }
+    }
+    __syncwarp();
+    const uint64_t keep = l2_evict_last_policy();
+    int g = 0;
+    bool ok = true;
+    for (int index = blockIdx.x; index < tiles && ok; index += gridDim.x) {
+      int b, t0, n0;
+      tile_coords(index, b, t0, n0);
+      const bool is_v = n0 >= p.width;
+      const CUtensorMap* map_w = is_v ? &map_wv : &map_wk;
+      const int row0 = is_v ? n0 - p.width : n0;
+      for (int kc = 0; kc < chunks; ++kc, ++g) {
+        const int s = g % S;
+        if (g >= S) ok = wait_warp(&empty[s], ((g / S) - 1) & 1);
+        if (!ok) break;
+        if (elect_one()) {
           uint8_t* stage = smem + s * Sh::kStageBytes;
           mbar_arrive_expect_tx(&full[s], Sh::kStageBytes);
           tma_load_3d(stage, &map_x, kc * kChunk, t0, b, &full[s]);
           tma_load_2d_hint(stage + Sh::kABytes, map_w, kc * kChunk, row0, &full[s], keep);
         }
+        __syncwarp();
       }
     }
+    timed_out = !ok;
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_bf16(kRows, kN, false);
-      const uint64_t a_desc = sw128_desc(smem_addr(smem), 16, 1024);
-      const uint64_t b_desc = sw128_desc(smem_addr(smem + Sh::kABytes), 16, 1024);
-      constexpr uint64_t kStage = Sh::kStageBytes >> 4;
-      int g = 0, lt = 0;
-      bool ok = true;
-      for (int index = blockIdx.x; index < tiles && ok; index += gridDim.x, ++lt) {
-        const int a = lt & 1;
-        if (lt >= 2) ok = mbar_wait_bounded(&acc_empty[a], ((lt >> 1) - 1) & 1);
+    constexpr uint32_t kIdesc = idesc_bf16(kRows, kN, false);
+    const uint64_t a_desc = sw128_desc(smem_addr(smem), 16, 1024);
+    const uint64_t b_desc = sw128_desc(smem_addr(smem + Sh::kABytes), 16, 1024);
+    constexpr uint64_t kStage = Sh::kStageBytes >> 4;
+    int g = 0, lt = 0;
+    bool ok = true;
+    for (int index = blockIdx.x; index < tiles && ok; index += gridDim.x, ++lt) {
+      const int a = lt & 1;
+      if (lt >= 2) ok = wait_warp(&acc_empty[a], ((lt >> 1) - 1) & 1);
+      tc_fence_after();
+      for (int kc = 0; kc < chunks && ok; ++kc, ++g) {
+        const int s = g % S;
+        ok = wait_warp(&full[s], (g / S) & 1);
+        if (!ok) break;
         tc_fence_after();
-        for (int kc = 0; kc < chunks && ok; ++kc, ++g) {
-          const int s = g % S;
-          ok = mbar_wait_bounded(&full[s], (g / S) & 1);
-          if (!ok) break;
-          tc_fence_after();
+        if (elect_one()) {
 #pragma unroll
           for (int k = 0; k < kChunk / 16; ++k)
             mma_ss(tmem + a * kN, a_desc + s * kStage + 2 * k, b_desc + s * kStage + 2 * k, kIdesc,
                    kc > 0 || k > 0);
           mma_commit(&empty[s]);
         }
-        if (ok) mma_commit(&acc_full[a]);
+        __syncwarp();
       }
-      timed_out = !ok;
+      if (ok) {
+        if (elect_one()) mma_commit(&acc_full[a]);
+        __syncwarp();
+      }
     }
+    timed_out = !ok;
   } else if (warp >= 4) {
     // Thread = token row of the tile (= TMEM lane).
     const int quarter = warp & 3;

@@ -289,46 +289,55 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t tmem = *tmem_slot;
   bool timed_out = false;
 
+  // The TMA and MMA warps run their loops warp-wide (waits by every lane, the
+  // loop state warp-uniform) and issue from one elected lane.
+  auto wait_warp = [](uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
+  };
   if (warp == 0) {
     // ---------------- TMA: weight tile and hidden rows per K chunk ----------------
-    if (lane == 0) {
+    if (elect_one()) {
       prefetch_tensormap(&map_w);
       prefetch_tensormap(&map_h);
-      const uint64_t stream = l2_evict_first_policy();
-      const uint64_t keep = l2_evict_last_policy();
-      int g = 0;
-      for (int tile = blockIdx.x; tile < tiles && !timed_out; tile += gridDim.x) {
-        for (int kc = 0; kc < chunks; ++kc, ++g) {
-          const int s = g % S;
-          if (g >= S && !mbar_wait_bounded(&empty[s], ((g / S) - 1) & 1)) {
-            timed_out = true;
-            break;
-          }
+    }
+    __syncwarp();
+    const uint64_t stream = l2_evict_first_policy();
+    const uint64_t keep = l2_evict_last_policy();
+    int g = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      for (int kc = 0; kc < chunks; ++kc, ++g) {
+        const int s = g % S;
+        if (g >= S) ok = wait_warp(&empty[s], ((g / S) - 1) & 1);
+        if (!ok) break;
+        if (elect_one()) {
           uint8_t* stage = smem + s * Sh::kStageBytes;
           mbar_arrive_expect_tx(&full[s], Sh::kStageBytes);
           tma_load_2d_hint(stage, &map_w, kc * kChunk, tile * kVocabTile, &full[s], stream);
           tma_load_2d_hint(stage + Sh::kWBytes, &map_h, kc * kChunk, 0, &full[s], keep);
         }
+        __syncwarp();
       }
     }
+    timed_out = !ok;
   } else if (warp == 1) {
     // ---------------- MMA: D[vocab row][batch row] in TMEM ----------------
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_bf16(kVocabTile, kN, false);
-      const uint64_t w_desc = sw128_desc(smem_addr(smem), 16, 1024);
-      const uint64_t h_desc = sw128_desc(smem_addr(smem + Sh::kWBytes), 16, 1024);
-      constexpr uint64_t kStage = Sh::kStageBytes >> 4;
-      int g = 0, lt = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++lt) {
-        const int a = lt & 1;
-        if (lt >= 2) ok = mbar_wait_bounded(&acc_empty[a], ((lt >> 1) - 1) & 1);
+    constexpr uint32_t kIdesc = idesc_bf16(kVocabTile, kN, false);
+    const uint64_t w_desc = sw128_desc(smem_addr(smem), 16, 1024);
+    const uint64_t h_desc = sw128_desc(smem_addr(smem + Sh::kWBytes), 16, 1024);
+    constexpr uint64_t kStage = Sh::kStageBytes >> 4;
+    int g = 0, lt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++lt) {
+      const int a = lt & 1;
+      if (lt >= 2) ok = wait_warp(&acc_empty[a], ((lt >> 1) - 1) & 1);
+      tc_fence_after();
+      for (int kc = 0; kc < chunks && ok; ++kc, ++g) {
+        const int s = g % S;
+        ok = wait_warp(&full[s], (g / S) & 1);
+        if (!ok) break;
         tc_fence_after();
-        for (int kc = 0; kc < chunks && ok; ++kc, ++g) {
-          const int s = g % S;
-          ok = mbar_wait_bounded(&full[s], (g / S) & 1);
-          if (!ok) break;
-          tc_fence_after();
+        if (elect_one()) {
           // K = 64 in steps of 16: 32 bytes along the 128-byte swizzled row.
 #pragma unroll
           for (int k = 0; k < kChunk / 16; ++k)
@@ -336,10 +345,14 @@ __global__ void __launch_bounds__(256, 1)
                    kc > 0 || k > 0);
           mma_commit(&empty[s]);
         }
-        if (ok) mma_commit(&acc_full[a]);
+        __syncwarp();
       }
-      timed_out = !ok;
+      if (ok) {
+        if (elect_one()) mma_commit(&acc_full[a]);
+        __syncwarp();
+      }
     }
+    timed_out = !ok;
   } else if (warp >= 4) {
     // ---------------- epilogue: bf16 logits, mask, column reductions ----------------
     const int tid = threadIdx.x - 128;  // = TMEM lane = vocabulary row within the tile
