@@ -2057,7 +2057,7 @@ def reference_whisper_module():
     return whisper
 
 
-def measure_admission(torch, dist, device, world: int, batches: int = 4) -> dict:
+def measure_admission(torch, dist, device, world: int, batches: int = 4, rounds: int = 3) -> dict:
     """Window admission at the caller's boundary, through the reference's own
     modules: log-mel windows copied in from pinned host memory, the encoder
     (``WhisperEncoder.forward``, ``whisper.py:140-153``: convolution stem, 32
@@ -2096,30 +2096,38 @@ def measure_admission(torch, dist, device, world: int, batches: int = 4) -> dict
         model.set_encoder_output(cache, model.model.encoder(mel))
         host_row.copy_(cache.cross_keys[3, windows - 1, 19], non_blocking=True)
 
-    out = {}
+    # The three legs alternate over `rounds` rounds and each keeps its best
+    # round: a leg timed once, after the others, saw the GPU's clocks drop as
+    # the power cap bit, whichever leg came last.
+    best: dict[str, float] = {}
+    legs = (("value", "all"), ("cross_only", "cross"), ("torch", None))
     with torch.inference_mode():
-        for label, patched in (("value", "all"), ("cross_only", "cross"), ("torch", None)):
-            if patched:
-                plugin.install(whisper, None, encoder=patched == "all")
-            try:
-                for _ in range(2):
-                    admit()
-                torch.cuda.synchronize()
-                if world > 1:
-                    dist.barrier()
-                start = torch.cuda.Event(enable_timing=True)
-                end = torch.cuda.Event(enable_timing=True)
-                start.record(stream)
-                for _ in range(batches):
-                    admit()
-                end.record(stream)
-                torch.cuda.synchronize()
-            finally:
+        for _ in range(rounds):
+            for label, patched in legs:
                 if patched:
-                    plugin.uninstall()
-            ranks = rank_times(torch, dist, world, start.elapsed_time(end))
-            out[label] = windows * batches * world / (max(ranks) / 1e3)
-            out[f"{label}_ms_per_batch"] = max(ranks) / batches
+                    plugin.install(whisper, None, encoder=patched == "all")
+                try:
+                    for _ in range(2):
+                        admit()
+                    torch.cuda.synchronize()
+                    if world > 1:
+                        dist.barrier()
+                    start = torch.cuda.Event(enable_timing=True)
+                    end = torch.cuda.Event(enable_timing=True)
+                    start.record(stream)
+                    for _ in range(batches):
+                        admit()
+                    end.record(stream)
+                    torch.cuda.synchronize()
+                finally:
+                    if patched:
+                        plugin.uninstall()
+                ranks = rank_times(torch, dist, world, start.elapsed_time(end))
+                best[label] = min(best.get(label, float("inf")), max(ranks))
+    out = {}
+    for label, _ in legs:
+        out[label] = windows * batches * world / (best[label] / 1e3)
+        out[f"{label}_ms_per_batch"] = best[label] / batches
     del model, cache
     torch.cuda.empty_cache()
     return {"value": out["value"], "unit": "windows/s", "ms_per_batch": out["value_ms_per_batch"],
@@ -2129,7 +2137,7 @@ def measure_admission(torch, dist, device, world: int, batches: int = 4) -> dict
             "what": "32 windows of host log-mel through the reference's encoder and "
                     "set_encoder_output (large-v3-turbo widths) into the cross cache, eager; "
                     "value with the plugin installed, cross_only with install(encoder=False), "
-                    "torch without"}
+                    "torch without; the legs alternate over 3 rounds, best round each"}
 
 
 def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, warmup: int,
