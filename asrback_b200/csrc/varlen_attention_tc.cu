@@ -312,7 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
-    constexpr uint32_t kIdescPV = idesc_bf16(kRows, 64, true);
+    // P V in one MMA per 16 keys over all head_dim columns: V is an MN-major
+    // operand whose 64-column blocks lie kAtomBytes apart (the descriptor's
+    // leading byte offset), so N = head_dim spans them.
+    constexpr uint32_t kIdescPV = idesc_bf16(kRows, D, true);
     // Descriptors are built once and stepped by adds of address >> 4:
     // 32 bytes per 16 elements along K inside a 128-byte block, one block
     // (kAtomBytes) per 64 elements, 2048 bytes per 16 rows of V.
@@ -332,15 +335,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // O_t (+)= P_t . V tile of ring slot s (called by the elected lane).
     auto issue_pv = [&](int t, int s, bool accumulate) {
-      // N = head_dim as 64-column blocks of V; K = 128 keys in steps of 16:
-      // P advances 8 TMEM columns (bf16 pairs), V 16 rows (2048 bytes).
+      // K = 128 keys in steps of 16: P advances 8 TMEM columns (bf16 pairs),
+      // V 16 rows (2048 bytes) within each of its column blocks.
 #pragma unroll
-      for (int a = 0; a < Sh::kAtoms; ++a)
-#pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k)
-          mma_ts(tmem + o_col(t) + 64 * a, tmem + s_col(t) + k * 8,
-                 v_desc + s * kTile + a * kAtom + k * (2048 >> 4), kIdescPV,
-                 accumulate || k > 0);
+      for (int k = 0; k < kKeys / 16; ++k)
+        mma_ts(tmem + o_col(t), tmem + s_col(t) + k * 8, v_desc + s * kTile + k * (2048 >> 4),
+               kIdescPV, accumulate || k > 0);
     };
     bool ok = true;
     if constexpr (kSingle) {
