@@ -111,8 +111,11 @@ __global__ void __launch_bounds__(256, 1)
   auto wait_warp = [](uint64_t* bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
   };
+  // One lane per warp, elected once: a tcgen05.commit tracks the MMAs of its
+  // own thread, so the MMA warp's issues and commits all come from it.
+  const bool leader = elect_one();
   if (warp == 0) {
-    if (elect_one()) {
+    if (leader) {
       prefetch_tensormap(&map_x);
       prefetch_tensormap(&map_wk);
       prefetch_tensormap(&map_wv);
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(256, 1)
         const int s = g % S;
         if (g >= S) ok = wait_warp(&empty[s], ((g / S) - 1) & 1);
         if (!ok) break;
-        if (elect_one()) {
+        if (leader) {
           uint8_t* stage = smem + s * Sh::kStageBytes;
           mbar_arrive_expect_tx(&full[s], Sh::kStageBytes);
           tma_load_3d(stage, &map_x, kc * kChunk, t0, b, &full[s]);
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(256, 1)
         ok = wait_warp(&full[s], (g / S) & 1);
         if (!ok) break;
         tc_fence_after();
-        if (elect_one()) {
+        if (leader) {
 #pragma unroll
           for (int k = 0; k < kChunk / 16; ++k)
             mma_ss(tmem + a * kN, a_desc + s * kStage + 2 * k, b_desc + s * kStage + 2 * k, kIdesc,
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(256, 1)
         __syncwarp();
       }
       if (ok) {
-        if (elect_one()) mma_commit(&acc_full[a]);
+        if (leader) mma_commit(&acc_full[a]);
         __syncwarp();
       }
     }

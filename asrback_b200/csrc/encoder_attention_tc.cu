@@ -195,6 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // branch, so the branches never rejoin.
   if (warp < 4) {
     reg_release<kControlRegs>();
+    // One lane per warp, elected once: a tcgen05.commit tracks the MMAs of
+    // its own thread, so the MMA warp's issues and commits all come from it.
+    const bool leader = elect_one();
     // Both control warps run their loops warp-wide (waits by every lane, so
     // the loop state stays warp-uniform) and issue from one elected lane.
     auto wait_warp = [](uint64_t* bar, uint32_t parity) {
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     if (warp == 0) {
       // ---------------- TMA producer ----------------
-      if (elect_one()) {
+      if (leader) {
         prefetch_tensormap(&map_q);
         prefetch_tensormap(&map_k);
         prefetch_tensormap(&map_v);
@@ -217,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int qb = li & 1;
         if (li >= 2) ok = wait_warp(&q_empty[qb], ((li >> 1) - 1) & 1);
         if (!ok) break;
-        if (elect_one()) {
+        if (leader) {
           uint8_t* qdst = smem + kOffQ + qb * 2 * kTileBytes;
           mbar_arrive_expect_tx(&q_full[qb], 2 * kTileBytes);
           tma_load_4d(qdst, &map_q, 0, h, (2 * pair) * kRows, b, &q_full[qb]);
@@ -228,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = g % kStages;
           if (g >= kStages) ok = wait_warp(&kv_empty[s], ((g / kStages) - 1) & 1);
           if (!ok) break;
-          if (elect_one()) {
+          if (leader) {
             // K and V of a key tile complete one barrier: the first MMA that
             // reads the tile (its S of query tile 0) waits once for both.
             mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const int s = c.s;
           const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
-          if (elect_one()) {
+          if (leader) {
             // K = 64 in four steps of 16 elements.
 #pragma unroll
             for (int k = 0; k < kDim / 16; ++k)
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) return;
           tc_fence_after();
           const int buf = t == 0 ? c.buf0 : (c.buf0 == 2 ? 0 : c.buf0 + 1);
-          if (elect_one()) {
+          if (leader) {
             // K = 128 keys in eight steps of 16: P advances 8 TMEM columns
             // (bf16 pairs), V two 8-row swizzle atoms.
 #pragma unroll
@@ -333,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ok) issue_pv(1, c0);
           if (ok && J + 2 < total) issue_qk(0, c2);
           if (ok && J + kStages < total) {
-            if (elect_one()) mma_commit(&kv_empty[c0.s]);
+            if (leader) mma_commit(&kv_empty[c0.s]);
             __syncwarp();
           }
           c0.next(n_k);

@@ -294,9 +294,12 @@ __global__ void __launch_bounds__(256, 1)
   auto wait_warp = [](uint64_t* bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
   };
+  // One lane per warp, elected once: a tcgen05.commit tracks the MMAs of its
+  // own thread, so the MMA warp's issues and commits all come from it.
+  const bool leader = elect_one();
   if (warp == 0) {
     // ---------------- TMA: weight tile and hidden rows per K chunk ----------------
-    if (elect_one()) {
+    if (leader) {
       prefetch_tensormap(&map_w);
       prefetch_tensormap(&map_h);
     }
@@ -310,7 +313,7 @@ __global__ void __launch_bounds__(256, 1)
         const int s = g % S;
         if (g >= S) ok = wait_warp(&empty[s], ((g / S) - 1) & 1);
         if (!ok) break;
-        if (elect_one()) {
+        if (leader) {
           uint8_t* stage = smem + s * Sh::kStageBytes;
           mbar_arrive_expect_tx(&full[s], Sh::kStageBytes);
           tma_load_2d_hint(stage, &map_w, kc * kChunk, tile * kVocabTile, &full[s], stream);
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(256, 1)
         ok = wait_warp(&full[s], (g / S) & 1);
         if (!ok) break;
         tc_fence_after();
-        if (elect_one()) {
+        if (leader) {
           // K = 64 in steps of 16: 32 bytes along the 128-byte swizzled row.
 #pragma unroll
           for (int k = 0; k < kChunk / 16; ++k)
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(256, 1)
         __syncwarp();
       }
       if (ok) {
-        if (elect_one()) mma_commit(&acc_full[a]);
+        if (leader) mma_commit(&acc_full[a]);
         __syncwarp();
       }
     }

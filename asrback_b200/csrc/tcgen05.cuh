@@ -72,10 +72,12 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // True in one lane of the (converged, full) warp. A role that issues
-// tcgen05.mma runs warp-wide and issues from the elected lane: the tensor
-// core's issue queue is shallow, and an issue loop run by the whole warp keeps
-// its descriptors and control in uniform registers (about twice the MMA issue
-// rate of the same loop run by one divergent lane).
+// tcgen05.mma runs warp-wide and issues from a lane elected once at the role's
+// start (a tcgen05.commit tracks the MMAs of its own thread, so every issue and
+// commit comes from that one lane): the tensor core's issue queue is shallow,
+// and an issue loop run by the whole warp keeps its descriptors and control in
+// uniform registers (about twice the MMA issue rate of the same loop run by
+// one divergent lane).
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

@@ -233,11 +233,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   // branch, so the branches never rejoin.
   if (warp < 4) {
   reg_release<kControlRegs>();
+  // One lane per warp, elected once: a tcgen05.commit tracks the MMAs of its
+  // own thread, so the MMA warp's issues and commits all come from it.
+  const bool leader = elect_one();
   // The TMA and MMA warps run their loops warp-wide (the loop state stays
   // warp-uniform) and issue from one elected lane.
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (elect_one()) {
+    if (leader) {
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
@@ -247,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto load_kv = [&](const Item& it, int j) {
       const int s = g % S;
       if (g >= S && !wait_warp(&kv_empty[s], ((g / S) - 1) & 1)) return false;
-      if (elect_one()) {
+      if (leader) {
         mbar_arrive_expect_tx(&kv_full[s], 2 * Sh::kTileBytes);
 #pragma unroll
         for (int a = 0; a < Sh::kAtoms; ++a)
@@ -277,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           timed_out = true;
           break;
         }
-        if (elect_one()) {
+        if (leader) {
           mbar_arrive_expect_tx(&q_full[b], Sh::kTileBytes);
 #pragma unroll
           for (int a = 0; a < Sh::kAtoms; ++a)
@@ -296,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int q_tiles = it.n_k[1] > 0 ? 2 : 1;
-        if (elect_one()) {
+        if (leader) {
           mbar_arrive_expect_tx(q_full, q_tiles * Sh::kTileBytes);
           for (int t = 0; t < q_tiles; ++t)
 #pragma unroll
@@ -364,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                wait_warp(&kv_full[k_s % S], (k_s / S) & 1);
           if (!ok) break;
           tc_fence_after();
-          if (elect_one()) {
+          if (leader) {
             issue_qk(t, k_s % S);
             mma_commit(&s_full[t]);
             mma_commit(&q_empty[t]);
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok && k >= 2) ok = wait_warp(&o_free[t], ((k >> 1) - 1) & 1);
         if (!ok) break;
         tc_fence_after();
-        if (elect_one()) {
+        if (leader) {
           issue_pv(t, k % S, false);
           mma_commit(&o_full[t]);
           mma_commit(&kv_empty[k % S]);
@@ -415,10 +418,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (ok && j == 1 && o_done[t] > 0) ok = wait_warp(&o_free[t], (o_done[t] - 1) & 1);
               if (!ok) break;
               tc_fence_after();
-              if (elect_one()) issue_pv(t, (g - 1) % S, j > 1);
+              if (leader) issue_pv(t, (g - 1) % S, j > 1);
               __syncwarp();
             }
-            if (elect_one()) {
+            if (leader) {
               if (j < it.n_k[t]) {
                 issue_qk(t, g % S);
                 mma_commit(&s_full[t]);
@@ -430,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (j >= it.n_k[t]) ++o_done[t];
           }
           if (!ok) break;
-          if (elect_one()) {
+          if (leader) {
             if (j == it.n_max - 1) mma_commit(q_empty);
             if (j > 0) mma_commit(&kv_empty[(g - 1) % S]);
           }
