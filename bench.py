@@ -2005,6 +2005,13 @@ def e2e_pipeline(torch, dist, work, world: int, first: int, steps: int) -> dict:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
+    # As for the device-resident replay: untimed replays keep the GPU's clocks
+    # up to the synchronize (and barrier) that opens the timed one.
+    for _ in range(2):
+        graph.replay()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     start.record(stream)
     graph.replay()
@@ -2159,14 +2166,7 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     timed.replay()  # uploads the graph; untimed
     torch.cuda.synchronize()
     if world > 1:
-        # Ranks finish their captures at different times, and a GPU left idle
-        # while its rank waits drops its clocks: after this barrier every rank
-        # keeps its GPU busy with untimed replays through the barrier that
-        # opens the timed region (the collective waits for them), so the timed
-        # replay starts on a GPU that is already running.
-        dist.barrier()
-        for _ in range(3):
-            timed.replay()
+        dist.barrier()  # ranks finish their captures at different times
 
     uuid = getattr(torch.cuda.get_device_properties(device), "uuid", None)
     uuid = str(uuid) if uuid else None
@@ -2174,8 +2174,15 @@ def measure(args, work, torch, dist, device, rank: int, world: int, steps: int, 
     # ---- timed region: exactly K steps, one graph replay, inputs in HBM ----
     start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(uuid) as clocks:
+        # A GPU left idle (a rank waiting for the others, the clock sampler
+        # starting) drops its clocks, and a timed replay begun on it ran up to
+        # 20 % slow. So untimed replays keep the GPU running up to the
+        # synchronize (and, with several ranks, the barrier, whose collective
+        # runs after them) that opens the timed region.
+        for _ in range(3):
+            timed.replay()
         if world > 1:
-            dist.barrier()  # its collective runs after this rank's queued replays
+            dist.barrier()
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed")
         start_ev.record(stream)
