@@ -537,6 +537,9 @@ int encoder_attention_tc(int batch, int heads, int length, const void* q, const 
                                                  kSmemBytes),
                             "cudaFuncSetAttribute(encoder attention)"))
       return rc;
+    if (int rc = check_launch_registers(encoder_attention_tc_kernel, kLaunchRegs,
+                                        "encoder attention"))
+      return rc;
     prepared_device = device;
   }
   const int q_pairs = (length + 2 * kRows - 1) / (2 * kRows);

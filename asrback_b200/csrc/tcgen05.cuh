@@ -306,6 +306,21 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major)
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// Refuses a kernel whose compiled register count per thread is below the
+// one its setmaxnreg split was sized for: the pool would then be smaller than
+// the acquiring warpgroups' total, and their setmaxnreg.inc would wait for
+// registers that never come.
+template <typename Kernel>
+int check_launch_registers(Kernel kernel, int need, const char* what) {
+  cudaFuncAttributes attr;
+  if (int rc = check_cuda(cudaFuncGetAttributes(&attr, kernel), "cudaFuncGetAttributes")) return rc;
+  if (attr.numRegs < need)
+    return fail(ASRBACK_ERR_CUDA,
+                "%s: built with %d registers per thread, its register split needs %d", what,
+                attr.numRegs, need);
+  return ASRBACK_OK;
+}
+
 // Driver entry point cuTensorMapEncodeTiled, looked up once.
 inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(int* rc) {
   static std::mutex lock;

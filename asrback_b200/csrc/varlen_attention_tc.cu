@@ -679,6 +679,7 @@ int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmemBytes),
             "cudaFuncSetAttribute(varlen attention)"))
       return rc;
+    if (int rc = check_launch_registers(kernel, kLaunchRegs, "varlen attention")) return rc;
     prepared_device = device;
   }
   // Persistent: one CTA per SM (512 TMEM columns each), at most one per item.
