@@ -30,7 +30,7 @@
 //               so that each store instruction writes whole 128-byte rows.
 // TMEM of query tile t: S_t [256t, 256t+128), the softmax writing P_t (packed
 // bf16 pairs) over its first 64 columns, and O_t [256t+128, 256t+128+D).
-// Per key tile j the MMA lane issues P_t(j-1) V, then S_t(j) into the same
+// Per key tile j the MMA warp issues P_t(j-1) V, then S_t(j) into the same
 // columns (the tensor core runs one thread's MMAs in order), so S_t(j)'s
 // completion also means O_t is idle: the lazy rescale (P uses a stale max
 // until a tile's max exceeds it by more than 8 in log2 units) needs no wait.
@@ -41,7 +41,7 @@
 // Single-tile mode (every segment at most 128 tokens, e.g. the audio windows):
 // an item is one (segment, query head), one query tile and one key tile. Item
 // k uses Q buffer, TMEM S/O columns and softmax warpgroup k & 1 (those of
-// query tile t = k & 1 above), and the MMA lane issues S(k + 1) before
+// query tile t = k & 1 above), and the MMA warp issues S(k + 1) before
 // P(k) V(k), so item k+1's S runs under item k's softmax and item k's
 // epilogue under item k+1's softmax.
 #include <algorithm>
@@ -69,7 +69,7 @@ static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs,
 constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;
 constexpr int kItemSlots = 8;        // entries of the shared-memory item ring
-constexpr int kItemReaders = 2 + 8;  // TMA lane, MMA lane, 8 softmax warps
+constexpr int kItemReaders = 2 + 8;  // TMA warp, MMA warp, 8 softmax warps
 constexpr int kStageRowBytes = 128;  // epilogue staging: 64 bf16 columns per row
 constexpr int kStageWarpBytes = 32 * kStageRowBytes;
 
@@ -209,17 +209,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool timed_out = false;
 
-  // Entry n of the CTA's item list, for a role run by one lane (`warp_wide`
-  // false) or a whole warp; false if the wait ran out. Every reader releases
-  // every entry, the end-of-list entry (n_max 0) included.
-  auto read_item = [&](int n, Item& it, bool warp_wide) {
+  // Entry n of the CTA's item list, read by a whole warp; false if the wait
+  // ran out. Every reader warp releases every entry, the end-of-list entry
+  // (n_max 0) included.
+  auto read_item = [&](int n, Item& it) {
     const int e = n % kItemSlots;
-    bool ok = mbar_wait_bounded(&item_full[e], (n / kItemSlots) & 1);
-    if (warp_wide) ok = __all_sync(0xffffffffu, ok);
-    if (!ok) return false;
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&item_full[e], (n / kItemSlots) & 1)))
+      return false;
     it = ring[e];
-    if (warp_wide) __syncwarp();
-    if (!warp_wide || lane == 0) mbar_arrive(&item_empty[e]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&item_empty[e]);
     return true;
   };
 
@@ -267,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     for (int n = 0;; ++n) {
       Item it;
-      if (!read_item(n, it, true)) {
+      if (!read_item(n, it)) {
         timed_out = true;
         break;
       }
@@ -356,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; ok; ++k) {
         while (more && k_s < k + 2) {
           Item it;
-          ok = read_item(k_s, it, true);
+          ok = read_item(k_s, it);
           if (!ok) break;
           if (it.n_max == 0) {
             more = false;
@@ -394,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int o_done[2] = {0, 0};  // items whose O_t is final (o_full commits)
       for (int n = 0; ok; ++n) {
         Item it;
-        ok = read_item(n, it, true);
+        ok = read_item(n, it);
         if (!ok || it.n_max == 0) break;
         ok = wait_warp(q_full, n & 1);
         // Step j: for each query tile still reading keys, P_t(j-1) V(j-1)
@@ -554,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     for (int n = 0; ok; ++n) {
       Item it;
-      ok = read_item(n, it, true);
+      ok = read_item(n, it);
       if (!ok || it.n_max == 0) break;
       if (kSingle ? ((n & 1) != t) : it.n_k[t] == 0) continue;
       const int tile = kSingle ? 0 : t;
