@@ -51,6 +51,12 @@ enum DecodeMode { kWhisperSelf = 0, kWhisperCross = 1, kQwen3 = 2 };
 
 constexpr int kMaxSplits = 64;
 
+// prefix_cross_tc.cu: the tensor-core prompt-pass cross-attention.
+int whisper_cross_prefix_tc(int windows, int tokens, int heads, int length, const void* q,
+                            int64_t q_st, int64_t q_sh, const void* k, const void* v,
+                            int64_t c_sb, int64_t c_sh, void* out, int64_t o_st, int64_t o_sh,
+                            float scale, int32_t* status, cudaStream_t stream);
+
 struct DecodeParams {
   // query (Whisper): element (b, h, d) at q[b*q_sb + h*q_sh + d]
   const void* q;
@@ -1021,6 +1027,15 @@ int check_strides_aligned(int dtype, std::initializer_list<int64_t> strides) {
   return ASRBACK_OK;
 }
 
+// The tensor-core prompt-pass cross-attention (prefix_cross_tc.cu), used for
+// bf16 prompt passes of at most 128 tokens unless ASRBACK_PREFIX_TC=0 (A/B
+// timing; read at every call so that one process can compare both).
+constexpr int kPrefixTcMaxTokens = 128;
+bool prefix_tc_enabled() {
+  const char* env = std::getenv("ASRBACK_PREFIX_TC");
+  return !(env && env[0] == '0');
+}
+
 int whisper_common(int dtype, int batch, int heads, int head_dim, int length, const void* query,
                    int64_t q_sb, int64_t q_sh, const void* kc, const void* vc, int64_t c_sb,
                    int64_t c_sh, const void* out, int64_t o_sb, int64_t o_sh) {
@@ -1211,7 +1226,12 @@ int asrback_whisper_cross_attention_prefix(
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc;
-  if (dtype == ASRBACK_BF16 && tokens >= kPrefixTokens) {
+  if (dtype == ASRBACK_BF16 && tokens <= kPrefixTcMaxTokens && prefix_tc_enabled()) {
+    rc = whisper_cross_prefix_tc(windows, tokens, heads, length, query, q_stride_token,
+                                 q_stride_head, key_cache, value_cache, cache_stride_batch,
+                                 cache_stride_head, out, out_stride_token, out_stride_head, scale,
+                                 status, s);
+  } else if (dtype == ASRBACK_BF16 && tokens >= kPrefixTokens) {
     // kPrefixTokens tokens of a window per CTA: each staged key serves them all.
     using C = WhisperCrossPrefixBf16;
     const int rows = windows * ((tokens + kPrefixTokens - 1) / kPrefixTokens);

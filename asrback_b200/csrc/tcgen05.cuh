@@ -64,6 +64,13 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
                : "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy accesses of the same memory (TMA writes, tcgen05.mma operand
+// reads).
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

@@ -210,6 +210,32 @@ def test_whisper_prefix_random(tag, batch, tokens, bucket):
     assert attention.read_status() == 0
 
 
+@pytest.mark.parametrize("windows,tokens,length", [(1, 1, 1500), (3, 4, 1500), (2, 31, 1500),
+                                                    (5, 32, 1500), (2, 33, 1500), (8, 100, 1500),
+                                                    (2, 128, 1500), (4, 7, 200), (1, 4, 128)])
+def test_whisper_cross_prefix_tensor_core(windows, tokens, length, monkeypatch):
+    """The tensor-core prompt-pass cross-attention (bf16, up to 128 tokens per
+    window: one, two, three or four softmax warps) against the oracle and the
+    CUDA-core prefix kernel, over the whole cache, over a view of the first
+    `length` frames of a longer one (keys past it never read), and with a last
+    key tile that ends inside or at the tile."""
+    gen = torch.Generator().manual_seed(windows * 1000 + tokens + length)
+    heads, dim, frames = 20, 64, 1500
+    ck = _rand(gen, (windows, heads, frames, dim), torch.bfloat16).to(DEV)
+    cv = _rand(gen, (windows, heads, frames, dim), torch.bfloat16).to(DEV)
+    x = _rand(gen, (windows, tokens, heads * dim), torch.bfloat16).to(DEV)
+    query = x.view(windows, tokens, heads, dim).transpose(1, 2)
+    monkeypatch.setenv("ASRBACK_PREFIX_TC", "1")
+    got = attention.whisper_cross_attention_prefix(query, ck[:, :, :length], cv[:, :, :length])
+    monkeypatch.setenv("ASRBACK_PREFIX_TC", "0")
+    old = attention.whisper_cross_attention_prefix(query, ck[:, :, :length], cv[:, :, :length])
+    want = oracle.whisper_cross_attention_prefix(host(query), host(ck[:, :, :length]),
+                                                 host(cv[:, :, :length]))
+    np.testing.assert_allclose(_heads_of(got, tokens, heads, dim), want, atol=2e-2, rtol=0)
+    np.testing.assert_allclose(host(got), host(old), atol=2e-2, rtol=0)
+    assert attention.read_status() == 0
+
+
 def test_whisper_prefix_rejects_bad_shapes():
     q = torch.zeros(2, 20, 4, 64, device=DEV, dtype=torch.bfloat16)
     kc = torch.zeros(2, 20, 448, 64, device=DEV, dtype=torch.bfloat16)
