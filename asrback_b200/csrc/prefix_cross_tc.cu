@@ -50,7 +50,9 @@ constexpr float kRescaleThreshold = 8.0f;
 constexpr int kOffQ = 0;  // two Q buffers
 constexpr int kOffK = 2 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffBar = kOffV + kStages * kTileBytes;
+// Small-prompt softmax staging: [16][128] float scores, [16][64] bf16 pairs.
+constexpr int kOffStage = kOffV + kStages * kTileBytes;
+constexpr int kOffBar = kOffStage + 16 * kKeys * 4 + 16 * (kKeys / 2) * 4;
 // barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], s_full[2],
 // p_full[2], o_full, o_final, o_free
 constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 + 2 + 3;
@@ -69,6 +71,9 @@ struct PrefixParams {
   int32_t* status;
 };
 
+// kPad > 0: prompts of at most kPad (a power of two up to 16) rows, whose
+// softmax shares each row's work out over 32 / kPad lanes; 0: a row per lane.
+template <int kPad>
 __global__ void __launch_bounds__(kThreads, 1)
     prefix_cross_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                            const __grid_constant__ CUtensorMap map_k,
@@ -244,6 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;  // prompt row of this thread (zeros past P)
     const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tO = tmem + lane_bits + kColO;
+    float* s_rows = reinterpret_cast<float*>(smem + kOffStage);  // [kPad][128] scores
+    uint32_t* p_rows = reinterpret_cast<uint32_t*>(smem + kOffStage + 16 * kKeys * 4);
     bool ok = true;
     for (int li = 0; li < n_items && ok; ++li) {
       float m_used = -INFINITY, l = 0.f;
@@ -257,70 +264,159 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int valid = min(kKeys, p.length - j * kKeys);
         float v[kKeys];
         tmem_ld128(tS, v);
-        if (valid < kKeys) {
+        if constexpr (kPad > 0) {
+          // Small prompt: each row's 128 scores go through shared memory to
+          // its G lanes, C columns each, so the exponentials are shared out.
+          // Row r is held by lanes r * G .. r * G + G - 1 (its max, sum and
+          // running state replicated in them); lane t < kPad holds TMEM row t.
+          constexpr int G = 32 / kPad, C = kKeys / G;
+          const int r = lane / G, part = lane % G;
+          if (lane < kPad) {
 #pragma unroll
-          for (int i = 0; i < kKeys; ++i)
-            if (i >= valid) v[i] = -INFINITY;
-        }
-        float acc[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
-#pragma unroll
-        for (int i = 16; i < kKeys; i += 16)
-#pragma unroll
-          for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
-        const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
-                               fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
-        const float m_tile = mx * p.scale_log2;
-        const bool move = m_tile > m_used + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, move)) {
-          const float m_new = move ? m_tile : m_used;
-          if (j > 0) {
-            // O must be idle: P(J-1) V done (the S just read was issued after
-            // P(J-2) V, not after P(J-1) V).
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(o_full, (li * (n_k - 1) + j - 1) & 1));
-            if (!ok) break;
-            tc_fence_after();
-            const float alpha = move ? fast_exp2(m_used - m_new) : 1.f;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              float o[16];
-              tmem_ld16(tO + 16 * c, o);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) o[i] *= alpha;
-              tmem_st16f(tO + 16 * c, o);
-            }
-            tmem_wait_st();
-            l *= alpha;
+            for (int i = 0; i < kKeys; i += 4)
+              *reinterpret_cast<float4*>(s_rows + lane * kKeys + i) =
+                  make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
           }
-          m_used = m_new;
-        }
-        const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
-        const uint64_t neg_m2 = pack2(-m_used, -m_used);
-        uint64_t sum2[4];
+          __syncwarp();
+          float x[C];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
+          for (int i = 0; i < C; i += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(s_rows + r * kKeys + part * C + i);
+            x[i] = part * C + i < valid ? f.x : -INFINITY;
+            x[i + 1] = part * C + i + 1 < valid ? f.y : -INFINITY;
+            x[i + 2] = part * C + i + 2 < valid ? f.z : -INFINITY;
+            x[i + 3] = part * C + i + 3 < valid ? f.w : -INFINITY;
+          }
+          float mx = x[0];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+          for (int i = 1; i < C; ++i) mx = fmaxf(mx, x[i]);
+#pragma unroll
+          for (int off = G / 2; off >= 1; off >>= 1)
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          const float m_tile = mx * p.scale_log2;
+          const bool move = m_tile > m_used + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, move)) {
+            const float m_new = move ? m_tile : m_used;
+            if (j > 0) {
+              ok = __all_sync(0xffffffffu,
+                              mbar_wait_bounded(o_full, (li * (n_k - 1) + j - 1) & 1));
+              if (!ok) break;
+              tc_fence_after();
+              const float alpha_row = move ? fast_exp2(m_used - m_new) : 1.f;
+              // TMEM row t's factor, from the first lane of row t's group.
+              const float a = __shfl_sync(0xffffffffu, alpha_row, lane < kPad ? lane * G : lane);
+              const float alpha = lane < kPad ? a : 1.f;
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                float o[16];
+                tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] *= alpha;
+                tmem_st16f(tO + 16 * c, o);
+              }
+              tmem_wait_st();
+              l *= alpha_row;
+            }
+            m_used = m_new;
+          }
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < C; i += 2) {
+            const float p0 = fast_exp2(fmaf(x[i], p.scale_log2, -m_used));
+            const float p1 = fast_exp2(fmaf(x[i + 1], p.scale_log2, -m_used));
+            sum += p0 + p1;
+            p_rows[r * (kKeys / 2) + (part * C + i) / 2] = bf16x2(p0, p1);
+          }
+#pragma unroll
+          for (int off = G / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+          l += sum;
+          __syncwarp();
+          // TMEM row t takes row t's P (rows past kPad: zeros).
           uint32_t packed[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = 64 * half + 2 * i;
-            float x0, x1;
-            unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
-            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-            sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
-            packed[i] = bf16x2(p0, p1);
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const uint4 u = lane < kPad ? *reinterpret_cast<const uint4*>(
+                                                p_rows + lane * (kKeys / 2) + 32 * half + i)
+                                          : make_uint4(0u, 0u, 0u, 0u);
+              packed[i] = u.x;
+              packed[i + 1] = u.y;
+              packed[i + 2] = u.z;
+              packed[i + 3] = u.w;
+            }
+            tmem_st32u(tS + 32 * half, packed);
           }
-          tmem_st32u(tS + 32 * half, packed);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[buf]);
+        } else {
+          if (valid < kKeys) {
+  #pragma unroll
+            for (int i = 0; i < kKeys; ++i)
+              if (i >= valid) v[i] = -INFINITY;
+          }
+          float acc[8];
+  #pragma unroll
+          for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
+  #pragma unroll
+          for (int i = 16; i < kKeys; i += 16)
+  #pragma unroll
+            for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
+          const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
+                                 fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
+          const float m_tile = mx * p.scale_log2;
+          const bool move = m_tile > m_used + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, move)) {
+            const float m_new = move ? m_tile : m_used;
+            if (j > 0) {
+              // O must be idle: P(J-1) V done (the S just read was issued after
+              // P(J-2) V, not after P(J-1) V).
+              ok = __all_sync(0xffffffffu, mbar_wait_bounded(o_full, (li * (n_k - 1) + j - 1) & 1));
+              if (!ok) break;
+              tc_fence_after();
+              const float alpha = move ? fast_exp2(m_used - m_new) : 1.f;
+  #pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                float o[16];
+                tmem_ld16(tO + 16 * c, o);
+  #pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] *= alpha;
+                tmem_st16f(tO + 16 * c, o);
+              }
+              tmem_wait_st();
+              l *= alpha;
+            }
+            m_used = m_new;
+          }
+          const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
+          const uint64_t neg_m2 = pack2(-m_used, -m_used);
+          uint64_t sum2[4];
+  #pragma unroll
+          for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
+  #pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t packed[32];
+  #pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = 64 * half + 2 * i;
+              float x0, x1;
+              unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
+              const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+              sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
+              packed[i] = bf16x2(p0, p1);
+            }
+            tmem_st32u(tS + 32 * half, packed);
+          }
+          float lo0, hi0;
+          unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
+          l += lo0 + hi0;
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[buf]);
         }
-        float lo0, hi0;
-        unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
-        l += lo0 + hi0;
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[buf]);
       }
       if (!ok) break;
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(o_final, li & 1));
@@ -328,7 +424,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int index = item_index(li);
       const int h = index % p.heads, w = index / p.heads;
-      const float inv = 1.f / l;
+      // Small prompt: row t's sum is held by the lanes of its group.
+      const float l_row =
+          kPad > 0 ? __shfl_sync(0xffffffffu, l, lane < kPad ? lane * (32 / (kPad > 0 ? kPad : 1))
+                                                              : lane)
+                   : l;
+      const float inv = 1.f / l_row;
       const int64_t off = row < p.tokens ? static_cast<int64_t>(w * p.tokens + row) * p.o_st +
                                                static_cast<int64_t>(h) * p.o_sh
                                          : 0;
@@ -408,6 +509,26 @@ int make_maps(CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv, const void* q, 
   return ASRBACK_OK;
 }
 
+template <int kPad>
+int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+           const PrefixParams& p, cudaStream_t stream) {
+  auto kernel = prefix_cross_tc_kernel<kPad>;
+  static thread_local int prepared_device = -1;
+  int device = 0;
+  if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
+  if (prepared_device != device) {
+    if (int rc = check_cuda(
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+            "cudaFuncSetAttribute(prompt-pass cross attention)"))
+      return rc;
+    prepared_device = device;
+  }
+  // Persistent: one CTA per SM (512 TMEM columns each), at most one per item.
+  const int ctas = p.items < sm_count() ? p.items : sm_count();
+  return launch_pdl(kernel, dim3(ctas), dim3(kThreads), kSmemBytes, stream,
+                    "prompt-pass cross attention (tensor core) launch", mq, mk, mv, p);
+}
+
 }  // namespace
 
 // Launches the tensor-core prompt-pass cross-attention; arguments already
@@ -421,23 +542,15 @@ int whisper_cross_prefix_tc(int windows, int tokens, int heads, int length, cons
   if (int rc = make_maps(&mq, &mk, &mv, q, windows * tokens, heads, tokens, q_st, q_sh, k, v,
                          windows, length, c_sb, c_sh))
     return rc;
-  static thread_local int prepared_device = -1;
-  int device = 0;
-  if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
-  if (prepared_device != device) {
-    if (int rc = check_cuda(cudaFuncSetAttribute(prefix_cross_tc_kernel,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 kSmemBytes),
-                            "cudaFuncSetAttribute(prompt-pass cross attention)"))
-      return rc;
-    prepared_device = device;
-  }
   PrefixParams p{out,     o_st,  o_sh, tokens, length, heads, windows * heads,
                  (tokens + 31) / 32, scale * 1.4426950408889634f, status};
-  // Persistent: one CTA per SM (512 TMEM columns each), at most one per item.
-  const int ctas = p.items < sm_count() ? p.items : sm_count();
-  return launch_pdl(prefix_cross_tc_kernel, dim3(ctas), dim3(kThreads), kSmemBytes, stream,
-                    "prompt-pass cross attention (tensor core) launch", mq, mk, mv, p);
+  // Prompts of up to 16 rows share each row's softmax out over the warp.
+  if (tokens <= 1) return launch<1>(mq, mk, mv, p, stream);
+  if (tokens <= 2) return launch<2>(mq, mk, mv, p, stream);
+  if (tokens <= 4) return launch<4>(mq, mk, mv, p, stream);
+  if (tokens <= 8) return launch<8>(mq, mk, mv, p, stream);
+  if (tokens <= 16) return launch<16>(mq, mk, mv, p, stream);
+  return launch<0>(mq, mk, mv, p, stream);
 }
 
 }  // namespace asrback

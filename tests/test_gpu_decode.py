@@ -212,7 +212,8 @@ def test_whisper_prefix_random(tag, batch, tokens, bucket):
 
 @pytest.mark.parametrize("windows,tokens,length", [(1, 1, 1500), (3, 4, 1500), (2, 31, 1500),
                                                     (5, 32, 1500), (2, 33, 1500), (8, 100, 1500),
-                                                    (2, 128, 1500), (4, 7, 200), (1, 4, 128)])
+                                                    (2, 128, 1500), (4, 7, 200), (1, 4, 128),
+                                                    (3, 2, 1500), (2, 12, 700), (6, 16, 1500)])
 def test_whisper_cross_prefix_tensor_core(windows, tokens, length, monkeypatch):
     """The tensor-core prompt-pass cross-attention (bf16, up to 128 tokens per
     window: one, two, three or four softmax warps) against the oracle and the
