@@ -181,8 +181,10 @@ ASRBACK_API int asrback_whisper_self_attention_prefix(
  * as in asrback_whisper_self_attention_prefix, caches as in
  * asrback_whisper_cross_attention_step; workspace
  * asrback_whisper_prefix_workspace_bytes(windows, tokens, heads, head_dim,
- * length). In bf16, from 4 tokens up, each CTA takes 4 tokens of a window, so
- * that every key staged in shared memory serves all 4 queries.
+ * length). In bf16 with at most 128 tokens the call runs on the tensor cores
+ * (a window's tokens are one query tile per head; no workspace used); past
+ * 128 tokens each CTA takes 4 tokens of a window, so that every key staged in
+ * shared memory serves all 4 queries; in float32 a CTA takes one token.
  */
 ASRBACK_API int asrback_whisper_cross_attention_prefix(
     int dtype, int windows, int tokens, int heads, int head_dim, int length,
