@@ -11,22 +11,26 @@
 // window's key tiles, so the scores and P V run on the tensor cores and the
 // launch is bound by reading the keys and values once.
 //
-// The structure follows the encoder kernel with one query tile per item:
+// Two items run at once, one per slot x = 0, 1 (a CTA's items 2i and 2i + 1;
+// with an odd count the last runs alone), each slot with its own Q buffer, S
+// buffer, O accumulator and softmax warps, so that one slot's softmax runs
+// while the other's is waiting for its scores. Roles:
 //   warp 0      TMA: each item's P query rows (3-D map over the prompt rows)
-//               into one of two Q buffers whose other rows stay zero, and the
-//               window's K/V tiles of 128 keys into a 4-stage ring that runs on
-//               across items (4-D maps over the cache's (window, head,
+//               into its slot's Q buffer, whose other rows stay zero, and the
+//               pair's K/V tiles of 128 keys, the two slots' tiles alternating,
+//               into a 4-stage ring (4-D maps over the cache's (window, head,
 //               position, 64) layout; rows past the window read as zeros);
 //   warp 1      allocates TMEM and issues the MMAs (warp-wide loop, one
-//               elected lane): S(J) = Q K(J)^T into S buffer J & 1, then, per
-//               key tile J, O (+)= P(J) V(J) and S(J + 2) into the buffer that
-//               P(J) V has read (the tensor core runs one thread's MMAs in
-//               order), so S(J + 1) is computed while the softmax of J runs;
-//   warps 4-7   softmax and output of query rows 32q .. 32q + 31 (thread =
-//               TMEM lane = row); only the ceil(P / 32) warps that hold prompt
-//               rows run, and the barriers they feed count them alone.
-// Key tiles are numbered J over all of a CTA's items. TMEM: S buffers [0,128)
-// and [128,256) (P written over their first 64 columns), O [256,320).
+//               elected lane), in the ring's order: per key tile of a slot,
+//               O_x (+)= P_x V then that slot's next S_x = Q_x K^T into the
+//               buffer P_x V has read (the tensor core runs one thread's MMAs
+//               in order);
+//   warps 4-7   softmax and output of slot 0, warps 8-11 of slot 1: query rows
+//               32q .. 32q + 31 (thread = TMEM lane = row); only the
+//               ceil(P / 32) warps of a slot that hold prompt rows run, and the
+//               barriers they feed count them alone.
+// TMEM: slot x's S at [192x, 192x + 128) (P written over its first 64
+// columns), its O at [192x + 128, 192x + 192).
 // The running max is rescaled lazily (by more than 8 in log2 units, once the
 // previous P V is done), as in the encoder kernel.
 #include "tcgen05.cuh"
@@ -42,20 +46,31 @@ constexpr int kKeys = 128;  // keys per tile
 constexpr int kDim = 64;
 constexpr int kStages = 4;
 constexpr int kTileBytes = kRows * kDim * 2;  // 16 KB: a Q, K or V tile
-constexpr int kThreads = 8 * 32;              // warps 0-3 control (2, 3 idle), 4-7 softmax
-constexpr int kTmemCols = 512;                // 320 used; allocations are powers of two
-constexpr int kColO = 256;
+constexpr int kThreads = 12 * 32;             // warps 0-3 control (2, 3 idle), 4-11 softmax
+constexpr int kTmemCols = 512;                // 384 used; allocations are powers of two
+__host__ __device__ constexpr int col_s(int x) { return 192 * x; }
+__host__ __device__ constexpr int col_o(int x) { return 192 * x + 128; }
 constexpr float kRescaleThreshold = 8.0f;
+// Registers per thread: 168 at launch (384 x 168 = 64512); the control
+// warpgroup keeps 56, the two softmax warpgroups take 224.
+constexpr int kLaunchRegs = 168;
+constexpr int kControlRegs = 56;
+constexpr int kSoftmaxRegs = 224;
+static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch's register pool");
 
-constexpr int kOffQ = 0;  // two Q buffers
+constexpr int kOffQ = 0;  // a Q buffer per slot
 constexpr int kOffK = 2 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
-// Small-prompt softmax staging: [16][128] float scores, [16][64] bf16 pairs.
+// Small-prompt softmax staging per slot: [8][128] float scores, [8][64] bf16
+// pairs.
+constexpr int kMaxPad = 8;
+constexpr int kStageBytes = kMaxPad * kKeys * 4 + kMaxPad * (kKeys / 2) * 4;
 constexpr int kOffStage = kOffV + kStages * kTileBytes;
-constexpr int kOffBar = kOffStage + 16 * kKeys * 4 + 16 * (kKeys / 2) * 4;
-// barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], s_full[2],
-// p_full[2], o_full, o_final, o_free
-constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 + 2 + 3;
+constexpr int kOffBar = kOffStage + 2 * kStageBytes;
+// barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], then per slot
+// s_full[2], p_full[2], o_full[2], o_final[2], o_free[2]
+constexpr int kNumBars = 2 + 2 + 2 * kStages + 5 * 2;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
 
@@ -66,12 +81,13 @@ struct PrefixParams {
   int length;          // keys per window
   int heads;
   int items;           // windows * heads
-  int softmax_warps;   // ceil(P / 32)
+  int softmax_warps;   // per slot: ceil(P / 32)
+  int row1;            // first query-tile row of slot 1's prompt (0, 32 or 64)
   float scale_log2;
   int32_t* status;
 };
 
-// kPad > 0: prompts of at most kPad (a power of two up to 16) rows, whose
+// kPad > 0: prompts of at most kPad (a power of two up to kMaxPad) rows, whose
 // softmax shares each row's work out over 32 / kPad lanes; 0: a row per lane.
 template <int kPad>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -79,19 +95,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                            const __grid_constant__ CUtensorMap map_k,
                            const __grid_constant__ CUtensorMap map_v,
                            const __grid_constant__ PrefixParams p) {
+  static_assert(kPad <= kMaxPad, "small-prompt staging holds kMaxPad rows");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars;  // [Q buffer]
+  uint64_t* q_full = bars;  // [slot]
   uint64_t* q_empty = q_full + 2;
   uint64_t* kv_full = q_empty + 2;  // K and V of a ring slot
   uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;  // [S buffer]
-  uint64_t* p_full = s_full + 2;          // [S buffer]
+  uint64_t* s_full = kv_empty + kStages;  // [slot]
+  uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
-  uint64_t* o_final = o_full + 1;
-  uint64_t* o_free = o_final + 1;
+  uint64_t* o_final = o_full + 2;
+  uint64_t* o_free = o_final + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -100,29 +117,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_items = p.items > (int)blockIdx.x
                           ? (p.items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
                           : 0;
-  const int total = n_items * n_k;
+  const int n_pairs = (n_items + 1) / 2;
+  const int total = n_items * n_k;  // key tiles over all items
   auto item_index = [&](int li) { return (int)blockIdx.x + li * (int)gridDim.x; };
+  // Items of pair i: 2i (slot 0) and 2i + 1 (slot 1, when there is one).
+  auto pair_size = [&](int i) { return 2 * i + 1 < n_items ? 2 : 1; };
+  // Ring index of key tile j of pair i's slot x: the two slots' tiles alternate.
+  auto ring_index = [&](int i, int j, int x) {
+    return 2 * n_k * i + (pair_size(i) == 2 ? 2 * j + x : j);
+  };
 
   // The Q buffers' rows past the prompt stay zero: TMA writes rows < P only.
   for (int i = threadIdx.x; i < 2 * kTileBytes / 16; i += kThreads)
     reinterpret_cast<uint4*>(smem + kOffQ)[i] = make_uint4(0u, 0u, 0u, 0u);
   fence_proxy_async();  // the generic-proxy zeros before the tensor core's reads
   if (threadIdx.x == 0) {
-    for (int q = 0; q < 2; ++q) {
-      mbar_init(&q_full[q], 1);
-      mbar_init(&q_empty[q], 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&q_full[x], 1);
+      mbar_init(&q_empty[x], 1);
+      mbar_init(&s_full[x], 1);
+      mbar_init(&p_full[x], p.softmax_warps);  // one arrival per running softmax warp
+      mbar_init(&o_full[x], 1);
+      mbar_init(&o_final[x], 1);
+      mbar_init(&o_free[x], p.softmax_warps);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], p.softmax_warps);  // one arrival per running softmax warp
-    }
-    mbar_init(o_full, 1);
-    mbar_init(o_final, 1);
-    mbar_init(o_free, p.softmax_warps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -137,332 +159,352 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto wait_warp = [](uint64_t* bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
   };
-  // One lane per warp, elected once: a tcgen05.commit tracks the MMAs of its
-  // own thread, so the MMA warp's issues and commits all come from it.
-  const bool leader = elect_one();
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (leader) {
-      prefetch_tensormap(&map_q);
-      prefetch_tensormap(&map_k);
-      prefetch_tensormap(&map_v);
-    }
-    __syncwarp();
-    bool ok = true;
-    int g = 0;  // key tiles loaded (= J)
-    for (int li = 0; li < n_items && ok; ++li) {
-      const int index = item_index(li);
-      const int h = index % p.heads, w = index / p.heads;
-      const int qb = li & 1;
-      if (li >= 2) ok = wait_warp(&q_empty[qb], ((li >> 1) - 1) & 1);
-      if (!ok) break;
+  // Each warpgroup leaves through its own branch (status, fences, one
+  // CTA-wide named barrier, the TMEM release): a register budget is fixed per
+  // branch, so the branches never rejoin.
+  if (warp < 4) {
+    reg_release<kControlRegs>();
+    // One lane per warp, elected once: a tcgen05.commit tracks the MMAs of
+    // its own thread, so the MMA warp's issues and commits all come from it.
+    const bool leader = elect_one();
+    if (warp == 0) {
+      // ---------------- TMA producer ----------------
       if (leader) {
-        mbar_arrive_expect_tx(&q_full[qb], static_cast<uint32_t>(p.tokens * kDim * 2));
-        tma_load_3d(smem + kOffQ + qb * kTileBytes, &map_q, 0, h, w * p.tokens, &q_full[qb]);
+        prefetch_tensormap(&map_q);
+        prefetch_tensormap(&map_k);
+        prefetch_tensormap(&map_v);
       }
       __syncwarp();
-      for (int j = 0; j < n_k; ++j, ++g) {
-        const int s = g % kStages;
-        if (g >= kStages) ok = wait_warp(&kv_empty[s], ((g / kStages) - 1) & 1);
-        if (!ok) break;
-        if (leader) {
-          mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
-          tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, w, &kv_full[s]);
-          tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, w, &kv_full[s]);
-        }
-        __syncwarp();
-      }
-    }
-    timed_out = !ok;
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (total > 0) {
-      constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
-      constexpr uint32_t kIdescPV = idesc_bf16(kRows, kDim, true);
-      const uint64_t q_desc = sw128_desc(smem_addr(smem + kOffQ), 16, 1024);
-      const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
-      const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
-      constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4, kTile = kTileBytes >> 4;
       bool ok = true;
-      // Key tile X's position: item li (Q buffer li & 1), tile j in it, ring
-      // slot s and lap; stepped without branches.
-      struct Pos {
-        int li, j, s, lap;
-      };
-      auto advance = [&](Pos c) {
-        c.j = c.j + 1 == n_k ? 0 : c.j + 1;
-        c.li += c.j == 0 ? 1 : 0;
-        c.s = c.s + 1 == kStages ? 0 : c.s + 1;
-        c.lap += c.s == 0 ? 1 : 0;
-        return c;
-      };
-      // S(X) into buffer `buf`: waits for the K/V tile (one barrier for both;
-      // P V of the tile comes later in this stream) and, first of an item, for
-      // its Q. After the item's last S the Q buffer is free.
-      auto qk = [&](const Pos& c, int buf) {
-        const int qb = c.li & 1;
-        if (c.j == 0) ok = ok && wait_warp(&q_full[qb], (c.li >> 1) & 1);
-        ok = ok && wait_warp(&kv_full[c.s], c.lap & 1);
-        if (!ok) return;
-        tc_fence_after();
-        if (leader) {
-#pragma unroll
-          for (int k = 0; k < kDim / 16; ++k)
-            mma_ss(tmem + 128 * buf, q_desc + qb * kTile + k * kStepK,
-                   k_desc + c.s * kTile + k * kStepK, kIdescQK, k > 0);
-          mma_commit(&s_full[buf]);
-          if (c.j == n_k - 1) mma_commit(&q_empty[qb]);
+      int g = 0;  // key tiles loaded, in ring order
+      for (int i = 0; i < n_pairs && ok; ++i) {
+        const int ps = pair_size(i);
+        for (int x = 0; x < ps && ok; ++x) {
+          // Slot x's Q buffer is free once its previous item has issued its
+          // last S.
+          if (i >= 1) ok = wait_warp(&q_empty[x], (i - 1) & 1);
+          if (!ok) break;
+          const int index = item_index(2 * i + x);
+          const int h = index % p.heads, w = index / p.heads;
+          if (leader) {
+            mbar_arrive_expect_tx(&q_full[x], static_cast<uint32_t>(p.tokens * kDim * 2));
+            tma_load_3d(smem + kOffQ + x * kTileBytes + x * p.row1 * 128, &map_q, 0, h,
+                        w * p.tokens, &q_full[x]);
+          }
+          __syncwarp();
         }
-        __syncwarp();
-      };
-      Pos c0{0, 0, 0, 0};
-      Pos c2 = advance(advance(c0));
-      qk(c0, 0);
-      if (total > 1) qk(advance(c0), 1);
-      for (int J = 0; J < total && ok; ++J) {
-        const int buf = J & 1;
-        // O (+)= P(J) V(J) once the softmax has written P(J) (an item's first
-        // also once the previous item's output has been read out of O).
-        ok = ok && wait_warp(&p_full[buf], (J >> 1) & 1);
-        if (c0.j == 0 && c0.li > 0) ok = ok && wait_warp(o_free, (c0.li - 1) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        if (leader) {
-#pragma unroll
-          for (int k = 0; k < kKeys / 16; ++k)
-            mma_ts(tmem + kColO, tmem + 128 * buf + k * 8, v_desc + c0.s * kTile + k * kStepV,
-                   kIdescPV, (c0.j > 0 || k > 0));
-          mma_commit(c0.j + 1 < n_k ? o_full : o_final);
-          if (J + kStages < total) mma_commit(&kv_empty[c0.s]);
+        for (int j = 0; j < n_k && ok; ++j) {
+          for (int x = 0; x < ps; ++x, ++g) {
+            const int s = g % kStages;
+            if (g >= kStages) ok = wait_warp(&kv_empty[s], ((g / kStages) - 1) & 1);
+            if (!ok) break;
+            const int index = item_index(2 * i + x);
+            const int h = index % p.heads, w = index / p.heads;
+            if (leader) {
+              mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+              tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, w, &kv_full[s]);
+              tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, w, &kv_full[s]);
+            }
+            __syncwarp();
+          }
         }
-        __syncwarp();
-        if (J + 2 < total) qk(c2, buf);
-        c0 = advance(c0);
-        c2 = advance(c2);
       }
       timed_out = !ok;
+    } else if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      if (total > 0) {
+        constexpr uint32_t kIdescQK = idesc_bf16(kRows, kKeys, false);
+        constexpr uint32_t kIdescPV = idesc_bf16(kRows, kDim, true);
+        const uint64_t q_desc = sw128_desc(smem_addr(smem + kOffQ), 16, 1024);
+        const uint64_t k_desc = sw128_desc(smem_addr(smem + kOffK), 16, 1024);
+        const uint64_t v_desc = sw128_desc(smem_addr(smem + kOffV), kTileBytes, 1024);
+        constexpr uint64_t kStepK = 32 >> 4, kStepV = 2048 >> 4, kTile = kTileBytes >> 4;
+        bool ok = true;
+        // S_x of key tile j of pair i: waits for the K/V tile (one barrier
+        // for both; the tile's P V comes later in this stream) and, first of an
+        // item, for its Q. After the item's last S slot x's Q buffer is free.
+        auto qk = [&](int i, int j, int x) {
+          const int g = ring_index(i, j, x), s = g % kStages;
+          if (j == 0) ok = ok && wait_warp(&q_full[x], i & 1);
+          ok = ok && wait_warp(&kv_full[s], (g / kStages) & 1);
+          if (!ok) return;
+          tc_fence_after();
+          if (leader) {
+#pragma unroll
+            for (int k = 0; k < kDim / 16; ++k)
+              mma_ss(tmem + col_s(x), q_desc + x * kTile + k * kStepK,
+                     k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
+            mma_commit(&s_full[x]);
+            if (j == n_k - 1) mma_commit(&q_empty[x]);
+          }
+          __syncwarp();
+        };
+        for (int x = 0; x < pair_size(0); ++x) qk(0, 0, x);
+        for (int i = 0; i < n_pairs && ok; ++i) {
+          const int ps = pair_size(i);
+          for (int j = 0; j < n_k && ok; ++j) {
+            for (int x = 0; x < ps && ok; ++x) {
+              // O_x (+)= P_x V once the softmax has written P_x (an item's
+              // first also once the slot's previous output has been read).
+              const int t = i * n_k + j;  // slot x's key tiles so far
+              ok = ok && wait_warp(&p_full[x], t & 1);
+              if (j == 0 && i > 0) ok = ok && wait_warp(&o_free[x], (i - 1) & 1);
+              if (!ok) break;
+              tc_fence_after();
+              const int g = ring_index(i, j, x), s = g % kStages;
+              if (leader) {
+#pragma unroll
+                for (int k = 0; k < kKeys / 16; ++k)
+                  mma_ts(tmem + col_o(x), tmem + col_s(x) + k * 8,
+                         v_desc + s * kTile + k * kStepV, kIdescPV, (j > 0 || k > 0));
+                mma_commit(j + 1 < n_k ? &o_full[x] : &o_final[x]);
+                if (g + kStages < total) mma_commit(&kv_empty[s]);
+              }
+              __syncwarp();
+              // Slot x's next S, into the buffer this P V has read.
+              if (j + 1 < n_k) {
+                qk(i, j + 1, x);
+              } else if (2 * (i + 1) + x < n_items) {
+                qk(i + 1, 0, x);
+              }
+            }
+          }
+        }
+        timed_out = !ok;
+      }
     }
-  } else if (warp >= 4 && warp - 4 < p.softmax_warps) {
+    if (timed_out && p.status && lane == 0) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+    tc_fence_before();
+    named_sync(1, kThreads);
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, kTmemCols);
+    }
+  } else {
+    reg_acquire<kSoftmaxRegs>();
     // ---------------- softmax and output (one query row per thread) ----------------
+    const int slot = (warp - 4) >> 2;
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // prompt row of this thread (zeros past P)
-    const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tO = tmem + lane_bits + kColO;
-    float* s_rows = reinterpret_cast<float*>(smem + kOffStage);  // [kPad][128] scores
-    uint32_t* p_rows = reinterpret_cast<uint32_t*>(smem + kOffStage + 16 * kKeys * 4);
+    // Slot 1's prompt rows start at row1 of its tile (a lane quarter of
+    // their own for prompts up to 64 rows, so that the two slots' softmax
+    // warps run on different sub-partitions).
+    const int q0 = slot * p.row1 / 32;
     bool ok = true;
-    for (int li = 0; li < n_items && ok; ++li) {
-      float m_used = -INFINITY, l = 0.f;
-      for (int j = 0; j < n_k && ok; ++j) {
-        const int J = li * n_k + j;
-        const int buf = J & 1;
-        const uint32_t tS = tmem + lane_bits + 128 * buf;
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[buf], (J >> 1) & 1));
+    if (quarter >= q0 && quarter < q0 + p.softmax_warps) {
+      const int row = (quarter - q0) * 32 + lane;  // prompt row of this thread (zeros past P)
+      const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
+      const uint32_t tS = tmem + lane_bits + col_s(slot);
+      const uint32_t tO = tmem + lane_bits + col_o(slot);
+      float* s_rows = reinterpret_cast<float*>(smem + kOffStage + slot * kStageBytes);
+      uint32_t* p_rows =
+          reinterpret_cast<uint32_t*>(smem + kOffStage + slot * kStageBytes + kMaxPad * kKeys * 4);
+      for (int it = 0; ok && 2 * it + slot < n_items; ++it) {
+        float m_used = -INFINITY, l = 0.f;
+        for (int j = 0; j < n_k && ok; ++j) {
+          const int t = it * n_k + j;  // this slot's key tiles so far
+          ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[slot], t & 1));
+          if (!ok) break;
+          tc_fence_after();
+          const int valid = min(kKeys, p.length - j * kKeys);
+          float v[kKeys];
+          tmem_ld128(tS, v);
+          if constexpr (kPad > 0) {
+            // Small prompt: each row's 128 scores go through shared memory to
+            // its G lanes, C columns each, so the exponentials are shared out.
+            // Row r is held by lanes r * G .. r * G + G - 1 (its max, sum and
+            // running state replicated in them); lane t < kPad holds TMEM row t.
+            constexpr int G = 32 / kPad, C = kKeys / G;
+            const int r = lane / G, part = lane % G;
+            if (lane < kPad) {
+#pragma unroll
+              for (int i = 0; i < kKeys; i += 4)
+                *reinterpret_cast<float4*>(s_rows + lane * kKeys + i) =
+                    make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            }
+            __syncwarp();
+            float x[C];
+#pragma unroll
+            for (int i = 0; i < C; i += 4) {
+              const float4 f = *reinterpret_cast<const float4*>(s_rows + r * kKeys + part * C + i);
+              x[i] = part * C + i < valid ? f.x : -INFINITY;
+              x[i + 1] = part * C + i + 1 < valid ? f.y : -INFINITY;
+              x[i + 2] = part * C + i + 2 < valid ? f.z : -INFINITY;
+              x[i + 3] = part * C + i + 3 < valid ? f.w : -INFINITY;
+            }
+            float mx = x[0];
+#pragma unroll
+            for (int i = 1; i < C; ++i) mx = fmaxf(mx, x[i]);
+#pragma unroll
+            for (int off = G / 2; off >= 1; off >>= 1)
+              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_tile = mx * p.scale_log2;
+            const bool move = m_tile > m_used + kRescaleThreshold;
+            if (__any_sync(0xffffffffu, move)) {
+              const float m_new = move ? m_tile : m_used;
+              if (j > 0) {
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait_bounded(&o_full[slot], (it * (n_k - 1) + j - 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                const float alpha_row = move ? fast_exp2(m_used - m_new) : 1.f;
+                // TMEM row t's factor, from the first lane of row t's group.
+                const float a = __shfl_sync(0xffffffffu, alpha_row, lane < kPad ? lane * G : lane);
+                const float alpha = lane < kPad ? a : 1.f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  float o[16];
+                  tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) o[i] *= alpha;
+                  tmem_st16f(tO + 16 * c, o);
+                }
+                tmem_wait_st();
+                l *= alpha_row;
+              }
+              m_used = m_new;
+            }
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < C; i += 2) {
+              const float p0 = fast_exp2(fmaf(x[i], p.scale_log2, -m_used));
+              const float p1 = fast_exp2(fmaf(x[i + 1], p.scale_log2, -m_used));
+              sum += p0 + p1;
+              p_rows[r * (kKeys / 2) + (part * C + i) / 2] = bf16x2(p0, p1);
+            }
+#pragma unroll
+            for (int off = G / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            l += sum;
+            __syncwarp();
+            // TMEM row t takes row t's P (rows past kPad: zeros).
+            uint32_t packed[32];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4) {
+                const uint4 u = lane < kPad ? *reinterpret_cast<const uint4*>(
+                                                  p_rows + lane * (kKeys / 2) + 32 * half + i)
+                                            : make_uint4(0u, 0u, 0u, 0u);
+                packed[i] = u.x;
+                packed[i + 1] = u.y;
+                packed[i + 2] = u.z;
+                packed[i + 3] = u.w;
+              }
+              tmem_st32u(tS + 32 * half, packed);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[slot]);
+          } else {
+            if (valid < kKeys) {
+#pragma unroll
+              for (int i = 0; i < kKeys; ++i)
+                if (i >= valid) v[i] = -INFINITY;
+            }
+            float acc[8];
+#pragma unroll
+            for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
+#pragma unroll
+            for (int i = 16; i < kKeys; i += 16)
+#pragma unroll
+              for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
+            const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
+                                   fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
+            const float m_tile = mx * p.scale_log2;
+            const bool move = m_tile > m_used + kRescaleThreshold;
+            if (__any_sync(0xffffffffu, move)) {
+              const float m_new = move ? m_tile : m_used;
+              if (j > 0) {
+                // O must be idle: P(J-1) V done (the S just read was issued after
+                // P(J-2) V, not after P(J-1) V).
+                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&o_full[slot], (it * (n_k - 1) + j - 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                const float alpha = move ? fast_exp2(m_used - m_new) : 1.f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  float o[16];
+                  tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) o[i] *= alpha;
+                  tmem_st16f(tO + 16 * c, o);
+                }
+                tmem_wait_st();
+                l *= alpha;
+              }
+              m_used = m_new;
+            }
+            const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
+            const uint64_t neg_m2 = pack2(-m_used, -m_used);
+            uint64_t sum2[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              uint32_t packed[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int col = 64 * half + 2 * i;
+                float x0, x1;
+                unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
+                const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+                sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
+                packed[i] = bf16x2(p0, p1);
+              }
+              tmem_st32u(tS + 32 * half, packed);
+            }
+            float lo0, hi0;
+            unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
+            l += lo0 + hi0;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[slot]);
+          }
+        }
+        if (!ok) break;
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&o_final[slot], it & 1));
         if (!ok) break;
         tc_fence_after();
-        const int valid = min(kKeys, p.length - j * kKeys);
-        float v[kKeys];
-        tmem_ld128(tS, v);
-        if constexpr (kPad > 0) {
-          // Small prompt: each row's 128 scores go through shared memory to
-          // its G lanes, C columns each, so the exponentials are shared out.
-          // Row r is held by lanes r * G .. r * G + G - 1 (its max, sum and
-          // running state replicated in them); lane t < kPad holds TMEM row t.
-          constexpr int G = 32 / kPad, C = kKeys / G;
-          const int r = lane / G, part = lane % G;
-          if (lane < kPad) {
+        const int index = item_index(2 * it + slot);
+        const int h = index % p.heads, w = index / p.heads;
+        // Small prompt: row t's sum is held by the lanes of its group.
+        const float l_row =
+            kPad > 0 ? __shfl_sync(0xffffffffu, l, lane < kPad ? lane * (32 / (kPad > 0 ? kPad : 1))
+                                                                : lane)
+                     : l;
+        const float inv = 1.f / l_row;
+        const int64_t off = row < p.tokens ? static_cast<int64_t>(w * p.tokens + row) * p.o_st +
+                                                 static_cast<int64_t>(h) * p.o_sh
+                                           : 0;
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + off;
 #pragma unroll
-            for (int i = 0; i < kKeys; i += 4)
-              *reinterpret_cast<float4*>(s_rows + lane * kKeys + i) =
-                  make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          }
-          __syncwarp();
-          float x[C];
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          tmem_ld32(tO + 32 * c, o);
+          if (row < p.tokens) {
 #pragma unroll
-          for (int i = 0; i < C; i += 4) {
-            const float4 f = *reinterpret_cast<const float4*>(s_rows + r * kKeys + part * C + i);
-            x[i] = part * C + i < valid ? f.x : -INFINITY;
-            x[i + 1] = part * C + i + 1 < valid ? f.y : -INFINITY;
-            x[i + 2] = part * C + i + 2 < valid ? f.z : -INFINITY;
-            x[i + 3] = part * C + i + 3 < valid ? f.w : -INFINITY;
-          }
-          float mx = x[0];
-#pragma unroll
-          for (int i = 1; i < C; ++i) mx = fmaxf(mx, x[i]);
-#pragma unroll
-          for (int off = G / 2; off >= 1; off >>= 1)
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-          const float m_tile = mx * p.scale_log2;
-          const bool move = m_tile > m_used + kRescaleThreshold;
-          if (__any_sync(0xffffffffu, move)) {
-            const float m_new = move ? m_tile : m_used;
-            if (j > 0) {
-              ok = __all_sync(0xffffffffu,
-                              mbar_wait_bounded(o_full, (li * (n_k - 1) + j - 1) & 1));
-              if (!ok) break;
-              tc_fence_after();
-              const float alpha_row = move ? fast_exp2(m_used - m_new) : 1.f;
-              // TMEM row t's factor, from the first lane of row t's group.
-              const float a = __shfl_sync(0xffffffffu, alpha_row, lane < kPad ? lane * G : lane);
-              const float alpha = lane < kPad ? a : 1.f;
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                float o[16];
-                tmem_ld16(tO + 16 * c, o);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) o[i] *= alpha;
-                tmem_st16f(tO + 16 * c, o);
-              }
-              tmem_wait_st();
-              l *= alpha_row;
+            for (int i = 0; i < 32; i += 8) {
+              uint4 u;
+              u.x = bf16x2(o[i] * inv, o[i + 1] * inv);
+              u.y = bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+              u.z = bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+              u.w = bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+              *reinterpret_cast<uint4*>(out + 32 * c + i) = u;
             }
-            m_used = m_new;
-          }
-          float sum = 0.f;
-#pragma unroll
-          for (int i = 0; i < C; i += 2) {
-            const float p0 = fast_exp2(fmaf(x[i], p.scale_log2, -m_used));
-            const float p1 = fast_exp2(fmaf(x[i + 1], p.scale_log2, -m_used));
-            sum += p0 + p1;
-            p_rows[r * (kKeys / 2) + (part * C + i) / 2] = bf16x2(p0, p1);
-          }
-#pragma unroll
-          for (int off = G / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-          l += sum;
-          __syncwarp();
-          // TMEM row t takes row t's P (rows past kPad: zeros).
-          uint32_t packed[32];
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              const uint4 u = lane < kPad ? *reinterpret_cast<const uint4*>(
-                                                p_rows + lane * (kKeys / 2) + 32 * half + i)
-                                          : make_uint4(0u, 0u, 0u, 0u);
-              packed[i] = u.x;
-              packed[i + 1] = u.y;
-              packed[i + 2] = u.z;
-              packed[i + 3] = u.w;
-            }
-            tmem_st32u(tS + 32 * half, packed);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&p_full[buf]);
-        } else {
-          if (valid < kKeys) {
-  #pragma unroll
-            for (int i = 0; i < kKeys; ++i)
-              if (i >= valid) v[i] = -INFINITY;
-          }
-          float acc[8];
-  #pragma unroll
-          for (int a = 0; a < 8; ++a) acc[a] = fmaxf(v[a], v[8 + a]);
-  #pragma unroll
-          for (int i = 16; i < kKeys; i += 16)
-  #pragma unroll
-            for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], v[i + a], v[i + 8 + a]);
-          const float mx = fmaxf(fmax3(acc[0], acc[1], acc[2]),
-                                 fmax3(fmax3(acc[3], acc[4], acc[5]), acc[6], acc[7]));
-          const float m_tile = mx * p.scale_log2;
-          const bool move = m_tile > m_used + kRescaleThreshold;
-          if (__any_sync(0xffffffffu, move)) {
-            const float m_new = move ? m_tile : m_used;
-            if (j > 0) {
-              // O must be idle: P(J-1) V done (the S just read was issued after
-              // P(J-2) V, not after P(J-1) V).
-              ok = __all_sync(0xffffffffu, mbar_wait_bounded(o_full, (li * (n_k - 1) + j - 1) & 1));
-              if (!ok) break;
-              tc_fence_after();
-              const float alpha = move ? fast_exp2(m_used - m_new) : 1.f;
-  #pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                float o[16];
-                tmem_ld16(tO + 16 * c, o);
-  #pragma unroll
-                for (int i = 0; i < 16; ++i) o[i] *= alpha;
-                tmem_st16f(tO + 16 * c, o);
-              }
-              tmem_wait_st();
-              l *= alpha;
-            }
-            m_used = m_new;
-          }
-          const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
-          const uint64_t neg_m2 = pack2(-m_used, -m_used);
-          uint64_t sum2[4];
-  #pragma unroll
-          for (int a = 0; a < 4; ++a) sum2[a] = pack2(0.f, 0.f);
-  #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t packed[32];
-  #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int col = 64 * half + 2 * i;
-              float x0, x1;
-              unpack2(ffma2(pack2(v[col], v[col + 1]), scale2, neg_m2), x0, x1);
-              const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-              sum2[i & 3] = fadd2(sum2[i & 3], pack2(p0, p1));
-              packed[i] = bf16x2(p0, p1);
-            }
-            tmem_st32u(tS + 32 * half, packed);
-          }
-          float lo0, hi0;
-          unpack2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), lo0, hi0);
-          l += lo0 + hi0;
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&p_full[buf]);
-        }
-      }
-      if (!ok) break;
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(o_final, li & 1));
-      if (!ok) break;
-      tc_fence_after();
-      const int index = item_index(li);
-      const int h = index % p.heads, w = index / p.heads;
-      // Small prompt: row t's sum is held by the lanes of its group.
-      const float l_row =
-          kPad > 0 ? __shfl_sync(0xffffffffu, l, lane < kPad ? lane * (32 / (kPad > 0 ? kPad : 1))
-                                                              : lane)
-                   : l;
-      const float inv = 1.f / l_row;
-      const int64_t off = row < p.tokens ? static_cast<int64_t>(w * p.tokens + row) * p.o_st +
-                                               static_cast<int64_t>(h) * p.o_sh
-                                         : 0;
-      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + off;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float o[32];
-        tmem_ld32(tO + 32 * c, o);
-        if (row < p.tokens) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 u;
-            u.x = bf16x2(o[i] * inv, o[i + 1] * inv);
-            u.y = bf16x2(o[i + 2] * inv, o[i + 3] * inv);
-            u.z = bf16x2(o[i + 4] * inv, o[i + 5] * inv);
-            u.w = bf16x2(o[i + 6] * inv, o[i + 7] * inv);
-            *reinterpret_cast<uint4*>(out + 32 * c + i) = u;
           }
         }
+        // O has been read: the next item's first P V may overwrite it.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[slot]);
       }
-      // O has been read: the next item's first P V may overwrite it.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_free);
     }
     timed_out = !ok;
-  }
-  if (timed_out && p.status && lane == 0) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if (timed_out && p.status && lane == 0) atomicOr(p.status, ASRBACK_STATUS_TIMEOUT);
+    tc_fence_before();
+    named_sync(1, kThreads);
   }
 }
 
@@ -521,6 +563,8 @@ int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
             "cudaFuncSetAttribute(prompt-pass cross attention)"))
       return rc;
+    if (int rc = check_launch_registers(kernel, kLaunchRegs, "prompt-pass cross attention"))
+      return rc;
     prepared_device = device;
   }
   // Persistent: one CTA per SM (512 TMEM columns each), at most one per item.
@@ -542,14 +586,23 @@ int whisper_cross_prefix_tc(int windows, int tokens, int heads, int length, cons
   if (int rc = make_maps(&mq, &mk, &mv, q, windows * tokens, heads, tokens, q_st, q_sh, k, v,
                          windows, length, c_sb, c_sh))
     return rc;
-  PrefixParams p{out,     o_st,  o_sh, tokens, length, heads, windows * heads,
-                 (tokens + 31) / 32, scale * 1.4426950408889634f, status};
-  // Prompts of up to 16 rows share each row's softmax out over the warp.
+  const int softmax_warps = (tokens + 31) / 32;
+  PrefixParams p{out,
+                 o_st,
+                 o_sh,
+                 tokens,
+                 length,
+                 heads,
+                 windows * heads,
+                 softmax_warps,
+                 softmax_warps <= 2 ? 32 * softmax_warps : 0,
+                 scale * 1.4426950408889634f,
+                 status};
+  // Prompts of up to kMaxPad rows share each row's softmax out over the warp.
   if (tokens <= 1) return launch<1>(mq, mk, mv, p, stream);
   if (tokens <= 2) return launch<2>(mq, mk, mv, p, stream);
   if (tokens <= 4) return launch<4>(mq, mk, mv, p, stream);
   if (tokens <= 8) return launch<8>(mq, mk, mv, p, stream);
-  if (tokens <= 16) return launch<16>(mq, mk, mv, p, stream);
   return launch<0>(mq, mk, mv, p, stream);
 }
 
