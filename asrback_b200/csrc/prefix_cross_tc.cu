@@ -18,7 +18,7 @@
 //   warp 0      TMA: each item's P query rows (3-D map over the prompt rows)
 //               into its slot's Q buffer, whose other rows stay zero, and the
 //               pair's K/V tiles of 128 keys, the two slots' tiles alternating,
-//               into a 4-stage ring (4-D maps over the cache's (window, head,
+//               into a 5-stage ring (4-D maps over the cache's (window, head,
 //               position, 64) layout; rows past the window read as zeros);
 //   warp 1      allocates TMEM and issues the MMAs (warp-wide loop, one
 //               elected lane), in the ring's order: per key tile of a slot,
@@ -28,7 +28,11 @@
 //   warps 4-7   softmax and output of slot 0, warps 8-11 of slot 1: query rows
 //               32q .. 32q + 31 (thread = TMEM lane = row); only the
 //               ceil(P / 32) warps of a slot that hold prompt rows run, and the
-//               barriers they feed count them alone.
+//               barriers they feed count them alone; prompts of up to 8 rows
+//               share each row out over four lanes (16-lane TMEM loads and
+//               stores). For prompts of up to 64 rows slot 1's rows start at
+//               row 32 or 64 of its tile, so that the two slots' softmax warps
+//               run on different sub-partitions.
 // TMEM: slot x's S at [192x, 192x + 128) (P written over its first 64
 // columns), its O at [192x + 128, 192x + 192).
 // The running max is rescaled lazily (by more than 8 in log2 units, once the
@@ -44,7 +48,7 @@ using namespace tc;
 constexpr int kRows = 128;  // query rows per tile (= TMEM lanes)
 constexpr int kKeys = 128;  // keys per tile
 constexpr int kDim = 64;
-constexpr int kStages = 4;
+constexpr int kStages = 5;
 constexpr int kTileBytes = kRows * kDim * 2;  // 16 KB: a Q, K or V tile
 constexpr int kThreads = 12 * 32;             // warps 0-3 control (2, 3 idle), 4-11 softmax
 constexpr int kTmemCols = 512;                // 384 used; allocations are powers of two
@@ -62,17 +66,20 @@ static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs,
 constexpr int kOffQ = 0;  // a Q buffer per slot
 constexpr int kOffK = 2 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
-// Small-prompt softmax staging per slot: [8][128] float scores, [8][64] bf16
-// pairs.
-constexpr int kMaxPad = 8;
-constexpr int kStageBytes = kMaxPad * kKeys * 4 + kMaxPad * (kKeys / 2) * 4;
-constexpr int kOffStage = kOffV + kStages * kTileBytes;
-constexpr int kOffBar = kOffStage + 2 * kStageBytes;
+// Split items: slot 1 hands its half's output rows (unnormalised O, padded to
+// 68 floats so that eight rows' 16-byte stores hit distinct banks) and each
+// row's (max, sum) to slot 0.
+constexpr int kXchStride = 68;
+constexpr int kOffXchO = kOffV + kStages * kTileBytes;
+constexpr int kOffXchML = kOffXchO + 8 * kXchStride * 4;
+constexpr int kOffBar = kOffXchML + 8 * 8;
 // barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], then per slot
-// s_full[2], p_full[2], o_full[2], o_final[2], o_free[2]
-constexpr int kNumBars = 2 + 2 + 2 * kStages + 5 * 2;
+// s_full[2], p_full[2], o_full[2], o_final[2], o_free[2], then xch_full,
+// xch_empty
+constexpr int kNumBars = 2 + 2 + 2 * kStages + 5 * 2 + 2;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 struct PrefixParams {
   void* out;
@@ -83,19 +90,19 @@ struct PrefixParams {
   int items;           // windows * heads
   int softmax_warps;   // per slot: ceil(P / 32)
   int row1;            // first query-tile row of slot 1's prompt (0, 32 or 64)
+  int split;           // 1: each item's key tiles in two halves, one per slot
   float scale_log2;
   int32_t* status;
 };
 
-// kPad > 0: prompts of at most kPad (a power of two up to kMaxPad) rows, whose
-// softmax shares each row's work out over 32 / kPad lanes; 0: a row per lane.
-template <int kPad>
+// kSmall: prompts of at most 8 rows, each row's softmax shared out over four
+// lanes; otherwise a row per lane.
+template <bool kSmall>
 __global__ void __launch_bounds__(kThreads, 1)
     prefix_cross_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                            const __grid_constant__ CUtensorMap map_k,
                            const __grid_constant__ CUtensorMap map_v,
                            const __grid_constant__ PrefixParams p) {
-  static_assert(kPad <= kMaxPad, "small-prompt staging holds kMaxPad rows");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -109,19 +116,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_full = p_full + 2;
   uint64_t* o_final = o_full + 2;
   uint64_t* o_free = o_final + 2;
+  uint64_t* xch_full = o_free + 2;
+  uint64_t* xch_empty = xch_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_k = (p.length + kKeys - 1) / kKeys;
   const int n_items = p.items > (int)blockIdx.x
                           ? (p.items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
                           : 0;
-  const int n_pairs = (n_items + 1) / 2;
-  const int total = n_items * n_k;  // key tiles over all items
-  auto item_index = [&](int li) { return (int)blockIdx.x + li * (int)gridDim.x; };
-  // Items of pair i: 2i (slot 0) and 2i + 1 (slot 1, when there is one).
-  auto pair_size = [&](int i) { return 2 * i + 1 < n_items ? 2 : 1; };
+  // A unit is an item (window, head) or, split, one half of its key tiles:
+  // unit u of this CTA runs in slot u & 1 as part of pair u / 2.
+  const int n_tiles = (p.length + kKeys - 1) / kKeys;  // key tiles per item
+  const int n_k = p.split ? (n_tiles + 1) / 2 : n_tiles;  // key tiles per unit
+  const int n_units = p.split ? 2 * n_items : n_items;
+  const int n_pairs = (n_units + 1) / 2;
+  const int total = n_units * n_k;  // key tiles over all units
+  auto item_index = [&](int u) {
+    return (int)blockIdx.x + (p.split ? u >> 1 : u) * (int)gridDim.x;
+  };
+  // First key tile of unit u (the second half of a split item starts at n_k).
+  auto first_tile = [&](int u) { return p.split ? (u & 1) * n_k : 0; };
+  // Units of pair i: 2i (slot 0) and 2i + 1 (slot 1, when there is one).
+  auto pair_size = [&](int i) { return 2 * i + 1 < n_units ? 2 : 1; };
   // Ring index of key tile j of pair i's slot x: the two slots' tiles alternate.
   auto ring_index = [&](int i, int j, int x) {
     return 2 * n_k * i + (pair_size(i) == 2 ? 2 * j + x : j);
@@ -145,6 +162,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
+    mbar_init(xch_full, 1);
+    mbar_init(xch_empty, 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -180,7 +199,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;  // key tiles loaded, in ring order
       for (int i = 0; i < n_pairs && ok; ++i) {
         const int ps = pair_size(i);
-        for (int x = 0; x < ps && ok; ++x) {
+        if (p.split) {
+          // Both slots run the same item: buffer i & 1 takes its rows twice
+          // (at row 0 for slot 0, at row1 for slot 1), free once the item
+          // two pairs back has issued its last S, long before this pair's
+          // keys are due.
+          const int b = i & 1;
+          if (i >= 2) ok = wait_warp(&q_empty[b], ((i >> 1) - 1) & 1);
+          if (!ok) break;
+          const int index = item_index(2 * i);
+          const int h = index % p.heads, w = index / p.heads;
+          if (leader) {
+            mbar_arrive_expect_tx(&q_full[b], static_cast<uint32_t>(2 * p.tokens * kDim * 2));
+            tma_load_3d(smem + kOffQ + b * kTileBytes, &map_q, 0, h, w * p.tokens, &q_full[b]);
+            tma_load_3d(smem + kOffQ + b * kTileBytes + p.row1 * 128, &map_q, 0, h, w * p.tokens,
+                        &q_full[b]);
+          }
+          __syncwarp();
+        }
+        for (int x = 0; x < ps && ok && !p.split; ++x) {
           // Slot x's Q buffer is free once its previous item has issued its
           // last S.
           if (i >= 1) ok = wait_warp(&q_empty[x], (i - 1) & 1);
@@ -201,10 +238,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             const int index = item_index(2 * i + x);
             const int h = index % p.heads, w = index / p.heads;
+            const int key = (first_tile(2 * i + x) + j) * kKeys;
             if (leader) {
               mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
-              tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, j * kKeys, w, &kv_full[s]);
-              tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, j * kKeys, w, &kv_full[s]);
+              tma_load_4d(smem + kOffK + s * kTileBytes, &map_k, 0, h, key, w, &kv_full[s]);
+              tma_load_4d(smem + kOffV + s * kTileBytes, &map_v, 0, h, key, w, &kv_full[s]);
             }
             __syncwarp();
           }
@@ -223,20 +261,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         // S_x of key tile j of pair i: waits for the K/V tile (one barrier
         // for both; the tile's P V comes later in this stream) and, first of an
-        // item, for its Q. After the item's last S slot x's Q buffer is free.
+        // item, for its Q. After the item's last S its Q buffer is free (split:
+        // the pair's buffer i & 1 after slot 1's last S; otherwise slot x's).
         auto qk = [&](int i, int j, int x) {
           const int g = ring_index(i, j, x), s = g % kStages;
-          if (j == 0) ok = ok && wait_warp(&q_full[x], i & 1);
+          const int b = p.split ? i & 1 : x;
+          if (j == 0) ok = ok && wait_warp(&q_full[b], (p.split ? i >> 1 : i) & 1);
           ok = ok && wait_warp(&kv_full[s], (g / kStages) & 1);
           if (!ok) return;
           tc_fence_after();
           if (leader) {
 #pragma unroll
             for (int k = 0; k < kDim / 16; ++k)
-              mma_ss(tmem + col_s(x), q_desc + x * kTile + k * kStepK,
+              mma_ss(tmem + col_s(x), q_desc + b * kTile + k * kStepK,
                      k_desc + s * kTile + k * kStepK, kIdescQK, k > 0);
             mma_commit(&s_full[x]);
-            if (j == n_k - 1) mma_commit(&q_empty[x]);
+            if (j == n_k - 1 && (!p.split || x == 1)) mma_commit(&q_empty[b]);
           }
           __syncwarp();
         };
@@ -265,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // Slot x's next S, into the buffer this P V has read.
               if (j + 1 < n_k) {
                 qk(i, j + 1, x);
-              } else if (2 * (i + 1) + x < n_items) {
+              } else if (2 * (i + 1) + x < n_units) {
                 qk(i + 1, 0, x);
               }
             }
@@ -296,50 +336,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
       const uint32_t tS = tmem + lane_bits + col_s(slot);
       const uint32_t tO = tmem + lane_bits + col_o(slot);
-      float* s_rows = reinterpret_cast<float*>(smem + kOffStage + slot * kStageBytes);
-      uint32_t* p_rows =
-          reinterpret_cast<uint32_t*>(smem + kOffStage + slot * kStageBytes + kMaxPad * kKeys * 4);
-      for (int it = 0; ok && 2 * it + slot < n_items; ++it) {
+      float* xch_o = reinterpret_cast<float*>(smem + kOffXchO);
+      float2* xch_ml = reinterpret_cast<float2*>(smem + kOffXchML);
+      for (int it = 0; ok && 2 * it + slot < n_units; ++it) {
+        const int tile0 = first_tile(2 * it + slot);
         float m_used = -INFINITY, l = 0.f;
         for (int j = 0; j < n_k && ok; ++j) {
           const int t = it * n_k + j;  // this slot's key tiles so far
           ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[slot], t & 1));
           if (!ok) break;
           tc_fence_after();
-          const int valid = min(kKeys, p.length - j * kKeys);
-          float v[kKeys];
-          tmem_ld128(tS, v);
-          if constexpr (kPad > 0) {
-            // Small prompt: each row's 128 scores go through shared memory to
-            // its G lanes, C columns each, so the exponentials are shared out.
-            // Row r is held by lanes r * G .. r * G + G - 1 (its max, sum and
-            // running state replicated in them); lane t < kPad holds TMEM row t.
-            constexpr int G = 32 / kPad, C = kKeys / G;
-            const int r = lane / G, part = lane % G;
-            if (lane < kPad) {
+          const int valid = min(kKeys, p.length - (tile0 + j) * kKeys);
+          if constexpr (kSmall) {
+            // Prompts of up to 8 rows: a 16x256b load hands row t's 128 scores
+            // to lanes 4t .. 4t + 3, 32 columns each (8k + c and 8k + c + 1,
+            // c = 2 (lane % 4)), which is also the 16x128b store's layout of
+            // the packed P words; the lanes of rows past P write zero P.
+            const int c = 2 * (lane & 3);
+            const bool live = (lane >> 2) < p.tokens;
+            uint32_t r[64];
+            tmem_ld_16x256b_x16(tS, r);
+            float x[32];
 #pragma unroll
-              for (int i = 0; i < kKeys; i += 4)
-                *reinterpret_cast<float4*>(s_rows + lane * kKeys + i) =
-                    make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            for (int k = 0; k < 16; ++k) {
+              x[2 * k] = 8 * k + c < valid ? __uint_as_float(r[4 * k]) : -INFINITY;
+              x[2 * k + 1] = 8 * k + c + 1 < valid ? __uint_as_float(r[4 * k + 1]) : -INFINITY;
             }
-            __syncwarp();
-            float x[C];
+            float mx = fmaxf(x[0], x[1]);
 #pragma unroll
-            for (int i = 0; i < C; i += 4) {
-              const float4 f = *reinterpret_cast<const float4*>(s_rows + r * kKeys + part * C + i);
-              x[i] = part * C + i < valid ? f.x : -INFINITY;
-              x[i + 1] = part * C + i + 1 < valid ? f.y : -INFINITY;
-              x[i + 2] = part * C + i + 2 < valid ? f.z : -INFINITY;
-              x[i + 3] = part * C + i + 3 < valid ? f.w : -INFINITY;
-            }
-            float mx = x[0];
-#pragma unroll
-            for (int i = 1; i < C; ++i) mx = fmaxf(mx, x[i]);
-#pragma unroll
-            for (int off = G / 2; off >= 1; off >>= 1)
-              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            for (int i = 2; i < 32; i += 2) mx = fmax3(mx, x[i], x[i + 1]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             const float m_tile = mx * p.scale_log2;
-            const bool move = m_tile > m_used + kRescaleThreshold;
+            const bool move = live && m_tile > m_used + kRescaleThreshold;
             if (__any_sync(0xffffffffu, move)) {
               const float m_new = move ? m_tile : m_used;
               if (j > 0) {
@@ -349,15 +378,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const float alpha_row = move ? fast_exp2(m_used - m_new) : 1.f;
                 // TMEM row t's factor, from the first lane of row t's group.
-                const float a = __shfl_sync(0xffffffffu, alpha_row, lane < kPad ? lane * G : lane);
-                const float alpha = lane < kPad ? a : 1.f;
+                const float a = __shfl_sync(0xffffffffu, alpha_row, lane < 8 ? 4 * lane : lane);
+                const float alpha = lane < 8 ? a : 1.f;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int q = 0; q < 4; ++q) {
                   float o[16];
-                  tmem_ld16(tO + 16 * c, o);
+                  tmem_ld16(tO + 16 * q, o);
 #pragma unroll
                   for (int i = 0; i < 16; ++i) o[i] *= alpha;
-                  tmem_st16f(tO + 16 * c, o);
+                  tmem_st16f(tO + 16 * q, o);
                 }
                 tmem_wait_st();
                 l *= alpha_row;
@@ -365,38 +394,26 @@ __global__ void __launch_bounds__(kThreads, 1)
               m_used = m_new;
             }
             float sum = 0.f;
-#pragma unroll
-            for (int i = 0; i < C; i += 2) {
-              const float p0 = fast_exp2(fmaf(x[i], p.scale_log2, -m_used));
-              const float p1 = fast_exp2(fmaf(x[i + 1], p.scale_log2, -m_used));
-              sum += p0 + p1;
-              p_rows[r * (kKeys / 2) + (part * C + i) / 2] = bf16x2(p0, p1);
-            }
-#pragma unroll
-            for (int off = G / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            l += sum;
-            __syncwarp();
-            // TMEM row t takes row t's P (rows past kPad: zeros).
             uint32_t packed[32];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 4) {
-                const uint4 u = lane < kPad ? *reinterpret_cast<const uint4*>(
-                                                  p_rows + lane * (kKeys / 2) + 32 * half + i)
-                                            : make_uint4(0u, 0u, 0u, 0u);
-                packed[i] = u.x;
-                packed[i + 1] = u.y;
-                packed[i + 2] = u.z;
-                packed[i + 3] = u.w;
-              }
-              tmem_st32u(tS + 32 * half, packed);
+            for (int k = 0; k < 16; ++k) {
+              const float p0 = fast_exp2(fmaf(x[2 * k], p.scale_log2, -m_used));
+              const float p1 = fast_exp2(fmaf(x[2 * k + 1], p.scale_log2, -m_used));
+              sum += p0 + p1;
+              packed[2 * k] = live ? bf16x2(p0, p1) : 0u;
+              packed[2 * k + 1] = 0u;  // rows 8.. of the quarter
             }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            l += sum;
+            tmem_st_16x128b_x16(tS, packed);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[slot]);
           } else {
+            float v[kKeys];
+            tmem_ld128(tS, v);
             if (valid < kKeys) {
 #pragma unroll
               for (int i = 0; i < kKeys; ++i)
@@ -469,11 +486,70 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const int index = item_index(2 * it + slot);
         const int h = index % p.heads, w = index / p.heads;
-        // Small prompt: row t's sum is held by the lanes of its group.
-        const float l_row =
-            kPad > 0 ? __shfl_sync(0xffffffffu, l, lane < kPad ? lane * (32 / (kPad > 0 ? kPad : 1))
-                                                                : lane)
-                     : l;
+        // Small prompt: row t's max and sum are held by lanes 4t .. 4t + 3.
+        const float l_row = kSmall ? __shfl_sync(0xffffffffu, l, lane < 8 ? 4 * lane : lane) : l;
+        if (kSmall && p.split) {
+          const float m_row = __shfl_sync(0xffffffffu, m_used, lane < 8 ? 4 * lane : lane);
+          if (slot == 1) {
+            // Second half: its rows' unnormalised O and (max, sum) go to slot 0
+            // once slot 0 has read the previous item's.
+            if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(xch_empty, (it - 1) & 1));
+            if (!ok) break;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              float o[32];
+              tmem_ld32(tO + 32 * c, o);
+              if (lane < 8) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                  *reinterpret_cast<float4*>(xch_o + lane * kXchStride + 32 * c + i) =
+                      make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+              }
+            }
+            if (lane < 8) xch_ml[lane] = make_float2(m_row, l_row);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(xch_full);
+              mbar_arrive(&o_free[slot]);
+            }
+            continue;
+          }
+          // First half: fold the second half's rows in and write the output.
+          float o[64];
+          tmem_ld32(tO, o);
+          tmem_ld32(tO + 32, o + 32);
+          ok = __all_sync(0xffffffffu, mbar_wait_bounded(xch_full, it & 1));
+          if (!ok) break;
+          const float2 ml = lane < 8 ? xch_ml[lane] : make_float2(0.f, 0.f);
+          const float m = fmaxf(m_row, ml.x);
+          const float a0 = fast_exp2(m_row - m), a1 = fast_exp2(ml.x - m);
+          const float inv = 1.f / (l_row * a0 + ml.y * a1);
+          const float b0 = a0 * inv, b1 = a1 * inv;
+          if (row < p.tokens) {
+            __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
+                                 static_cast<int64_t>(w * p.tokens + row) * p.o_st +
+                                 static_cast<int64_t>(h) * p.o_sh;
+#pragma unroll
+            for (int i = 0; i < 64; i += 8) {
+              const float4 f0 = *reinterpret_cast<const float4*>(xch_o + lane * kXchStride + i);
+              const float4 f1 = *reinterpret_cast<const float4*>(xch_o + lane * kXchStride + i + 4);
+              uint4 u;
+              u.x = bf16x2(o[i] * b0 + f0.x * b1, o[i + 1] * b0 + f0.y * b1);
+              u.y = bf16x2(o[i + 2] * b0 + f0.z * b1, o[i + 3] * b0 + f0.w * b1);
+              u.z = bf16x2(o[i + 4] * b0 + f1.x * b1, o[i + 5] * b0 + f1.y * b1);
+              u.w = bf16x2(o[i + 6] * b0 + f1.z * b1, o[i + 7] * b0 + f1.w * b1);
+              *reinterpret_cast<uint4*>(out + i) = u;
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(xch_empty);
+            mbar_arrive(&o_free[slot]);
+          }
+          continue;
+        }
         const float inv = 1.f / l_row;
         const int64_t off = row < p.tokens ? static_cast<int64_t>(w * p.tokens + row) * p.o_st +
                                                  static_cast<int64_t>(h) * p.o_sh
@@ -551,10 +627,10 @@ int make_maps(CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv, const void* q, 
   return ASRBACK_OK;
 }
 
-template <int kPad>
+template <bool kSmall>
 int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
            const PrefixParams& p, cudaStream_t stream) {
-  auto kernel = prefix_cross_tc_kernel<kPad>;
+  auto kernel = prefix_cross_tc_kernel<kSmall>;
   static thread_local int prepared_device = -1;
   int device = 0;
   if (int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return rc;
@@ -587,6 +663,11 @@ int whisper_cross_prefix_tc(int windows, int tokens, int heads, int length, cons
                          windows, length, c_sb, c_sh))
     return rc;
   const int softmax_warps = (tokens + 31) / 32;
+  // Prompts of up to 8 rows over an even number (2 or more) of key tiles run
+  // each item as two halves, one per slot, merged in the CTA: the two slots
+  // then share every item, so a CTA's last item does not run alone.
+  const int n_tiles = (length + kKeys - 1) / kKeys;
+  const int split = tokens <= 8 && n_tiles >= 2 && n_tiles % 2 == 0 ? 1 : 0;
   PrefixParams p{out,
                  o_st,
                  o_sh,
@@ -596,14 +677,11 @@ int whisper_cross_prefix_tc(int windows, int tokens, int heads, int length, cons
                  windows * heads,
                  softmax_warps,
                  softmax_warps <= 2 ? 32 * softmax_warps : 0,
+                 split,
                  scale * 1.4426950408889634f,
                  status};
-  // Prompts of up to kMaxPad rows share each row's softmax out over the warp.
-  if (tokens <= 1) return launch<1>(mq, mk, mv, p, stream);
-  if (tokens <= 2) return launch<2>(mq, mk, mv, p, stream);
-  if (tokens <= 4) return launch<4>(mq, mk, mv, p, stream);
-  if (tokens <= 8) return launch<8>(mq, mk, mv, p, stream);
-  return launch<0>(mq, mk, mv, p, stream);
+  // Prompts of up to 8 rows share each row's softmax out over four lanes.
+  return tokens <= 8 ? launch<true>(mq, mk, mv, p, stream) : launch<false>(mq, mk, mv, p, stream);
 }
 
 }  // namespace asrback

@@ -210,19 +210,31 @@ def test_whisper_prefix_random(tag, batch, tokens, bucket):
     assert attention.read_status() == 0
 
 
-@pytest.mark.parametrize("windows,tokens,length", [(1, 1, 1500), (3, 4, 1500), (2, 31, 1500),
-                                                    (5, 32, 1500), (2, 33, 1500), (8, 100, 1500),
-                                                    (2, 128, 1500), (4, 7, 200), (1, 4, 128),
-                                                    (3, 2, 1500), (2, 12, 700), (6, 16, 1500)])
-def test_whisper_cross_prefix_tensor_core(windows, tokens, length, monkeypatch):
+@pytest.mark.parametrize("windows,tokens,length,plant",
+                         [(1, 1, 1500, False), (3, 4, 1500, False), (2, 31, 1500, False),
+                          (5, 32, 1500, False), (2, 33, 1500, False), (8, 100, 1500, False),
+                          (2, 128, 1500, False), (4, 7, 200, False), (1, 4, 128, False),
+                          (3, 2, 1500, False), (2, 12, 700, False), (6, 16, 1500, False),
+                          (3, 3, 1500, False), (2, 5, 333, False), (4, 8, 1500, False),
+                          (3, 9, 1500, False), (5, 64, 1500, False), (2, 6, 700, False),
+                          (3, 4, 1500, True),
+                          (2, 8, 1500, True), (3, 40, 1500, True)])
+def test_whisper_cross_prefix_tensor_core(windows, tokens, length, plant, monkeypatch):
     """The tensor-core prompt-pass cross-attention (bf16, up to 128 tokens per
-    window: one, two, three or four softmax warps) against the oracle and the
-    CUDA-core prefix kernel, over the whole cache, over a view of the first
-    `length` frames of a longer one (keys past it never read), and with a last
-    key tile that ends inside or at the tile."""
+    window: one, two, three or four softmax warps; up to 8 tokens with a row
+    shared by four lanes) against the oracle and the CUDA-core prefix kernel,
+    over the whole cache, over a view of the first `length` frames of a longer
+    one (keys past it never read), and with a last key tile that ends inside or
+    at the tile. Up to 8 tokens over an even number of key tiles, an item's two
+    halves run in the two slots and merge in the CTA. `plant` scales a few keys of later tiles up so that the running
+    maximum moves by more than the rescale threshold after the first tile."""
     gen = torch.Generator().manual_seed(windows * 1000 + tokens + length)
     heads, dim, frames = 20, 64, 1500
-    ck = _rand(gen, (windows, heads, frames, dim), torch.bfloat16).to(DEV)
+    ck = _rand(gen, (windows, heads, frames, dim), torch.bfloat16)
+    if plant:
+        ck[:, :, 700:704] *= 12
+        ck[:, :, 1300:1302] *= 24
+    ck = ck.to(DEV)
     cv = _rand(gen, (windows, heads, frames, dim), torch.bfloat16).to(DEV)
     x = _rand(gen, (windows, tokens, heads * dim), torch.bfloat16).to(DEV)
     query = x.view(windows, tokens, heads, dim).transpose(1, 2)
