@@ -33,8 +33,15 @@
 //               stores). For prompts of up to 64 rows slot 1's rows start at
 //               row 32 or 64 of its tile, so that the two slots' softmax warps
 //               run on different sub-partitions.
-// TMEM: slot x's S at [192x, 192x + 128) (P written over its first 64
-// columns), its O at [192x + 128, 192x + 192).
+// Split items (up to 8 rows over an even number of key tiles): the two slots
+// run the two halves of one item's keys, and warps 8 and 5 (idle otherwise,
+// on slot 0's and slot 1's lane quarters) take the epilogue: slot 1's half
+// goes through shared memory to warp 8, which merges it with slot 0's and
+// writes the output, while the softmax warps run the next item into the
+// slot's other O buffer.
+// TMEM: slot x's S at [256x, 256x + 128) (P written over its first 64
+// columns), its O at [256x + 128, 256x + 192) and, for split items of odd
+// pair index, [256x + 192, 256x + 256).
 // The running max is rescaled lazily (by more than 8 in log2 units, once the
 // previous P V is done), as in the encoder kernel.
 #include "tcgen05.cuh"
@@ -52,8 +59,8 @@ constexpr int kStages = 5;
 constexpr int kTileBytes = kRows * kDim * 2;  // 16 KB: a Q, K or V tile
 constexpr int kThreads = 12 * 32;             // warps 0-3 control (2, 3 idle), 4-11 softmax
 constexpr int kTmemCols = 512;                // 384 used; allocations are powers of two
-__host__ __device__ constexpr int col_s(int x) { return 192 * x; }
-__host__ __device__ constexpr int col_o(int x) { return 192 * x + 128; }
+__host__ __device__ constexpr int col_s(int x) { return 256 * x; }
+__host__ __device__ constexpr int col_o(int x) { return 256 * x + 128; }  // + 64: split's 2nd
 constexpr float kRescaleThreshold = 8.0f;
 // Registers per thread: 168 at launch (384 x 168 = 64512); the control
 // warpgroup keeps 56, the two softmax warpgroups take 224.
@@ -72,11 +79,14 @@ constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kXchStride = 68;
 constexpr int kOffXchO = kOffV + kStages * kTileBytes;
 constexpr int kOffXchML = kOffXchO + 8 * kXchStride * 4;
-constexpr int kOffBar = kOffXchML + 8 * 8;
-// barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], then per slot
-// s_full[2], p_full[2], o_full[2], o_final[2], o_free[2], then xch_full,
-// xch_empty
-constexpr int kNumBars = 2 + 2 + 2 * kStages + 5 * 2 + 2;
+// Split items: each slot's softmax hands its rows' (max, sum) to the epilogue
+// warp, per O buffer: [slot][buffer][8] float2.
+constexpr int kOffML = kOffXchML + 8 * 8;
+constexpr int kOffBar = kOffML + 2 * 2 * 8 * 8;
+// barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], per slot s_full,
+// p_full, o_full, per (slot, O buffer) o_final, o_free, ml_full, ml_empty,
+// then xch_full, xch_empty
+constexpr int kNumBars = 2 + 2 + 2 * kStages + 3 * 2 + 4 * 4 + 2;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
@@ -114,9 +124,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = kv_empty + kStages;  // [slot]
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
-  uint64_t* o_final = o_full + 2;
-  uint64_t* o_free = o_final + 2;
-  uint64_t* xch_full = o_free + 2;
+  uint64_t* o_final = o_full + 2;  // [2 * slot + O buffer]
+  uint64_t* o_free = o_final + 4;
+  uint64_t* ml_full = o_free + 4;
+  uint64_t* ml_empty = ml_full + 4;
+  uint64_t* xch_full = ml_empty + 4;
   uint64_t* xch_empty = xch_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
@@ -155,8 +167,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], p.softmax_warps);  // one arrival per running softmax warp
       mbar_init(&o_full[x], 1);
-      mbar_init(&o_final[x], 1);
-      mbar_init(&o_free[x], p.softmax_warps);
+    }
+    for (int e = 0; e < 4; ++e) {
+      mbar_init(&o_final[e], 1);
+      // Split items: the epilogue warp frees O; otherwise each softmax warp.
+      mbar_init(&o_free[e], p.split ? 1 : p.softmax_warps);
+      mbar_init(&ml_full[e], 1);
+      mbar_init(&ml_empty[e], 1);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -288,17 +305,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               // O_x (+)= P_x V once the softmax has written P_x (an item's
               // first also once the slot's previous output has been read).
               const int t = i * n_k + j;  // slot x's key tiles so far
+              // Split items alternate between the slot's two O buffers, so an
+              // item's first P V waits for the epilogue of the item two back.
+              const int ob = p.split ? i & 1 : 0;
               ok = ok && wait_warp(&p_full[x], t & 1);
-              if (j == 0 && i > 0) ok = ok && wait_warp(&o_free[x], (i - 1) & 1);
+              if (j == 0 && i >= (p.split ? 2 : 1))
+                ok = ok && wait_warp(&o_free[2 * x + ob], (p.split ? (i >> 1) - 1 : i - 1) & 1);
               if (!ok) break;
               tc_fence_after();
               const int g = ring_index(i, j, x), s = g % kStages;
               if (leader) {
 #pragma unroll
                 for (int k = 0; k < kKeys / 16; ++k)
-                  mma_ts(tmem + col_o(x), tmem + col_s(x) + k * 8,
+                  mma_ts(tmem + col_o(x) + 64 * ob, tmem + col_s(x) + k * 8,
                          v_desc + s * kTile + k * kStepV, kIdescPV, (j > 0 || k > 0));
-                mma_commit(j + 1 < n_k ? &o_full[x] : &o_final[x]);
+                mma_commit(j + 1 < n_k ? &o_full[x] : &o_final[2 * x + ob]);
                 if (g + kStages < total) mma_commit(&kv_empty[s]);
               }
               __syncwarp();
@@ -331,15 +352,93 @@ __global__ void __launch_bounds__(kThreads, 1)
     // warps run on different sub-partitions).
     const int q0 = slot * p.row1 / 32;
     bool ok = true;
-    if (quarter >= q0 && quarter < q0 + p.softmax_warps) {
+    float* xch_o = reinterpret_cast<float*>(smem + kOffXchO);
+    float2* xch_ml = reinterpret_cast<float2*>(smem + kOffXchML);
+    float2* ml = reinterpret_cast<float2*>(smem + kOffML);
+    if (kSmall && p.split && (warp == 5 || warp == 8)) {
+      // ---------------- split items: epilogue ----------------
+      // Warp 8 shares slot 0's lane quarter (rows at lane 0..), warp 5 slot
+      // 1's (rows at lane 32..). Per item: its O buffer once the last P V is
+      // done and the softmax has handed over each row's (max, sum); slot 1's
+      // half goes through shared memory to warp 8, which folds it into slot
+      // 0's and writes the output. The softmax warps meanwhile run the next
+      // item into the slot's other O buffer.
+      const int es = warp == 5 ? 1 : 0;
+      const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
+      const int row = lane;
+      for (int it = 0; ok && 2 * it + es < n_units; ++it) {
+        const int e = 2 * es + (it & 1);
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&o_final[e], (it >> 1) & 1));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait_bounded(&ml_full[e], (it >> 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+        const float2 mine = lane < 8 ? ml[8 * e + lane] : make_float2(0.f, 0.f);
+        float o[64];
+        tmem_ld32(tmem + lane_bits + col_o(es) + 64 * (it & 1), o);
+        tmem_ld32(tmem + lane_bits + col_o(es) + 64 * (it & 1) + 32, o + 32);
+        if (es == 1) {
+          // Second half: rows' unnormalised O and (max, sum) to warp 8 once it
+          // has read the previous item's.
+          if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(xch_empty, (it - 1) & 1));
+          if (!ok) break;
+          if (lane < 8) {
+#pragma unroll
+            for (int i = 0; i < 64; i += 4)
+              *reinterpret_cast<float4*>(xch_o + lane * kXchStride + i) =
+                  make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+            xch_ml[lane] = mine;
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(xch_full);
+            mbar_arrive(&ml_empty[e]);
+            mbar_arrive(&o_free[e]);
+          }
+          continue;
+        }
+        // First half: fold the second half's rows in and write the output.
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(xch_full, it & 1));
+        if (!ok) break;
+        const float2 other = lane < 8 ? xch_ml[lane] : make_float2(0.f, 0.f);
+        const float m = fmaxf(mine.x, other.x);
+        const float a0 = fast_exp2(mine.x - m), a1 = fast_exp2(other.x - m);
+        const float inv = 1.f / (mine.y * a0 + other.y * a1);
+        const float b0 = a0 * inv, b1 = a1 * inv;
+        if (row < p.tokens) {
+          const int index = item_index(2 * it);
+          const int h = index % p.heads, w = index / p.heads;
+          __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
+                               static_cast<int64_t>(w * p.tokens + row) * p.o_st +
+                               static_cast<int64_t>(h) * p.o_sh;
+#pragma unroll
+          for (int i = 0; i < 64; i += 8) {
+            const float4 f0 = *reinterpret_cast<const float4*>(xch_o + lane * kXchStride + i);
+            const float4 f1 = *reinterpret_cast<const float4*>(xch_o + lane * kXchStride + i + 4);
+            uint4 u;
+            u.x = bf16x2(o[i] * b0 + f0.x * b1, o[i + 1] * b0 + f0.y * b1);
+            u.y = bf16x2(o[i + 2] * b0 + f0.z * b1, o[i + 3] * b0 + f0.w * b1);
+            u.z = bf16x2(o[i + 4] * b0 + f1.x * b1, o[i + 5] * b0 + f1.y * b1);
+            u.w = bf16x2(o[i + 6] * b0 + f1.z * b1, o[i + 7] * b0 + f1.w * b1);
+            *reinterpret_cast<uint4*>(out + i) = u;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(xch_empty);
+          mbar_arrive(&ml_empty[e]);
+          mbar_arrive(&o_free[e]);
+        }
+      }
+    } else if (quarter >= q0 && quarter < q0 + p.softmax_warps) {
       const int row = (quarter - q0) * 32 + lane;  // prompt row of this thread (zeros past P)
       const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
       const uint32_t tS = tmem + lane_bits + col_s(slot);
-      const uint32_t tO = tmem + lane_bits + col_o(slot);
-      float* xch_o = reinterpret_cast<float*>(smem + kOffXchO);
-      float2* xch_ml = reinterpret_cast<float2*>(smem + kOffXchML);
       for (int it = 0; ok && 2 * it + slot < n_units; ++it) {
         const int tile0 = first_tile(2 * it + slot);
+        const int ob = p.split ? it & 1 : 0;  // O buffer of this item
+        const uint32_t tO = tmem + lane_bits + col_o(slot) + 64 * ob;
         float m_used = -INFINITY, l = 0.f;
         for (int j = 0; j < n_k && ok; ++j) {
           const int t = it * n_k + j;  // this slot's key tiles so far
@@ -481,75 +580,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&o_final[slot], it & 1));
+        // Small prompt: row t's max and sum are held by lanes 4t .. 4t + 3.
+        const float l_row = kSmall ? __shfl_sync(0xffffffffu, l, lane < 8 ? 4 * lane : lane) : l;
+        if (kSmall && p.split) {
+          // The epilogue warp takes over: each row's (max, sum) for this O
+          // buffer, once it has read those of the item two back.
+          const float m_row = __shfl_sync(0xffffffffu, m_used, lane < 8 ? 4 * lane : lane);
+          const int e = 2 * slot + ob;
+          if (it >= 2)
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ml_empty[e], ((it >> 1) - 1) & 1));
+          if (!ok) break;
+          if (lane < 8) ml[8 * e + lane] = make_float2(m_row, l_row);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ml_full[e]);
+          continue;
+        }
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&o_final[2 * slot], it & 1));
         if (!ok) break;
         tc_fence_after();
         const int index = item_index(2 * it + slot);
         const int h = index % p.heads, w = index / p.heads;
-        // Small prompt: row t's max and sum are held by lanes 4t .. 4t + 3.
-        const float l_row = kSmall ? __shfl_sync(0xffffffffu, l, lane < 8 ? 4 * lane : lane) : l;
-        if (kSmall && p.split) {
-          const float m_row = __shfl_sync(0xffffffffu, m_used, lane < 8 ? 4 * lane : lane);
-          if (slot == 1) {
-            // Second half: its rows' unnormalised O and (max, sum) go to slot 0
-            // once slot 0 has read the previous item's.
-            if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(xch_empty, (it - 1) & 1));
-            if (!ok) break;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              float o[32];
-              tmem_ld32(tO + 32 * c, o);
-              if (lane < 8) {
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                  *reinterpret_cast<float4*>(xch_o + lane * kXchStride + 32 * c + i) =
-                      make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-              }
-            }
-            if (lane < 8) xch_ml[lane] = make_float2(m_row, l_row);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              mbar_arrive(xch_full);
-              mbar_arrive(&o_free[slot]);
-            }
-            continue;
-          }
-          // First half: fold the second half's rows in and write the output.
-          float o[64];
-          tmem_ld32(tO, o);
-          tmem_ld32(tO + 32, o + 32);
-          ok = __all_sync(0xffffffffu, mbar_wait_bounded(xch_full, it & 1));
-          if (!ok) break;
-          const float2 ml = lane < 8 ? xch_ml[lane] : make_float2(0.f, 0.f);
-          const float m = fmaxf(m_row, ml.x);
-          const float a0 = fast_exp2(m_row - m), a1 = fast_exp2(ml.x - m);
-          const float inv = 1.f / (l_row * a0 + ml.y * a1);
-          const float b0 = a0 * inv, b1 = a1 * inv;
-          if (row < p.tokens) {
-            __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
-                                 static_cast<int64_t>(w * p.tokens + row) * p.o_st +
-                                 static_cast<int64_t>(h) * p.o_sh;
-#pragma unroll
-            for (int i = 0; i < 64; i += 8) {
-              const float4 f0 = *reinterpret_cast<const float4*>(xch_o + lane * kXchStride + i);
-              const float4 f1 = *reinterpret_cast<const float4*>(xch_o + lane * kXchStride + i + 4);
-              uint4 u;
-              u.x = bf16x2(o[i] * b0 + f0.x * b1, o[i + 1] * b0 + f0.y * b1);
-              u.y = bf16x2(o[i + 2] * b0 + f0.z * b1, o[i + 3] * b0 + f0.w * b1);
-              u.z = bf16x2(o[i + 4] * b0 + f1.x * b1, o[i + 5] * b0 + f1.y * b1);
-              u.w = bf16x2(o[i + 6] * b0 + f1.z * b1, o[i + 7] * b0 + f1.w * b1);
-              *reinterpret_cast<uint4*>(out + i) = u;
-            }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(xch_empty);
-            mbar_arrive(&o_free[slot]);
-          }
-          continue;
-        }
         const float inv = 1.f / l_row;
         const int64_t off = row < p.tokens ? static_cast<int64_t>(w * p.tokens + row) * p.o_st +
                                                  static_cast<int64_t>(h) * p.o_sh
@@ -574,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // O has been read: the next item's first P V may overwrite it.
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&o_free[slot]);
+        if (lane == 0) mbar_arrive(&o_free[2 * slot]);
       }
     }
     timed_out = !ok;
