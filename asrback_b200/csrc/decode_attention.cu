@@ -230,13 +230,15 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   const int grp = blockIdx.y;
   const int b = blockIdx.z;  // query row (grouped prefix: token group)
   const bool prefix = p.tokens_per_row > 0;
-  // Grouped prefix (cross-attention with QPK > 1): blockIdx.z is a group of
-  // QPK consecutive tokens of one window, so every staged key serves QPK
+  // Grouped prefix (Whisper prompt pass with QPK > 1): blockIdx.z is a group
+  // of QPK consecutive tokens of one window, so every staged key serves QPK
   // queries. Query row qrow0 + qi is token tok0 + qi, present while below
-  // tokens_per_row; absent ones compute on zeros and write nothing.
+  // tokens_per_row; absent ones compute on zeros and write nothing. Causal
+  // self-attention reads keys 0 .. the group's last token and masks key k
+  // for token tok0 + qi < k.
   constexpr bool kGrouped = MODE != kQwen3 && QPK > 1;
-  static_assert(!kGrouped || (MODE == kWhisperCross && G == 1),
-                "token groups serve the Whisper cross-attention prompt pass only");
+  static_assert(!kGrouped || G == 1, "token groups serve the Whisper prompt pass only");
+  constexpr bool kCausalGroup = kGrouped && MODE == kWhisperSelf;
   int cb = b, tok0 = 0;  // cache row, first token
   int64_t qrow0 = b;
   if constexpr (kGrouped) {
@@ -302,7 +304,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
   if constexpr (MODE == kWhisperCross) {
     n_cached = n_total = p.length;
   } else if (MODE == kWhisperSelf && prefix) {
-    n_cached = n_total = b % p.tokens_per_row + 1;
+    n_cached = n_total = kGrouped ? min(tok0 + QPK, p.tokens_per_row) : b % p.tokens_per_row + 1;
   } else {
     const int64_t given = p.positions[b];
     if (given < 0 || given >= p.length) {
@@ -475,6 +477,16 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
     float sc[QPK][NP];
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
+      // Grouped causal prompt pass (a few keys per group): a pass wholly past
+      // the tile's keys is skipped by the whole CTA, its scores masked. (In
+      // the decode steps the same skip made the launches 3 % slower.)
+      if constexpr (kCausalGroup) {
+        if (i * (WPH * KPW) >= rows) {
+#pragma unroll
+          for (int qi = 0; qi < QPK; ++qi) sc[qi][i] = -INFINITY;
+          continue;
+        }
+      }
       const int kt = wh * KPW + ks + i * (WPH * KPW);
       float kv[8];
       if (kt < rows) {
@@ -489,7 +501,8 @@ __global__ void __launch_bounds__(C::THREADS, C::MIN_BLOCKS)
 #pragma unroll
         for (int j = 0; j < 8; ++j) dot = fmaf(q[qi][j], kv[j], dot);
         dot = group_sum<LPK>(dot);
-        sc[qi][i] = kt < rows ? dot : -INFINITY;
+        const bool seen = !kCausalGroup || k0 + t * TP + kt <= tok0 + qi;
+        sc[qi][i] = kt < rows && seen ? dot : -INFINITY;
       }
     }
     float pr[QPK][NP];
@@ -824,6 +837,11 @@ void choose_split(int units, int max_keys, int tile, int granule_tiles, int ctas
 #ifndef ASRBACK_SHAPE_WHISPER_PREFIX_BF16
 #define ASRBACK_SHAPE_WHISPER_PREFIX_BF16 4, 64, 4
 #endif
+// Prompt-pass causal self-attention with kPrefixTokens tokens per CTA (keys:
+// the prompt so far, a few tiles at most).
+#ifndef ASRBACK_SHAPE_WHISPER_SELF_PREFIX_BF16
+#define ASRBACK_SHAPE_WHISPER_SELF_PREFIX_BF16 1, 64, 2
+#endif
 constexpr int kPrefixTokens = 4;
 // Qwen3: key/value heads per CTA (a divisor of 8), then the shape.
 #ifndef ASRBACK_QWEN3_GROUP
@@ -845,6 +863,8 @@ using WhisperCrossBf16 = DecodeConfig<bf16, 64, 1, 1, ASRBACK_SHAPE_WHISPER_CROS
 using WhisperCrossF32 = DecodeConfig<float, 64, 1, 1, ASRBACK_SHAPE_WHISPER_F32, kWhisperCross>;
 using WhisperCrossPrefixBf16 =
     DecodeConfig<bf16, 64, 1, kPrefixTokens, ASRBACK_SHAPE_WHISPER_PREFIX_BF16, kWhisperCross>;
+using WhisperSelfPrefixBf16 =
+    DecodeConfig<bf16, 64, 1, kPrefixTokens, ASRBACK_SHAPE_WHISPER_SELF_PREFIX_BF16, kWhisperSelf>;
 template <int QPK>
 using Qwen3Bf16 = DecodeConfig<bf16, 128, ASRBACK_QWEN3_GROUP, QPK, ASRBACK_SHAPE_QWEN3_BF16, kQwen3>;
 template <int QPK>
@@ -1069,6 +1089,8 @@ size_t prefix_workspace_bytes(int windows, int tokens, int heads, int head_dim, 
     need = n > need ? n : need;
   if (tokens >= kPrefixTokens) {
     const int grouped = windows * ((tokens + kPrefixTokens - 1) / kPrefixTokens) * heads;
+    const size_t self = workspace_for<WhisperSelfPrefixBf16>(grouped, kPrefixTokens, tokens);
+    need = self > need ? self : need;
     int chunk, splits;
     choose_split_waves(grouped, length, WhisperCrossPrefixBf16::TP,
                        WhisperCrossPrefixBf16::MIN_BLOCKS, &chunk, &splits);
@@ -1186,11 +1208,20 @@ int asrback_whisper_self_attention_prefix(
   p.groups = heads;
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int rows = windows * tokens;
-  const int units = rows * heads;
-  int rc = dtype == ASRBACK_BF16
-               ? run<WhisperSelfBf16>(p, rows, units, 1, workspace, workspace_bytes, s)
-               : run<WhisperSelfF32>(p, rows, units, 1, workspace, workspace_bytes, s);
+  int rc;
+  if (dtype == ASRBACK_BF16 && tokens >= kPrefixTokens) {
+    // kPrefixTokens tokens of a window per CTA: a quarter of the CTAs, each
+    // staged key serving the group's tokens that see it.
+    const int rows = windows * ((tokens + kPrefixTokens - 1) / kPrefixTokens);
+    rc = run<WhisperSelfPrefixBf16>(p, rows, rows * heads, kPrefixTokens, workspace,
+                                    workspace_bytes, s);
+  } else {
+    const int rows = windows * tokens;
+    const int units = rows * heads;
+    rc = dtype == ASRBACK_BF16
+             ? run<WhisperSelfBf16>(p, rows, units, 1, workspace, workspace_bytes, s)
+             : run<WhisperSelfF32>(p, rows, units, 1, workspace, workspace_bytes, s);
+  }
   return rc ? rc : ok();
 }
 
