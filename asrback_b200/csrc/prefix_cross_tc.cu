@@ -33,12 +33,14 @@
 //               stores). For prompts of up to 64 rows slot 1's rows start at
 //               row 32 or 64 of its tile, so that the two slots' softmax warps
 //               run on different sub-partitions.
-// Split items (up to 8 rows over an even number of key tiles): the two slots
-// run the two halves of one item's keys, and warps 8 and 5 (idle otherwise,
-// on slot 0's and slot 1's lane quarters) take the epilogue: slot 1's half
-// goes through shared memory to warp 8, which merges it with slot 0's and
-// writes the output, while the softmax warps run the next item into the
-// slot's other O buffer.
+// Split items (up to 64 rows over an even number of key tiles): the two slots
+// run the two halves of one item's keys (its rows in one Q buffer twice, the
+// two Q buffers alternating by item), and the warps of each warpgroup on the
+// other slot's lane quarters (idle otherwise: warps 8.. for slot 0, 4 + s..
+// for slot 1, s = the softmax warps per slot) take the epilogue: slot 1's half
+// goes through shared memory to slot 0's epilogue warps, which merge it with
+// slot 0's and write the output, while the softmax warps run the next item
+// into the slot's other O buffer.
 // TMEM: slot x's S at [256x, 256x + 128) (P written over its first 64
 // columns), its O at [256x + 128, 256x + 192) and, for split items of odd
 // pair index, [256x + 192, 256x + 256).
@@ -73,16 +75,17 @@ static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs,
 constexpr int kOffQ = 0;  // a Q buffer per slot
 constexpr int kOffK = 2 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
-// Split items: slot 1 hands its half's output rows (unnormalised O, padded to
-// 68 floats so that eight rows' 16-byte stores hit distinct banks) and each
-// row's (max, sum) to slot 0.
+// Split items (prompts of up to kSplitRows rows): slot 1 hands its half's
+// output rows (unnormalised O, rows padded to 68 floats so that eight rows'
+// 16-byte stores hit distinct banks) and each row's (max, sum) to slot 0.
+constexpr int kSplitRows = 64;
 constexpr int kXchStride = 68;
 constexpr int kOffXchO = kOffV + kStages * kTileBytes;
-constexpr int kOffXchML = kOffXchO + 8 * kXchStride * 4;
+constexpr int kOffXchML = kOffXchO + kSplitRows * kXchStride * 4;
 // Split items: each slot's softmax hands its rows' (max, sum) to the epilogue
-// warp, per O buffer: [slot][buffer][8] float2.
-constexpr int kOffML = kOffXchML + 8 * 8;
-constexpr int kOffBar = kOffML + 2 * 2 * 8 * 8;
+// warps, per O buffer: [slot][buffer][kSplitRows] float2.
+constexpr int kOffML = kOffXchML + kSplitRows * 8;
+constexpr int kOffBar = kOffML + 2 * 2 * kSplitRows * 8;
 // barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], per slot s_full,
 // p_full, o_full, per (slot, O buffer) o_final, o_free, ml_full, ml_empty,
 // then xch_full, xch_empty
@@ -171,16 +174,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int e = 0; e < 4; ++e) {
       mbar_init(&o_final[e], 1);
       // Split items: the epilogue warp frees O; otherwise each softmax warp.
-      mbar_init(&o_free[e], p.split ? 1 : p.softmax_warps);
-      mbar_init(&ml_full[e], 1);
-      mbar_init(&ml_empty[e], 1);
+      // Split items: the slot's epilogue warps free O (as many as it has
+      // softmax warps); otherwise each softmax warp.
+      mbar_init(&o_free[e], p.softmax_warps);
+      mbar_init(&ml_full[e], p.softmax_warps);
+      mbar_init(&ml_empty[e], p.softmax_warps);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(xch_full, 1);
-    mbar_init(xch_empty, 1);
+    mbar_init(xch_full, p.softmax_warps);
+    mbar_init(xch_empty, p.softmax_warps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -355,38 +360,51 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* xch_o = reinterpret_cast<float*>(smem + kOffXchO);
     float2* xch_ml = reinterpret_cast<float2*>(smem + kOffXchML);
     float2* ml = reinterpret_cast<float2*>(smem + kOffML);
-    if (kSmall && p.split && (warp == 5 || warp == 8)) {
+    // Split items: a warpgroup's warps on the other slot's row quarters are
+    // that slot's epilogue warps (es: the slot a warp finishes; its rows
+    // start at erow0).
+    const int sw = p.softmax_warps;
+    int es = -1, erow0 = 0;
+    if (p.split) {
+      if (slot == 1 && quarter < sw) {
+        es = 0;
+        erow0 = quarter * 32;
+      } else if (slot == 0 && quarter >= sw && quarter < 2 * sw) {
+        es = 1;
+        erow0 = (quarter - sw) * 32;
+      }
+    }
+    if (es >= 0) {
       // ---------------- split items: epilogue ----------------
-      // Warp 8 shares slot 0's lane quarter (rows at lane 0..), warp 5 slot
-      // 1's (rows at lane 32..). Per item: its O buffer once the last P V is
-      // done and the softmax has handed over each row's (max, sum); slot 1's
-      // half goes through shared memory to warp 8, which folds it into slot
-      // 0's and writes the output. The softmax warps meanwhile run the next
-      // item into the slot's other O buffer.
-      const int es = warp == 5 ? 1 : 0;
+      // Per item: the O buffer once the last P V is done and the softmax has
+      // handed over each row's (max, sum). Slot 1's half goes through shared
+      // memory to slot 0's epilogue warps, which fold it into slot 0's half
+      // and write the output. The softmax warps meanwhile run the next item
+      // into the slot's other O buffer.
       const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
-      const int row = lane;
+      const int row = erow0 + lane;
+      const bool live = row < p.tokens;
       for (int it = 0; ok && 2 * it + es < n_units; ++it) {
         const int e = 2 * es + (it & 1);
         ok = __all_sync(0xffffffffu, mbar_wait_bounded(&o_final[e], (it >> 1) & 1));
         ok = ok && __all_sync(0xffffffffu, mbar_wait_bounded(&ml_full[e], (it >> 1) & 1));
         if (!ok) break;
         tc_fence_after();
-        const float2 mine = lane < 8 ? ml[8 * e + lane] : make_float2(0.f, 0.f);
+        const float2 mine = live ? ml[kSplitRows * e + row] : make_float2(0.f, 0.f);
         float o[64];
         tmem_ld32(tmem + lane_bits + col_o(es) + 64 * (it & 1), o);
         tmem_ld32(tmem + lane_bits + col_o(es) + 64 * (it & 1) + 32, o + 32);
         if (es == 1) {
-          // Second half: rows' unnormalised O and (max, sum) to warp 8 once it
-          // has read the previous item's.
+          // Second half: rows' unnormalised O and (max, sum) to slot 0's
+          // epilogue warps once they have read the previous item's.
           if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(xch_empty, (it - 1) & 1));
           if (!ok) break;
-          if (lane < 8) {
+          if (live) {
 #pragma unroll
             for (int i = 0; i < 64; i += 4)
-              *reinterpret_cast<float4*>(xch_o + lane * kXchStride + i) =
+              *reinterpret_cast<float4*>(xch_o + row * kXchStride + i) =
                   make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-            xch_ml[lane] = mine;
+            xch_ml[row] = mine;
           }
           tc_fence_before();
           __syncwarp();
@@ -400,12 +418,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // First half: fold the second half's rows in and write the output.
         ok = __all_sync(0xffffffffu, mbar_wait_bounded(xch_full, it & 1));
         if (!ok) break;
-        const float2 other = lane < 8 ? xch_ml[lane] : make_float2(0.f, 0.f);
-        const float m = fmaxf(mine.x, other.x);
-        const float a0 = fast_exp2(mine.x - m), a1 = fast_exp2(other.x - m);
-        const float inv = 1.f / (mine.y * a0 + other.y * a1);
-        const float b0 = a0 * inv, b1 = a1 * inv;
-        if (row < p.tokens) {
+        if (live) {
+          const float2 other = xch_ml[row];
+          const float m = fmaxf(mine.x, other.x);
+          const float a0 = fast_exp2(mine.x - m), a1 = fast_exp2(other.x - m);
+          const float inv = 1.f / (mine.y * a0 + other.y * a1);
+          const float b0 = a0 * inv, b1 = a1 * inv;
           const int index = item_index(2 * it);
           const int h = index % p.heads, w = index / p.heads;
           __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
@@ -413,8 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                static_cast<int64_t>(h) * p.o_sh;
 #pragma unroll
           for (int i = 0; i < 64; i += 8) {
-            const float4 f0 = *reinterpret_cast<const float4*>(xch_o + lane * kXchStride + i);
-            const float4 f1 = *reinterpret_cast<const float4*>(xch_o + lane * kXchStride + i + 4);
+            const float4 f0 = *reinterpret_cast<const float4*>(xch_o + row * kXchStride + i);
+            const float4 f1 = *reinterpret_cast<const float4*>(xch_o + row * kXchStride + i + 4);
             uint4 u;
             u.x = bf16x2(o[i] * b0 + f0.x * b1, o[i + 1] * b0 + f0.y * b1);
             u.y = bf16x2(o[i + 2] * b0 + f0.z * b1, o[i + 3] * b0 + f0.w * b1);
@@ -582,15 +600,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         // Small prompt: row t's max and sum are held by lanes 4t .. 4t + 3.
         const float l_row = kSmall ? __shfl_sync(0xffffffffu, l, lane < 8 ? 4 * lane : lane) : l;
-        if (kSmall && p.split) {
-          // The epilogue warp takes over: each row's (max, sum) for this O
-          // buffer, once it has read those of the item two back.
-          const float m_row = __shfl_sync(0xffffffffu, m_used, lane < 8 ? 4 * lane : lane);
+        if (p.split) {
+          // The epilogue warps take over: each row's (max, sum) for this O
+          // buffer, once they have read those of the item two back.
+          const float m_row =
+              kSmall ? __shfl_sync(0xffffffffu, m_used, lane < 8 ? 4 * lane : lane) : m_used;
           const int e = 2 * slot + ob;
           if (it >= 2)
             ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ml_empty[e], ((it >> 1) - 1) & 1));
           if (!ok) break;
-          if (lane < 8) ml[8 * e + lane] = make_float2(m_row, l_row);
+          if (!kSmall || lane < 8) ml[kSplitRows * e + row] = make_float2(m_row, l_row);
           __syncwarp();
           if (lane == 0) mbar_arrive(&ml_full[e]);
           continue;
@@ -713,11 +732,10 @@ int whisper_cross_prefix_tc(int windows, int tokens, int heads, int length, cons
                          windows, length, c_sb, c_sh))
     return rc;
   const int softmax_warps = (tokens + 31) / 32;
-  // Prompts of up to 8 rows over an even number (2 or more) of key tiles run
-  // each item as two halves, one per slot, merged in the CTA: the two slots
-  // then share every item, so a CTA's last item does not run alone.
+  // Prompts of up to kSplitRows rows over an even number (2 or more) of key
+  // tiles run each item as two halves, one per slot, merged in the CTA.
   const int n_tiles = (length + kKeys - 1) / kKeys;
-  const int split = tokens <= 8 && n_tiles >= 2 && n_tiles % 2 == 0 ? 1 : 0;
+  const int split = tokens <= kSplitRows && n_tiles >= 2 && n_tiles % 2 == 0 ? 1 : 0;
   PrefixParams p{out,
                  o_st,
                  o_sh,
