@@ -59,8 +59,8 @@ constexpr int kKeys = 128;  // keys per tile
 constexpr int kDim = 64;
 constexpr int kStages = 5;
 constexpr int kTileBytes = kRows * kDim * 2;  // 16 KB: a Q, K or V tile
-constexpr int kThreads = 12 * 32;             // warps 0-3 control (2, 3 idle), 4-11 softmax
-constexpr int kTmemCols = 512;                // 384 used; allocations are powers of two
+constexpr int kThreads = 12 * 32;  // warps 0-3 control (2, 3 idle), 4-11 softmax and epilogue
+constexpr int kTmemCols = 512;     // per slot: S 128 + two O buffers of 64
 __host__ __device__ constexpr int col_s(int x) { return 256 * x; }
 __host__ __device__ constexpr int col_o(int x) { return 256 * x + 128; }  // + 64: split's 2nd
 constexpr float kRescaleThreshold = 8.0f;
@@ -72,7 +72,7 @@ constexpr int kSoftmaxRegs = 224;
 static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs,
               "register split exceeds the launch's register pool");
 
-constexpr int kOffQ = 0;  // a Q buffer per slot
+constexpr int kOffQ = 0;  // two Q buffers: one per slot, or (split items) per item parity
 constexpr int kOffK = 2 * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
 // Split items (prompts of up to kSplitRows rows): slot 1 hands its half's
@@ -173,7 +173,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int e = 0; e < 4; ++e) {
       mbar_init(&o_final[e], 1);
-      // Split items: the epilogue warp frees O; otherwise each softmax warp.
       // Split items: the slot's epilogue warps free O (as many as it has
       // softmax warps); otherwise each softmax warp.
       mbar_init(&o_free[e], p.softmax_warps);
@@ -349,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     reg_acquire<kSoftmaxRegs>();
-    // ---------------- softmax and output (one query row per thread) ----------------
+    // ---------------- softmax, epilogue and output ----------------
     const int slot = (warp - 4) >> 2;
     const int quarter = warp & 3;
     // Slot 1's prompt rows start at row1 of its tile (a lane quarter of
